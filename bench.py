@@ -1,0 +1,547 @@
+#!/usr/bin/env python
+"""Layer-op chain benchmark: tokens/s and achieved HBM GB/s on B200.
+
+One step = the whole non-GEMM op chain of one decoder forward step
+(embedding; per layer add+RMSNorm, fused bias+RoPE+KV append, add+RMSNorm,
+SwiGLU; final add+RMSNorm; select_last_rows) over one batch of seeded
+synthetic inputs, launched by the native chain executor and replayed as a CUDA
+graph. Default workload: Qwen2.5-0.5B shapes, 8 sequences x 512 tokens = 4096
+tokens per GPU, 24 layers, KV cache [24, 2, 8, 2, 4096, 64] fp16.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU)
+    python bench.py --impl reference ...   (the reference CPU implementation)
+
+Rank 0 prints one JSON line. `value` is whole-job tokens/s from CUDA-event
+device time, max over ranks; `e2e` is the same metric through the C ABI with
+the step's inputs copied from pinned host memory and the result copied back
+inside the timed region; `roofline` is the dominant kernel (SwiGLU) timed
+alone over its per-layer buffers; `cpu_baseline` times the reference's own
+CPU operators (compiled from its sources, oracle/_ref) on a bounded sample.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from datetime import timedelta
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "layer-op tokens/s"
+UNIT = "tokens/s"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="qwen_prefill")
+    ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample length")
+    ap.add_argument("--settle-seconds", type=float, default=1.5,
+                    help="untimed graph replays before timing so clocks settle under load")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# environment / distributed plumbing
+# ---------------------------------------------------------------------------
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def load_peaks() -> dict:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": float(p["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def ncu_traffic(kernel: str, workload: str):
+    """dram bytes per launch of `kernel` from the committed ncu summary
+    (profiles/<kernel>_<workload>.txt, a line `traffic_bytes_per_launch: N`),
+    or None when no capture has been summarised."""
+    path = os.path.join(ROOT, "profiles", f"{kernel}_{workload}.txt")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        for line in f:
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(float(line.split(":", 1)[1]))
+    return None
+
+
+class ClockSampler:
+    """Samples SM clock, power and throttle reasons of one GPU with nvidia-smi
+    every 200 ms while running."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, torch_device):
+        import torch
+        p = torch.cuda.get_device_properties(torch_device)
+        self.bus = f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
+        self.proc = None
+        self.lines: list[str] = []
+        self._t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self.bus, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self._t = threading.Thread(target=self._read, daemon=True)
+        self._t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self._t.join(timeout=5)
+        sm, mx, power, reasons = [], [], [], set()
+        for line in self.lines:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+                power.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(self.REASONS, parts[4:8]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm), "power_w_max": max(power)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's own CPU operators (oracle/_ref), or the oracle port
+# ---------------------------------------------------------------------------
+
+
+def time_reference_cpu(model, tokens: int, threads: int, seconds: float, steps: int | None = None,
+                       warmup: int = 0):
+    """Runs the reference's non-GEMM chain (all layers of `model`) on one
+    sequence of `tokens` tokens per thread, `threads` threads in parallel,
+    through the reference's public kllm::op API on fp32 CPU tensors.
+    Returns (tokens/s, per-step seconds list, kind)."""
+    import ctypes
+    from concurrent.futures import ThreadPoolExecutor
+
+    from oracle.oracle import Reference, reference_available
+    if not reference_available():
+        return time_oracle_port(model, tokens, seconds)
+    ref = Reference()
+    lib = ref.lib
+    table = lib.kref_table_create(model.vocab, model.hidden, 0x4B4C4C4D)
+    if not table:
+        raise RuntimeError(lib.kref_last_error().decode())
+    chains = []
+    for i in range(threads):
+        c = lib.kref_chain_create(table, tokens, model.n_heads, model.n_kv_heads, model.head_dim,
+                                  model.intermediate, max(tokens, 512), ctypes.c_float(model.eps),
+                                  ctypes.c_float(model.theta), 1000 + i)
+        if not c:
+            raise RuntimeError(lib.kref_last_error().decode())
+        chains.append(c)
+
+    def one(c):
+        rc = lib.kref_chain_run(c, model.n_layers)
+        if rc != 0:
+            raise RuntimeError(lib.kref_last_error().decode())
+
+    step_times = []
+    with ThreadPoolExecutor(threads) as ex:
+        for _ in range(warmup):
+            list(ex.map(one, chains))
+        t_start = time.perf_counter()
+        while True:
+            t0 = time.perf_counter()
+            list(ex.map(one, chains))
+            step_times.append(time.perf_counter() - t0)
+            if steps is not None and len(step_times) >= steps:
+                break
+            if steps is None and time.perf_counter() - t_start >= seconds:
+                break
+    for c in chains:
+        lib.kref_chain_destroy(c)
+    lib.kref_table_destroy(table)
+    total = sum(step_times)
+    return threads * tokens * len(step_times) / total, step_times, "reference"
+
+
+def time_oracle_port(model, tokens: int, seconds: float):
+    """Fallback when oracle/_ref is absent: the oracle restatement of the same
+    chain, single-threaded."""
+    import numpy as np
+
+    from oracle.oracle import Oracle
+    o = Oracle()
+    rng = np.random.default_rng(0)
+    H, D = model.hidden, model.head_dim
+    table = rng.normal(0, 0.02, (model.vocab, H)).astype(np.float32)
+    ids = rng.integers(0, model.vocab, tokens).astype(np.int32)
+    q = rng.standard_normal((tokens, model.n_heads, D)).astype(np.float32)
+    k = rng.standard_normal((tokens, model.n_kv_heads, D)).astype(np.float32)
+    x = rng.standard_normal((tokens, H)).astype(np.float32)
+    g = rng.standard_normal((tokens, model.intermediate)).astype(np.float32)
+    w = np.ones(H, np.float32)
+    steps = []
+    t_start = time.perf_counter()
+    while time.perf_counter() - t_start < seconds or not steps:
+        t0 = time.perf_counter()
+        res = o.embedding(table, ids)
+        for _ in range(model.n_layers):
+            o.rms_norm(res, w, model.eps)
+            o.rope(q, 0, model.theta)
+            o.rope(k, 0, model.theta)
+            res = o.add(res, x)
+            o.rms_norm(res, w, model.eps)
+            o.silu_mul(g, g)
+            res = o.add(res, x)
+        o.rms_norm(res, w, model.eps)
+        steps.append(time.perf_counter() - t0)
+    return tokens * len(steps) / sum(steps), steps, "port"
+
+
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+# ---------------------------------------------------------------------------
+# reference arm
+# ---------------------------------------------------------------------------
+
+
+def run_reference(args):
+    from littlellm_b200.chain import WORKLOADS
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    w = WORKLOADS[args.workload]
+    threads = host_threads()
+    tokens = 128
+    value, steps, kind = time_reference_cpu(w.model, tokens, threads, 0.0, steps=args.steps,
+                                            warmup=args.warmup)
+    ms = 1000.0 * statistics.mean(steps)
+    sample = (f"{threads} threads x one {tokens}-token sequence each through all {w.model.n_layers} layers "
+              f"of the {w.model.name} non-GEMM chain per step (fp32 CPU tensors, kllm::op API)")
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak" if args.workload == "qwen_prefill" else "strong", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
+        "config": {"workload": w.name, "model": w.model.name, "layers": w.model.n_layers,
+                   "tokens_per_step": threads * tokens, "impl_detail": "reference CPU operators (src/op/cpu)"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind, "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+
+def time_graph(g, stream, reps: int) -> float:
+    """ms per replay of a CUDA graph, CUDA events on its stream."""
+    import torch
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(reps):
+            g.replay()
+        end.record(stream)
+    end.synchronize()
+    return start.elapsed_time(end) / reps
+
+
+def capture(fn, stream):
+    import torch
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        fn()
+    return g
+
+
+def per_op_timing(runner, stream, reps: int) -> dict:
+    """Each op kind timed alone: one graph of that op over all layers' buffers
+    (several GB, larger than L2), replayed `reps` times."""
+    import torch
+
+    from littlellm_b200 import ops
+    w, m = runner.w, runner.w.model
+    T, H, D = w.n_tokens, m.hidden, m.head_dim
+    L = runner.layers
+    eps, theta = m.eps, m.theta
+
+    # distinct ids per launch so table rows are not re-read from L2
+    gen = torch.Generator(device=runner.device)
+    gen.manual_seed(7)
+    ids = [torch.randint(0, m.vocab, (T,), generator=gen, device=runner.device, dtype=torch.int32) for _ in L]
+
+    def embed():
+        for layer, idx in zip(L, ids):
+            ops.embedding(runner.table, idx, out=layer["attn_norm_out"])
+
+    def norm():
+        # per-layer residual buffers (attn_norm_out stands in), so no launch
+        # re-reads another's data from L2
+        for layer in L:
+            ops.add_rms_norm(layer["attn_norm_out"], layer["attn_out"], layer["post_norm_w"], eps,
+                             out=layer["ffn_norm_out"])
+
+    def qkv():
+        for layer in L:
+            ops.qkv_bias_rope_kv_append(layer["q"].view(T, m.n_heads, D), layer["k"].view(T, m.n_kv_heads, D),
+                                        layer["v"].view(T, m.n_kv_heads, D), layer["q_bias"], layer["k_bias"],
+                                        layer["v_bias"], runner.positions, runner.slots, theta,
+                                        layer["k_cache"], layer["v_cache"], runner.err_flags)
+
+    def silu():
+        for layer in L:
+            ops.silu_mul(layer["gate"], layer["up"], out=layer["swiglu_out"])
+
+    qkv_bytes = 2 * T * (m.n_heads + 2 * m.n_kv_heads) * D * 2 + 8 * T
+    table = {
+        "embedding": (embed, 2 * T * H * 2 + 4 * T),
+        "add_rms_norm": (norm, 4 * T * H * 2),
+        "qkv_bias_rope_kv_append": (qkv, qkv_bytes),
+        "silu_mul": (silu, 3 * T * m.intermediate * 2),
+    }
+    out = {}
+    with torch.cuda.stream(stream):
+        for name, (fn, nbytes) in table.items():
+            fn()  # warm (occupancy caches, clocks)
+            g = capture(fn, stream)
+            g.replay()
+            ms = time_graph(g, stream, reps) / len(L)
+            out[name] = {"us_per_launch": ms * 1000.0, "bytes_per_launch": nbytes,
+                         "gbs": nbytes / (ms * 1e-3) / 1e9}
+            del g
+    return out
+
+
+def run_ours(args):
+    import torch
+
+    from littlellm_b200 import build as kbuild
+    from littlellm_b200.chain import WORKLOADS, ChainRunner, chain_bytes, shard
+
+    world, rank, local = dist_env()
+    if world != args.gpus:
+        if world == 1 and args.gpus > 1:
+            raise SystemExit("--gpus N > 1 must be launched with torchrun (one rank per GPU)")
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA GPU")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    kbuild.build()
+
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=300))
+
+    base = WORKLOADS[args.workload]
+    weak = args.workload == "qwen_prefill"
+    w = base if weak else shard(base, rank, world)
+    runner = ChainRunner(w, device=device, seed=1000 + rank, use_pdl=not args.no_pdl)
+    stream = torch.cuda.Stream(device)
+    torch.cuda.synchronize(device)
+
+    # one chain step = one CUDA graph replay
+    launches = runner.run(stream)
+    stream.synchronize()
+    graph = capture(lambda: runner.run(stream), stream)
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    stream.synchronize()
+
+    sampler = ClockSampler(device)
+    sampler.start()
+    # let clocks settle under load (untimed)
+    t_end = time.perf_counter() + args.settle_seconds
+    while time.perf_counter() < t_end:
+        for _ in range(20):
+            graph.replay()
+        stream.synchronize()
+
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.steps):
+        graph.replay()
+    end.record(stream)
+    end.synchronize()
+    torch.cuda.synchronize(device)
+    if dist is not None:
+        dist.barrier()
+    elapsed_ms = start.elapsed_time(end)
+    t = torch.tensor([elapsed_ms], dtype=torch.float64, device=device)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    clocks = sampler.stop()
+
+    ms_per_step = max_ms / args.steps
+    tokens_total = w.n_tokens * world
+    value = tokens_total / (ms_per_step * 1e-3)
+    bytes_step = chain_bytes(w)
+    chain_gbs = bytes_step["total"] / (ms_per_step * 1e-3) / 1e9
+    peaks = load_peaks()
+
+    # dominant kernel and per-op breakdown, each op alone
+    op_stats = per_op_timing(runner, stream, max(args.steps, 5))
+    silu = op_stats["silu_mul"]
+    roofline = {
+        "bound": "hbm", "kernel": "silu_mul_f16_kernel", "achieved": silu["gbs"], "peak": peaks["hbm_gbs"],
+        "unit": "GB/s", "frac": silu["gbs"] / peaks["hbm_gbs"],
+        "traffic": ncu_traffic("silu_mul", w.name), "peak_source": peaks["source"],
+        "bytes_per_launch": silu["bytes_per_launch"], "us_per_launch": silu["us_per_launch"],
+    }
+    for s in op_stats.values():
+        s["frac_of_measured"] = s["gbs"] / peaks["hbm_gbs"]
+
+    # end to end through the C ABI with host buffers
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(runner, stream, args.steps, device, dist, world)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = 1
+        tokens = 128
+        v, steps, kind = time_reference_cpu(w.model, tokens, threads, args.cpu_seconds)
+        cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": kind,
+               "sample": f"one {tokens}-token sequence through all {w.model.n_layers} layers of the "
+                         f"{w.model.name} non-GEMM chain, repeated {len(steps)}x "
+                         f"({sum(steps):.1f} s), fp32, single thread (the reference CPU path is single-threaded)"}
+
+    del graph
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "weak" if weak else "strong", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic",
+            "config": {
+                "workload": w.name, "model": w.model.name, "layers": w.model.n_layers,
+                "tokens_per_gpu": w.n_tokens, "sequences_per_gpu": w.n_seqs, "seq_len": w.seq_len,
+                "kv_cache": [w.model.n_layers, 2, w.n_seqs, w.model.n_kv_heads, w.max_seq, w.model.head_dim],
+                "parallelism": f"dp{world} (sequences split, no collective on the path)",
+                "math": "fp16 storage, fp32 arithmetic",
+                "l2": "no flush: each step streams %.2f GB of distinct per-layer buffers (>> 126 MB L2)"
+                      % (bytes_step["total"] / 1e9),
+                "pdl": not args.no_pdl, "cuda_graph": True,
+            },
+            "hbm_gbs_chain": chain_gbs,
+            "hbm_frac_chain": chain_gbs / peaks["hbm_gbs"],
+            "chain_bytes_per_step": bytes_step["total"],
+            "roofline": roofline,
+            "ops": op_stats,
+            "clocks": clocks,
+            "gpu_launches": launches * args.steps,
+            "launches_per_step": launches,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_e2e(runner, stream, steps: int, device, dist, world: int) -> dict:
+    """tokens/s through the C ABI with host buffers: every step copies its
+    inputs (ids, positions, slots, each layer's GEMM outputs) from pinned host
+    memory, runs the chain and copies the result (last rows) back."""
+    import torch
+    inputs = runner.step_inputs()
+    hosts = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in inputs]
+    for h, t in zip(hosts, inputs):
+        h.copy_(t.cpu())
+    result_host = torch.empty(runner.last_rows.shape, dtype=runner.last_rows.dtype, pin_memory=True)
+    h2d = sum(t.numel() * t.element_size() for t in inputs)
+    d2h = runner.last_rows.numel() * runner.last_rows.element_size()
+
+    def step():
+        for h, t in zip(hosts, inputs):
+            t.copy_(h, non_blocking=True)
+        runner.run(stream)
+        result_host.copy_(runner.last_rows, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            step()
+        stream.synchronize()
+        if dist is not None:
+            dist.barrier()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(steps):
+            step()
+        end.record(stream)
+        end.synchronize()
+    ms = start.elapsed_time(end)
+    t = torch.tensor([ms], dtype=torch.float64, device=device)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_step = float(t.item()) / steps
+    return {"value": runner.w.n_tokens * world / (ms_step * 1e-3), "unit": UNIT, "ms_per_step": ms_step,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "path": "pinned host -> cudaMemcpyAsync -> kllm_b200_chain_run -> last rows -> pinned host"}
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,247 @@
+/*
+ * kllm_b200.h — C ABI of the B200 (sm_100a) backend for LittleLLM's non-GEMM
+ * decoder-layer operators.
+ *
+ * Every entry point takes plain device pointers, element counts, scalar
+ * parameters and a CUDA stream handle (passed as `void*`; NULL means the
+ * legacy default stream, which is what the reference backend uses). Nothing
+ * here allocates device memory, synchronises the host, or keeps per-call
+ * state: every call is stream-ordered and re-entrant.
+ *
+ * Return value: KLLM_B200_OK (0) or a negative KLLM_B200_ERR_* code. The text
+ * of the most recent failure on the calling thread is returned by
+ * kllm_b200_last_error(). A C++ caller turns a non-zero code into
+ * std::runtime_error, the same convention the reference uses for CUDA errors
+ * (include/kllm/op/detail/cuda_helpers.cuh:11-15).
+ *
+ * Element types use the reference's DType numbering
+ * (include/kllm/base/tensor.h:13-18): F32 = 0, F16 = 1, I32 = 2, I8 = 3.
+ *
+ * Values that only the device can check (token ids, positions, cache slots
+ * held in device memory) are checked in the kernel: an offending row is
+ * skipped (embedding rows are zero-filled) and, when the caller passes a
+ * device word `err_flags`, the matching KLLM_B200_FLAG_* bit is OR-ed into it.
+ * No kernel traps, asserts or spins.
+ */
+#ifndef KLLM_B200_H_
+#define KLLM_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- element types (reference DType, include/kllm/base/tensor.h:13-18) ---- */
+enum {
+  KLLM_B200_F32 = 0,
+  KLLM_B200_F16 = 1,
+  KLLM_B200_I32 = 2,
+  KLLM_B200_I8 = 3
+};
+
+/* ---- status codes ---- */
+enum {
+  KLLM_B200_OK = 0,
+  KLLM_B200_ERR_INVALID_ARG = -1, /* null pointer where one is required, negative size */
+  KLLM_B200_ERR_SHAPE = -2,       /* inconsistent or unsupported shape */
+  KLLM_B200_ERR_DTYPE = -3,       /* unsupported element-type combination */
+  KLLM_B200_ERR_ALIGN = -4,       /* pointer alignment a kernel requires is not met */
+  KLLM_B200_ERR_RANGE = -5,       /* host-visible id / position out of range */
+  KLLM_B200_ERR_CAPACITY = -6,    /* KV cache capacity exceeded */
+  KLLM_B200_ERR_CUDA = -7         /* CUDA runtime / launch error */
+};
+
+/* ---- bits OR-ed into the optional device word `err_flags` ---- */
+enum {
+  KLLM_B200_FLAG_BAD_TOKEN = 1,    /* embedding id outside [0, vocab) */
+  KLLM_B200_FLAG_BAD_POSITION = 2, /* RoPE/KV position outside [0, max_seq) */
+  KLLM_B200_FLAG_BAD_SLOT = 4,     /* KV cache slot outside [0, n_slots) */
+  KLLM_B200_FLAG_BAD_SEQ_END = 8   /* select_last_rows end index outside [1, rows] */
+};
+
+/* Copies the calling thread's most recent error message into buf (always
+ * NUL-terminated when len > 0). Returns the full message length. */
+size_t kllm_b200_last_error(char* buf, size_t len);
+
+/* Static text for a status code. */
+const char* kllm_b200_status_string(int status);
+
+/* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
+int kllm_b200_version(void);
+
+/* ======================================================================== *
+ *  Reference-compatible operators (same semantics as kllm::op::cuda_*)      *
+ * ======================================================================== */
+
+/* out[t, :] = table[ids[t], :].
+ * Replaces cuda_embedding (src/op/cuda/embedding.cu:83-108); the reference
+ * copies host ids with a blocking cudaMemcpy on every call, here `ids` is
+ * already a device array of n_tokens int32. table_dtype/out_dtype in {F32,F16};
+ * equal dtypes are a bit-exact copy, mixed dtypes convert (F32->F16 rounds to
+ * nearest even, like the reference kernel's __float2half). Ids outside
+ * [0, vocab) zero-fill the row and set KLLM_B200_FLAG_BAD_TOKEN. */
+int kllm_b200_embedding(const void* table, int64_t vocab, int64_t hidden, int table_dtype,
+                        const int32_t* ids, int64_t n_tokens, void* out, int out_dtype,
+                        int32_t* err_flags, void* stream);
+
+/* out = x * (mean(x^2) + eps)^-1/2 * weight, per row of `hidden` elements.
+ * Replaces cuda_rms_norm (src/op/cuda/rms_norm.cu:177-188). x/out share
+ * act_dtype in {F32,F16}; weight_dtype in {F32,F16}; fp32 accumulation. */
+int kllm_b200_rms_norm(const void* x, const void* weight, void* out, int64_t rows,
+                       int64_t hidden, float eps, int act_dtype, int weight_dtype,
+                       void* stream);
+
+/* x[i] += y[i] for n elements (add_inplace, src/op/cuda/add.cu:71-76).
+ * x_dtype, y_dtype in {F32,F16}. */
+int kllm_b200_add_inplace(void* x, const void* y, int64_t n, int x_dtype, int y_dtype,
+                          void* stream);
+
+/* x[r, c] += bias[c] for a [rows, cols] matrix (add_bias_inplace,
+ * src/op/cuda/add.cu:59-69). A NULL bias is a no-op, as in the reference. */
+int kllm_b200_add_bias_inplace(void* x, const void* bias, int64_t rows, int64_t cols,
+                               int x_dtype, int bias_dtype, void* stream);
+
+/* out[0, :] = x[rows-1, :] (select_last_row, src/op/cuda/add.cu:78-84). */
+int kllm_b200_select_last_row(const void* x, int64_t rows, int64_t cols, void* out,
+                              int dtype, void* stream);
+
+/* out = silu(gate) * up = gate * sigmoid(gate) * up, n elements
+ * (silu_mul, src/op/cuda/silu.cu:30-36). All three share dtype in {F32,F16}. */
+int kllm_b200_silu_mul(const void* gate, const void* up, void* out, int64_t n, int dtype,
+                       void* stream);
+
+/* Rotate-half RoPE in place on x[seq, heads, head_dim] at positions
+ * past_len + t, angle = pos * theta^(-2d/head_dim)
+ * (rope_inplace, src/op/cuda/rope.cu:188-201). head_dim must be even. */
+int kllm_b200_rope_inplace(void* x, int64_t seq, int64_t heads, int64_t head_dim,
+                           int32_t past_len, float theta, int dtype, void* stream);
+
+/* k_cache[past_len + t, :, :] = k[t, :, :], same for v, with caches laid out
+ * [max_seq, kv_heads, head_dim] (copy_kv_to_cache,
+ * src/op/cuda/kv_cache.cu:32-41). Fails with KLLM_B200_ERR_CAPACITY when
+ * past_len + seq > max_seq, as the reference CPU path does
+ * (src/op/cpu/kv_cache.cpp:19-21). One launch covers K and V. */
+int kllm_b200_copy_kv_to_cache(const void* k, const void* v, int64_t seq, int64_t kv_heads,
+                               int64_t head_dim, void* k_cache, void* v_cache,
+                               int64_t max_seq, int32_t past_len, int src_dtype,
+                               int cache_dtype, void* stream);
+
+/* INT8 per-tensor dequantisation: out[i] = q[i] * scale[0].
+ *  - out_dtype F32: the reference GPU op (src/op/cuda/quantize.cu:110-121).
+ *  - out_dtype F16: the reference weight-load path
+ *    (src/model/weights.cpp:139-148): the product is formed in fp32 and
+ *    rounded with the reference's own float_to_half (src/base/half.cpp:38-61),
+ *    bit for bit, including its tie and carry behaviour.
+ * `scale` points to one float in device memory. */
+int kllm_b200_dequantize_int8(const int8_t* data, const float* scale, void* out, int64_t n,
+                              int out_dtype, void* stream);
+
+/* ======================================================================== *
+ *  Fused / batched operators (additive to include/kllm/op/ops.h)           *
+ * ======================================================================== */
+
+/* Residual add fused with RMSNorm, the pair at src/model/llama.cpp:135-143
+ * (and :166 -> :83 across layers, :176 at the end):
+ *     residual[r, :] = fp16(residual[r, :] + delta[r, :])   (stored)
+ *     out[r, :]      = residual[r, :] * (mean(residual^2) + eps)^-1/2 * weight
+ * The norm reads the stored (rounded) residual, exactly as the reference's
+ * separate add_inplace then rms_norm do. delta == NULL gives a plain RMSNorm
+ * of `residual` (left unmodified). act_dtype in {F32,F16}. */
+int kllm_b200_add_rms_norm(void* residual, const void* delta, const void* weight, void* out,
+                           int64_t rows, int64_t hidden, float eps, int act_dtype,
+                           int weight_dtype, void* stream);
+
+/* q/k/v bias add + rotate-half RoPE + KV-cache append, one launch.
+ * Replaces, per layer, add_bias_inplace x3 (src/model/llama.cpp:89-106 via
+ * :22), rope_inplace x2 (:111-112) and copy_kv_to_cache (:114).
+ *   q  [n_tokens, n_heads,    head_dim] fp16, rotated in place (after +bq)
+ *   k  [n_tokens, n_kv_heads, head_dim] fp16, read only
+ *   v  [n_tokens, n_kv_heads, head_dim] fp16, read only
+ *   bq/bk/bv: [heads*head_dim] biases of bias_dtype (F32/F16), each may be NULL
+ *   positions[t], slots[t]: device int32 per token (position in its sequence,
+ *       sequence slot in the cache)
+ *   k_cache, v_cache: this layer's planes, [n_slots, n_kv_heads, max_seq,
+ *       head_dim] fp16 (the [layer, k/v, slot, kv_head, max_seq, head_dim]
+ *       cache indexed at one layer).
+ * Written: q (rotated), k_cache[slot, h, pos, :] = rope(k + bk),
+ * v_cache[slot, h, pos, :] = fp16(v + bv). The biased values are rounded to
+ * fp16 before the rotation, as the reference's separate bias-add writes them.
+ * Tokens with an out-of-range position or slot skip the cache write and set
+ * KLLM_B200_FLAG_BAD_POSITION / _BAD_SLOT in *err_flags (if given).
+ * head_dim must be even and at most 256. */
+int kllm_b200_qkv_bias_rope_kv_append(void* q, const void* k, const void* v, const void* bq,
+                                      const void* bk, const void* bv, int bias_dtype,
+                                      const int32_t* positions, const int32_t* slots,
+                                      int64_t n_tokens, int64_t n_heads, int64_t n_kv_heads,
+                                      int64_t head_dim, float theta, void* k_cache,
+                                      void* v_cache, int64_t n_slots, int64_t max_seq,
+                                      int32_t* err_flags, void* stream);
+
+/* Batched select_last_row (src/op/cuda/add.cu:78-84, called at
+ * src/model/llama.cpp:178): out[b, :] = x[end_b - 1, :] with
+ * end_b = seq_ends[b] when seq_ends (device int32[n_seqs]) is given, else
+ * end_b = (b + 1) * seq_len. Out-of-range ends zero-fill the row and set
+ * KLLM_B200_FLAG_BAD_SEQ_END. */
+int kllm_b200_select_last_rows(const void* x, int64_t rows, int64_t cols,
+                               const int32_t* seq_ends, int64_t seq_len, int64_t n_seqs,
+                               void* out, int dtype, int32_t* err_flags, void* stream);
+
+/* ======================================================================== *
+ *  Layer-op chain executor                                                  *
+ * ======================================================================== */
+
+/* Per-layer buffers of the non-GEMM chain of LlamaRunner::forward
+ * (src/model/llama.cpp:81-168). The GEMM outputs (q, k, v, attn_out, gate,
+ * up, ffn_out) are inputs here; the norm / SwiGLU outputs feed the GEMMs. */
+typedef struct kllm_b200_layer_buffers {
+  void* q;                   /* [T, n_heads*head_dim] fp16, rotated in place */
+  const void* k;             /* [T, n_kv_heads*head_dim] fp16 */
+  const void* v;             /* [T, n_kv_heads*head_dim] fp16 */
+  const void* q_bias;        /* [n_heads*head_dim] or NULL */
+  const void* k_bias;        /* [n_kv_heads*head_dim] or NULL */
+  const void* v_bias;        /* [n_kv_heads*head_dim] or NULL */
+  const void* attn_out;      /* [T, hidden] o_proj output */
+  const void* ffn_out;       /* [T, hidden] down_proj output */
+  const void* gate;          /* [T, intermediate] */
+  const void* up;            /* [T, intermediate] */
+  const void* input_norm_w;  /* [hidden] */
+  const void* post_norm_w;   /* [hidden] */
+  void* attn_norm_out;       /* [T, hidden] */
+  void* ffn_norm_out;        /* [T, hidden] */
+  void* swiglu_out;          /* [T, intermediate] */
+  void* k_cache;             /* [n_slots, n_kv_heads, max_seq, head_dim] */
+  void* v_cache;             /* [n_slots, n_kv_heads, max_seq, head_dim] */
+} kllm_b200_layer_buffers;
+
+typedef struct kllm_b200_chain {
+  int64_t n_tokens, hidden, n_heads, n_kv_heads, head_dim, intermediate, vocab;
+  int64_t n_layers, n_slots, max_seq, n_seqs, seq_len;
+  float eps, theta;
+  int weight_dtype;               /* F16 or F32 for norm weights and biases */
+  int use_pdl;                    /* launch with programmatic dependent launch */
+  const void* embed_table;        /* [vocab, hidden] fp16 */
+  const int32_t* ids;             /* [T] device */
+  const int32_t* positions;       /* [T] device */
+  const int32_t* slots;           /* [T] device */
+  const int32_t* seq_ends;        /* [n_seqs] device, or NULL for uniform seq_len */
+  void* residual;                 /* [T, hidden] fp16 running residual stream */
+  const void* final_norm_w;       /* [hidden] */
+  void* final_norm_out;           /* [T, hidden] */
+  void* last_rows;                /* [n_seqs, hidden] */
+  const kllm_b200_layer_buffers* layers; /* host array of n_layers entries */
+  int32_t* err_flags;             /* device word or NULL */
+} kllm_b200_chain;
+
+/* Launches the whole non-GEMM chain on `stream`: embedding, then per layer
+ * add+RMSNorm, fused bias+RoPE+KV append, add+RMSNorm, SwiGLU, then the final
+ * add+RMSNorm and select_last_rows. *n_launches (if given) receives the
+ * number of kernels launched. Can be captured into a CUDA graph. */
+int kllm_b200_chain_run(const kllm_b200_chain* chain, int* n_launches, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KLLM_B200_H_ */

@@ -1,0 +1,199 @@
+"""The non-GEMM layer-op chain of a decoder forward step on one GPU.
+
+``ChainRunner`` owns the device buffers of one step of LlamaRunner::forward's
+non-GEMM work (src/model/llama.cpp:78-178) for a model shape and a batch, fills
+them with seeded synthetic data (GEMM outputs ~N(0,1), norm weights
+~U(0.5,1.5), biases and the embedding table ~N(0,0.02)) and launches the whole
+chain through ``kllm_b200_chain_run``. Every layer has its own input and output
+buffers, so one step streams its whole working set (several GB) and nothing is
+served from the 126 MB L2 across layers or steps.
+
+Model shapes and workloads are the ones the benchmark is quoted on:
+Qwen2.5-0.5B (hidden 896, 14/2 heads x 64, intermediate 4864, vocab 151936,
+24 layers, eps 1e-6, theta 1e6) and Llama-2-7B (4096, 32/32 x 128, 11008,
+32000, 32 layers, eps 1e-5, theta 1e4).
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, replace
+
+import torch
+
+from . import _capi
+
+
+@dataclass(frozen=True)
+class ModelShape:
+    name: str
+    hidden: int
+    n_heads: int
+    n_kv_heads: int
+    head_dim: int
+    intermediate: int
+    vocab: int
+    n_layers: int
+    eps: float
+    theta: float
+
+
+QWEN2_5_0_5B = ModelShape("qwen2.5-0.5b", 896, 14, 2, 64, 4864, 151936, 24, 1e-6, 1e6)
+LLAMA2_7B = ModelShape("llama-2-7b", 4096, 32, 32, 128, 11008, 32000, 32, 1e-5, 1e4)
+
+
+@dataclass(frozen=True)
+class Workload:
+    name: str
+    model: ModelShape
+    n_seqs: int        # sequences in the step (per GPU for weak scaling)
+    seq_len: int       # new tokens per sequence in this step
+    max_seq: int       # KV cache capacity per sequence
+    decode: bool       # decode: one token per sequence at a random position
+
+    @property
+    def n_tokens(self) -> int:
+        return self.n_seqs * self.seq_len
+
+
+WORKLOADS = {
+    # B=8 x 512 prefill of Qwen2.5-0.5B, cache [24, 2, 8, 2, 4096, 64]
+    "qwen_prefill": Workload("qwen_prefill", QWEN2_5_0_5B, 8, 512, 4096, False),
+    # B=32 x 512 prefill of Llama-2-7B
+    "llama_prefill": Workload("llama_prefill", LLAMA2_7B, 32, 512, 512, False),
+    # 2048 sequences x 1 token, positions U[0, 4095), cache [24, 2, 2048, 2, 4096, 64]
+    "qwen_decode": Workload("qwen_decode", QWEN2_5_0_5B, 2048, 1, 4096, True),
+    # 128 x 512 Llama-2-7B prefill; 16 sequences per GPU at 8 GPUs
+    "llama_prefill_64k": Workload("llama_prefill_64k", LLAMA2_7B, 128, 512, 512, False),
+}
+
+
+def shard(workload: Workload, rank: int, world: int) -> Workload:
+    """The slice of a workload one rank runs when sequences are split evenly."""
+    if workload.n_seqs % world != 0:
+        raise ValueError(f"{workload.n_seqs} sequences do not split over {world} ranks")
+    return replace(workload, n_seqs=workload.n_seqs // world)
+
+
+def chain_bytes(w: Workload) -> dict:
+    """Algorithmic HBM bytes of one chain step: every logical fp16 tensor read
+    once and written once; norm weights and biases are negligible and not
+    counted; ids/positions/slots are int32."""
+    m, T = w.model, w.n_tokens
+    H, I, L = m.hidden, m.intermediate, m.n_layers
+    qkv_elems = T * (m.n_heads + 2 * m.n_kv_heads) * m.head_dim
+    per = {
+        "embedding": 2 * T * H * 2 + 4 * T,
+        "add_rms_norm": (L + 1) * 4 * T * H * 2 + (L - 1) * 4 * T * H * 2 + 2 * T * H * 2,
+        "qkv_bias_rope_kv_append": L * (2 * qkv_elems * 2 + 8 * T),
+        "silu_mul": L * 3 * T * I * 2,
+        "select_last_rows": 2 * w.n_seqs * H * 2,
+    }
+    per["total"] = sum(per.values())
+    return per
+
+
+def silu_bytes_per_launch(w: Workload) -> int:
+    return 3 * w.n_tokens * w.model.intermediate * 2
+
+
+class ChainRunner:
+    """Device buffers + launch descriptor of one chain step."""
+
+    def __init__(self, workload: Workload, device: torch.device | str = "cuda:0", seed: int = 0,
+                 use_pdl: bool = True, n_layers: int | None = None,
+                 weight_dtype: torch.dtype = torch.float16):
+        self.w = workload
+        m = workload.model
+        self.device = torch.device(device)
+        self.n_layers = n_layers or m.n_layers
+        T, H, I = workload.n_tokens, m.hidden, m.intermediate
+        qd, kvd = m.n_heads * m.head_dim, m.n_kv_heads * m.head_dim
+        dev = self.device
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(seed)
+        f16 = torch.float16
+
+        def normal(shape, std=1.0, dtype=f16):
+            return (torch.randn(shape, generator=gen, device=dev, dtype=torch.float32) * std).to(dtype)
+
+        def uniform(shape, lo, hi, dtype):
+            return (torch.rand(shape, generator=gen, device=dev, dtype=torch.float32) * (hi - lo) + lo).to(dtype)
+
+        with torch.cuda.device(dev):
+            self.table = normal((m.vocab, H), 0.02)
+            self.ids = torch.randint(0, m.vocab, (T,), generator=gen, device=dev, dtype=torch.int32)
+            if workload.decode:
+                self.positions = torch.randint(0, workload.max_seq - 1, (T,), generator=gen, device=dev,
+                                               dtype=torch.int32)
+                self.slots = torch.arange(T, device=dev, dtype=torch.int32)
+            else:
+                t = torch.arange(T, device=dev, dtype=torch.int32)
+                self.positions = t % workload.seq_len
+                self.slots = t // workload.seq_len
+            self.residual = torch.empty((T, H), dtype=f16, device=dev)
+            self.final_norm_w = uniform((H,), 0.5, 1.5, weight_dtype)
+            self.final_norm_out = torch.empty((T, H), dtype=f16, device=dev)
+            self.last_rows = torch.empty((workload.n_seqs, H), dtype=f16, device=dev)
+            self.err_flags = torch.zeros((1,), dtype=torch.int32, device=dev)
+            self.layers = []
+            for _ in range(self.n_layers):
+                L = {
+                    "q": normal((T, qd)), "k": normal((T, kvd)), "v": normal((T, kvd)),
+                    "q_bias": normal((qd,), 0.02, weight_dtype), "k_bias": normal((kvd,), 0.02, weight_dtype),
+                    "v_bias": normal((kvd,), 0.02, weight_dtype),
+                    "attn_out": normal((T, H)), "ffn_out": normal((T, H)),
+                    "gate": normal((T, I)), "up": normal((T, I)),
+                    "input_norm_w": uniform((H,), 0.5, 1.5, weight_dtype),
+                    "post_norm_w": uniform((H,), 0.5, 1.5, weight_dtype),
+                    "attn_norm_out": torch.empty((T, H), dtype=f16, device=dev),
+                    "ffn_norm_out": torch.empty((T, H), dtype=f16, device=dev),
+                    "swiglu_out": torch.empty((T, I), dtype=f16, device=dev),
+                    "k_cache": torch.empty((workload.n_seqs, m.n_kv_heads, workload.max_seq, m.head_dim),
+                                           dtype=f16, device=dev),
+                    "v_cache": torch.empty((workload.n_seqs, m.n_kv_heads, workload.max_seq, m.head_dim),
+                                           dtype=f16, device=dev),
+                }
+                self.layers.append(L)
+        self.weight_dtype = weight_dtype
+        self._build_desc(use_pdl)
+
+    def _build_desc(self, use_pdl: bool) -> None:
+        w, m = self.w, self.w.model
+        arr = (_capi.LayerBuffers * self.n_layers)()
+        for i, L in enumerate(self.layers):
+            for name, t in L.items():
+                setattr(arr[i], name, t.data_ptr())
+        self._layer_arr = arr
+        c = _capi.Chain()
+        c.n_tokens, c.hidden, c.n_heads, c.n_kv_heads = w.n_tokens, m.hidden, m.n_heads, m.n_kv_heads
+        c.head_dim, c.intermediate, c.vocab, c.n_layers = m.head_dim, m.intermediate, m.vocab, self.n_layers
+        c.n_slots, c.max_seq, c.n_seqs, c.seq_len = w.n_seqs, w.max_seq, w.n_seqs, w.seq_len
+        c.eps, c.theta = m.eps, m.theta
+        c.weight_dtype = _capi.F16 if self.weight_dtype == torch.float16 else _capi.F32
+        c.use_pdl = int(use_pdl)
+        c.embed_table, c.ids = self.table.data_ptr(), self.ids.data_ptr()
+        c.positions, c.slots, c.seq_ends = self.positions.data_ptr(), self.slots.data_ptr(), None
+        c.residual, c.final_norm_w = self.residual.data_ptr(), self.final_norm_w.data_ptr()
+        c.final_norm_out, c.last_rows = self.final_norm_out.data_ptr(), self.last_rows.data_ptr()
+        c.layers = ctypes.cast(arr, ctypes.POINTER(_capi.LayerBuffers))
+        c.err_flags = self.err_flags.data_ptr()
+        self.desc = c
+
+    def set_pdl(self, use_pdl: bool) -> None:
+        self.desc.use_pdl = int(use_pdl)
+
+    def run(self, stream: torch.cuda.Stream | None = None) -> int:
+        """Enqueues one chain step; returns the number of kernels launched."""
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        n = ctypes.c_int(0)
+        with torch.cuda.device(self.device):
+            _capi.check(_capi.lib.kllm_b200_chain_run(ctypes.byref(self.desc), ctypes.byref(n), s.cuda_stream))
+        return n.value
+
+    def step_inputs(self) -> list[torch.Tensor]:
+        """Tensors a step consumes that a real forward would produce afresh
+        each step (ids, positions, slots and the GEMM outputs)."""
+        out = [self.ids, self.positions, self.slots]
+        for L in self.layers:
+            out += [L[k] for k in ("q", "k", "v", "attn_out", "ffn_out", "gate", "up")]
+        return out

@@ -1,0 +1,65 @@
+// chain.cu — the non-GEMM op chain of one forward step, launched natively.
+//
+// Mirrors the op order of LlamaRunner::forward (src/model/llama.cpp:78-178)
+// with the GEMM outputs supplied as inputs:
+//   embedding                               (llama.cpp:79)
+//   per layer l:
+//     add+RMSNorm  r += ffn_out[l-1]; attn_norm = norm(r)   (l=0: norm only; :83-87, :166)
+//     bias+RoPE+KV q/k/v -> q rotated, cache[l] appended    (:89-114)
+//     add+RMSNorm  r += attn_out[l]; ffn_norm = norm(r)      (:135-143)
+//     SwiGLU       swiglu = silu(gate) * up                  (:158)
+//   add+RMSNorm  r += ffn_out[L-1]; normed = norm(r)         (:166, :171)
+//   select_last_rows                                          (:173)
+// Everything goes to one stream; with use_pdl every launch carries the
+// programmatic-dependent-launch attribute so a kernel's CTAs are scheduled
+// while its predecessor drains. The sequence contains no host sync and no
+// allocation, so it can be captured into a CUDA graph.
+#include "ops.cuh"
+
+extern "C" int kllm_b200_chain_run(const kllm_b200_chain* c, int* n_launches, void* stream) {
+  using namespace kb;
+  if (n_launches) *n_launches = 0;
+  if (c == nullptr || c->layers == nullptr) return fail(KLLM_B200_ERR_INVALID_ARG, "chain_run: null chain");
+  if (c->n_tokens <= 0 || c->hidden <= 0 || c->n_layers <= 0 || c->n_seqs <= 0 || c->intermediate <= 0 ||
+      c->n_heads <= 0 || c->head_dim <= 0) {
+    return fail(KLLM_B200_ERR_SHAPE, "chain_run: all dimensions must be positive");
+  }
+  if (c->weight_dtype != KLLM_B200_F16 && c->weight_dtype != KLLM_B200_F32) {
+    return fail(KLLM_B200_ERR_DTYPE, "chain_run: weight dtype %d not supported", c->weight_dtype);
+  }
+  LaunchOpts o;
+  o.stream = static_cast<cudaStream_t>(stream);
+  o.pdl = c->use_pdl != 0;
+  const int64_t T = c->n_tokens, H = c->hidden;
+  const int wdt = c->weight_dtype;
+  int launched = 0;
+  int rc = embedding(c->embed_table, c->vocab, H, KLLM_B200_F16, c->ids, T, c->residual, KLLM_B200_F16,
+                     c->err_flags, o);
+  if (rc != KLLM_B200_OK) return rc;
+  ++launched;
+  for (int64_t l = 0; l < c->n_layers; ++l) {
+    const kllm_b200_layer_buffers& L = c->layers[l];
+    const void* delta = l == 0 ? nullptr : c->layers[l - 1].ffn_out;
+    rc = add_rms_norm(c->residual, delta, L.input_norm_w, L.attn_norm_out, T, H, c->eps, KLLM_B200_F16, wdt, o);
+    if (rc != KLLM_B200_OK) return rc;
+    rc = qkv_bias_rope_kv_append(L.q, L.k, L.v, L.q_bias, L.k_bias, L.v_bias, wdt, c->positions, c->slots, T,
+                                 c->n_heads, c->n_kv_heads, c->head_dim, c->theta, L.k_cache, L.v_cache,
+                                 c->n_slots, c->max_seq, c->err_flags, o);
+    if (rc != KLLM_B200_OK) return rc;
+    rc = add_rms_norm(c->residual, L.attn_out, L.post_norm_w, L.ffn_norm_out, T, H, c->eps, KLLM_B200_F16, wdt,
+                      o);
+    if (rc != KLLM_B200_OK) return rc;
+    rc = silu_mul(L.gate, L.up, L.swiglu_out, T * c->intermediate, KLLM_B200_F16, o);
+    if (rc != KLLM_B200_OK) return rc;
+    launched += 4;
+  }
+  rc = add_rms_norm(c->residual, c->layers[c->n_layers - 1].ffn_out, c->final_norm_w, c->final_norm_out, T, H,
+                    c->eps, KLLM_B200_F16, wdt, o);
+  if (rc != KLLM_B200_OK) return rc;
+  rc = select_last_rows(c->final_norm_out, T, H, c->seq_ends, c->seq_len, c->n_seqs, c->last_rows, KLLM_B200_F16,
+                        c->err_flags, o);
+  if (rc != KLLM_B200_OK) return rc;
+  launched += 2;
+  if (n_launches) *n_launches = launched;
+  return KLLM_B200_OK;
+}

@@ -1,0 +1,178 @@
+// common.cuh — shared host/device helpers of the kllm_b200 CUDA library.
+//
+// Host side: status reporting (thread-local message behind the C ABI's
+// negative return codes), a per-device SM-count cache, occupancy-sized grids
+// and a launcher that can attach programmatic dependent launch (PDL).
+// Device side: 16-byte global loads/stores with cache hints, fp16 packing,
+// warp reductions and the PDL grid-dependency controls.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "kllm_b200.h"
+
+namespace kb {
+
+// ---------------------------------------------------------------------------
+// Host: errors and launch helpers
+// ---------------------------------------------------------------------------
+
+// Records `message` (printf-style) as the calling thread's last error and
+// returns `code`.
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+
+// Maps the launch status of the kernel just enqueued to a C-ABI code.
+int launch_status(cudaError_t err, const char* what);
+
+inline bool is_float_dtype(int dt) { return dt == KLLM_B200_F32 || dt == KLLM_B200_F16; }
+inline int dtype_size(int dt) { return dt == KLLM_B200_F32 || dt == KLLM_B200_I32 ? 4 : dt == KLLM_B200_F16 ? 2 : 1; }
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Number of SMs of the current device (cached per device ordinal).
+int sm_count();
+
+// Resident CTAs per SM for `kernel` at `threads` threads and `smem` bytes of
+// dynamic shared memory; computed once per kernel (all devices of one box are
+// the same part).
+template <typename Kernel>
+int resident_ctas(Kernel kernel, int threads, size_t smem) {
+  static int cached = 0;
+  int v = __atomic_load_n(&cached, __ATOMIC_RELAXED);
+  if (v == 0) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, smem) != cudaSuccess || n < 1) {
+      (void)cudaGetLastError();
+      n = 1;
+    }
+    __atomic_store_n(&cached, n, __ATOMIC_RELAXED);
+    v = n;
+  }
+  return v;
+}
+
+// Grid for a grid-stride kernel: one full wave of resident CTAs, never more
+// CTAs than work items.
+template <typename Kernel>
+unsigned persistent_grid(Kernel kernel, int threads, size_t smem, int64_t work_items_per_cta_unit,
+                         int64_t work_items) {
+  const int64_t wave = static_cast<int64_t>(sm_count()) * resident_ctas(kernel, threads, smem);
+  int64_t need = (work_items + work_items_per_cta_unit - 1) / work_items_per_cta_unit;
+  if (need < 1) need = 1;
+  return static_cast<unsigned>(need < wave ? need : wave);
+}
+
+// Launches `kernel` on `stream`; with `pdl` the launch carries the
+// programmatic-stream-serialization attribute, so it may begin while the
+// previous kernel on the stream drains (kernels call grid_dep_wait() before
+// touching memory the predecessor writes).
+template <typename... KArgs, typename... Args>
+cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                   bool pdl, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  if (pdl) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+// Launch options shared by the individual entry points and the chain runner.
+struct LaunchOpts {
+  cudaStream_t stream = nullptr;
+  bool pdl = false;
+};
+
+// ---------------------------------------------------------------------------
+// Device helpers
+// ---------------------------------------------------------------------------
+
+// Wait until the grid this launch depends on (PDL) has completed and its
+// writes are visible; a no-op for launches without the PDL attribute.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Allow the next PDL launch on the stream to start scheduling its CTAs.
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+// 16-byte load through the non-coherent path, not allocated in L1: for
+// inputs read exactly once.
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// 16-byte coherent load (for buffers the same kernel also writes).
+__device__ __forceinline__ uint4 ld_cg(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// 16-byte read-only load kept in L1 (small tensors reused by many rows).
+__device__ __forceinline__ uint4 ld_keep(const void* p) {
+  return __ldg(reinterpret_cast<const uint4*>(p));
+}
+
+// 16-byte store, streaming (evict-first): outputs not re-read by this kernel.
+__device__ __forceinline__ void st_stream(void* p, uint4 v) {
+  asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+
+// 16-byte plain store.
+__device__ __forceinline__ void st_plain(void* p, uint4 v) {
+  *reinterpret_cast<uint4*>(p) = v;
+}
+
+__device__ __forceinline__ float2 h2_to_f2(uint32_t w) {
+  return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+
+__device__ __forceinline__ uint32_t f2_to_h2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ float round_f16(float x) { return __half2float(__float2half_rn(x)); }
+
+template <int WIDTH>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+  for (int m = WIDTH / 2; m > 0; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+  return v;
+}
+
+// Element load/store as float for the generic (any dtype / any shape) paths.
+template <typename T>
+__device__ __forceinline__ float to_f(T v);
+template <>
+__device__ __forceinline__ float to_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
+
+template <typename T>
+__device__ __forceinline__ T from_f(float v);
+template <>
+__device__ __forceinline__ float from_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
+
+__device__ __forceinline__ void set_flag(int32_t* flags, int32_t bit) {
+  if (flags != nullptr) atomicOr(flags, bit);
+}
+
+}  // namespace kb

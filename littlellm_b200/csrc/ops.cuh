@@ -1,0 +1,31 @@
+// ops.cuh — internal (C++) launchers behind the C ABI; the chain runner
+// calls these directly with its own LaunchOpts (stream, PDL).
+#pragma once
+
+#include "common.cuh"
+
+namespace kb {
+
+int embedding(const void* table, int64_t vocab, int64_t hidden, int table_dtype, const int32_t* ids,
+              int64_t n_tokens, void* out, int out_dtype, int32_t* err_flags, const LaunchOpts& o);
+
+int add_rms_norm(void* residual, const void* delta, const void* weight, void* out, int64_t rows,
+                 int64_t hidden, float eps, int act_dtype, int weight_dtype, const LaunchOpts& o);
+
+int silu_mul(const void* gate, const void* up, void* out, int64_t n, int dtype, const LaunchOpts& o);
+
+int add_inplace(void* x, const void* y, int64_t n, int x_dtype, int y_dtype, const LaunchOpts& o);
+
+int add_bias_inplace(void* x, const void* bias, int64_t rows, int64_t cols, int x_dtype, int bias_dtype,
+                     const LaunchOpts& o);
+
+int qkv_bias_rope_kv_append(void* q, const void* k, const void* v, const void* bq, const void* bk,
+                            const void* bv, int bias_dtype, const int32_t* positions, const int32_t* slots,
+                            int64_t n_tokens, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim,
+                            float theta, void* k_cache, void* v_cache, int64_t n_slots, int64_t max_seq,
+                            int32_t* err_flags, const LaunchOpts& o);
+
+int select_last_rows(const void* x, int64_t rows, int64_t cols, const int32_t* seq_ends, int64_t seq_len,
+                     int64_t n_seqs, void* out, int dtype, int32_t* err_flags, const LaunchOpts& o);
+
+}  // namespace kb

@@ -1,0 +1,287 @@
+// rms_norm.cu — residual add fused with RMSNorm, and plain RMSNorm.
+//
+// Replaces add_inplace (src/op/cuda/add.cu:71-76) + rms_norm
+// (src/op/cuda/rms_norm.cu:177-188) at src/model/llama.cpp:135-143/166/176.
+//
+// fp16 fast path (hidden % 8 == 0, 16-byte aligned rows, hidden <= 16384):
+// a group of G threads (8..256) owns a row; each thread holds VPT 16-byte
+// vectors of the row in registers, so the row is read from HBM once, the
+// residual written once and the output written once (4*H*2 bytes per row
+// with a delta, 2*H*2 without). G and VPT are picked per hidden size to
+// leave no idle lanes where possible (H=896: G=16 x VPT=7; H=4096: G=128 x
+// VPT=4). Sub-warp groups reduce with shuffles; multi-warp groups add one
+// shared-memory exchange. CTAs stride over row groups (one wave of CTAs).
+//
+// Arithmetic: r = fp16_rn(a + d) (what the reference's fp16 add_inplace
+// stores), sum of r^2 in fp32, scale = rsqrt(sum / H + eps), y = (r * scale)
+// * w rounded to fp16.
+#include "ops.cuh"
+
+namespace kb {
+namespace {
+
+constexpr int kThreads = 256;
+
+template <typename TW>
+struct WeightVec;
+
+template <>
+struct WeightVec<__half> {
+  __device__ __forceinline__ static void load(const __half* w, int64_t col, float (&out)[8]) {
+    const uint4 v = ld_keep(w + col);
+    const float2 a = h2_to_f2(v.x), b = h2_to_f2(v.y), c = h2_to_f2(v.z), d = h2_to_f2(v.w);
+    out[0] = a.x; out[1] = a.y; out[2] = b.x; out[3] = b.y;
+    out[4] = c.x; out[5] = c.y; out[6] = d.x; out[7] = d.y;
+  }
+};
+
+template <>
+struct WeightVec<float> {
+  __device__ __forceinline__ static void load(const float* w, int64_t col, float (&out)[8]) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(w + col));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(w + col + 4));
+    out[0] = a.x; out[1] = a.y; out[2] = a.z; out[3] = a.w;
+    out[4] = b.x; out[5] = b.y; out[6] = b.z; out[7] = b.w;
+  }
+};
+
+__device__ __forceinline__ float sumsq_h2(uint32_t w) {
+  const float2 f = h2_to_f2(w);
+  return f.x * f.x + f.y * f.y;
+}
+
+template <int VPT, typename TW, bool HAS_DELTA>
+__global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __restrict__ residual,
+                                                                    const __half* __restrict__ delta,
+                                                                    const TW* __restrict__ weight,
+                                                                    __half* __restrict__ out, int64_t rows,
+                                                                    int hidden, int group, float eps) {
+  __shared__ float partial[2][kThreads / 32];
+  grid_dep_wait();
+  grid_dep_launch();
+
+  const int nvec = hidden >> 3;
+  const int rows_per_cta = kThreads / group;
+  const int lane_g = threadIdx.x % group;          // position inside the row group
+  const int row_in_cta = threadIdx.x / group;
+  const int warp = threadIdx.x >> 5;
+  const int warps_per_group = group >> 5;          // 0 for sub-warp groups
+  const float inv_h = 1.0f / static_cast<float>(hidden);
+  const int64_t n_groups = (rows + rows_per_cta - 1) / rows_per_cta;
+
+  int parity = 0;
+  for (int64_t g = blockIdx.x; g < n_groups; g += gridDim.x, parity ^= 1) {
+    const int64_t row = g * rows_per_cta + row_in_cta;
+    const bool live = row < rows;
+    __half* rrow = residual + row * hidden;
+    uint4 r[VPT];
+    float ss = 0.0f;
+    if (live) {
+      uint4 d[VPT];
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        const int v = j * group + lane_g;
+        if (v < nvec) {
+          r[j] = HAS_DELTA ? ld_cg(rrow + v * 8) : ld_stream(rrow + v * 8);
+          if (HAS_DELTA) d[j] = ld_stream(delta + row * hidden + v * 8);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        const int v = j * group + lane_g;
+        if (v < nvec) {
+          if (HAS_DELTA) {
+            const float2 a0 = h2_to_f2(r[j].x), a1 = h2_to_f2(r[j].y), a2 = h2_to_f2(r[j].z), a3 = h2_to_f2(r[j].w);
+            const float2 b0 = h2_to_f2(d[j].x), b1 = h2_to_f2(d[j].y), b2 = h2_to_f2(d[j].z), b3 = h2_to_f2(d[j].w);
+            r[j] = make_uint4(f2_to_h2(a0.x + b0.x, a0.y + b0.y), f2_to_h2(a1.x + b1.x, a1.y + b1.y),
+                              f2_to_h2(a2.x + b2.x, a2.y + b2.y), f2_to_h2(a3.x + b3.x, a3.y + b3.y));
+            st_plain(rrow + v * 8, r[j]);
+          }
+          ss += sumsq_h2(r[j].x) + sumsq_h2(r[j].y) + sumsq_h2(r[j].z) + sumsq_h2(r[j].w);
+        }
+      }
+    }
+    // Reduce over the row group: shuffles inside the warp, then (groups
+    // wider than a warp) one exchange of per-warp partials in shared memory.
+    const int sub = group < 32 ? group : 32;
+    for (int m = sub >> 1; m > 0; m >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
+    if (warps_per_group > 1) {
+      if ((threadIdx.x & 31) == 0) partial[parity][warp] = ss;
+      __syncthreads();
+      const int first = (threadIdx.x / group) * warps_per_group;
+      ss = 0.0f;
+      for (int w = 0; w < warps_per_group; ++w) ss += partial[parity][first + w];
+    }
+    if (live) {
+      const float scale = rsqrtf(ss * inv_h + eps);
+      __half* orow = out + row * hidden;
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        const int v = j * group + lane_g;
+        if (v < nvec) {
+          float w[8];
+          WeightVec<TW>::load(weight, static_cast<int64_t>(v) * 8, w);
+          const float2 a0 = h2_to_f2(r[j].x), a1 = h2_to_f2(r[j].y), a2 = h2_to_f2(r[j].z), a3 = h2_to_f2(r[j].w);
+          st_plain(orow + v * 8,
+                   make_uint4(f2_to_h2(a0.x * scale * w[0], a0.y * scale * w[1]),
+                              f2_to_h2(a1.x * scale * w[2], a1.y * scale * w[3]),
+                              f2_to_h2(a2.x * scale * w[4], a2.y * scale * w[5]),
+                              f2_to_h2(a3.x * scale * w[6], a3.y * scale * w[7])));
+        }
+      }
+    }
+  }
+}
+
+// Any dtype / hidden size: one CTA per row, element per thread, two passes
+// (the second re-reads the row from L1/L2).
+template <typename TA, typename TW>
+__global__ void __launch_bounds__(kThreads) add_rms_norm_generic_kernel(TA* residual, const TA* delta,
+                                                                        const TW* weight, TA* out,
+                                                                        int64_t rows, int64_t hidden,
+                                                                        float eps) {
+  __shared__ float partial[kThreads / 32];
+  grid_dep_wait();
+  grid_dep_launch();
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    TA* x = residual + row * hidden;
+    float ss = 0.0f;
+    for (int64_t c = threadIdx.x; c < hidden; c += blockDim.x) {
+      float v = to_f(x[c]);
+      if (delta != nullptr) {
+        const TA r = from_f<TA>(v + to_f(delta[row * hidden + c]));
+        x[c] = r;
+        v = to_f(r);
+      }
+      ss += v * v;
+    }
+    ss = group_sum<32>(ss);
+    if ((threadIdx.x & 31) == 0) partial[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    ss = 0.0f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) ss += partial[w];
+    __syncthreads();
+    const float scale = rsqrtf(ss / static_cast<float>(hidden) + eps);
+    for (int64_t c = threadIdx.x; c < hidden; c += blockDim.x) {
+      out[row * hidden + c] = from_f<TA>(to_f(x[c]) * scale * to_f(weight[c]));
+    }
+  }
+}
+
+struct FastConfig {
+  int group = 0;
+  int vpt = 0;
+};
+
+// Smallest number of idle lanes, then VPT closest to 4.
+FastConfig pick_config(int nvec) {
+  FastConfig best;
+  int best_waste = 1 << 30, best_dist = 1 << 30;
+  for (int g = 8; g <= kThreads; g <<= 1) {
+    const int vpt = (nvec + g - 1) / g;
+    if (vpt < 1 || vpt > 8) continue;
+    const int waste = g * vpt - nvec;
+    const int dist = vpt > 4 ? vpt - 4 : 4 - vpt;
+    if (waste < best_waste || (waste == best_waste && dist < best_dist)) {
+      best = {g, vpt};
+      best_waste = waste;
+      best_dist = dist;
+    }
+  }
+  return best;
+}
+
+template <int VPT, typename TW, bool HAS_DELTA>
+int launch_fast(void* residual, const void* delta, const void* weight, void* out, int64_t rows, int hidden,
+                int group, float eps, const LaunchOpts& o) {
+  auto k = add_rms_norm_f16_kernel<VPT, TW, HAS_DELTA>;
+  const int rows_per_cta = kThreads / group;
+  const unsigned grid = persistent_grid(k, kThreads, 0, rows_per_cta, rows);
+  return launch_status(launch(k, grid, kThreads, 0, o.stream, o.pdl, static_cast<__half*>(residual),
+                              static_cast<const __half*>(delta), static_cast<const TW*>(weight),
+                              static_cast<__half*>(out), rows, hidden, group, eps),
+                       "add_rms_norm");
+}
+
+template <int VPT, typename TW>
+int launch_fast_d(void* residual, const void* delta, const void* weight, void* out, int64_t rows, int hidden,
+                  int group, float eps, const LaunchOpts& o) {
+  return delta ? launch_fast<VPT, TW, true>(residual, delta, weight, out, rows, hidden, group, eps, o)
+               : launch_fast<VPT, TW, false>(residual, delta, weight, out, rows, hidden, group, eps, o);
+}
+
+template <typename TW>
+int dispatch_fast(const FastConfig& c, void* residual, const void* delta, const void* weight, void* out,
+                  int64_t rows, int hidden, float eps, const LaunchOpts& o) {
+  switch (c.vpt) {
+    case 1: return launch_fast_d<1, TW>(residual, delta, weight, out, rows, hidden, c.group, eps, o);
+    case 2: return launch_fast_d<2, TW>(residual, delta, weight, out, rows, hidden, c.group, eps, o);
+    case 3: return launch_fast_d<3, TW>(residual, delta, weight, out, rows, hidden, c.group, eps, o);
+    case 4: return launch_fast_d<4, TW>(residual, delta, weight, out, rows, hidden, c.group, eps, o);
+    case 5: return launch_fast_d<5, TW>(residual, delta, weight, out, rows, hidden, c.group, eps, o);
+    case 6: return launch_fast_d<6, TW>(residual, delta, weight, out, rows, hidden, c.group, eps, o);
+    case 7: return launch_fast_d<7, TW>(residual, delta, weight, out, rows, hidden, c.group, eps, o);
+    default: return launch_fast_d<8, TW>(residual, delta, weight, out, rows, hidden, c.group, eps, o);
+  }
+}
+
+template <typename TA, typename TW>
+int launch_generic(void* residual, const void* delta, const void* weight, void* out, int64_t rows,
+                   int64_t hidden, float eps, const LaunchOpts& o) {
+  auto k = add_rms_norm_generic_kernel<TA, TW>;
+  const unsigned grid = persistent_grid(k, kThreads, 0, 1, rows);
+  return launch_status(launch(k, grid, kThreads, 0, o.stream, o.pdl, static_cast<TA*>(residual),
+                              static_cast<const TA*>(delta), static_cast<const TW*>(weight), static_cast<TA*>(out),
+                              rows, hidden, eps),
+                       "add_rms_norm");
+}
+
+}  // namespace
+
+int add_rms_norm(void* residual, const void* delta, const void* weight, void* out, int64_t rows, int64_t hidden,
+                 float eps, int act_dtype, int weight_dtype, const LaunchOpts& o) {
+  if (rows < 0 || hidden < 0) return fail(KLLM_B200_ERR_INVALID_ARG, "rms_norm: negative size");
+  if (rows == 0) return KLLM_B200_OK;
+  if (hidden == 0) return fail(KLLM_B200_ERR_SHAPE, "rms_norm: hidden must be positive");
+  if (!residual || !weight || !out) return fail(KLLM_B200_ERR_INVALID_ARG, "rms_norm: null pointer");
+  if (!is_float_dtype(act_dtype) || !is_float_dtype(weight_dtype)) {
+    return fail(KLLM_B200_ERR_DTYPE, "rms_norm: dtypes %d/%d not supported", act_dtype, weight_dtype);
+  }
+  if (act_dtype == KLLM_B200_F16) {
+    const bool fast = hidden % 8 == 0 && hidden <= 8 * 8 * kThreads && aligned16(residual) && aligned16(out) &&
+                      aligned16(weight) && (delta == nullptr || aligned16(delta));
+    if (fast) {
+      const FastConfig c = pick_config(static_cast<int>(hidden / 8));
+      if (c.vpt > 0) {
+        return weight_dtype == KLLM_B200_F16
+                   ? dispatch_fast<__half>(c, residual, delta, weight, out, rows, (int)hidden, eps, o)
+                   : dispatch_fast<float>(c, residual, delta, weight, out, rows, (int)hidden, eps, o);
+      }
+    }
+    return weight_dtype == KLLM_B200_F16
+               ? launch_generic<__half, __half>(residual, delta, weight, out, rows, hidden, eps, o)
+               : launch_generic<__half, float>(residual, delta, weight, out, rows, hidden, eps, o);
+  }
+  return weight_dtype == KLLM_B200_F16
+             ? launch_generic<float, __half>(residual, delta, weight, out, rows, hidden, eps, o)
+             : launch_generic<float, float>(residual, delta, weight, out, rows, hidden, eps, o);
+}
+
+}  // namespace kb
+
+extern "C" int kllm_b200_add_rms_norm(void* residual, const void* delta, const void* weight, void* out,
+                                      int64_t rows, int64_t hidden, float eps, int act_dtype, int weight_dtype,
+                                      void* stream) {
+  kb::LaunchOpts o;
+  o.stream = static_cast<cudaStream_t>(stream);
+  return kb::add_rms_norm(residual, delta, weight, out, rows, hidden, eps, act_dtype, weight_dtype, o);
+}
+
+extern "C" int kllm_b200_rms_norm(const void* x, const void* weight, void* out, int64_t rows, int64_t hidden,
+                                  float eps, int act_dtype, int weight_dtype, void* stream) {
+  kb::LaunchOpts o;
+  o.stream = static_cast<cudaStream_t>(stream);
+  // With no delta the kernel only reads `x`.
+  return kb::add_rms_norm(const_cast<void*>(x), nullptr, weight, out, rows, hidden, eps, act_dtype, weight_dtype,
+                          o);
+}

@@ -1,0 +1,468 @@
+// rope_kv.cu — q/k/v bias add + rotate-half RoPE + KV-cache append (fused),
+// plus the reference-compatible rope_inplace and copy_kv_to_cache.
+//
+// Fused op (replaces, per layer, 3x add_bias_inplace src/op/cuda/add.cu:59-69,
+// 2x rope_inplace src/op/cuda/rope.cu:188-201 and copy_kv_to_cache
+// src/op/cuda/kv_cache.cu:32-41, as called at src/model/llama.cpp:89-114).
+//
+// A CTA owns a tile of tokens. Phase 1 computes cos/sin of every
+// (token, frequency) of the tile once into shared memory — the angle depends
+// only on the position and d, so all q and k heads of a token share it.
+// Phase 2 walks work units over the tile:
+//   rotation unit = 8 consecutive pairs (d0..d0+7 with d0+half..) of one q or
+//                   k head: two 16-byte loads, two 16-byte stores;
+//   copy unit     = 16 bytes of one v head.
+// q is rotated in place; k (rotated) and v (biased) go straight to the
+// head-major cache [slot, kv_head, pos, d], so neither is written back.
+//
+// Frequencies: inv_freq[d] = powf(theta, (-2 * d) / head_dim) evaluated on
+// the host in fp32 (the expression of src/op/cpu/rope.cpp:24, which is also
+// how the reference CUDA path builds its table, src/op/cuda/rope.cu:51-55)
+// and passed by value. Angles use the accurate sincosf (the reference CUDA
+// kernel's __sincosf loses accuracy at the large angles positions up to
+// 4095 produce).
+#include <cmath>
+
+#include "ops.cuh"
+
+namespace kb {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kMaxHalf = 128;   // head_dim <= 256
+constexpr int kMaxTok = 32;     // tokens per CTA tile
+
+struct RopeArgs {
+  __half* q;
+  const __half* k;
+  const __half* v;
+  const void* bq;
+  const void* bk;
+  const void* bv;
+  const int32_t* positions;  // NULL: position = past_len + t
+  const int32_t* slots;      // NULL: slot 0
+  int32_t past_len;
+  int64_t n_tokens;
+  int n_heads, n_kv_heads, head_dim;
+  __half* k_cache;
+  __half* v_cache;
+  int64_t n_slots, max_seq;
+  int32_t* err_flags;
+  int tok_per_cta;
+  float inv_freq[kMaxHalf];
+};
+
+template <typename TB>
+__device__ __forceinline__ void load_bias8(const void* bias, int64_t off, float (&b)[8]);
+
+template <>
+__device__ __forceinline__ void load_bias8<__half>(const void* bias, int64_t off, float (&b)[8]) {
+  const uint4 v = ld_keep(static_cast<const __half*>(bias) + off);
+  const float2 a = h2_to_f2(v.x), c = h2_to_f2(v.y), d = h2_to_f2(v.z), e = h2_to_f2(v.w);
+  b[0] = a.x; b[1] = a.y; b[2] = c.x; b[3] = c.y; b[4] = d.x; b[5] = d.y; b[6] = e.x; b[7] = e.y;
+}
+
+template <>
+__device__ __forceinline__ void load_bias8<float>(const void* bias, int64_t off, float (&b)[8]) {
+  const float* p = static_cast<const float*>(bias) + off;
+  const float4 x = __ldg(reinterpret_cast<const float4*>(p));
+  const float4 y = __ldg(reinterpret_cast<const float4*>(p + 4));
+  b[0] = x.x; b[1] = x.y; b[2] = x.z; b[3] = x.w; b[4] = y.x; b[5] = y.y; b[6] = y.z; b[7] = y.w;
+}
+
+__device__ __forceinline__ void unpack8(uint4 v, float (&f)[8]) {
+  const float2 a = h2_to_f2(v.x), b = h2_to_f2(v.y), c = h2_to_f2(v.z), d = h2_to_f2(v.w);
+  f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y; f[4] = c.x; f[5] = c.y; f[6] = d.x; f[7] = d.y;
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  return make_uint4(f2_to_h2(f[0], f[1]), f2_to_h2(f[2], f[3]), f2_to_h2(f[4], f[5]), f2_to_h2(f[6], f[7]));
+}
+
+// The per-pair rotation shared by every path (fused, legacy, generic) so that
+// the fused op equals the composition of the separate ops bit for bit.
+__device__ __forceinline__ void rotate(float x1, float x2, float c, float s, float& y1, float& y2) {
+  y1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+  y2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+}
+
+__device__ __forceinline__ float2 angle_cs(int32_t pos, float inv_freq) {
+  float s, c;
+  sincosf(__fmul_rn(static_cast<float>(pos), inv_freq), &s, &c);
+  return make_float2(c, s);
+}
+
+template <typename TB>
+__global__ void __launch_bounds__(kThreads) qkv_rope_f16_kernel(const __grid_constant__ RopeArgs a) {
+  extern __shared__ float2 cs[];  // [tok_per_cta][half] = (cos, sin)
+  __shared__ int32_t s_pos[kMaxTok];
+  __shared__ int64_t s_dst[kMaxTok];  // element offset of (slot, head 0, pos, 0); -1 = skip cache write
+
+  grid_dep_wait();
+  grid_dep_launch();
+
+  const int half = a.head_dim >> 1;
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * a.tok_per_cta;
+  const int64_t left = a.n_tokens - t0;
+  const int ntok = left < a.tok_per_cta ? static_cast<int>(left) : a.tok_per_cta;
+
+  if (threadIdx.x < ntok) {
+    const int64_t t = t0 + threadIdx.x;
+    const int32_t pos = a.positions ? __ldg(a.positions + t) : a.past_len + static_cast<int32_t>(t);
+    const int32_t slot = a.slots ? __ldg(a.slots + t) : 0;
+    s_pos[threadIdx.x] = pos;
+    int64_t dst = -1;
+    if (a.k_cache != nullptr || a.v_cache != nullptr) {
+      const bool pos_ok = pos >= 0 && pos < a.max_seq;
+      const bool slot_ok = slot >= 0 && slot < a.n_slots;
+      if (!pos_ok) set_flag(a.err_flags, KLLM_B200_FLAG_BAD_POSITION);
+      if (!slot_ok) set_flag(a.err_flags, KLLM_B200_FLAG_BAD_SLOT);
+      if (pos_ok && slot_ok) dst = (static_cast<int64_t>(slot) * a.n_kv_heads * a.max_seq + pos) * a.head_dim;
+    }
+    s_dst[threadIdx.x] = dst;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < ntok * half; i += blockDim.x) {
+    const int tl = i / half;
+    const int d = i - tl * half;
+    cs[i] = angle_cs(s_pos[tl], a.inv_freq[d]);
+  }
+  __syncthreads();
+
+  const int chunks = a.head_dim >> 4;   // rotation units per head
+  const int vchunks = a.head_dim >> 3;  // copy units per v head
+  const int rot_q = a.n_heads * chunks;
+  const int rot_k = a.k ? a.n_kv_heads * chunks : 0;
+  const int cp_v = a.v ? a.n_kv_heads * vchunks : 0;
+  const int per_tok = rot_q + rot_k + cp_v;
+  const int64_t head_stride_cache = a.max_seq * a.head_dim;
+
+  for (int u = threadIdx.x; u < ntok * per_tok; u += blockDim.x) {
+    const int tl = u / per_tok;
+    const int w = u - tl * per_tok;
+    const int64_t t = t0 + tl;
+    if (w < rot_q + rot_k) {
+      const bool is_q = w < rot_q;
+      const int ww = is_q ? w : w - rot_q;
+      const int h = ww / chunks;
+      const int d0 = (ww - h * chunks) << 3;
+      const int heads = is_q ? a.n_heads : a.n_kv_heads;
+      const __half* src = (is_q ? static_cast<const __half*>(a.q) : a.k) + (t * heads + h) * a.head_dim;
+      float x1[8], x2[8];
+      unpack8(is_q ? ld_cg(src + d0) : ld_stream(src + d0), x1);
+      unpack8(is_q ? ld_cg(src + d0 + half) : ld_stream(src + d0 + half), x2);
+      const void* bias = is_q ? a.bq : a.bk;
+      if (bias != nullptr) {
+        float b1[8], b2[8];
+        load_bias8<TB>(bias, static_cast<int64_t>(h) * a.head_dim + d0, b1);
+        load_bias8<TB>(bias, static_cast<int64_t>(h) * a.head_dim + d0 + half, b2);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          x1[i] = round_f16(x1[i] + b1[i]);
+          x2[i] = round_f16(x2[i] + b2[i]);
+        }
+      }
+      const float2* csr = cs + tl * half + d0;
+      float y1[8], y2[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float2 c = csr[i];
+        rotate(x1[i], x2[i], c.x, c.y, y1[i], y2[i]);
+      }
+      if (is_q) {
+        __half* dst = a.q + (t * a.n_heads + h) * a.head_dim;
+        st_plain(dst + d0, pack8(y1));
+        st_plain(dst + d0 + half, pack8(y2));
+      } else if (a.k_cache != nullptr && s_dst[tl] >= 0) {
+        __half* dst = a.k_cache + s_dst[tl] + h * head_stride_cache;
+        st_plain(dst + d0, pack8(y1));
+        st_plain(dst + d0 + half, pack8(y2));
+      }
+    } else {
+      const int ww = w - rot_q - rot_k;
+      const int h = ww / vchunks;
+      const int d0 = (ww - h * vchunks) << 3;
+      uint4 x = ld_stream(a.v + (t * a.n_kv_heads + h) * a.head_dim + d0);
+      if (a.bv != nullptr) {
+        float xf[8], b[8];
+        unpack8(x, xf);
+        load_bias8<TB>(a.bv, static_cast<int64_t>(h) * a.head_dim + d0, b);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) xf[i] = xf[i] + b[i];
+        x = pack8(xf);
+      }
+      if (a.v_cache != nullptr && s_dst[tl] >= 0) st_plain(a.v_cache + s_dst[tl] + h * head_stride_cache + d0, x);
+    }
+  }
+}
+
+// Any even head_dim, fp16 or fp32 activations: one thread per rotation pair
+// or per v element; no shared tables.
+template <typename TA, typename TB>
+__global__ void __launch_bounds__(kThreads) qkv_rope_generic_kernel(const __grid_constant__ RopeArgs a) {
+  grid_dep_wait();
+  grid_dep_launch();
+  TA* q = reinterpret_cast<TA*>(a.q);
+  const TA* k = reinterpret_cast<const TA*>(a.k);
+  const TA* v = reinterpret_cast<const TA*>(a.v);
+  TA* kc = reinterpret_cast<TA*>(a.k_cache);
+  TA* vc = reinterpret_cast<TA*>(a.v_cache);
+  const TB* bq = static_cast<const TB*>(a.bq);
+  const TB* bk = static_cast<const TB*>(a.bk);
+  const TB* bv = static_cast<const TB*>(a.bv);
+  const int D = a.head_dim, half = D >> 1;
+  const int rot_q = a.n_heads * half;
+  const int rot_k = k ? a.n_kv_heads * half : 0;
+  const int cp_v = v ? a.n_kv_heads * D : 0;
+  const int per_tok = rot_q + rot_k + cp_v;
+  const int64_t total = a.n_tokens * per_tok;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t u = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; u < total; u += stride) {
+    const int64_t t = u / per_tok;
+    const int w = static_cast<int>(u - t * per_tok);
+    const int32_t pos = a.positions ? a.positions[t] : a.past_len + static_cast<int32_t>(t);
+    const int32_t slot = a.slots ? a.slots[t] : 0;
+    bool ok = true;
+    if (kc != nullptr || vc != nullptr) {
+      const bool pos_ok = pos >= 0 && pos < a.max_seq;
+      const bool slot_ok = slot >= 0 && slot < a.n_slots;
+      if (w == 0) {
+        if (!pos_ok) set_flag(a.err_flags, KLLM_B200_FLAG_BAD_POSITION);
+        if (!slot_ok) set_flag(a.err_flags, KLLM_B200_FLAG_BAD_SLOT);
+      }
+      ok = pos_ok && slot_ok;
+    }
+    if (w < rot_q + rot_k) {
+      const bool is_q = w < rot_q;
+      const int ww = is_q ? w : w - rot_q;
+      const int h = ww / half;
+      const int d = ww - h * half;
+      const int heads = is_q ? a.n_heads : a.n_kv_heads;
+      const TA* src = (is_q ? q : k) + (t * heads + h) * D;
+      float x1 = to_f(src[d]), x2 = to_f(src[d + half]);
+      const TB* b = is_q ? bq : bk;
+      if (b != nullptr) {
+        x1 = to_f(from_f<TA>(x1 + to_f(b[h * D + d])));
+        x2 = to_f(from_f<TA>(x2 + to_f(b[h * D + d + half])));
+      }
+      const float2 c = angle_cs(pos, a.inv_freq[d]);
+      float y1, y2;
+      rotate(x1, x2, c.x, c.y, y1, y2);
+      if (is_q) {
+        q[(t * a.n_heads + h) * D + d] = from_f<TA>(y1);
+        q[(t * a.n_heads + h) * D + d + half] = from_f<TA>(y2);
+      } else if (kc != nullptr && ok) {
+        const int64_t dst = ((static_cast<int64_t>(slot) * a.n_kv_heads + h) * a.max_seq + pos) * D;
+        kc[dst + d] = from_f<TA>(y1);
+        kc[dst + d + half] = from_f<TA>(y2);
+      }
+    } else {
+      const int ww = w - rot_q - rot_k;
+      const int h = ww / D;
+      const int d = ww - h * D;
+      float x = to_f(v[(t * a.n_kv_heads + h) * D + d]);
+      if (bv != nullptr) x = x + to_f(bv[h * D + d]);
+      if (vc != nullptr && ok) {
+        vc[((static_cast<int64_t>(slot) * a.n_kv_heads + h) * a.max_seq + pos) * D + d] = from_f<TA>(x);
+      }
+    }
+  }
+}
+
+void fill_inv_freq(RopeArgs& a, float theta) {
+  const int half = a.head_dim / 2;
+  for (int d = 0; d < half; ++d) {
+    a.inv_freq[d] = std::pow(theta, -2.0f * static_cast<float>(d) / static_cast<float>(a.head_dim));
+  }
+}
+
+int run_rope(RopeArgs& a, int act_dtype, int bias_dtype, const LaunchOpts& o, const char* what) {
+  const int D = a.head_dim;
+  const bool bias16 = bias_dtype == KLLM_B200_F16;
+  auto al = [](const void* p) { return p == nullptr || aligned16(p); };
+  const bool fast = act_dtype == KLLM_B200_F16 && D % 16 == 0 && al(a.q) && al(a.k) && al(a.v) && al(a.bq) &&
+                    al(a.bk) && al(a.bv) && al(a.k_cache) && al(a.v_cache);
+  if (fast) {
+    const int chunks = D / 16;
+    const int per_tok = a.n_heads * chunks + (a.k ? a.n_kv_heads * chunks : 0) + (a.v ? a.n_kv_heads * D / 8 : 0);
+    int tok = per_tok > 0 ? (320 + per_tok - 1) / per_tok : kMaxTok;
+    tok = tok < 1 ? 1 : tok > kMaxTok ? kMaxTok : tok;
+    a.tok_per_cta = tok;
+    const size_t smem = static_cast<size_t>(tok) * (D / 2) * sizeof(float2);
+    const unsigned grid = static_cast<unsigned>((a.n_tokens + tok - 1) / tok);
+    auto k = bias16 ? qkv_rope_f16_kernel<__half> : qkv_rope_f16_kernel<float>;
+    return launch_status(launch(k, grid, kThreads, smem, o.stream, o.pdl, a), what);
+  }
+  const int per_tok = a.n_heads * (D / 2) + (a.k ? a.n_kv_heads * (D / 2) : 0) + (a.v ? a.n_kv_heads * D : 0);
+  const int64_t total = a.n_tokens * per_tok;
+  if (act_dtype == KLLM_B200_F16) {
+    auto k = bias16 ? qkv_rope_generic_kernel<__half, __half> : qkv_rope_generic_kernel<__half, float>;
+    const unsigned grid = persistent_grid(k, kThreads, 0, kThreads, total);
+    return launch_status(launch(k, grid, kThreads, 0, o.stream, o.pdl, a), what);
+  }
+  auto k = bias16 ? qkv_rope_generic_kernel<float, __half> : qkv_rope_generic_kernel<float, float>;
+  const unsigned grid = persistent_grid(k, kThreads, 0, kThreads, total);
+  return launch_status(launch(k, grid, kThreads, 0, o.stream, o.pdl, a), what);
+}
+
+// ---- reference copy_kv_to_cache: contiguous block copy of K and V --------
+
+__global__ void __launch_bounds__(kThreads) copy_kv_vec_kernel(const uint4* __restrict__ k,
+                                                               const uint4* __restrict__ v, uint4* __restrict__ kc,
+                                                               uint4* __restrict__ vc, int64_t nvec) {
+  grid_dep_wait();
+  grid_dep_launch();
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < 2 * nvec; i += stride) {
+    if (i < nvec) {
+      st_plain(kc + i, ld_stream(k + i));
+    } else {
+      st_plain(vc + (i - nvec), ld_stream(v + (i - nvec)));
+    }
+  }
+}
+
+template <typename TS, typename TC>
+__global__ void __launch_bounds__(kThreads) copy_kv_generic_kernel(const TS* k, const TS* v, TC* kc, TC* vc,
+                                                                   int64_t n) {
+  grid_dep_wait();
+  grid_dep_launch();
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < 2 * n; i += stride) {
+    if (i < n) {
+      kc[i] = from_f<TC>(to_f(k[i]));
+    } else {
+      vc[i - n] = from_f<TC>(to_f(v[i - n]));
+    }
+  }
+}
+
+template <typename TS, typename TC>
+int run_copy_kv_generic(const void* k, const void* v, void* kc, void* vc, int64_t n, const LaunchOpts& o) {
+  auto kern = copy_kv_generic_kernel<TS, TC>;
+  const unsigned grid = persistent_grid(kern, kThreads, 0, kThreads * 4, 2 * n);
+  return launch_status(launch(kern, grid, kThreads, 0, o.stream, o.pdl, static_cast<const TS*>(k),
+                              static_cast<const TS*>(v), static_cast<TC*>(kc), static_cast<TC*>(vc), n),
+                       "copy_kv_to_cache");
+}
+
+}  // namespace
+
+int qkv_bias_rope_kv_append(void* q, const void* k, const void* v, const void* bq, const void* bk, const void* bv,
+                            int bias_dtype, const int32_t* positions, const int32_t* slots, int64_t n_tokens,
+                            int64_t n_heads, int64_t n_kv_heads, int64_t head_dim, float theta, void* k_cache,
+                            void* v_cache, int64_t n_slots, int64_t max_seq, int32_t* err_flags,
+                            const LaunchOpts& o) {
+  if (n_tokens < 0 || n_heads < 0 || n_kv_heads < 0 || head_dim < 0 || n_slots < 0 || max_seq < 0) {
+    return fail(KLLM_B200_ERR_INVALID_ARG, "qkv_bias_rope_kv_append: negative size");
+  }
+  if (n_tokens == 0) return KLLM_B200_OK;
+  if (head_dim == 0 || head_dim % 2 != 0 || head_dim > 2 * kMaxHalf) {
+    return fail(KLLM_B200_ERR_SHAPE, "qkv_bias_rope_kv_append: head_dim %lld must be even and <= %d",
+                (long long)head_dim, 2 * kMaxHalf);
+  }
+  if (!q || !k || !v || !positions || !slots || !k_cache || !v_cache) {
+    return fail(KLLM_B200_ERR_INVALID_ARG, "qkv_bias_rope_kv_append: null pointer");
+  }
+  if (n_slots < 1 || max_seq < 1) return fail(KLLM_B200_ERR_SHAPE, "qkv_bias_rope_kv_append: empty cache");
+  if ((bq || bk || bv) && !is_float_dtype(bias_dtype)) {
+    return fail(KLLM_B200_ERR_DTYPE, "qkv_bias_rope_kv_append: bias dtype %d not supported", bias_dtype);
+  }
+  if (n_heads * head_dim > (1 << 24) || n_kv_heads * head_dim > (1 << 24)) {
+    return fail(KLLM_B200_ERR_SHAPE, "qkv_bias_rope_kv_append: rows too wide");
+  }
+  RopeArgs a = {};
+  a.q = static_cast<__half*>(q);
+  a.k = static_cast<const __half*>(k);
+  a.v = static_cast<const __half*>(v);
+  a.bq = bq;
+  a.bk = bk;
+  a.bv = bv;
+  a.positions = positions;
+  a.slots = slots;
+  a.n_tokens = n_tokens;
+  a.n_heads = static_cast<int>(n_heads);
+  a.n_kv_heads = static_cast<int>(n_kv_heads);
+  a.head_dim = static_cast<int>(head_dim);
+  a.k_cache = static_cast<__half*>(k_cache);
+  a.v_cache = static_cast<__half*>(v_cache);
+  a.n_slots = n_slots;
+  a.max_seq = max_seq;
+  a.err_flags = err_flags;
+  fill_inv_freq(a, theta);
+  return run_rope(a, KLLM_B200_F16, bias_dtype, o, "qkv_bias_rope_kv_append");
+}
+
+}  // namespace kb
+
+extern "C" int kllm_b200_qkv_bias_rope_kv_append(void* q, const void* k, const void* v, const void* bq,
+                                                 const void* bk, const void* bv, int bias_dtype,
+                                                 const int32_t* positions, const int32_t* slots, int64_t n_tokens,
+                                                 int64_t n_heads, int64_t n_kv_heads, int64_t head_dim,
+                                                 float theta, void* k_cache, void* v_cache, int64_t n_slots,
+                                                 int64_t max_seq, int32_t* err_flags, void* stream) {
+  kb::LaunchOpts o;
+  o.stream = static_cast<cudaStream_t>(stream);
+  return kb::qkv_bias_rope_kv_append(q, k, v, bq, bk, bv, bias_dtype, positions, slots, n_tokens, n_heads,
+                                     n_kv_heads, head_dim, theta, k_cache, v_cache, n_slots, max_seq, err_flags, o);
+}
+
+extern "C" int kllm_b200_rope_inplace(void* x, int64_t seq, int64_t heads, int64_t head_dim, int32_t past_len,
+                                      float theta, int dtype, void* stream) {
+  using namespace kb;
+  if (seq < 0 || heads < 0 || head_dim < 0) return fail(KLLM_B200_ERR_INVALID_ARG, "rope_inplace: negative size");
+  if (head_dim % 2 != 0) return fail(KLLM_B200_ERR_SHAPE, "rope requires an even head_dim");
+  if (seq == 0 || heads == 0 || head_dim == 0) return KLLM_B200_OK;
+  if (head_dim > 2 * kMaxHalf) return fail(KLLM_B200_ERR_SHAPE, "rope_inplace: head_dim > %d", 2 * kMaxHalf);
+  if (!x) return fail(KLLM_B200_ERR_INVALID_ARG, "rope_inplace: null pointer");
+  if (!is_float_dtype(dtype)) return fail(KLLM_B200_ERR_DTYPE, "rope_inplace: dtype %d not supported", dtype);
+  if (heads * head_dim > (1 << 24)) return fail(KLLM_B200_ERR_SHAPE, "rope_inplace: rows too wide");
+  RopeArgs a = {};
+  a.q = static_cast<__half*>(x);
+  a.past_len = past_len;
+  a.n_tokens = seq;
+  a.n_heads = static_cast<int>(heads);
+  a.head_dim = static_cast<int>(head_dim);
+  fill_inv_freq(a, theta);
+  LaunchOpts o;
+  o.stream = static_cast<cudaStream_t>(stream);
+  return run_rope(a, dtype, KLLM_B200_F16, o, "rope_inplace");
+}
+
+extern "C" int kllm_b200_copy_kv_to_cache(const void* k, const void* v, int64_t seq, int64_t kv_heads,
+                                          int64_t head_dim, void* k_cache, void* v_cache, int64_t max_seq,
+                                          int32_t past_len, int src_dtype, int cache_dtype, void* stream) {
+  using namespace kb;
+  if (seq < 0 || kv_heads < 0 || head_dim < 0 || max_seq < 0) {
+    return fail(KLLM_B200_ERR_INVALID_ARG, "copy_kv_to_cache: negative size");
+  }
+  if (past_len < 0) return fail(KLLM_B200_ERR_RANGE, "copy_kv_to_cache: negative past_len %d", past_len);
+  if (static_cast<int64_t>(past_len) + seq > max_seq) return fail(KLLM_B200_ERR_CAPACITY, "KV cache capacity exceeded");
+  if (!is_float_dtype(src_dtype) || !is_float_dtype(cache_dtype)) {
+    return fail(KLLM_B200_ERR_DTYPE, "copy_kv_to_cache: dtypes %d/%d not supported", src_dtype, cache_dtype);
+  }
+  const int64_t row = kv_heads * head_dim;
+  const int64_t n = seq * row;
+  if (n == 0) return KLLM_B200_OK;
+  if (!k || !v || !k_cache || !v_cache) return fail(KLLM_B200_ERR_INVALID_ARG, "copy_kv_to_cache: null pointer");
+  LaunchOpts o;
+  o.stream = static_cast<cudaStream_t>(stream);
+  const int esz = dtype_size(cache_dtype);
+  char* kc = static_cast<char*>(k_cache) + static_cast<int64_t>(past_len) * row * esz;
+  char* vc = static_cast<char*>(v_cache) + static_cast<int64_t>(past_len) * row * esz;
+  if (src_dtype == cache_dtype && (n * esz) % 16 == 0 && aligned16(k) && aligned16(v) && aligned16(kc) &&
+      aligned16(vc)) {
+    const int64_t nvec = n * esz / 16;
+    const unsigned grid = persistent_grid(copy_kv_vec_kernel, kThreads, 0, kThreads, 2 * nvec);
+    return launch_status(launch(copy_kv_vec_kernel, grid, kThreads, 0, o.stream, o.pdl,
+                                static_cast<const uint4*>(k), static_cast<const uint4*>(v),
+                                reinterpret_cast<uint4*>(kc), reinterpret_cast<uint4*>(vc), nvec),
+                         "copy_kv_to_cache");
+  }
+  if (src_dtype == KLLM_B200_F16) {
+    return cache_dtype == KLLM_B200_F16 ? run_copy_kv_generic<__half, __half>(k, v, kc, vc, n, o)
+                                        : run_copy_kv_generic<__half, float>(k, v, kc, vc, n, o);
+  }
+  return cache_dtype == KLLM_B200_F16 ? run_copy_kv_generic<float, __half>(k, v, kc, vc, n, o)
+                                      : run_copy_kv_generic<float, float>(k, v, kc, vc, n, o);
+}

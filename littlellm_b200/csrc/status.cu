@@ -1,0 +1,78 @@
+// status.cu — error reporting and device queries for the C ABI.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "common.cuh"
+
+namespace kb {
+namespace {
+thread_local std::string t_last_error;
+constexpr int kMaxDevices = 64;
+int g_sm_count[kMaxDevices];  // 0 = not yet queried; benign racy cache of a constant
+}  // namespace
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  return code;
+}
+
+int launch_status(cudaError_t err, const char* what) {
+  if (err == cudaSuccess) err = cudaGetLastError();
+  if (err != cudaSuccess) {
+    (void)cudaGetLastError();
+    return fail(KLLM_B200_ERR_CUDA, "%s: %s", what, cudaGetErrorString(err));
+  }
+  return KLLM_B200_OK;
+}
+
+int sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    (void)cudaGetLastError();
+    return 148;
+  }
+  int v = __atomic_load_n(&g_sm_count[dev], __ATOMIC_RELAXED);
+  if (v == 0) {
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v < 1) {
+      (void)cudaGetLastError();
+      v = 148;
+    }
+    __atomic_store_n(&g_sm_count[dev], v, __ATOMIC_RELAXED);
+  }
+  return v;
+}
+
+}  // namespace kb
+
+extern "C" size_t kllm_b200_last_error(char* buf, size_t len) {
+  const std::string& m = kb::t_last_error;
+  if (buf != nullptr && len > 0) {
+    const size_t n = m.size() < len - 1 ? m.size() : len - 1;
+    std::memcpy(buf, m.data(), n);
+    buf[n] = '\0';
+  }
+  return m.size();
+}
+
+extern "C" const char* kllm_b200_status_string(int status) {
+  switch (status) {
+    case KLLM_B200_OK: return "ok";
+    case KLLM_B200_ERR_INVALID_ARG: return "invalid argument";
+    case KLLM_B200_ERR_SHAPE: return "shape mismatch";
+    case KLLM_B200_ERR_DTYPE: return "unsupported dtype";
+    case KLLM_B200_ERR_ALIGN: return "misaligned pointer";
+    case KLLM_B200_ERR_RANGE: return "value out of range";
+    case KLLM_B200_ERR_CAPACITY: return "KV cache capacity exceeded";
+    case KLLM_B200_ERR_CUDA: return "CUDA error";
+    default: return "unknown status";
+  }
+}
+
+extern "C" int kllm_b200_version(void) { return 100; }

@@ -1,0 +1,218 @@
+"""torch-facing wrappers of the C ABI.
+
+One function per operator of the reference interface
+(``include/kllm/op/ops.h:10-35``: embedding, rms_norm, add_bias_inplace,
+add_inplace, select_last_row, silu_mul, rope_inplace, copy_kv_to_cache,
+dequantize_int8) plus the fused/batched entry points (add_rms_norm,
+qkv_bias_rope_kv_append, select_last_rows). Each takes CUDA tensors, passes
+their device pointers to ``libkllm_b200.so`` on the tensor's current stream
+and raises ``KllmError`` with the library's message on a non-zero status,
+the way the reference throws ``std::runtime_error``.
+
+torch supplies device memory and streams here; all arithmetic happens in the
+library's kernels.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _capi
+from ._capi import F16, F32, I8, I32, KllmError, check, lib
+
+_DTYPES = {torch.float32: F32, torch.float16: F16, torch.int32: I32, torch.int8: I8}
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DTYPES[t.dtype]
+    except KeyError:
+        raise KllmError(_capi.ERR_DTYPE, f"unsupported tensor dtype {t.dtype}") from None
+
+
+def _dev(*tensors):
+    """Checks that every given tensor is a contiguous CUDA tensor on one device
+    and returns that device."""
+    device = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise KllmError(_capi.ERR_INVALID_ARG, "expected a CUDA tensor")
+        if not t.is_contiguous():
+            raise KllmError(_capi.ERR_SHAPE, "expected a contiguous tensor")
+        if device is None:
+            device = t.device
+        elif t.device != device:
+            raise KllmError(_capi.ERR_INVALID_ARG, "tensors are on different devices")
+    return device
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def embedding(table: torch.Tensor, ids: torch.Tensor, out: torch.Tensor | None = None,
+              err_flags: torch.Tensor | None = None) -> torch.Tensor:
+    """out[t] = table[ids[t]] (reference embedding, ids on the device)."""
+    if out is None:
+        out = torch.empty((ids.numel(), table.shape[1]), dtype=table.dtype, device=table.device)
+    dev = _dev(table, ids, out, err_flags)
+    if ids.dtype != torch.int32:
+        raise KllmError(_capi.ERR_DTYPE, "ids must be int32")
+    with torch.cuda.device(dev):
+        check(lib.kllm_b200_embedding(_ptr(table), table.shape[0], table.shape[1], dtype_code(table),
+                                      _ptr(ids), ids.numel(), _ptr(out), dtype_code(out),
+                                      _ptr(err_flags), _stream(dev)))
+    return out
+
+
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float,
+             out: torch.Tensor | None = None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty_like(x)
+    dev = _dev(x, weight, out)
+    hidden = x.shape[-1]
+    with torch.cuda.device(dev):
+        check(lib.kllm_b200_rms_norm(_ptr(x), _ptr(weight), _ptr(out), x.numel() // hidden, hidden,
+                                     eps, dtype_code(x), dtype_code(weight), _stream(dev)))
+    return out
+
+
+def add_rms_norm(residual: torch.Tensor, delta: torch.Tensor | None, weight: torch.Tensor,
+                 eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    """residual += delta (stored, fp16-rounded); returns RMSNorm(residual) * weight."""
+    if out is None:
+        out = torch.empty_like(residual)
+    dev = _dev(residual, delta, weight, out)
+    hidden = residual.shape[-1]
+    with torch.cuda.device(dev):
+        check(lib.kllm_b200_add_rms_norm(_ptr(residual), _ptr(delta), _ptr(weight), _ptr(out),
+                                         residual.numel() // hidden, hidden, eps,
+                                         dtype_code(residual), dtype_code(weight), _stream(dev)))
+    return out
+
+
+def add_inplace(x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
+    dev = _dev(x, y)
+    if x.numel() != y.numel():
+        raise KllmError(_capi.ERR_SHAPE, "add shape mismatch")
+    with torch.cuda.device(dev):
+        check(lib.kllm_b200_add_inplace(_ptr(x), _ptr(y), x.numel(), dtype_code(x), dtype_code(y),
+                                        _stream(dev)))
+    return x
+
+
+def add_bias_inplace(x: torch.Tensor, bias: torch.Tensor | None) -> torch.Tensor:
+    if bias is None:
+        return x
+    dev = _dev(x, bias)
+    cols = x.shape[-1]
+    with torch.cuda.device(dev):
+        check(lib.kllm_b200_add_bias_inplace(_ptr(x), _ptr(bias), x.numel() // cols, cols,
+                                             dtype_code(x), dtype_code(bias), _stream(dev)))
+    return x
+
+
+def select_last_row(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty((1, x.shape[-1]), dtype=x.dtype, device=x.device)
+    dev = _dev(x, out)
+    cols = x.shape[-1]
+    with torch.cuda.device(dev):
+        check(lib.kllm_b200_select_last_row(_ptr(x), x.numel() // cols, cols, _ptr(out),
+                                            dtype_code(x), _stream(dev)))
+    return out
+
+
+def select_last_rows(x: torch.Tensor, seq_len: int = 0, n_seqs: int | None = None,
+                     seq_ends: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                     err_flags: torch.Tensor | None = None) -> torch.Tensor:
+    cols = x.shape[-1]
+    rows = x.numel() // cols
+    if seq_ends is not None:
+        n_seqs = seq_ends.numel()
+    elif n_seqs is None:
+        n_seqs = rows // seq_len
+    if out is None:
+        out = torch.empty((n_seqs, cols), dtype=x.dtype, device=x.device)
+    dev = _dev(x, out, seq_ends, err_flags)
+    with torch.cuda.device(dev):
+        check(lib.kllm_b200_select_last_rows(_ptr(x), rows, cols, _ptr(seq_ends), seq_len, n_seqs,
+                                             _ptr(out), dtype_code(x), _ptr(err_flags),
+                                             _stream(dev)))
+    return out
+
+
+def silu_mul(gate: torch.Tensor, up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty_like(gate)
+    dev = _dev(gate, up, out)
+    if not (gate.numel() == up.numel() == out.numel()):
+        raise KllmError(_capi.ERR_SHAPE, "silu_mul shape mismatch")
+    if not (gate.dtype == up.dtype == out.dtype):
+        raise KllmError(_capi.ERR_DTYPE, "silu_mul dtype mismatch")
+    with torch.cuda.device(dev):
+        check(lib.kllm_b200_silu_mul(_ptr(gate), _ptr(up), _ptr(out), gate.numel(),
+                                     dtype_code(gate), _stream(dev)))
+    return out
+
+
+def rope_inplace(x: torch.Tensor, past_len: int, theta: float) -> torch.Tensor:
+    """x [seq, heads, head_dim] rotated in place at positions past_len + t."""
+    dev = _dev(x)
+    seq, heads, head_dim = x.shape
+    with torch.cuda.device(dev):
+        check(lib.kllm_b200_rope_inplace(_ptr(x), seq, heads, head_dim, past_len, theta,
+                                         dtype_code(x), _stream(dev)))
+    return x
+
+
+def copy_kv_to_cache(k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor,
+                     v_cache: torch.Tensor, past_len: int) -> None:
+    """k/v [seq, kv_heads, head_dim] -> caches [max_seq, kv_heads, head_dim] at past_len."""
+    dev = _dev(k, v, k_cache, v_cache)
+    seq, kv_heads, head_dim = k.shape
+    with torch.cuda.device(dev):
+        check(lib.kllm_b200_copy_kv_to_cache(_ptr(k), _ptr(v), seq, kv_heads, head_dim,
+                                             _ptr(k_cache), _ptr(v_cache), k_cache.shape[0],
+                                             past_len, dtype_code(k), dtype_code(k_cache),
+                                             _stream(dev)))
+
+
+def qkv_bias_rope_kv_append(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                            bq: torch.Tensor | None, bk: torch.Tensor | None,
+                            bv: torch.Tensor | None, positions: torch.Tensor,
+                            slots: torch.Tensor, theta: float, k_cache: torch.Tensor,
+                            v_cache: torch.Tensor,
+                            err_flags: torch.Tensor | None = None) -> None:
+    """q [T, Hq, D] rotated in place; k/v [T, Hkv, D] appended (rotated /
+    biased) into caches [n_slots, Hkv, max_seq, D]."""
+    dev = _dev(q, k, v, bq, bk, bv, positions, slots, k_cache, v_cache, err_flags)
+    T, Hq, D = q.shape
+    Hkv = k.shape[1]
+    bias = next((b for b in (bq, bk, bv) if b is not None), None)
+    bias_dtype = dtype_code(bias) if bias is not None else F16
+    with torch.cuda.device(dev):
+        check(lib.kllm_b200_qkv_bias_rope_kv_append(
+            _ptr(q), _ptr(k), _ptr(v), _ptr(bq), _ptr(bk), _ptr(bv), bias_dtype, _ptr(positions),
+            _ptr(slots), T, Hq, Hkv, D, theta, _ptr(k_cache), _ptr(v_cache), k_cache.shape[0],
+            k_cache.shape[2], _ptr(err_flags), _stream(dev)))
+
+
+def dequantize_int8(data: torch.Tensor, scale: torch.Tensor,
+                    out_dtype: torch.dtype = torch.float16,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    """out = data * scale[0]; fp16 output rounds like the reference weight loader."""
+    if out is None:
+        out = torch.empty(data.shape, dtype=out_dtype, device=data.device)
+    dev = _dev(data, scale, out)
+    if data.dtype != torch.int8 or scale.dtype != torch.float32:
+        raise KllmError(_capi.ERR_DTYPE, "dequantize_int8 expects int8 data and an fp32 scale")
+    with torch.cuda.device(dev):
+        check(lib.kllm_b200_dequantize_int8(_ptr(data), _ptr(scale), _ptr(out), data.numel(),
+                                            dtype_code(out), _stream(dev)))
+    return out

@@ -1,0 +1,120 @@
+"""The C ABI on the CPU: the library loads, exports exactly what
+include/kllm_b200.h declares, and rejects bad arguments with the documented
+status codes before touching a GPU."""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "kllm_b200.h")
+
+
+@pytest.fixture(scope="module")
+def capi():
+    from littlellm_b200 import build
+    build.build()
+    from littlellm_b200 import _capi
+    return _capi
+
+
+def declared_functions() -> set[str]:
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return set(re.findall(r"\b(kllm_b200_[a-z0-9_]+)\s*\(", text))
+
+
+def test_exports_match_header(capi):
+    declared = declared_functions()
+    assert len(declared) >= 16
+    out = subprocess.run(["nm", "-D", "--defined-only", capi.LIB_PATH if hasattr(capi, "LIB_PATH")
+                          else capi.lib._name], capture_output=True, text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line and "kllm_b200_" in line}
+    assert declared == exported, (declared ^ exported)
+    for name in declared:
+        assert hasattr(capi.lib, name)
+    assert set(capi.SIGNATURES) == declared
+
+
+def test_version_and_messages(capi):
+    assert capi.lib.kllm_b200_version() >= 100
+    assert capi.lib.kllm_b200_status_string(capi.ERR_CAPACITY) == b"KV cache capacity exceeded"
+    assert capi.lib.kllm_b200_status_string(12345) == b"unknown status"
+
+
+def _rc_msg(capi, rc):
+    return rc, capi.last_error()
+
+
+def test_argument_validation_without_gpu(capi):
+    lib = capi.lib
+    # null pointers
+    rc, msg = _rc_msg(capi, lib.kllm_b200_silu_mul(None, None, None, 8, capi.F16, None))
+    assert rc == capi.ERR_INVALID_ARG and "null" in msg
+    # negative sizes
+    assert lib.kllm_b200_add_inplace(1, 1, -1, capi.F16, capi.F16, None) == capi.ERR_INVALID_ARG
+    # unsupported dtypes
+    assert lib.kllm_b200_rms_norm(16, 16, 16, 4, 8, 1e-6, capi.I8, capi.F16, None) == capi.ERR_DTYPE
+    assert lib.kllm_b200_dequantize_int8(16, 16, 16, 8, capi.I32, None) == capi.ERR_DTYPE
+    # odd head_dim (the reference: "rope requires an even head_dim")
+    rc, msg = _rc_msg(capi, lib.kllm_b200_rope_inplace(16, 2, 2, 7, 0, 1e4, capi.F16, None))
+    assert rc == capi.ERR_SHAPE and "even" in msg
+    rc = lib.kllm_b200_qkv_bias_rope_kv_append(16, 16, 16, None, None, None, capi.F16, 16, 16, 4, 2, 2, 258,
+                                               1e4, 16, 16, 1, 8, None, None)
+    assert rc == capi.ERR_SHAPE
+    # KV capacity, as the reference CPU path checks it
+    rc, msg = _rc_msg(capi, lib.kllm_b200_copy_kv_to_cache(16, 16, 4, 2, 8, 16, 16, 10, 7, capi.F16, capi.F16,
+                                                           None))
+    assert rc == capi.ERR_CAPACITY and "capacity" in msg
+    assert lib.kllm_b200_copy_kv_to_cache(16, 16, 1, 2, 8, 16, 16, 10, -1, capi.F16, capi.F16,
+                                          None) == capi.ERR_RANGE
+    # select_last_rows with more rows requested than exist
+    assert lib.kllm_b200_select_last_rows(16, 10, 8, None, 4, 3, 16, capi.F16, None, None) == capi.ERR_SHAPE
+    # chain: null descriptor
+    assert lib.kllm_b200_chain_run(None, None, None) == capi.ERR_INVALID_ARG
+
+
+def test_empty_inputs_are_noops(capi):
+    lib = capi.lib
+    assert lib.kllm_b200_silu_mul(None, None, None, 0, capi.F16, None) == capi.OK
+    assert lib.kllm_b200_embedding(None, 10, 8, capi.F16, None, 0, None, capi.F16, None, None) == capi.OK
+    assert lib.kllm_b200_add_bias_inplace(16, None, 4, 4, capi.F16, capi.F16, None) == capi.OK  # null bias
+    assert lib.kllm_b200_dequantize_int8(None, None, None, 0, capi.F16, None) == capi.OK
+
+
+def test_python_wrappers_refuse_host_tensors(capi):
+    import torch
+
+    from littlellm_b200 import ops
+    x = torch.zeros(16, dtype=torch.float16)
+    with pytest.raises(capi.KllmError) as e:
+        ops.silu_mul(x, x)
+    assert e.value.status == capi.ERR_INVALID_ARG
+
+
+def test_last_error_is_per_thread(capi):
+    import threading
+    lib = capi.lib
+    lib.kllm_b200_rope_inplace(16, 2, 2, 7, 0, 1e4, capi.F16, None)
+    seen = {}
+
+    def other():
+        lib.kllm_b200_silu_mul(None, None, None, 8, capi.F16, None)
+        seen["msg"] = capi.last_error()
+
+    t = threading.Thread(target=other)
+    t.start()
+    t.join()
+    assert "null" in seen["msg"]
+    assert "even" in capi.last_error()
+
+
+def test_chain_struct_layout(capi):
+    # the ctypes mirror of kllm_b200_chain must match the C layout: 12 int64,
+    # 2 floats, 2 ints, 9 pointers, the layers pointer and err_flags
+    assert ctypes.sizeof(capi.Chain) == 12 * 8 + 2 * 4 + 2 * 4 + 11 * 8
+    assert ctypes.sizeof(capi.LayerBuffers) == 17 * 8

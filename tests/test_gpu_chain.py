@@ -1,0 +1,90 @@
+"""The native chain executor (kllm_b200_chain_run) against the oracle applied
+op by op in the reference's order (src/model/llama.cpp:78-178), with the
+residual stream held in fp16 as the reference's CUDA runner holds it."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import assert_tol, bits16, host
+
+pytestmark = pytest.mark.gpu
+
+
+def f16r(a):
+    return np.asarray(a, np.float32).astype(np.float16).astype(np.float32)
+
+
+def _tiny(decode: bool):
+    from littlellm_b200.chain import ModelShape, Workload
+    shape = ModelShape("tiny", 128, 4, 2, 32, 384, 1000, 3, 1e-6, 1e4)
+    if decode:
+        return Workload("tiny_decode", shape, n_seqs=9, seq_len=1, max_seq=64, decode=True)
+    return Workload("tiny_prefill", shape, n_seqs=3, seq_len=17, max_seq=64, decode=False)
+
+
+@pytest.mark.parametrize("decode", [False, True])
+@pytest.mark.parametrize("use_pdl", [False, True])
+def test_chain_matches_oracle(cuda, oracle, decode, use_pdl):
+    from littlellm_b200.chain import ChainRunner
+    w = _tiny(decode)
+    m = w.model
+    r = ChainRunner(w, device=cuda, seed=3, use_pdl=use_pdl)
+    snap = [{k: host(t) for k, t in L.items()} for L in r.layers]
+    table, ids = host(r.table), r.ids.cpu().numpy()
+    pos, slots = r.positions.cpu().numpy(), r.slots.cpu().numpy()
+    launches = r.run()
+    torch.cuda.synchronize()
+    assert launches == 1 + 4 * m.n_layers + 2
+    assert int(r.err_flags.item()) == 0
+
+    T, D = w.n_tokens, m.head_dim
+    res = oracle.embedding(table, ids)
+    for l, L in enumerate(snap):
+        if l > 0:
+            res = f16r(res + snap[l - 1]["ffn_out"])
+        assert_tol(host(r.layers[l]["attn_norm_out"]), oracle.rms_norm(res, L["input_norm_w"], m.eps),
+                   what=f"attn_norm {l}")
+        zeros = np.zeros((w.n_seqs, m.n_kv_heads, w.max_seq, D), np.float32)
+        q_ref, kc_ref, vc_ref, skipped = oracle.qkv_bias_rope_kv_append(
+            L["q"].reshape(T, m.n_heads, D), L["k"].reshape(T, m.n_kv_heads, D),
+            L["v"].reshape(T, m.n_kv_heads, D), L["q_bias"], L["k_bias"], L["v_bias"], pos, slots,
+            m.theta, zeros, zeros)
+        assert skipped == 0
+        assert_tol(host(r.layers[l]["q"]).reshape(T, m.n_heads, D), q_ref, what=f"q {l}")
+        kc, vc = host(r.layers[l]["k_cache"]), host(r.layers[l]["v_cache"])
+        assert_tol(kc[slots, :, pos], kc_ref[slots, :, pos], what=f"k cache {l}")
+        assert_tol(vc[slots, :, pos], vc_ref[slots, :, pos], what=f"v cache {l}")
+        res = f16r(res + L["attn_out"])
+        assert_tol(host(r.layers[l]["ffn_norm_out"]), oracle.rms_norm(res, L["post_norm_w"], m.eps),
+                   what=f"ffn_norm {l}")
+        assert_tol(host(r.layers[l]["swiglu_out"]), oracle.silu_mul(L["gate"], L["up"]), what=f"swiglu {l}")
+    res = f16r(res + snap[-1]["ffn_out"])
+    # the running residual is bit-exact: fp32 sums of the same fp16 values, rounded to nearest even
+    assert np.array_equal(bits16(r.residual), res.astype(np.float16).view(np.uint16))
+    final = oracle.rms_norm(res, host(r.final_norm_w), m.eps)
+    assert_tol(host(r.final_norm_out), final, what="final norm")
+    last = final[w.seq_len - 1::w.seq_len]
+    assert np.array_equal(bits16(r.last_rows), bits16(r.final_norm_out)[w.seq_len - 1::w.seq_len])
+    assert_tol(host(r.last_rows), last, what="last rows")
+
+
+def test_chain_graph_replay_equals_eager(cuda):
+    """A CUDA graph of the chain (as the benchmark replays it) writes what an
+    eager launch writes."""
+    from littlellm_b200.chain import ChainRunner
+    w = _tiny(False)
+    a = ChainRunner(w, device=cuda, seed=9, use_pdl=True)
+    b = ChainRunner(w, device=cuda, seed=9, use_pdl=True)
+    a.run()
+    s = torch.cuda.Stream(cuda)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        b.run(s)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(a.final_norm_out, b.final_norm_out)
+    assert torch.equal(a.layers[-1]["swiglu_out"], b.layers[-1]["swiglu_out"])
+    assert torch.equal(a.layers[0]["q"], b.layers[0]["q"])
+    del g
