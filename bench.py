@@ -390,33 +390,35 @@ def run_ours(args):
     stream = torch.cuda.Stream(device)
     torch.cuda.synchronize(device)
 
-    # one chain step = one CUDA graph replay
-    launches = runner.run(stream)
-    stream.synchronize()
-    graph = capture(lambda: runner.run(stream), stream)
-    for _ in range(max(args.warmup, 3)):
-        graph.replay()
-    stream.synchronize()
-
-    sampler = ClockSampler(device)
-    sampler.start()
-    # let clocks settle under load (untimed)
-    t_end = time.perf_counter() + args.settle_seconds
-    while time.perf_counter() < t_end:
-        for _ in range(20):
+    # one chain step = one CUDA graph replay; every replay, event and sync
+    # below is issued on `stream` (CUDAGraph.replay() uses the current stream)
+    with torch.cuda.stream(stream):
+        launches = runner.run(stream)
+        stream.synchronize()
+        graph = capture(lambda: runner.run(stream), stream)
+        for _ in range(max(args.warmup, 3)):
             graph.replay()
         stream.synchronize()
 
-    if dist is not None:
-        dist.barrier()
-    torch.cuda.synchronize(device)
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record(stream)
-    for _ in range(args.steps):
-        graph.replay()
-    end.record(stream)
-    end.synchronize()
-    torch.cuda.synchronize(device)
+        sampler = ClockSampler(device)
+        sampler.start()
+        # let clocks settle under load (untimed)
+        t_end = time.perf_counter() + args.settle_seconds
+        while time.perf_counter() < t_end:
+            for _ in range(20):
+                graph.replay()
+            stream.synchronize()
+
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        end.record(stream)
+        end.synchronize()
+        torch.cuda.synchronize(device)
     if dist is not None:
         dist.barrier()
     elapsed_ms = start.elapsed_time(end)

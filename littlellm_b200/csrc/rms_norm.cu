@@ -7,10 +7,11 @@
 // a group of G threads (8..256) owns a row; each thread holds VPT 16-byte
 // vectors of the row in registers, so the row is read from HBM once, the
 // residual written once and the output written once (4*H*2 bytes per row
-// with a delta, 2*H*2 without). G and VPT are picked per hidden size to
-// leave no idle lanes where possible (H=896: G=16 x VPT=7; H=4096: G=128 x
-// VPT=4). Sub-warp groups reduce with shuffles; multi-warp groups add one
-// shared-memory exchange. CTAs stride over row groups (one wave of CTAs).
+// with a delta, 2*H*2 without). G and VPT are picked per hidden size (H=896:
+// one warp per row, VPT=4; H=4096: G=128, VPT=4) so registers stay at 64 and
+// small CTAs (128 threads) spread the rows evenly over the SMs. Sub-warp
+// groups reduce with shuffles; multi-warp groups add one shared-memory
+// exchange. CTAs stride over row groups (one wave of CTAs).
 //
 // Arithmetic: r = fp16_rn(a + d) (what the reference's fp16 add_inplace
 // stores), sum of r^2 in fp32, scale = rsqrt(sum / H + eps), y = (r * scale)
@@ -20,7 +21,8 @@
 namespace kb {
 namespace {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 256;      // largest CTA (generic path, widest rows)
+constexpr int kFastThreads = 128;  // CTA of the fast path unless a row needs more
 
 template <typename TW>
 struct WeightVec;
@@ -61,7 +63,7 @@ __global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __re
   grid_dep_launch();
 
   const int nvec = hidden >> 3;
-  const int rows_per_cta = kThreads / group;
+  const int rows_per_cta = blockDim.x / group;
   const int lane_g = threadIdx.x % group;          // position inside the row group
   const int row_in_cta = threadIdx.x / group;
   const int warp = threadIdx.x >> 5;
@@ -173,31 +175,30 @@ struct FastConfig {
   int vpt = 0;
 };
 
-// Smallest number of idle lanes, then VPT closest to 4.
+// Row-group width G and 16-byte vectors per thread VPT for a row of nvec
+// vectors: rows of up to 128 vectors (H <= 1024) get one warp each (or a
+// quarter/half warp when tiny), wider rows the smallest multi-warp group that
+// keeps VPT <= 4 (VPT <= 8 above 1024 vectors). Small VPT keeps registers at
+// or below 64 so enough rows are resident per SM to cover DRAM latency.
 FastConfig pick_config(int nvec) {
-  FastConfig best;
-  int best_waste = 1 << 30, best_dist = 1 << 30;
-  for (int g = 8; g <= kThreads; g <<= 1) {
-    const int vpt = (nvec + g - 1) / g;
-    if (vpt < 1 || vpt > 8) continue;
-    const int waste = g * vpt - nvec;
-    const int dist = vpt > 4 ? vpt - 4 : 4 - vpt;
-    if (waste < best_waste || (waste == best_waste && dist < best_dist)) {
-      best = {g, vpt};
-      best_waste = waste;
-      best_dist = dist;
-    }
+  if (nvec <= 8) return {8, 1};
+  if (nvec <= 16) return {16, 1};
+  if (nvec <= 128) return {32, (nvec + 31) / 32};
+  for (int g = 64; g <= kThreads; g <<= 1) {
+    if (nvec <= 4 * g) return {g, (nvec + g - 1) / g};
   }
-  return best;
+  if (nvec <= 8 * kThreads) return {kThreads, (nvec + kThreads - 1) / kThreads};
+  return {};
 }
 
 template <int VPT, typename TW, bool HAS_DELTA>
 int launch_fast(void* residual, const void* delta, const void* weight, void* out, int64_t rows, int hidden,
                 int group, float eps, const LaunchOpts& o) {
   auto k = add_rms_norm_f16_kernel<VPT, TW, HAS_DELTA>;
-  const int rows_per_cta = kThreads / group;
-  const unsigned grid = persistent_grid(k, kThreads, 0, rows_per_cta, rows);
-  return launch_status(launch(k, grid, kThreads, 0, o.stream, o.pdl, static_cast<__half*>(residual),
+  const int threads = group > kFastThreads ? group : kFastThreads;
+  const int rows_per_cta = threads / group;
+  const unsigned grid = persistent_grid(k, threads, 0, rows_per_cta, rows);
+  return launch_status(launch(k, grid, threads, 0, o.stream, o.pdl, static_cast<__half*>(residual),
                               static_cast<const __half*>(delta), static_cast<const TW*>(weight),
                               static_cast<__half*>(out), rows, hidden, group, eps),
                        "add_rms_norm");

@@ -5,15 +5,15 @@
 // 2x rope_inplace src/op/cuda/rope.cu:188-201 and copy_kv_to_cache
 // src/op/cuda/kv_cache.cu:32-41, as called at src/model/llama.cpp:89-114).
 //
-// A CTA owns a tile of tokens. Phase 1 computes cos/sin of every
-// (token, frequency) of the tile once into shared memory — the angle depends
-// only on the position and d, so all q and k heads of a token share it.
-// Phase 2 walks work units over the tile:
-//   rotation unit = 8 consecutive pairs (d0..d0+7 with d0+half..) of one q or
-//                   k head: two 16-byte loads, two 16-byte stores;
-//   copy unit     = 16 bytes of one v head.
-// q is rotated in place; k (rotated) and v (biased) go straight to the
-// head-major cache [slot, kv_head, pos, d], so neither is written back.
+// Work unit = 8 consecutive rotation pairs of one q or k head (d0..d0+7 with
+// d0+half..: two 16-byte loads, two 16-byte stores) or 16 bytes of one v
+// head. Each token is owned by one or more warps (enough that a lane holds at
+// most 4 units); a warp issues all its loads first, computes the cos/sin of
+// the token's frequencies into its slice of shared memory while they are in
+// flight, then rotates and stores. The angle depends only on position and d,
+// so all q and k heads of the token share one sincos per frequency. q is
+// rotated in place; k (rotated) and v (biased) go straight to the head-major
+// cache [slot, kv_head, pos, d], so neither is written back.
 //
 // Frequencies: inv_freq[d] = powf(theta, (-2 * d) / head_dim) evaluated on
 // the host in fp32 (the expression of src/op/cpu/rope.cpp:24, which is also
@@ -30,7 +30,8 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kMaxHalf = 128;   // head_dim <= 256
-constexpr int kMaxTok = 32;     // tokens per CTA tile
+constexpr int kWarpsPerCta = 4;
+constexpr int kWarpThreads = 32 * kWarpsPerCta;
 
 struct RopeArgs {
   __half* q;
@@ -48,7 +49,7 @@ struct RopeArgs {
   __half* v_cache;
   int64_t n_slots, max_seq;
   int32_t* err_flags;
-  int tok_per_cta;
+  int warps_per_token;
   float inv_freq[kMaxHalf];
 };
 
@@ -92,65 +93,100 @@ __device__ __forceinline__ float2 angle_cs(int32_t pos, float inv_freq) {
   return make_float2(c, s);
 }
 
-template <typename TB>
-__global__ void __launch_bounds__(kThreads) qkv_rope_f16_kernel(const __grid_constant__ RopeArgs a) {
-  extern __shared__ float2 cs[];  // [tok_per_cta][half] = (cos, sin)
-  __shared__ int32_t s_pos[kMaxTok];
-  __shared__ int64_t s_dst[kMaxTok];  // element offset of (slot, head 0, pos, 0); -1 = skip cache write
+// One token is owned by `warps_per_token` warps; the token's work units are
+// dealt to its warps' lanes round-robin (consecutive units on consecutive
+// lanes, so loads and stores coalesce), UPL units per lane. A warp first
+// issues the global loads of all its units, then computes the cos/sin of the
+// token's frequencies (one or a few per lane, into the warp's slice of shared
+// memory) while those loads are in flight, and only then rotates and stores.
+// No CTA-wide barrier sits between the loads and the math.
+template <int UPL, typename TB>
+__global__ void __launch_bounds__(kWarpThreads) qkv_rope_warp_kernel(const __grid_constant__ RopeArgs a) {
+  __shared__ float s_freq[kMaxHalf];
+  __shared__ float2 s_cs[kWarpsPerCta][kMaxHalf];
 
   grid_dep_wait();
   grid_dep_launch();
 
   const int half = a.head_dim >> 1;
-  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * a.tok_per_cta;
-  const int64_t left = a.n_tokens - t0;
-  const int ntok = left < a.tok_per_cta ? static_cast<int>(left) : a.tok_per_cta;
+  for (int i = threadIdx.x; i < half; i += blockDim.x) s_freq[i] = a.inv_freq[i];
 
-  if (threadIdx.x < ntok) {
-    const int64_t t = t0 + threadIdx.x;
-    const int32_t pos = a.positions ? __ldg(a.positions + t) : a.past_len + static_cast<int32_t>(t);
-    const int32_t slot = a.slots ? __ldg(a.slots + t) : 0;
-    s_pos[threadIdx.x] = pos;
-    int64_t dst = -1;
-    if (a.k_cache != nullptr || a.v_cache != nullptr) {
-      const bool pos_ok = pos >= 0 && pos < a.max_seq;
-      const bool slot_ok = slot >= 0 && slot < a.n_slots;
-      if (!pos_ok) set_flag(a.err_flags, KLLM_B200_FLAG_BAD_POSITION);
-      if (!slot_ok) set_flag(a.err_flags, KLLM_B200_FLAG_BAD_SLOT);
-      if (pos_ok && slot_ok) dst = (static_cast<int64_t>(slot) * a.n_kv_heads * a.max_seq + pos) * a.head_dim;
-    }
-    s_dst[threadIdx.x] = dst;
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < ntok * half; i += blockDim.x) {
-    const int tl = i / half;
-    const int d = i - tl * half;
-    cs[i] = angle_cs(s_pos[tl], a.inv_freq[d]);
-  }
-  __syncthreads();
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t gw = static_cast<int64_t>(blockIdx.x) * kWarpsPerCta + warp;
+  const int64_t t = gw / a.warps_per_token;
+  const int part = static_cast<int>(gw - t * a.warps_per_token);
+  const bool live = t < a.n_tokens;  // uniform per warp
 
-  const int chunks = a.head_dim >> 4;   // rotation units per head
-  const int vchunks = a.head_dim >> 3;  // copy units per v head
+  const int chunks = a.head_dim >> 4;   // rotation units per head (8 pairs each)
+  const int vchunks = a.head_dim >> 3;  // copy units per v head (16 bytes each)
   const int rot_q = a.n_heads * chunks;
   const int rot_k = a.k ? a.n_kv_heads * chunks : 0;
-  const int cp_v = a.v ? a.n_kv_heads * vchunks : 0;
-  const int per_tok = rot_q + rot_k + cp_v;
-  const int64_t head_stride_cache = a.max_seq * a.head_dim;
+  const int n_rot = rot_q + rot_k;
+  const int n_units = n_rot + (a.v ? a.n_kv_heads * vchunks : 0);
 
-  for (int u = threadIdx.x; u < ntok * per_tok; u += blockDim.x) {
-    const int tl = u / per_tok;
-    const int w = u - tl * per_tok;
-    const int64_t t = t0 + tl;
-    if (w < rot_q + rot_k) {
-      const bool is_q = w < rot_q;
-      const int ww = is_q ? w : w - rot_q;
-      const int h = ww / chunks;
-      const int d0 = (ww - h * chunks) << 3;
-      const int heads = is_q ? a.n_heads : a.n_kv_heads;
-      const __half* src = (is_q ? static_cast<const __half*>(a.q) : a.k) + (t * heads + h) * a.head_dim;
-      float x1[8], x2[8];
-      unpack8(is_q ? ld_cg(src + d0) : ld_stream(src + d0), x1);
-      unpack8(is_q ? ld_cg(src + d0 + half) : ld_stream(src + d0 + half), x2);
+  uint4 x1[UPL], x2[UPL];
+  int unit[UPL];
+  int32_t pos = 0, slot = 0;
+  if (live) {
+    pos = a.positions ? __ldg(a.positions + t) : a.past_len + static_cast<int32_t>(t);
+    slot = a.slots ? __ldg(a.slots + t) : 0;
+#pragma unroll
+    for (int j = 0; j < UPL; ++j) {
+      const int u = (part * UPL + j) * 32 + lane;
+      unit[j] = u < n_units ? u : -1;
+      if (u < n_rot) {
+        const bool is_q = u < rot_q;
+        const int w = is_q ? u : u - rot_q;
+        const int h = w / chunks;
+        const int d0 = (w - h * chunks) << 3;
+        const int64_t row = is_q ? (t * a.n_heads + h) * a.head_dim : (t * a.n_kv_heads + h) * a.head_dim;
+        const __half* src = (is_q ? static_cast<const __half*>(a.q) : a.k) + row + d0;
+        x1[j] = is_q ? ld_cg(src) : ld_stream(src);
+        x2[j] = is_q ? ld_cg(src + half) : ld_stream(src + half);
+      } else if (u < n_units) {
+        const int w = u - n_rot;
+        const int h = w / vchunks;
+        const int d0 = (w - h * vchunks) << 3;
+        x1[j] = ld_stream(a.v + (t * a.n_kv_heads + h) * a.head_dim + d0);
+      }
+    }
+  }
+  __syncthreads();  // s_freq visible; every thread reaches this point
+  if (!live) return;
+  for (int d = lane; d < half; d += 32) {
+    float s, c;
+    sincosf(__fmul_rn(static_cast<float>(pos), s_freq[d]), &s, &c);
+    s_cs[warp][d] = make_float2(c, s);
+  }
+  __syncwarp();
+
+  bool cache_ok = true;
+  if (a.k_cache != nullptr || a.v_cache != nullptr) {
+    const bool pos_ok = pos >= 0 && pos < a.max_seq;
+    const bool slot_ok = slot >= 0 && slot < a.n_slots;
+    if (part == 0 && lane == 0) {
+      if (!pos_ok) set_flag(a.err_flags, KLLM_B200_FLAG_BAD_POSITION);
+      if (!slot_ok) set_flag(a.err_flags, KLLM_B200_FLAG_BAD_SLOT);
+    }
+    cache_ok = pos_ok && slot_ok;
+  }
+  // element offset of [slot, head 0, pos, 0] in a [n_slots, n_kv_heads, max_seq, head_dim] plane
+  const int64_t cache_base = (static_cast<int64_t>(slot) * a.n_kv_heads * a.max_seq + pos) * a.head_dim;
+  const int64_t head_stride = a.max_seq * a.head_dim;
+
+#pragma unroll
+  for (int j = 0; j < UPL; ++j) {
+    const int u = unit[j];
+    if (u < 0) continue;
+    if (u < n_rot) {
+      const bool is_q = u < rot_q;
+      const int w = is_q ? u : u - rot_q;
+      const int h = w / chunks;
+      const int d0 = (w - h * chunks) << 3;
+      float f1[8], f2[8];
+      unpack8(x1[j], f1);
+      unpack8(x2[j], f2);
       const void* bias = is_q ? a.bq : a.bk;
       if (bias != nullptr) {
         float b1[8], b2[8];
@@ -158,31 +194,32 @@ __global__ void __launch_bounds__(kThreads) qkv_rope_f16_kernel(const __grid_con
         load_bias8<TB>(bias, static_cast<int64_t>(h) * a.head_dim + d0 + half, b2);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          x1[i] = round_f16(x1[i] + b1[i]);
-          x2[i] = round_f16(x2[i] + b2[i]);
+          f1[i] = round_f16(f1[i] + b1[i]);
+          f2[i] = round_f16(f2[i] + b2[i]);
         }
       }
-      const float2* csr = cs + tl * half + d0;
+      const float2* csr = &s_cs[warp][d0];
       float y1[8], y2[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const float2 c = csr[i];
-        rotate(x1[i], x2[i], c.x, c.y, y1[i], y2[i]);
+        rotate(f1[i], f2[i], c.x, c.y, y1[i], y2[i]);
       }
+      __half* dst;
       if (is_q) {
-        __half* dst = a.q + (t * a.n_heads + h) * a.head_dim;
-        st_plain(dst + d0, pack8(y1));
-        st_plain(dst + d0 + half, pack8(y2));
-      } else if (a.k_cache != nullptr && s_dst[tl] >= 0) {
-        __half* dst = a.k_cache + s_dst[tl] + h * head_stride_cache;
-        st_plain(dst + d0, pack8(y1));
-        st_plain(dst + d0 + half, pack8(y2));
+        dst = a.q + (t * a.n_heads + h) * a.head_dim + d0;
+      } else {
+        if (a.k_cache == nullptr || !cache_ok) continue;
+        dst = a.k_cache + cache_base + h * head_stride + d0;
       }
+      st_plain(dst, pack8(y1));
+      st_plain(dst + half, pack8(y2));
     } else {
-      const int ww = w - rot_q - rot_k;
-      const int h = ww / vchunks;
-      const int d0 = (ww - h * vchunks) << 3;
-      uint4 x = ld_stream(a.v + (t * a.n_kv_heads + h) * a.head_dim + d0);
+      if (a.v_cache == nullptr || !cache_ok) continue;
+      const int w = u - n_rot;
+      const int h = w / vchunks;
+      const int d0 = (w - h * vchunks) << 3;
+      uint4 x = x1[j];
       if (a.bv != nullptr) {
         float xf[8], b[8];
         unpack8(x, xf);
@@ -191,7 +228,7 @@ __global__ void __launch_bounds__(kThreads) qkv_rope_f16_kernel(const __grid_con
         for (int i = 0; i < 8; ++i) xf[i] = xf[i] + b[i];
         x = pack8(xf);
       }
-      if (a.v_cache != nullptr && s_dst[tl] >= 0) st_plain(a.v_cache + s_dst[tl] + h * head_stride_cache + d0, x);
+      st_plain(a.v_cache + cache_base + h * head_stride + d0, x);
     }
   }
 }
@@ -284,14 +321,21 @@ int run_rope(RopeArgs& a, int act_dtype, int bias_dtype, const LaunchOpts& o, co
                     al(a.bk) && al(a.bv) && al(a.k_cache) && al(a.v_cache);
   if (fast) {
     const int chunks = D / 16;
-    const int per_tok = a.n_heads * chunks + (a.k ? a.n_kv_heads * chunks : 0) + (a.v ? a.n_kv_heads * D / 8 : 0);
-    int tok = per_tok > 0 ? (320 + per_tok - 1) / per_tok : kMaxTok;
-    tok = tok < 1 ? 1 : tok > kMaxTok ? kMaxTok : tok;
-    a.tok_per_cta = tok;
-    const size_t smem = static_cast<size_t>(tok) * (D / 2) * sizeof(float2);
-    const unsigned grid = static_cast<unsigned>((a.n_tokens + tok - 1) / tok);
-    auto k = bias16 ? qkv_rope_f16_kernel<__half> : qkv_rope_f16_kernel<float>;
-    return launch_status(launch(k, grid, kThreads, smem, o.stream, o.pdl, a), what);
+    const int units = a.n_heads * chunks + (a.k ? a.n_kv_heads * chunks : 0) + (a.v ? a.n_kv_heads * D / 8 : 0);
+    // spread a token over enough warps that each lane holds at most 4 units
+    const int wpt = units > 0 ? (units + 32 * 4 - 1) / (32 * 4) : 1;
+    const int upl = units > 0 ? (units + 32 * wpt - 1) / (32 * wpt) : 1;
+    a.warps_per_token = wpt;
+    const int64_t warps = a.n_tokens * wpt;
+    const unsigned grid = static_cast<unsigned>((warps + kWarpsPerCta - 1) / kWarpsPerCta);
+    void (*k)(RopeArgs);
+    switch (upl) {
+      case 1: k = bias16 ? qkv_rope_warp_kernel<1, __half> : qkv_rope_warp_kernel<1, float>; break;
+      case 2: k = bias16 ? qkv_rope_warp_kernel<2, __half> : qkv_rope_warp_kernel<2, float>; break;
+      case 3: k = bias16 ? qkv_rope_warp_kernel<3, __half> : qkv_rope_warp_kernel<3, float>; break;
+      default: k = bias16 ? qkv_rope_warp_kernel<4, __half> : qkv_rope_warp_kernel<4, float>; break;
+    }
+    return launch_status(launch(k, grid, kWarpThreads, 0, o.stream, o.pdl, a), what);
   }
   const int per_tok = a.n_heads * (D / 2) + (a.k ? a.n_kv_heads * (D / 2) : 0) + (a.v ? a.n_kv_heads * D : 0);
   const int64_t total = a.n_tokens * per_tok;

@@ -33,12 +33,12 @@ def assert_tol(actual, expected, tol: float = TOL, what: str = "") -> None:
                            f"max abs err {err.max():.3g} at {np.unravel_index(err.argmax(), err.shape)}")
 
 
-def padded(n: int, dtype, canary: float = 12345.0, pad: int = 64, device="cuda:0"):
+def padded(n: int, dtype, canary: float = -1234.0, pad: int = 64, device="cuda:0"):
     """A buffer of n elements followed by `pad` canary elements; returns
     (whole, view_of_first_n)."""
     whole = torch.full((n + pad,), canary, dtype=dtype, device=device)
     return whole, whole[:n]
 
 
-def canary_intact(whole: torch.Tensor, n: int, canary: float = 12345.0) -> bool:
+def canary_intact(whole: torch.Tensor, n: int, canary: float = -1234.0) -> bool:
     return bool((whole[n:].float() == canary).all().item())

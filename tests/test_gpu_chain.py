@@ -71,8 +71,9 @@ def test_chain_matches_oracle(cuda, oracle, decode, use_pdl):
 
 
 def test_chain_graph_replay_equals_eager(cuda):
-    """A CUDA graph of the chain (as the benchmark replays it) writes what an
-    eager launch writes."""
+    """A CUDA graph of the chain (as the benchmark replays it) does the work
+    of an eager launch: outputs cleared after capture are rewritten by the
+    replay with the eager values."""
     from littlellm_b200.chain import ChainRunner
     w = _tiny(False)
     a = ChainRunner(w, device=cuda, seed=9, use_pdl=True)
@@ -82,9 +83,18 @@ def test_chain_graph_replay_equals_eager(cuda):
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g, stream=s):
         b.run(s)
-    g.replay()
+    torch.cuda.synchronize()
+    b.final_norm_out.zero_()
+    b.last_rows.zero_()
+    for L in b.layers:
+        L["swiglu_out"].zero_()
+        L["attn_norm_out"].zero_()
+    with torch.cuda.stream(s):
+        g.replay()
     torch.cuda.synchronize()
     assert torch.equal(a.final_norm_out, b.final_norm_out)
+    assert torch.equal(a.last_rows, b.last_rows)
     assert torch.equal(a.layers[-1]["swiglu_out"], b.layers[-1]["swiglu_out"])
+    assert torch.equal(a.layers[1]["attn_norm_out"], b.layers[1]["attn_norm_out"])
     assert torch.equal(a.layers[0]["q"], b.layers[0]["q"])
     del g
