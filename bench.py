@@ -49,6 +49,8 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample length")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="run only this many decoder layers (small profiling cases; not a bench line)")
     ap.add_argument("--settle-seconds", type=float, default=1.5,
                     help="untimed graph replays before timing so clocks settle under load")
     return ap.parse_args()
@@ -386,7 +388,7 @@ def run_ours(args):
     base = WORKLOADS[args.workload]
     weak = args.workload == "qwen_prefill"
     w = base if weak else shard(base, rank, world)
-    runner = ChainRunner(w, device=device, seed=1000 + rank, use_pdl=not args.no_pdl)
+    runner = ChainRunner(w, device=device, seed=1000 + rank, use_pdl=not args.no_pdl, n_layers=args.layers)
     stream = torch.cuda.Stream(device)
     torch.cuda.synchronize(device)
 
@@ -431,7 +433,7 @@ def run_ours(args):
     ms_per_step = max_ms / args.steps
     tokens_total = w.n_tokens * world
     value = tokens_total / (ms_per_step * 1e-3)
-    bytes_step = chain_bytes(w)
+    bytes_step = chain_bytes(w, runner.n_layers)
     chain_gbs = bytes_step["total"] / (ms_per_step * 1e-3) / 1e9
     peaks = load_peaks()
 
@@ -470,9 +472,9 @@ def run_ours(args):
             "scaling": "weak" if weak else "strong", "vs_baseline": None, "dtype": "f16",
             "data": "synthetic",
             "config": {
-                "workload": w.name, "model": w.model.name, "layers": w.model.n_layers,
+                "workload": w.name, "model": w.model.name, "layers": runner.n_layers,
                 "tokens_per_gpu": w.n_tokens, "sequences_per_gpu": w.n_seqs, "seq_len": w.seq_len,
-                "kv_cache": [w.model.n_layers, 2, w.n_seqs, w.model.n_kv_heads, w.max_seq, w.model.head_dim],
+                "kv_cache": [runner.n_layers, 2, w.n_seqs, w.model.n_kv_heads, w.max_seq, w.model.head_dim],
                 "parallelism": f"dp{world} (sequences split, no collective on the path)",
                 "math": "fp16 storage, fp32 arithmetic",
                 "l2": "no flush: each step streams %.2f GB of distinct per-layer buffers (>> 126 MB L2)"

@@ -74,12 +74,12 @@ def shard(workload: Workload, rank: int, world: int) -> Workload:
     return replace(workload, n_seqs=workload.n_seqs // world)
 
 
-def chain_bytes(w: Workload) -> dict:
+def chain_bytes(w: Workload, n_layers: int | None = None) -> dict:
     """Algorithmic HBM bytes of one chain step: every logical fp16 tensor read
     once and written once; norm weights and biases are negligible and not
     counted; ids/positions/slots are int32."""
     m, T = w.model, w.n_tokens
-    H, I, L = m.hidden, m.intermediate, m.n_layers
+    H, I, L = m.hidden, m.intermediate, n_layers or m.n_layers
     qkv_elems = T * (m.n_heads + 2 * m.n_kv_heads) * m.head_dim
     per = {
         "embedding": 2 * T * H * 2 + 4 * T,

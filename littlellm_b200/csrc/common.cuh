@@ -35,23 +35,18 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 int sm_count();
 
 // Resident CTAs per SM for `kernel` at `threads` threads and `smem` bytes of
-// dynamic shared memory; computed once per kernel (all devices of one box are
-// the same part).
+// dynamic shared memory (cached per (kernel, threads, smem); all devices of
+// one box are the same part).
+int resident_ctas_raw(const void* kernel, int threads, size_t smem);
+
 template <typename Kernel>
 int resident_ctas(Kernel kernel, int threads, size_t smem) {
-  static int cached = 0;
-  int v = __atomic_load_n(&cached, __ATOMIC_RELAXED);
-  if (v == 0) {
-    int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, smem) != cudaSuccess || n < 1) {
-      (void)cudaGetLastError();
-      n = 1;
-    }
-    __atomic_store_n(&cached, n, __ATOMIC_RELAXED);
-    v = n;
-  }
-  return v;
+  return resident_ctas_raw(reinterpret_cast<const void*>(kernel), threads, smem);
 }
+
+// Opt `kernel` in to `smem` bytes of dynamic shared memory when that exceeds
+// the 48 KB default (once per kernel and size).
+cudaError_t allow_smem(const void* kernel, size_t smem);
 
 // Grid for a grid-stride kernel: one full wave of resident CTAs, never more
 // CTAs than work items.
@@ -131,6 +126,11 @@ __device__ __forceinline__ void st_stream(void* p, uint4 v) {
   asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
                "r"(v.w)
                : "memory");
+}
+
+// Pull the line holding `p` into L1 ahead of a later load.
+__device__ __forceinline__ void prefetch_l1(const void* p) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
 }
 
 // 16-byte plain store.

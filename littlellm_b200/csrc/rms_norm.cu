@@ -24,13 +24,15 @@ namespace {
 constexpr int kThreads = 256;      // largest CTA (generic path, widest rows)
 constexpr int kFastThreads = 128;  // CTA of the fast path unless a row needs more
 
+// Eight weights starting at element `col` of the weight vector (shared or
+// global memory, generic loads).
 template <typename TW>
 struct WeightVec;
 
 template <>
 struct WeightVec<__half> {
-  __device__ __forceinline__ static void load(const __half* w, int64_t col, float (&out)[8]) {
-    const uint4 v = ld_keep(w + col);
+  __device__ __forceinline__ static void load(const __half* w, int col, float (&out)[8]) {
+    const uint4 v = *reinterpret_cast<const uint4*>(w + col);
     const float2 a = h2_to_f2(v.x), b = h2_to_f2(v.y), c = h2_to_f2(v.z), d = h2_to_f2(v.w);
     out[0] = a.x; out[1] = a.y; out[2] = b.x; out[3] = b.y;
     out[4] = c.x; out[5] = c.y; out[6] = d.x; out[7] = d.y;
@@ -39,9 +41,9 @@ struct WeightVec<__half> {
 
 template <>
 struct WeightVec<float> {
-  __device__ __forceinline__ static void load(const float* w, int64_t col, float (&out)[8]) {
-    const float4 a = __ldg(reinterpret_cast<const float4*>(w + col));
-    const float4 b = __ldg(reinterpret_cast<const float4*>(w + col + 4));
+  __device__ __forceinline__ static void load(const float* w, int col, float (&out)[8]) {
+    const float4 a = *reinterpret_cast<const float4*>(w + col);
+    const float4 b = *reinterpret_cast<const float4*>(w + col + 4);
     out[0] = a.x; out[1] = a.y; out[2] = a.z; out[3] = a.w;
     out[4] = b.x; out[5] = b.y; out[6] = b.z; out[7] = b.w;
   }
@@ -52,13 +54,29 @@ __device__ __forceinline__ float sumsq_h2(uint32_t w) {
   return f.x * f.x + f.y * f.y;
 }
 
-template <int VPT, typename TW, bool HAS_DELTA>
+template <int VPT, typename TW, bool HAS_DELTA, bool EARLY>
 __global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __restrict__ residual,
                                                                     const __half* __restrict__ delta,
                                                                     const TW* __restrict__ weight,
                                                                     __half* __restrict__ out, int64_t rows,
                                                                     int hidden, int group, float eps) {
+  extern __shared__ __align__(16) unsigned char s_raw[];
   __shared__ float partial[2][kThreads / 32];
+  // With EARLY (the PDL launch of the chain executor) the norm weight, which
+  // no chain kernel writes, is staged into shared memory before the
+  // grid-dependency wait, overlapping the previous kernel's tail, and the
+  // output phase reads it from shared memory. A standalone launch reads it
+  // from global memory (L1/L2) instead, keeping the staging off its critical
+  // path.
+  const TW* w_src = weight;
+  if (EARLY) {
+    const int wvec = static_cast<int>(hidden * sizeof(TW) / 16);
+    const uint4* wsrc = reinterpret_cast<const uint4*>(weight);
+    uint4* wdst = reinterpret_cast<uint4*>(s_raw);
+    for (int i = threadIdx.x; i < wvec; i += blockDim.x) wdst[i] = ld_keep(wsrc + i);
+    __syncthreads();
+    w_src = reinterpret_cast<const TW*>(s_raw);
+  }
   grid_dep_wait();
   grid_dep_launch();
 
@@ -122,7 +140,7 @@ __global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __re
         const int v = j * group + lane_g;
         if (v < nvec) {
           float w[8];
-          WeightVec<TW>::load(weight, static_cast<int64_t>(v) * 8, w);
+          WeightVec<TW>::load(w_src, v * 8, w);
           const float2 a0 = h2_to_f2(r[j].x), a1 = h2_to_f2(r[j].y), a2 = h2_to_f2(r[j].z), a3 = h2_to_f2(r[j].w);
           st_plain(orow + v * 8,
                    make_uint4(f2_to_h2(a0.x * scale * w[0], a0.y * scale * w[1]),
@@ -194,11 +212,14 @@ FastConfig pick_config(int nvec) {
 template <int VPT, typename TW, bool HAS_DELTA>
 int launch_fast(void* residual, const void* delta, const void* weight, void* out, int64_t rows, int hidden,
                 int group, float eps, const LaunchOpts& o) {
-  auto k = add_rms_norm_f16_kernel<VPT, TW, HAS_DELTA>;
+  auto k = o.pdl ? add_rms_norm_f16_kernel<VPT, TW, HAS_DELTA, true> : add_rms_norm_f16_kernel<VPT, TW, HAS_DELTA, false>;
   const int threads = group > kFastThreads ? group : kFastThreads;
   const int rows_per_cta = threads / group;
-  const unsigned grid = persistent_grid(k, threads, 0, rows_per_cta, rows);
-  return launch_status(launch(k, grid, threads, 0, o.stream, o.pdl, static_cast<__half*>(residual),
+  const size_t smem = o.pdl ? static_cast<size_t>(hidden) * sizeof(TW) : 0;
+  const cudaError_t attr = allow_smem(reinterpret_cast<const void*>(k), smem);
+  if (attr != cudaSuccess) return launch_status(attr, "add_rms_norm");
+  const unsigned grid = persistent_grid(k, threads, smem, rows_per_cta, rows);
+  return launch_status(launch(k, grid, threads, smem, o.stream, o.pdl, static_cast<__half*>(residual),
                               static_cast<const __half*>(delta), static_cast<const TW*>(weight),
                               static_cast<__half*>(out), rows, hidden, group, eps),
                        "add_rms_norm");

@@ -31,6 +31,7 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kMaxHalf = 128;   // head_dim <= 256
 constexpr int kWarpsPerCta = 4;
+constexpr size_t kMaxBiasStage = 16 * 1024;  // bytes of q/k/v bias staged per CTA
 constexpr int kWarpThreads = 32 * kWarpsPerCta;
 
 struct RopeArgs {
@@ -50,15 +51,18 @@ struct RopeArgs {
   int64_t n_slots, max_seq;
   int32_t* err_flags;
   int warps_per_token;
+  int stage_bias;  // biases fit the shared-memory staging area
   float inv_freq[kMaxHalf];
 };
 
+// Eight bias values at element `off`; `bias` may point to global or shared
+// memory (generic loads).
 template <typename TB>
 __device__ __forceinline__ void load_bias8(const void* bias, int64_t off, float (&b)[8]);
 
 template <>
 __device__ __forceinline__ void load_bias8<__half>(const void* bias, int64_t off, float (&b)[8]) {
-  const uint4 v = ld_keep(static_cast<const __half*>(bias) + off);
+  const uint4 v = *reinterpret_cast<const uint4*>(static_cast<const __half*>(bias) + off);
   const float2 a = h2_to_f2(v.x), c = h2_to_f2(v.y), d = h2_to_f2(v.z), e = h2_to_f2(v.w);
   b[0] = a.x; b[1] = a.y; b[2] = c.x; b[3] = c.y; b[4] = d.x; b[5] = d.y; b[6] = e.x; b[7] = e.y;
 }
@@ -66,9 +70,17 @@ __device__ __forceinline__ void load_bias8<__half>(const void* bias, int64_t off
 template <>
 __device__ __forceinline__ void load_bias8<float>(const void* bias, int64_t off, float (&b)[8]) {
   const float* p = static_cast<const float*>(bias) + off;
-  const float4 x = __ldg(reinterpret_cast<const float4*>(p));
-  const float4 y = __ldg(reinterpret_cast<const float4*>(p + 4));
+  const float4 x = *reinterpret_cast<const float4*>(p);
+  const float4 y = *reinterpret_cast<const float4*>(p + 4);
   b[0] = x.x; b[1] = x.y; b[2] = x.z; b[3] = x.w; b[4] = y.x; b[5] = y.y; b[6] = y.z; b[7] = y.w;
+}
+
+// Copies `bytes` (a multiple of 16) from global `src` to shared `dst` with the
+// whole CTA.
+__device__ __forceinline__ void stage16(void* dst, const void* src, int bytes) {
+  const uint4* s = static_cast<const uint4*>(src);
+  uint4* d = static_cast<uint4*>(dst);
+  for (int i = threadIdx.x; i < (bytes >> 4); i += blockDim.x) d[i] = ld_keep(s + i);
 }
 
 __device__ __forceinline__ void unpack8(uint4 v, float (&f)[8]) {
@@ -95,18 +107,20 @@ __device__ __forceinline__ float2 angle_cs(int32_t pos, float inv_freq) {
 
 // One token is owned by `warps_per_token` warps; the token's work units are
 // dealt to its warps' lanes round-robin (consecutive units on consecutive
-// lanes, so loads and stores coalesce), UPL units per lane. A warp first
-// issues the global loads of all its units, then computes the cos/sin of the
-// token's frequencies (one or a few per lane, into the warp's slice of shared
-// memory) while those loads are in flight, and only then rotates and stores.
-// No CTA-wide barrier sits between the loads and the math.
-template <int UPL, typename TB>
+// lanes, so loads and stores coalesce), UPL units per lane. The cos/sin of
+// the token's frequencies go into the warp's slice of shared memory (one or
+// a few sincosf per lane); the q/k/v biases are staged in shared memory.
+//
+// Positions, slots, biases and the frequency table are never written by a
+// kernel of the chain, so with EARLY (the PDL launch of the chain executor)
+// the bias staging, position load and sincos run before the grid-dependency
+// wait, overlapping the previous kernel's tail, and only the activation loads
+// wait. Without PDL the activation loads are issued first and the staging
+// and sincos run while they are in flight.
+template <int UPL, typename TB, bool EARLY>
 __global__ void __launch_bounds__(kWarpThreads) qkv_rope_warp_kernel(const __grid_constant__ RopeArgs a) {
   __shared__ float s_freq[kMaxHalf];
   __shared__ float2 s_cs[kWarpsPerCta][kMaxHalf];
-
-  grid_dep_wait();
-  grid_dep_launch();
 
   const int half = a.head_dim >> 1;
   for (int i = threadIdx.x; i < half; i += blockDim.x) s_freq[i] = a.inv_freq[i];
@@ -125,40 +139,86 @@ __global__ void __launch_bounds__(kWarpThreads) qkv_rope_warp_kernel(const __gri
   const int n_rot = rot_q + rot_k;
   const int n_units = n_rot + (a.v ? a.n_kv_heads * vchunks : 0);
 
+  // unit j of this lane: kind 0 = q rotation, 1 = k rotation, 2 = v copy, -1 none
+  int kind[UPL], head[UPL], dcol[UPL];
+#pragma unroll
+  for (int j = 0; j < UPL; ++j) {
+    const int u = (part * UPL + j) * 32 + lane;
+    if (!live || u >= n_units) {
+      kind[j] = -1; head[j] = 0; dcol[j] = 0;
+    } else if (u < n_rot) {
+      const bool is_q = u < rot_q;
+      const int w = is_q ? u : u - rot_q;
+      kind[j] = is_q ? 0 : 1;
+      head[j] = w / chunks;
+      dcol[j] = (w - head[j] * chunks) << 3;
+    } else {
+      const int w = u - n_rot;
+      kind[j] = 2;
+      head[j] = w / vchunks;
+      dcol[j] = (w - head[j] * vchunks) << 3;
+    }
+  }
+
   uint4 x1[UPL], x2[UPL];
-  int unit[UPL];
+  auto issue_loads = [&]() {
+#pragma unroll
+    for (int j = 0; j < UPL; ++j) {
+      if (kind[j] < 0) continue;
+      if (kind[j] < 2) {
+        const bool is_q = kind[j] == 0;
+        const int64_t row = (t * (is_q ? a.n_heads : a.n_kv_heads) + head[j]) * a.head_dim;
+        const __half* src = (is_q ? static_cast<const __half*>(a.q) : a.k) + row + dcol[j];
+        x1[j] = is_q ? ld_cg(src) : ld_stream(src);
+        x2[j] = is_q ? ld_cg(src + half) : ld_stream(src + half);
+      } else {
+        x1[j] = ld_stream(a.v + (t * a.n_kv_heads + head[j]) * a.head_dim + dcol[j]);
+      }
+    }
+  };
+  // Without PDL nothing precedes this kernel's start: issue the activation
+  // loads first, then stage biases and compute cos/sin while they fly.
+  if (!EARLY) {
+    grid_dep_wait();
+    grid_dep_launch();
+    issue_loads();
+  }
+
+  // Biases are small and never written by a chain kernel: stage them in
+  // shared memory (q, k, v back to back) before the dependency wait.
+  extern __shared__ __align__(16) unsigned char s_bias[];
+  const void* bq = a.bq;
+  const void* bk = a.bk;
+  const void* bv = a.bv;
+  if (a.stage_bias) {
+    const int qb = a.n_heads * a.head_dim * static_cast<int>(sizeof(TB));
+    const int kb = a.n_kv_heads * a.head_dim * static_cast<int>(sizeof(TB));
+    if (a.bq) { stage16(s_bias, a.bq, qb); bq = s_bias; }
+    if (a.bk) { stage16(s_bias + qb, a.bk, kb); bk = s_bias + qb; }
+    if (a.bv) { stage16(s_bias + qb + kb, a.bv, kb); bv = s_bias + qb + kb; }
+  }
+
   int32_t pos = 0, slot = 0;
   if (live) {
     pos = a.positions ? __ldg(a.positions + t) : a.past_len + static_cast<int32_t>(t);
     slot = a.slots ? __ldg(a.slots + t) : 0;
-#pragma unroll
-    for (int j = 0; j < UPL; ++j) {
-      const int u = (part * UPL + j) * 32 + lane;
-      unit[j] = u < n_units ? u : -1;
-      if (u < n_rot) {
-        const bool is_q = u < rot_q;
-        const int w = is_q ? u : u - rot_q;
-        const int h = w / chunks;
-        const int d0 = (w - h * chunks) << 3;
-        const int64_t row = is_q ? (t * a.n_heads + h) * a.head_dim : (t * a.n_kv_heads + h) * a.head_dim;
-        const __half* src = (is_q ? static_cast<const __half*>(a.q) : a.k) + row + d0;
-        x1[j] = is_q ? ld_cg(src) : ld_stream(src);
-        x2[j] = is_q ? ld_cg(src + half) : ld_stream(src + half);
-      } else if (u < n_units) {
-        const int w = u - n_rot;
-        const int h = w / vchunks;
-        const int d0 = (w - h * vchunks) << 3;
-        x1[j] = ld_stream(a.v + (t * a.n_kv_heads + h) * a.head_dim + d0);
-      }
+  }
+  __syncthreads();  // s_freq and staged biases visible; every thread reaches this point
+
+  auto fill_cs = [&]() {
+    for (int d = lane; d < half; d += 32) {
+      float sn, cs;
+      sincosf(__fmul_rn(static_cast<float>(pos), s_freq[d]), &sn, &cs);
+      s_cs[warp][d] = make_float2(cs, sn);
     }
+  };
+  if (live) fill_cs();
+  if (EARLY) {
+    grid_dep_wait();
+    grid_dep_launch();
+    issue_loads();
   }
-  __syncthreads();  // s_freq visible; every thread reaches this point
   if (!live) return;
-  for (int d = lane; d < half; d += 32) {
-    float s, c;
-    sincosf(__fmul_rn(static_cast<float>(pos), s_freq[d]), &s, &c);
-    s_cs[warp][d] = make_float2(c, s);
-  }
   __syncwarp();
 
   bool cache_ok = true;
@@ -177,17 +237,15 @@ __global__ void __launch_bounds__(kWarpThreads) qkv_rope_warp_kernel(const __gri
 
 #pragma unroll
   for (int j = 0; j < UPL; ++j) {
-    const int u = unit[j];
-    if (u < 0) continue;
-    if (u < n_rot) {
-      const bool is_q = u < rot_q;
-      const int w = is_q ? u : u - rot_q;
-      const int h = w / chunks;
-      const int d0 = (w - h * chunks) << 3;
+    if (kind[j] < 0) continue;
+    const int h = head[j];
+    const int d0 = dcol[j];
+    if (kind[j] < 2) {
+      const bool is_q = kind[j] == 0;
       float f1[8], f2[8];
       unpack8(x1[j], f1);
       unpack8(x2[j], f2);
-      const void* bias = is_q ? a.bq : a.bk;
+      const void* bias = is_q ? bq : bk;
       if (bias != nullptr) {
         float b1[8], b2[8];
         load_bias8<TB>(bias, static_cast<int64_t>(h) * a.head_dim + d0, b1);
@@ -216,14 +274,11 @@ __global__ void __launch_bounds__(kWarpThreads) qkv_rope_warp_kernel(const __gri
       st_plain(dst + half, pack8(y2));
     } else {
       if (a.v_cache == nullptr || !cache_ok) continue;
-      const int w = u - n_rot;
-      const int h = w / vchunks;
-      const int d0 = (w - h * vchunks) << 3;
       uint4 x = x1[j];
-      if (a.bv != nullptr) {
+      if (bv != nullptr) {
         float xf[8], b[8];
         unpack8(x, xf);
-        load_bias8<TB>(a.bv, static_cast<int64_t>(h) * a.head_dim + d0, b);
+        load_bias8<TB>(bv, static_cast<int64_t>(h) * a.head_dim + d0, b);
 #pragma unroll
         for (int i = 0; i < 8; ++i) xf[i] = xf[i] + b[i];
         x = pack8(xf);
@@ -328,14 +383,27 @@ int run_rope(RopeArgs& a, int act_dtype, int bias_dtype, const LaunchOpts& o, co
     a.warps_per_token = wpt;
     const int64_t warps = a.n_tokens * wpt;
     const unsigned grid = static_cast<unsigned>((warps + kWarpsPerCta - 1) / kWarpsPerCta);
+    const size_t bias_bytes = static_cast<size_t>(a.n_heads + 2 * a.n_kv_heads) * D * (bias16 ? 2 : 4);
+    const bool any_bias = a.bq || a.bk || a.bv;
+    a.stage_bias = any_bias && bias_bytes <= kMaxBiasStage;
+    const size_t smem = a.stage_bias ? bias_bytes : 0;
     void (*k)(RopeArgs);
-    switch (upl) {
-      case 1: k = bias16 ? qkv_rope_warp_kernel<1, __half> : qkv_rope_warp_kernel<1, float>; break;
-      case 2: k = bias16 ? qkv_rope_warp_kernel<2, __half> : qkv_rope_warp_kernel<2, float>; break;
-      case 3: k = bias16 ? qkv_rope_warp_kernel<3, __half> : qkv_rope_warp_kernel<3, float>; break;
-      default: k = bias16 ? qkv_rope_warp_kernel<4, __half> : qkv_rope_warp_kernel<4, float>; break;
+    if (o.pdl) {
+      switch (upl) {
+        case 1: k = bias16 ? qkv_rope_warp_kernel<1, __half, true> : qkv_rope_warp_kernel<1, float, true>; break;
+        case 2: k = bias16 ? qkv_rope_warp_kernel<2, __half, true> : qkv_rope_warp_kernel<2, float, true>; break;
+        case 3: k = bias16 ? qkv_rope_warp_kernel<3, __half, true> : qkv_rope_warp_kernel<3, float, true>; break;
+        default: k = bias16 ? qkv_rope_warp_kernel<4, __half, true> : qkv_rope_warp_kernel<4, float, true>; break;
+      }
+    } else {
+      switch (upl) {
+        case 1: k = bias16 ? qkv_rope_warp_kernel<1, __half, false> : qkv_rope_warp_kernel<1, float, false>; break;
+        case 2: k = bias16 ? qkv_rope_warp_kernel<2, __half, false> : qkv_rope_warp_kernel<2, float, false>; break;
+        case 3: k = bias16 ? qkv_rope_warp_kernel<3, __half, false> : qkv_rope_warp_kernel<3, float, false>; break;
+        default: k = bias16 ? qkv_rope_warp_kernel<4, __half, false> : qkv_rope_warp_kernel<4, float, false>; break;
+      }
     }
-    return launch_status(launch(k, grid, kWarpThreads, 0, o.stream, o.pdl, a), what);
+    return launch_status(launch(k, grid, kWarpThreads, smem, o.stream, o.pdl, a), what);
   }
   const int per_tok = a.n_heads * (D / 2) + (a.k ? a.n_kv_heads * (D / 2) : 0) + (a.v ? a.n_kv_heads * D : 0);
   const int64_t total = a.n_tokens * per_tok;

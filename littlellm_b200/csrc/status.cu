@@ -2,6 +2,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "common.cuh"
@@ -47,6 +48,51 @@ int sm_count() {
     __atomic_store_n(&g_sm_count[dev], v, __ATOMIC_RELAXED);
   }
   return v;
+}
+
+namespace {
+struct OccEntry {
+  const void* kernel;
+  int threads;
+  size_t smem;
+  int ctas;
+};
+std::mutex g_occ_mutex;
+OccEntry g_occ[256];
+int g_occ_n = 0;
+
+struct SmemEntry {
+  const void* kernel;
+  size_t smem;
+};
+SmemEntry g_smem[64];
+int g_smem_n = 0;
+}  // namespace
+
+int resident_ctas_raw(const void* kernel, int threads, size_t smem) {
+  std::lock_guard<std::mutex> lock(g_occ_mutex);
+  for (int i = 0; i < g_occ_n; ++i) {
+    if (g_occ[i].kernel == kernel && g_occ[i].threads == threads && g_occ[i].smem == smem) return g_occ[i].ctas;
+  }
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, smem) != cudaSuccess || n < 1) {
+    (void)cudaGetLastError();
+    n = 1;
+  }
+  if (g_occ_n < 256) g_occ[g_occ_n++] = {kernel, threads, smem, n};
+  return n;
+}
+
+cudaError_t allow_smem(const void* kernel, size_t smem) {
+  if (smem <= 48 * 1024) return cudaSuccess;
+  std::lock_guard<std::mutex> lock(g_occ_mutex);
+  for (int i = 0; i < g_smem_n; ++i) {
+    if (g_smem[i].kernel == kernel && g_smem[i].smem >= smem) return cudaSuccess;
+  }
+  const cudaError_t err =
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (err == cudaSuccess && g_smem_n < 64) g_smem[g_smem_n++] = {kernel, smem};
+  return err;
 }
 
 }  // namespace kb

@@ -16,19 +16,26 @@ def f16r(a):
     return np.asarray(a, np.float32).astype(np.float16).astype(np.float32)
 
 
-def _tiny(decode: bool):
+def _tiny(decode: bool, shape: str = "tiny"):
     from littlellm_b200.chain import ModelShape, Workload
-    shape = ModelShape("tiny", 128, 4, 2, 32, 384, 1000, 3, 1e-6, 1e4)
+    shapes = {
+        "tiny": ModelShape("tiny", 128, 4, 2, 32, 384, 1000, 3, 1e-6, 1e4),
+        # Qwen2.5-0.5B and Llama-2-7B layer shapes, 2 layers, small vocab
+        "qwen": ModelShape("qwen-2l", 896, 14, 2, 64, 4864, 2000, 2, 1e-6, 1e6),
+        "llama": ModelShape("llama-2l", 4096, 32, 32, 128, 11008, 2000, 2, 1e-5, 1e4),
+    }
+    m = shapes[shape]
     if decode:
-        return Workload("tiny_decode", shape, n_seqs=9, seq_len=1, max_seq=64, decode=True)
-    return Workload("tiny_prefill", shape, n_seqs=3, seq_len=17, max_seq=64, decode=False)
+        return Workload(f"{shape}_decode", m, n_seqs=9, seq_len=1, max_seq=64, decode=True)
+    return Workload(f"{shape}_prefill", m, n_seqs=3, seq_len=17, max_seq=64, decode=False)
 
 
+@pytest.mark.parametrize("shape", ["tiny", "qwen", "llama"])
 @pytest.mark.parametrize("decode", [False, True])
 @pytest.mark.parametrize("use_pdl", [False, True])
-def test_chain_matches_oracle(cuda, oracle, decode, use_pdl):
+def test_chain_matches_oracle(cuda, oracle, shape, decode, use_pdl):
     from littlellm_b200.chain import ChainRunner
-    w = _tiny(decode)
+    w = _tiny(decode, shape)
     m = w.model
     r = ChainRunner(w, device=cuda, seed=3, use_pdl=use_pdl)
     snap = [{k: host(t) for k, t in L.items()} for L in r.layers]
