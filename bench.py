@@ -29,7 +29,6 @@ import subprocess
 import sys
 import threading
 import time
-from datetime import timedelta
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
@@ -277,7 +276,7 @@ def run_reference(args):
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind, "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # ---------------------------------------------------------------------------
@@ -380,10 +379,11 @@ def run_ours(args):
     device = torch.device("cuda", local)
     kbuild.build()
 
+    from littlellm_b200 import dist as kd
     dist = None
     if world > 1:
         import torch.distributed as dist
-        dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=300))
+        kd.init("nccl", device, timeout_s=300)
 
     base = WORKLOADS[args.workload]
     weak = args.workload == "qwen_prefill"
@@ -429,6 +429,15 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     max_ms = float(t.item())
     clocks = sampler.stop()
+
+    # verification: every rank's last rows gathered to rank 0 (NCCL all_gather,
+    # off the timed path) and the device error flags OR-ed over ranks
+    flags = kd.or_over_ranks(int(runner.err_flags.item()), device)
+    last = kd.gather_rows(runner.last_rows)
+    verification = None
+    if rank == 0:
+        verification = {"ranks": world, "rows_gathered": int(last.shape[0]),
+                        "finite": bool(torch.isfinite(last).all().item()), "err_flags": flags}
 
     ms_per_step = max_ms / args.steps
     tokens_total = w.n_tokens * world
@@ -491,8 +500,9 @@ def run_ours(args):
             "launches_per_step": launches,
             "e2e": e2e,
             "cpu_baseline": cpu,
+            "verification": verification,
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -539,8 +549,25 @@ def run_e2e(runner, stream, steps: int, device, dist, world: int) -> dict:
             "path": "pinned host -> cudaMemcpyAsync -> kllm_b200_chain_run -> last rows -> pinned host"}
 
 
+_JSON_OUT = None
+
+
+def emit(line: dict) -> None:
+    """Writes the result line to the process's real stdout (libraries such as
+    NCCL may print banners; those go to stderr, see main())."""
+    out = _JSON_OUT if _JSON_OUT is not None else sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
 def main():
+    global _JSON_OUT
     args = parse_args()
+    # keep stdout for the one JSON line: everything else written to fd 1
+    # (library banners, warnings) is redirected to stderr
+    sys.stdout.flush()
+    _JSON_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     if args.impl == "reference":
         run_reference(args)
     else:

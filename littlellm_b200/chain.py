@@ -97,16 +97,32 @@ def silu_bytes_per_launch(w: Workload) -> int:
 
 
 class ChainRunner:
-    """Device buffers + launch descriptor of one chain step."""
+    """Device buffers + launch descriptor of one chain step.
+
+    With ``shard=(rank, world)`` the workload is the global batch: data is
+    generated for all of it (same seed on every rank, so identical to an
+    unsharded run) and the runner keeps only this rank's sequences. That is
+    for exact sharded-vs-unsharded checks on small cases; the benchmark gives
+    each rank its own workload and seed instead.
+    """
+
+    TOKEN_TENSORS = ("q", "k", "v", "attn_out", "ffn_out", "gate", "up")
 
     def __init__(self, workload: Workload, device: torch.device | str = "cuda:0", seed: int = 0,
                  use_pdl: bool = True, n_layers: int | None = None,
-                 weight_dtype: torch.dtype = torch.float16):
-        self.w = workload
+                 weight_dtype: torch.dtype = torch.float16, shard: tuple[int, int] | None = None):
         m = workload.model
         self.device = torch.device(device)
         self.n_layers = n_layers or m.n_layers
+        if shard is not None:
+            from .dist import shard_range
+            s0, s1 = shard_range(workload.n_seqs, *shard)
+            self.w = replace(workload, n_seqs=s1 - s0)
+        else:
+            s0, s1 = 0, workload.n_seqs
+            self.w = workload
         T, H, I = workload.n_tokens, m.hidden, m.intermediate
+        t0, t1 = s0 * workload.seq_len, s1 * workload.seq_len
         qd, kvd = m.n_heads * m.head_dim, m.n_kv_heads * m.head_dim
         dev = self.device
         gen = torch.Generator(device=dev)
@@ -119,38 +135,42 @@ class ChainRunner:
         def uniform(shape, lo, hi, dtype):
             return (torch.rand(shape, generator=gen, device=dev, dtype=torch.float32) * (hi - lo) + lo).to(dtype)
 
+        def rows(t):
+            return t if (t0, t1) == (0, T) else t[t0:t1].contiguous()
+
+        Tl = t1 - t0
         with torch.cuda.device(dev):
             self.table = normal((m.vocab, H), 0.02)
-            self.ids = torch.randint(0, m.vocab, (T,), generator=gen, device=dev, dtype=torch.int32)
+            self.ids = rows(torch.randint(0, m.vocab, (T,), generator=gen, device=dev, dtype=torch.int32))
             if workload.decode:
-                self.positions = torch.randint(0, workload.max_seq - 1, (T,), generator=gen, device=dev,
-                                               dtype=torch.int32)
-                self.slots = torch.arange(T, device=dev, dtype=torch.int32)
+                self.positions = rows(torch.randint(0, workload.max_seq - 1, (T,), generator=gen, device=dev,
+                                                    dtype=torch.int32))
+                self.slots = torch.arange(Tl, device=dev, dtype=torch.int32)
             else:
-                t = torch.arange(T, device=dev, dtype=torch.int32)
+                t = torch.arange(Tl, device=dev, dtype=torch.int32)
                 self.positions = t % workload.seq_len
                 self.slots = t // workload.seq_len
-            self.residual = torch.empty((T, H), dtype=f16, device=dev)
+            self.residual = torch.empty((Tl, H), dtype=f16, device=dev)
             self.final_norm_w = uniform((H,), 0.5, 1.5, weight_dtype)
-            self.final_norm_out = torch.empty((T, H), dtype=f16, device=dev)
-            self.last_rows = torch.empty((workload.n_seqs, H), dtype=f16, device=dev)
+            self.final_norm_out = torch.empty((Tl, H), dtype=f16, device=dev)
+            self.last_rows = torch.empty((s1 - s0, H), dtype=f16, device=dev)
             self.err_flags = torch.zeros((1,), dtype=torch.int32, device=dev)
             self.layers = []
             for _ in range(self.n_layers):
                 L = {
-                    "q": normal((T, qd)), "k": normal((T, kvd)), "v": normal((T, kvd)),
+                    "q": rows(normal((T, qd))), "k": rows(normal((T, kvd))), "v": rows(normal((T, kvd))),
                     "q_bias": normal((qd,), 0.02, weight_dtype), "k_bias": normal((kvd,), 0.02, weight_dtype),
                     "v_bias": normal((kvd,), 0.02, weight_dtype),
-                    "attn_out": normal((T, H)), "ffn_out": normal((T, H)),
-                    "gate": normal((T, I)), "up": normal((T, I)),
+                    "attn_out": rows(normal((T, H))), "ffn_out": rows(normal((T, H))),
+                    "gate": rows(normal((T, I))), "up": rows(normal((T, I))),
                     "input_norm_w": uniform((H,), 0.5, 1.5, weight_dtype),
                     "post_norm_w": uniform((H,), 0.5, 1.5, weight_dtype),
-                    "attn_norm_out": torch.empty((T, H), dtype=f16, device=dev),
-                    "ffn_norm_out": torch.empty((T, H), dtype=f16, device=dev),
-                    "swiglu_out": torch.empty((T, I), dtype=f16, device=dev),
-                    "k_cache": torch.empty((workload.n_seqs, m.n_kv_heads, workload.max_seq, m.head_dim),
+                    "attn_norm_out": torch.empty((Tl, H), dtype=f16, device=dev),
+                    "ffn_norm_out": torch.empty((Tl, H), dtype=f16, device=dev),
+                    "swiglu_out": torch.empty((Tl, I), dtype=f16, device=dev),
+                    "k_cache": torch.empty((s1 - s0, m.n_kv_heads, workload.max_seq, m.head_dim),
                                            dtype=f16, device=dev),
-                    "v_cache": torch.empty((workload.n_seqs, m.n_kv_heads, workload.max_seq, m.head_dim),
+                    "v_cache": torch.empty((s1 - s0, m.n_kv_heads, workload.max_seq, m.head_dim),
                                            dtype=f16, device=dev),
                 }
                 self.layers.append(L)
