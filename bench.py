@@ -363,6 +363,103 @@ def per_op_timing(runner, stream, reps: int) -> dict:
     return out
 
 
+LLAMA7B_INT8_TENSORS = (
+    # (rows, cols, count): q/k/v/o, gate/up, down per layer x 32, embed + lm_head
+    (4096, 4096, 4 * 32), (11008, 4096, 2 * 32), (4096, 11008, 32), (32000, 4096, 2),
+)
+
+
+def run_dequant(args):
+    """INT8 -> fp16 dequant of every Llama-2-7B linear/embedding tensor
+    (6.74 B parameters, int8 ~U[-127,127], fp32 scale ~U(1e-3,1e-2) per
+    tensor) with the reference weight loader's rounding; one step = the whole
+    checkpoint. Metric: algorithmic GB/s (1 B read + 2 B written per value)."""
+    import torch
+
+    from littlellm_b200 import build as kbuild
+    from littlellm_b200 import ops
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA GPU")
+    world, rank, local = dist_env()
+    if world > 1:
+        raise SystemExit("the dequant workload runs on one GPU")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    kbuild.build()
+    gen = torch.Generator(device=device)
+    gen.manual_seed(5)
+    data, scales, outs = [], [], []
+    for rows, cols, count in LLAMA7B_INT8_TENSORS:
+        for _ in range(count):
+            data.append(torch.randint(-127, 128, (rows, cols), generator=gen, device=device, dtype=torch.int8))
+            scales.append(torch.rand((1,), generator=gen, device=device) * 9e-3 + 1e-3)
+            outs.append(torch.empty((rows, cols), dtype=torch.float16, device=device))
+    n_params = sum(d.numel() for d in data)
+    nbytes = 3 * n_params + 4 * len(data)
+    log(f"dequant: {len(data)} tensors, {n_params} params allocated")
+    stream = torch.cuda.Stream(device)
+    peaks = load_peaks()
+    results = {}
+    with torch.cuda.stream(stream):
+        for name, fn in (("batched", lambda: ops.dequantize_int8_batched(data, scales, outs)),
+                         ("per_tensor", lambda: [ops.dequantize_int8(d, sc, out=o)
+                                                 for d, sc, o in zip(data, scales, outs)])):
+            fn()
+            stream.synchronize()
+            log(f"dequant {name}: eager ok")
+            g = capture(fn, stream)
+            log(f"dequant {name}: captured")
+            for _ in range(max(args.warmup, 3)):
+                g.replay()
+            stream.synchronize()
+            ms = time_graph(g, stream, args.steps)
+            results[name] = {"ms_per_step": ms, "gbs": nbytes / (ms * 1e-3) / 1e9,
+                             "frac_of_measured": nbytes / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+                             "launches_per_step": 1 if name == "batched" else len(data)}
+            del g
+    # spot check against the oracle (first and last tensor, 1 M values each)
+    import numpy as np
+
+    from oracle.oracle import Oracle
+    o = Oracle()
+    ok = True
+    for i in (0, len(data) - 1):
+        q = data[i].flatten()[: 1 << 20].cpu().numpy()
+        got = outs[i].flatten()[: 1 << 20].cpu().view(torch.int16).numpy().view(np.uint16)
+        ok &= bool(np.array_equal(got, o.dequantize_int8_f16_bits(q, float(scales[i].item()))))
+    cpu = None
+    if not args.no_cpu_baseline:
+        from oracle.oracle import Reference, reference_available
+        q = np.ascontiguousarray(data[0].flatten()[: 1 << 26].cpu().numpy())
+        sample = q.size
+        out16 = np.empty(sample, np.uint16)
+        fn = (Reference().lib.kref_dequantize_int8_f16 if reference_available()
+              else o.lib.kllm_oracle_dequantize_int8_f16)
+        import ctypes
+        t0 = time.perf_counter()
+        reps = 0
+        while time.perf_counter() - t0 < args.cpu_seconds / 2 or reps == 0:
+            fn(ctypes.c_void_p(q.ctypes.data), sample, ctypes.c_float(float(scales[0].item())),
+               ctypes.c_void_p(out16.ctypes.data))
+            reps += 1
+        dt = time.perf_counter() - t0
+        cpu = {"value": 3 * sample * reps / dt / 1e9, "unit": "GB/s", "cores": 1,
+               "kind": "reference" if reference_available() else "port",
+               "sample": f"{sample} values x {reps} through the weight loader's loop body "
+                         "(float(q) * scale, float_to_half), single thread"}
+    b = results["batched"]
+    emit({"metric": "int8->fp16 dequant throughput", "value": b["gbs"], "unit": "GB/s", "n_gpus": 1,
+          "steps": args.steps, "warmup": args.warmup, "ms_per_step": b["ms_per_step"], "higher_is_better": True,
+          "scaling": "none", "vs_baseline": None, "dtype": "i8->f16", "data": "synthetic",
+          "config": {"workload": "llama_int8_dequant", "tensors": len(data), "params": n_params,
+                     "bytes_per_step": nbytes, "l2": "no flush: 20.2 GB per step >> 126 MB L2"},
+          "roofline": {"bound": "hbm", "kernel": "dequant_batched_kernel", "achieved": b["gbs"],
+                       "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": b["frac_of_measured"],
+                       "traffic": None, "peak_source": peaks["source"]},
+          "variants": results, "bit_exact_spot_check": ok, "gpu_launches": args.steps,
+          "cpu_baseline": cpu})
+
+
 def run_ours(args):
     import torch
 
@@ -552,6 +649,12 @@ def run_e2e(runner, stream, steps: int, device, dist, world: int) -> dict:
 _JSON_OUT = None
 
 
+def log(msg: str) -> None:
+    """Progress markers on stderr (stdout carries only the JSON line)."""
+    sys.stderr.write(f"[bench] {msg}\n")
+    sys.stderr.flush()
+
+
 def emit(line: dict) -> None:
     """Writes the result line to the process's real stdout (libraries such as
     NCCL may print banners; those go to stderr, see main())."""
@@ -562,6 +665,8 @@ def emit(line: dict) -> None:
 
 def main():
     global _JSON_OUT
+    import faulthandler
+    faulthandler.enable()
     args = parse_args()
     # keep stdout for the one JSON line: everything else written to fd 1
     # (library banners, warnings) is redirected to stderr
@@ -570,6 +675,8 @@ def main():
     os.dup2(2, 1)
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "llama_int8_dequant":
+        run_dequant(args)
     else:
         run_ours(args)
 

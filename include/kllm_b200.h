@@ -142,6 +142,18 @@ int kllm_b200_dequantize_int8(const int8_t* data, const float* scale, void* out,
  *  Fused / batched operators (additive to include/kllm/op/ops.h)           *
  * ======================================================================== */
 
+/* Many INT8 tensors in one launch: for each i, outs[i][j] = data[i][j] *
+ * scales[i][0], rounded exactly as kllm_b200_dequantize_int8 rounds for
+ * out_dtype. This is the dequant step of the weight loader
+ * (src/model/weights.cpp:95-154, which dequantises record by record on the
+ * host) applied to a whole checkpoint on the device. data/scales/outs/counts
+ * are HOST arrays of n_tensors entries holding device pointers and element
+ * counts; they are read during the call only. Tensors whose data or output
+ * is not 16-byte aligned are dequantised by single-tensor launches. */
+int kllm_b200_dequantize_int8_batched(const int8_t* const* data, const float* const* scales,
+                                      void* const* outs, const int64_t* counts, int n_tensors,
+                                      int out_dtype, void* stream);
+
 /* Residual add fused with RMSNorm, the pair at src/model/llama.cpp:135-143
  * (and :166 -> :83 across layers, :176 at the end):
  *     residual[r, :] = fp16(residual[r, :] + delta[r, :])   (stored)

@@ -80,6 +80,8 @@ SIGNATURES = {
     "kllm_b200_rope_inplace": [_vp, _i64, _i64, _i64, _i32, _f32, _int, _vp],
     "kllm_b200_copy_kv_to_cache": [_vp, _vp, _i64, _i64, _i64, _vp, _vp, _i64, _i32, _int, _int, _vp],
     "kllm_b200_dequantize_int8": [_vp, _vp, _vp, _i64, _int, _vp],
+    "kllm_b200_dequantize_int8_batched": [ctypes.POINTER(_vp), ctypes.POINTER(_vp), ctypes.POINTER(_vp),
+                                          ctypes.POINTER(_i64), _int, _int, _vp],
     "kllm_b200_add_rms_norm": [_vp, _vp, _vp, _vp, _i64, _i64, _f32, _int, _int, _vp],
     "kllm_b200_qkv_bias_rope_kv_append": [_vp, _vp, _vp, _vp, _vp, _vp, _int, _vp, _vp, _i64, _i64,
                                           _i64, _i64, _f32, _vp, _vp, _i64, _i64, _vp, _vp],

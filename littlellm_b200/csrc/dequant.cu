@@ -150,6 +150,121 @@ __global__ void __launch_bounds__(kThreads) dequant_generic_kernel(const int8_t*
   }
 }
 
+// ---- many tensors in one launch -----------------------------------------
+//
+// The weight loader dequantises every INT8 record of a checkpoint
+// (src/model/weights.cpp:95-154, one tensor at a time on the host). Here a
+// whole batch of tensors is one persistent launch: each tensor is cut into
+// chunks of kChunk int8 elements, the chunks of all tensors are numbered
+// consecutively, and CTA b processes the contiguous chunk range
+// [b * n / grid, (b + 1) * n / grid), so it meets only a few tensors and
+// rebuilds its rounding table only when it crosses into the next one. The
+// task table travels by value in the kernel parameters.
+
+constexpr int kMaxTasks = 96;  // keeps the parameter block under the classic 4 KB limit
+constexpr int kVecsPerThread = 4;
+constexpr int kChunkVecs = kVecsPerThread * kThreads;  // 16-byte vectors per chunk
+constexpr int64_t kChunk = 16 * kChunkVecs;    // int8 elements per chunk
+
+struct DequantTask {
+  const int8_t* q;
+  const float* scale;
+  void* out;
+  int64_t n;            // elements
+  int64_t first_chunk;  // index of the task's first chunk in the batch
+};
+
+struct DequantBatch {
+  int n_tasks;
+  int64_t n_chunks;
+  DequantTask task[kMaxTasks];
+};
+static_assert(sizeof(DequantBatch) <= 4000, "kernel parameter block must stay below 4 KB");
+
+__device__ __forceinline__ void build_lut(uint32_t* lut, float s) {
+  const uint32_t b = threadIdx.x;
+  const uint32_t h = ref_float_to_half(dequant_value(b, s));
+#pragma unroll 8
+  for (int l = 0; l < 32; ++l) lut[b * 32 + ((l + b) & 31)] = h;
+}
+
+template <bool F16>
+__global__ void __launch_bounds__(kThreads) dequant_batched_kernel(const __grid_constant__ DequantBatch batch) {
+  __shared__ uint32_t lut[256 * 32];
+  grid_dep_wait();
+  grid_dep_launch();
+  const int64_t c_begin = batch.n_chunks * blockIdx.x / gridDim.x;
+  const int64_t c_end = batch.n_chunks * (blockIdx.x + 1) / gridDim.x;
+  if (c_begin >= c_end) return;
+  // task holding chunk c_begin: last task whose first_chunk <= c_begin
+  int lo = 0, hi = batch.n_tasks - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (batch.task[mid].first_chunk <= c_begin) lo = mid; else hi = mid - 1;
+  }
+  int ti = lo;
+  float s = __ldg(batch.task[ti].scale);
+  if (F16) build_lut(lut, s);
+  __syncthreads();
+  const uint32_t* my = lut + (threadIdx.x & 31);
+  for (int64_t c = c_begin; c < c_end; ++c) {
+    bool moved = false;
+    while (ti + 1 < batch.n_tasks && batch.task[ti + 1].first_chunk <= c) {
+      ++ti;
+      moved = true;
+    }
+    if (moved) {
+      s = __ldg(batch.task[ti].scale);
+      if (F16) {
+        __syncthreads();  // everyone is done with the previous table
+        build_lut(lut, s);
+        __syncthreads();
+      }
+    }
+    const DequantTask& t = batch.task[ti];
+    const int64_t e0 = (c - t.first_chunk) * kChunk;     // first element of this chunk
+    const int64_t e1 = e0 + kChunk < t.n ? e0 + kChunk : t.n;
+    const int64_t nvec = (e1 - e0) >> 4;
+    const uint4* src = reinterpret_cast<const uint4*>(t.q + e0);
+    uint4 w[kVecsPerThread];
+#pragma unroll
+    for (int k = 0; k < kVecsPerThread; ++k) {
+      const int64_t i = threadIdx.x + k * kThreads;
+      if (i < nvec) w[k] = ld_stream(src + i);
+    }
+#pragma unroll
+    for (int k = 0; k < kVecsPerThread; ++k) {
+      const int64_t i = threadIdx.x + k * kThreads;
+      if (i >= nvec) continue;
+      if (F16) {
+        uint4 o0, o1;
+        lut16(my, w[k], o0, o1);
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(t.out) + e0);
+        st_plain(dst + 2 * i, o0);
+        st_plain(dst + 2 * i + 1, o1);
+      } else {
+        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(t.out) + e0);
+        const uint32_t words[4] = {w[k].x, w[k].y, w[k].z, w[k].w};
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          const uint32_t x = words[m];
+          dst[4 * i + m] = make_float4(dequant_value(x & 0xffu, s), dequant_value((x >> 8) & 0xffu, s),
+                                       dequant_value((x >> 16) & 0xffu, s), dequant_value(x >> 24, s));
+        }
+      }
+    }
+    // scalar tail of the tensor's last chunk (fewer than 16 elements)
+    for (int64_t j = e0 + (nvec << 4) + threadIdx.x; j < e1; j += blockDim.x) {
+      if (F16) {
+        static_cast<unsigned short*>(t.out)[j] =
+            static_cast<unsigned short>(my[static_cast<uint32_t>(static_cast<uint8_t>(t.q[j])) << 5]);
+      } else {
+        static_cast<float*>(t.out)[j] = __fmul_rn(static_cast<float>(t.q[j]), s);
+      }
+    }
+  }
+}
+
 }  // namespace
 
 int dequantize_int8(const int8_t* data, const float* scale, void* out, int64_t n, int out_dtype,
@@ -178,6 +293,54 @@ int dequantize_int8(const int8_t* data, const float* scale, void* out, int64_t n
   return launch_status(launch(k, grid, kThreads, 0, o.stream, o.pdl, data, scale, out, n), "dequantize_int8");
 }
 
+
+int dequantize_int8_batched(const int8_t* const* data, const float* const* scales, void* const* outs,
+                            const int64_t* counts, int n_tensors, int out_dtype, const LaunchOpts& o) {
+  if (n_tensors < 0) return fail(KLLM_B200_ERR_INVALID_ARG, "dequantize_int8_batched: negative tensor count");
+  if (n_tensors == 0) return KLLM_B200_OK;
+  if (!data || !scales || !outs || !counts) {
+    return fail(KLLM_B200_ERR_INVALID_ARG, "dequantize_int8_batched: null array");
+  }
+  if (!is_float_dtype(out_dtype)) {
+    return fail(KLLM_B200_ERR_DTYPE, "dequantize_int8_batched: output dtype %d not supported (F32/F16)", out_dtype);
+  }
+  for (int i = 0; i < n_tensors; ++i) {
+    if (counts[i] < 0) return fail(KLLM_B200_ERR_INVALID_ARG, "dequantize_int8_batched: tensor %d has negative size", i);
+    if (counts[i] > 0 && (!data[i] || !scales[i] || !outs[i])) {
+      return fail(KLLM_B200_ERR_INVALID_ARG, "dequantize_int8_batched: tensor %d has a null pointer", i);
+    }
+  }
+  DequantBatch batch;
+  int i = 0;
+  while (i < n_tensors) {
+    batch.n_tasks = 0;
+    batch.n_chunks = 0;
+    // fill one launch with up to kMaxTasks aligned tensors; unaligned ones
+    // go through the single-tensor entry point
+    for (; i < n_tensors && batch.n_tasks < kMaxTasks; ++i) {
+      if (counts[i] == 0) continue;
+      if (!aligned16(data[i]) || !aligned16(outs[i])) {
+        const int rc = dequantize_int8(data[i], scales[i], outs[i], counts[i], out_dtype, o);
+        if (rc != KLLM_B200_OK) return rc;
+        continue;
+      }
+      DequantTask& t = batch.task[batch.n_tasks++];
+      t.q = data[i];
+      t.scale = scales[i];
+      t.out = outs[i];
+      t.n = counts[i];
+      t.first_chunk = batch.n_chunks;
+      batch.n_chunks += (counts[i] + kChunk - 1) / kChunk;
+    }
+    if (batch.n_tasks == 0) continue;
+    auto k = out_dtype == KLLM_B200_F16 ? dequant_batched_kernel<true> : dequant_batched_kernel<false>;
+    const unsigned grid = persistent_grid(k, kThreads, 0, 1, batch.n_chunks);
+    const int rc = launch_status(launch(k, grid, kThreads, 0, o.stream, o.pdl, batch), "dequantize_int8_batched");
+    if (rc != KLLM_B200_OK) return rc;
+  }
+  return KLLM_B200_OK;
+}
+
 }  // namespace kb
 
 extern "C" int kllm_b200_dequantize_int8(const int8_t* data, const float* scale, void* out, int64_t n,
@@ -185,4 +348,12 @@ extern "C" int kllm_b200_dequantize_int8(const int8_t* data, const float* scale,
   kb::LaunchOpts o;
   o.stream = static_cast<cudaStream_t>(stream);
   return kb::dequantize_int8(data, scale, out, n, out_dtype, o);
+}
+
+extern "C" int kllm_b200_dequantize_int8_batched(const int8_t* const* data, const float* const* scales,
+                                                 void* const* outs, const int64_t* counts, int n_tensors,
+                                                 int out_dtype, void* stream) {
+  kb::LaunchOpts o;
+  o.stream = static_cast<cudaStream_t>(stream);
+  return kb::dequantize_int8_batched(data, scales, outs, counts, n_tensors, out_dtype, o);
 }

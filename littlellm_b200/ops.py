@@ -216,3 +216,31 @@ def dequantize_int8(data: torch.Tensor, scale: torch.Tensor,
         check(lib.kllm_b200_dequantize_int8(_ptr(data), _ptr(scale), _ptr(out), data.numel(),
                                             dtype_code(out), _stream(dev)))
     return out
+
+
+def dequantize_int8_batched(data: list[torch.Tensor], scales: list[torch.Tensor],
+                            outs: list[torch.Tensor]) -> list[torch.Tensor]:
+    """outs[i] = data[i] * scales[i][0] for every i in one launch (rounding
+    as in dequantize_int8 for the outputs' dtype, which must all match)."""
+    import ctypes
+    n = len(data)
+    if not (len(scales) == len(outs) == n):
+        raise KllmError(_capi.ERR_SHAPE, "dequantize_int8_batched: list lengths differ")
+    if n == 0:
+        return outs
+    dev = _dev(*data, *scales, *outs)
+    out_dtypes = {dtype_code(o) for o in outs}
+    if len(out_dtypes) != 1:
+        raise KllmError(_capi.ERR_DTYPE, "dequantize_int8_batched: outputs must share one dtype")
+    for d, sc, o in zip(data, scales, outs):
+        if d.dtype != torch.int8 or sc.dtype != torch.float32 or d.numel() != o.numel():
+            raise KllmError(_capi.ERR_DTYPE, "dequantize_int8_batched: int8 data, fp32 scale, matching sizes")
+    arr = ctypes.c_void_p * n
+    d_arr = arr(*[d.data_ptr() for d in data])
+    s_arr = arr(*[sc.data_ptr() for sc in scales])
+    o_arr = arr(*[o.data_ptr() for o in outs])
+    c_arr = (ctypes.c_int64 * n)(*[d.numel() for d in data])
+    with torch.cuda.device(dev):
+        check(lib.kllm_b200_dequantize_int8_batched(d_arr, s_arr, o_arr, c_arr, n, out_dtypes.pop(),
+                                                    _stream(dev)))
+    return outs

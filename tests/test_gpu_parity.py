@@ -281,3 +281,39 @@ def test_add_inplace_and_bias(ops, rows, cols):
     x = dev(a)
     ops.add_bias_inplace(x, dev(bias))
     assert np.array_equal(bits16(x), (a + bias).astype(np.float16).view(np.uint16))
+
+
+@pytest.mark.parametrize("out_dtype", [F16, F32])
+def test_dequant_batched(ops, oracle, out_dtype):
+    """Many tensors in one launch, including empty ones, ragged tails, an
+    unaligned tensor (single-tensor fallback) and chunk boundaries."""
+    rng = np.random.default_rng(21)
+    sizes = [4096 * 4096 // 16, 0, 17, 8192, 8193, 3 * 16384 + 5, 1, 65536 * 3, 1000]
+    qs = [rng.integers(-128, 128, n, dtype=np.int8) for n in sizes]
+    scales = [np.float32(rng.uniform(1e-3, 1e-2)) for _ in sizes]
+    scales[3] = np.float32(0.12499202 / 127)  # a scale that hits the carry quirk for q=127
+    data = [dev(q, torch.int8) for q in qs]
+    unaligned = dev(np.concatenate([[0], qs[-1]]).astype(np.int8), torch.int8)[1:]
+    data[-1] = unaligned
+    sc = [torch.tensor([s], dtype=F32, device="cuda:0") for s in scales]
+    outs = [torch.empty(n, dtype=out_dtype, device="cuda:0") for n in sizes]
+    ops.dequantize_int8_batched(data, sc, outs)
+    for q, s, o in zip(qs, scales, outs):
+        if out_dtype == F16:
+            assert np.array_equal(bits16(o), oracle.dequantize_int8_f16_bits(q, float(s)))
+        else:
+            assert np.array_equal(host(o), oracle.dequantize_int8_f32(q, float(s)))
+
+
+def test_dequant_batched_many_tensors(ops, oracle):
+    """More tensors than one launch's task table holds (split launches)."""
+    rng = np.random.default_rng(22)
+    sizes = [int(n) for n in rng.integers(1, 5000, 300)]
+    qs = [rng.integers(-128, 128, n, dtype=np.int8) for n in sizes]
+    scales = [np.float32(rng.uniform(1e-3, 1e-2)) for _ in sizes]
+    data = [dev(q, torch.int8) for q in qs]
+    sc = [torch.tensor([s], dtype=F32, device="cuda:0") for s in scales]
+    outs = [torch.empty(n, dtype=F16, device="cuda:0") for n in sizes]
+    ops.dequantize_int8_batched(data, sc, outs)
+    for q, s, o in zip(qs, scales, outs):
+        assert np.array_equal(bits16(o), oracle.dequantize_int8_f16_bits(q, float(s)))
