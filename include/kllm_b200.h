@@ -227,12 +227,25 @@ typedef struct kllm_b200_layer_buffers {
   void* v_cache;             /* [n_slots, n_kv_heads, max_seq, head_dim] */
 } kllm_b200_layer_buffers;
 
+/* op_mask bits of kllm_b200_chain */
+enum {
+  KLLM_B200_OP_EMBEDDING = 1,
+  KLLM_B200_OP_INPUT_NORM = 2,  /* per layer: residual add (from layer 1) + RMSNorm */
+  KLLM_B200_OP_QKV_ROPE = 4,    /* per layer: bias + RoPE + KV append */
+  KLLM_B200_OP_POST_NORM = 8,   /* per layer: residual add + RMSNorm */
+  KLLM_B200_OP_SWIGLU = 16,     /* per layer */
+  KLLM_B200_OP_FINAL_NORM = 32,
+  KLLM_B200_OP_SELECT = 64
+};
+
 typedef struct kllm_b200_chain {
   int64_t n_tokens, hidden, n_heads, n_kv_heads, head_dim, intermediate, vocab;
   int64_t n_layers, n_slots, max_seq, n_seqs, seq_len;
   float eps, theta;
   int weight_dtype;               /* F16 or F32 for norm weights and biases */
   int use_pdl;                    /* launch with programmatic dependent launch */
+  int op_mask;                    /* 0 = the whole chain; else only the KLLM_B200_OP_* bits set
+                                     (profiling: one op kind timed in chain context) */
   const void* embed_table;        /* [vocab, hidden] fp16 */
   const int32_t* ids;             /* [T] device */
   const int32_t* positions;       /* [T] device */
@@ -248,8 +261,9 @@ typedef struct kllm_b200_chain {
 
 /* Launches the whole non-GEMM chain on `stream`: embedding, then per layer
  * add+RMSNorm, fused bias+RoPE+KV append, add+RMSNorm, SwiGLU, then the final
- * add+RMSNorm and select_last_rows. *n_launches (if given) receives the
- * number of kernels launched. Can be captured into a CUDA graph. */
+ * add+RMSNorm and select_last_rows (the op kinds selected by op_mask, all
+ * when it is 0). *n_launches (if given) receives the number of kernels
+ * launched. Can be captured into a CUDA graph. */
 int kllm_b200_chain_run(const kllm_b200_chain* chain, int* n_launches, void* stream);
 
 #ifdef __cplusplus

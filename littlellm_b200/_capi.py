@@ -26,6 +26,9 @@ FLAG_BAD_POSITION = 2
 FLAG_BAD_SLOT = 4
 FLAG_BAD_SEQ_END = 8
 
+OP_EMBEDDING, OP_INPUT_NORM, OP_QKV_ROPE, OP_POST_NORM, OP_SWIGLU, OP_FINAL_NORM, OP_SELECT = (
+    1, 2, 4, 8, 16, 32, 64)
+
 
 class KllmError(RuntimeError):
     """A non-zero status from the C ABI, with the library's message."""
@@ -50,7 +53,7 @@ class Chain(ctypes.Structure):
         ("n_layers", ctypes.c_int64), ("n_slots", ctypes.c_int64), ("max_seq", ctypes.c_int64),
         ("n_seqs", ctypes.c_int64), ("seq_len", ctypes.c_int64),
         ("eps", ctypes.c_float), ("theta", ctypes.c_float),
-        ("weight_dtype", ctypes.c_int), ("use_pdl", ctypes.c_int),
+        ("weight_dtype", ctypes.c_int), ("use_pdl", ctypes.c_int), ("op_mask", ctypes.c_int),
         ("embed_table", ctypes.c_void_p), ("ids", ctypes.c_void_p),
         ("positions", ctypes.c_void_p), ("slots", ctypes.c_void_p),
         ("seq_ends", ctypes.c_void_p), ("residual", ctypes.c_void_p),

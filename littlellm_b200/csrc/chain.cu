@@ -32,34 +32,55 @@ extern "C" int kllm_b200_chain_run(const kllm_b200_chain* c, int* n_launches, vo
   o.pdl = c->use_pdl != 0;
   const int64_t T = c->n_tokens, H = c->hidden;
   const int wdt = c->weight_dtype;
+  const int mask = c->op_mask == 0 ? 0x7f : c->op_mask;
+  auto on = [mask](int bit) { return (mask & bit) != 0; };
   int launched = 0;
-  int rc = embedding(c->embed_table, c->vocab, H, KLLM_B200_F16, c->ids, T, c->residual, KLLM_B200_F16,
-                     c->err_flags, o);
-  if (rc != KLLM_B200_OK) return rc;
-  ++launched;
+  int rc = KLLM_B200_OK;
+  if (on(KLLM_B200_OP_EMBEDDING)) {
+    rc = embedding(c->embed_table, c->vocab, H, KLLM_B200_F16, c->ids, T, c->residual, KLLM_B200_F16,
+                   c->err_flags, o);
+    if (rc != KLLM_B200_OK) return rc;
+    ++launched;
+  }
   for (int64_t l = 0; l < c->n_layers; ++l) {
     const kllm_b200_layer_buffers& L = c->layers[l];
     const void* delta = l == 0 ? nullptr : c->layers[l - 1].ffn_out;
-    rc = add_rms_norm(c->residual, delta, L.input_norm_w, L.attn_norm_out, T, H, c->eps, KLLM_B200_F16, wdt, o);
-    if (rc != KLLM_B200_OK) return rc;
-    rc = qkv_bias_rope_kv_append(L.q, L.k, L.v, L.q_bias, L.k_bias, L.v_bias, wdt, c->positions, c->slots, T,
-                                 c->n_heads, c->n_kv_heads, c->head_dim, c->theta, L.k_cache, L.v_cache,
-                                 c->n_slots, c->max_seq, c->err_flags, o);
-    if (rc != KLLM_B200_OK) return rc;
-    rc = add_rms_norm(c->residual, L.attn_out, L.post_norm_w, L.ffn_norm_out, T, H, c->eps, KLLM_B200_F16, wdt,
-                      o);
-    if (rc != KLLM_B200_OK) return rc;
-    rc = silu_mul(L.gate, L.up, L.swiglu_out, T * c->intermediate, KLLM_B200_F16, o);
-    if (rc != KLLM_B200_OK) return rc;
-    launched += 4;
+    if (on(KLLM_B200_OP_INPUT_NORM)) {
+      rc = add_rms_norm(c->residual, delta, L.input_norm_w, L.attn_norm_out, T, H, c->eps, KLLM_B200_F16, wdt, o);
+      if (rc != KLLM_B200_OK) return rc;
+      ++launched;
+    }
+    if (on(KLLM_B200_OP_QKV_ROPE)) {
+      rc = qkv_bias_rope_kv_append(L.q, L.k, L.v, L.q_bias, L.k_bias, L.v_bias, wdt, c->positions, c->slots, T,
+                                   c->n_heads, c->n_kv_heads, c->head_dim, c->theta, L.k_cache, L.v_cache,
+                                   c->n_slots, c->max_seq, c->err_flags, o);
+      if (rc != KLLM_B200_OK) return rc;
+      ++launched;
+    }
+    if (on(KLLM_B200_OP_POST_NORM)) {
+      rc = add_rms_norm(c->residual, L.attn_out, L.post_norm_w, L.ffn_norm_out, T, H, c->eps, KLLM_B200_F16, wdt,
+                        o);
+      if (rc != KLLM_B200_OK) return rc;
+      ++launched;
+    }
+    if (on(KLLM_B200_OP_SWIGLU)) {
+      rc = silu_mul(L.gate, L.up, L.swiglu_out, T * c->intermediate, KLLM_B200_F16, o);
+      if (rc != KLLM_B200_OK) return rc;
+      ++launched;
+    }
   }
-  rc = add_rms_norm(c->residual, c->layers[c->n_layers - 1].ffn_out, c->final_norm_w, c->final_norm_out, T, H,
-                    c->eps, KLLM_B200_F16, wdt, o);
-  if (rc != KLLM_B200_OK) return rc;
-  rc = select_last_rows(c->final_norm_out, T, H, c->seq_ends, c->seq_len, c->n_seqs, c->last_rows, KLLM_B200_F16,
-                        c->err_flags, o);
-  if (rc != KLLM_B200_OK) return rc;
-  launched += 2;
+  if (on(KLLM_B200_OP_FINAL_NORM)) {
+    rc = add_rms_norm(c->residual, c->layers[c->n_layers - 1].ffn_out, c->final_norm_w, c->final_norm_out, T, H,
+                      c->eps, KLLM_B200_F16, wdt, o);
+    if (rc != KLLM_B200_OK) return rc;
+    ++launched;
+  }
+  if (on(KLLM_B200_OP_SELECT)) {
+    rc = select_last_rows(c->final_norm_out, T, H, c->seq_ends, c->seq_len, c->n_seqs, c->last_rows,
+                          KLLM_B200_F16, c->err_flags, o);
+    if (rc != KLLM_B200_OK) return rc;
+    ++launched;
+  }
   if (n_launches) *n_launches = launched;
   return KLLM_B200_OK;
 }

@@ -62,23 +62,30 @@ __global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __re
                                                                     int hidden, int group, float eps) {
   extern __shared__ __align__(16) unsigned char s_raw[];
   __shared__ float partial[2][kThreads / 32];
-  // With EARLY (the PDL launch of the chain executor) the norm weight, which
-  // no chain kernel writes, is staged into shared memory before the
-  // grid-dependency wait, overlapping the previous kernel's tail, and the
-  // output phase reads it from shared memory. A standalone launch reads it
-  // from global memory (L1/L2) instead, keeping the staging off its critical
-  // path.
-  const TW* w_src = weight;
-  if (EARLY) {
-    const int wvec = static_cast<int>(hidden * sizeof(TW) / 16);
+  // The norm weight is staged into shared memory once per CTA and the
+  // output phase reads it from there. With EARLY (the PDL launch of the chain
+  // executor) the staging runs before the grid-dependency wait, overlapping
+  // the previous kernel's tail (no chain kernel writes the weight).
+  auto stage_weight = [&]() {
+    const int wvec = static_cast<int>(hidden * sizeof(TW) / 16);  // NOLINT(shadow)
     const uint4* wsrc = reinterpret_cast<const uint4*>(weight);
     uint4* wdst = reinterpret_cast<uint4*>(s_raw);
     for (int i = threadIdx.x; i < wvec; i += blockDim.x) wdst[i] = ld_keep(wsrc + i);
     __syncthreads();
-    w_src = reinterpret_cast<const TW*>(s_raw);
-  }
+  };
+  const TW* w_src = reinterpret_cast<const TW*>(s_raw);
+  const int wvec = static_cast<int>(hidden * sizeof(TW) / 16);
+  // Without PDL, a weight that fits one 16-byte vector per thread is loaded
+  // into a register first and parked in shared memory after the first row
+  // loads are issued, so the two round trips overlap; wider weights are
+  // staged up front.
+  const bool park = !EARLY && wvec <= static_cast<int>(blockDim.x);
+  uint4 wreg = make_uint4(0, 0, 0, 0);
+  if (park && static_cast<int>(threadIdx.x) < wvec) wreg = ld_keep(reinterpret_cast<const uint4*>(weight) + threadIdx.x);
+  if (!park) stage_weight();
   grid_dep_wait();
   grid_dep_launch();
+  bool staged = !park;
 
   const int nvec = hidden >> 3;
   const int rows_per_cta = blockDim.x / group;
@@ -94,10 +101,9 @@ __global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __re
     const int64_t row = g * rows_per_cta + row_in_cta;
     const bool live = row < rows;
     __half* rrow = residual + row * hidden;
-    uint4 r[VPT];
+    uint4 r[VPT], d[VPT];
     float ss = 0.0f;
     if (live) {
-      uint4 d[VPT];
 #pragma unroll
       for (int j = 0; j < VPT; ++j) {
         const int v = j * group + lane_g;
@@ -106,6 +112,15 @@ __global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __re
           if (HAS_DELTA) d[j] = ld_stream(delta + row * hidden + v * 8);
         }
       }
+    }
+    // `staged` and the loop trip count are uniform over the CTA, so every
+    // thread reaches this barrier.
+    if (!staged) {
+      if (static_cast<int>(threadIdx.x) < wvec) reinterpret_cast<uint4*>(s_raw)[threadIdx.x] = wreg;
+      __syncthreads();
+      staged = true;
+    }
+    if (live) {
 #pragma unroll
       for (int j = 0; j < VPT; ++j) {
         const int v = j * group + lane_g;
@@ -215,7 +230,7 @@ int launch_fast(void* residual, const void* delta, const void* weight, void* out
   auto k = o.pdl ? add_rms_norm_f16_kernel<VPT, TW, HAS_DELTA, true> : add_rms_norm_f16_kernel<VPT, TW, HAS_DELTA, false>;
   const int threads = group > kFastThreads ? group : kFastThreads;
   const int rows_per_cta = threads / group;
-  const size_t smem = o.pdl ? static_cast<size_t>(hidden) * sizeof(TW) : 0;
+  const size_t smem = static_cast<size_t>(hidden) * sizeof(TW);
   const cudaError_t attr = allow_smem(reinterpret_cast<const void*>(k), smem);
   if (attr != cudaSuccess) return launch_status(attr, "add_rms_norm");
   const unsigned grid = persistent_grid(k, threads, smem, rows_per_cta, rows);

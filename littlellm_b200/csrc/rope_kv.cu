@@ -92,11 +92,40 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
   return make_uint4(f2_to_h2(f[0], f[1]), f2_to_h2(f[2], f[3]), f2_to_h2(f[4], f[5]), f2_to_h2(f[6], f[7]));
 }
 
+// fp16(x + b) for 8 lanes, b at element `off` of a bias vector (shared or
+// global memory): the fp32 sum rounded to nearest even, which is what the
+// reference's bias add stores. For an fp16 bias this is one packed fp16 add
+// per pair: rounding the fp32 sum of two fp16 values to fp16 equals rounding
+// the exact sum once, because fp32 carries 24 >= 2*11 + 2 significand bits
+// (double rounding through such a format is innocuous for addition).
+template <typename TB>
+__device__ __forceinline__ uint4 add_bias8(uint4 x, const TB* bias, int off);
+
+template <>
+__device__ __forceinline__ uint4 add_bias8<__half>(uint4 x, const __half* bias, int off) {
+  const uint4 b = *reinterpret_cast<const uint4*>(bias + off);
+  auto add = [](uint32_t u, uint32_t v) {
+    __half2 r = __hadd2(*reinterpret_cast<const __half2*>(&u), *reinterpret_cast<const __half2*>(&v));
+    return *reinterpret_cast<uint32_t*>(&r);
+  };
+  return make_uint4(add(x.x, b.x), add(x.y, b.y), add(x.z, b.z), add(x.w, b.w));
+}
+
+template <>
+__device__ __forceinline__ uint4 add_bias8<float>(uint4 x, const float* bias, int off) {
+  float b[8];
+  load_bias8<float>(bias, off, b);
+  const float2 a0 = h2_to_f2(x.x), a1 = h2_to_f2(x.y), a2 = h2_to_f2(x.z), a3 = h2_to_f2(x.w);
+  return make_uint4(f2_to_h2(a0.x + b[0], a0.y + b[1]), f2_to_h2(a1.x + b[2], a1.y + b[3]),
+                    f2_to_h2(a2.x + b[4], a2.y + b[5]), f2_to_h2(a3.x + b[6], a3.y + b[7]));
+}
+
 // The per-pair rotation shared by every path (fused, legacy, generic) so that
-// the fused op equals the composition of the separate ops bit for bit.
+// the fused op equals the composition of the separate ops bit for bit:
+// y1 = x1*c - x2*s, y2 = x2*c + x1*s, each as one fp32 product and one FMA.
 __device__ __forceinline__ void rotate(float x1, float x2, float c, float s, float& y1, float& y2) {
-  y1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
-  y2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+  y1 = __fmaf_rn(x1, c, -__fmul_rn(x2, s));
+  y2 = __fmaf_rn(x2, c, __fmul_rn(x1, s));
 }
 
 __device__ __forceinline__ float2 angle_cs(int32_t pos, float inv_freq) {
@@ -109,7 +138,12 @@ __device__ __forceinline__ float2 angle_cs(int32_t pos, float inv_freq) {
 // dealt to its warps' lanes round-robin (consecutive units on consecutive
 // lanes, so loads and stores coalesce), UPL units per lane. The cos/sin of
 // the token's frequencies go into the warp's slice of shared memory (one or
-// a few sincosf per lane); the q/k/v biases are staged in shared memory.
+// a few sincosf per lane); the q/k/v biases are staged in shared memory with
+// each head's row padded by 16 bytes, so the lanes of one instruction, which
+// read the same column of different heads, hit different banks.
+//
+// DT is the head_dim when it is a compile-time constant (64, 128: unit
+// geometry becomes shifts), 0 for a runtime head_dim.
 //
 // Positions, slots, biases and the frequency table are never written by a
 // kernel of the chain, so with EARLY (the PDL launch of the chain executor)
@@ -117,13 +151,18 @@ __device__ __forceinline__ float2 angle_cs(int32_t pos, float inv_freq) {
 // wait, overlapping the previous kernel's tail, and only the activation loads
 // wait. Without PDL the activation loads are issued first and the staging
 // and sincos run while they are in flight.
-template <int UPL, typename TB, bool EARLY>
+template <int DT, int UPL, typename TB, bool EARLY>
 __global__ void __launch_bounds__(kWarpThreads) qkv_rope_warp_kernel(const __grid_constant__ RopeArgs a) {
   __shared__ float s_freq[kMaxHalf];
-  __shared__ float2 s_cs[kWarpsPerCta][kMaxHalf];
+  __shared__ __align__(16) float s_cos[kWarpsPerCta][kMaxHalf];
+  __shared__ __align__(16) float s_sin[kWarpsPerCta][kMaxHalf];
+  extern __shared__ __align__(16) unsigned char s_bias[];
 
-  const int half = a.head_dim >> 1;
-  for (int i = threadIdx.x; i < half; i += blockDim.x) s_freq[i] = a.inv_freq[i];
+  const int D = DT != 0 ? DT : a.head_dim;
+  const int half = D >> 1;
+  const int chunks = D >> 4;   // rotation units per head (8 pairs each)
+  const int vchunks = D >> 3;  // copy units per v head (16 bytes each)
+  const int brow = D + 16 / static_cast<int>(sizeof(TB));  // padded bias row, elements
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -132,87 +171,106 @@ __global__ void __launch_bounds__(kWarpThreads) qkv_rope_warp_kernel(const __gri
   const int part = static_cast<int>(gw - t * a.warps_per_token);
   const bool live = t < a.n_tokens;  // uniform per warp
 
-  const int chunks = a.head_dim >> 4;   // rotation units per head (8 pairs each)
-  const int vchunks = a.head_dim >> 3;  // copy units per v head (16 bytes each)
   const int rot_q = a.n_heads * chunks;
   const int rot_k = a.k ? a.n_kv_heads * chunks : 0;
   const int n_rot = rot_q + rot_k;
   const int n_units = n_rot + (a.v ? a.n_kv_heads * vchunks : 0);
 
-  // unit j of this lane: kind 0 = q rotation, 1 = k rotation, 2 = v copy, -1 none
-  int kind[UPL], head[UPL], dcol[UPL];
+  // The position feeds the sincos: load it before any other global access.
+  int32_t pos = 0, slot = 0;
+  if (live) {
+    pos = a.positions ? __ldg(a.positions + t) : a.past_len + static_cast<int32_t>(t);
+    slot = a.slots ? __ldg(a.slots + t) : 0;
+  }
+
+  // unit j of this lane: kind 0 = q rotation, 1 = k rotation, 2 = v copy, -1 none;
+  // `off` = element offset of the unit inside its token row (head * D + d0)
+  int kind[UPL], off[UPL], boff[UPL];
 #pragma unroll
   for (int j = 0; j < UPL; ++j) {
     const int u = (part * UPL + j) * 32 + lane;
+    int h = 0, d0 = 0;
     if (!live || u >= n_units) {
-      kind[j] = -1; head[j] = 0; dcol[j] = 0;
+      kind[j] = -1;
     } else if (u < n_rot) {
       const bool is_q = u < rot_q;
       const int w = is_q ? u : u - rot_q;
       kind[j] = is_q ? 0 : 1;
-      head[j] = w / chunks;
-      dcol[j] = (w - head[j] * chunks) << 3;
+      h = w / chunks;
+      d0 = (w - h * chunks) << 3;
     } else {
       const int w = u - n_rot;
       kind[j] = 2;
-      head[j] = w / vchunks;
-      dcol[j] = (w - head[j] * vchunks) << 3;
+      h = w / vchunks;
+      d0 = (w - h * vchunks) << 3;
     }
+    off[j] = h * D + d0;
+    boff[j] = h * brow + d0;
   }
 
+  const __half* q_tok = a.q + t * a.n_heads * D;
+  const __half* k_tok = a.k + t * a.n_kv_heads * D;
+  const __half* v_tok = a.v + t * a.n_kv_heads * D;
   uint4 x1[UPL], x2[UPL];
   auto issue_loads = [&]() {
 #pragma unroll
     for (int j = 0; j < UPL; ++j) {
-      if (kind[j] < 0) continue;
-      if (kind[j] < 2) {
-        const bool is_q = kind[j] == 0;
-        const int64_t row = (t * (is_q ? a.n_heads : a.n_kv_heads) + head[j]) * a.head_dim;
-        const __half* src = (is_q ? static_cast<const __half*>(a.q) : a.k) + row + dcol[j];
-        x1[j] = is_q ? ld_cg(src) : ld_stream(src);
-        x2[j] = is_q ? ld_cg(src + half) : ld_stream(src + half);
-      } else {
-        x1[j] = ld_stream(a.v + (t * a.n_kv_heads + head[j]) * a.head_dim + dcol[j]);
+      if (kind[j] == 0) {
+        x1[j] = ld_cg(q_tok + off[j]);
+        x2[j] = ld_cg(q_tok + off[j] + half);
+      } else if (kind[j] == 1) {
+        x1[j] = ld_stream(k_tok + off[j]);
+        x2[j] = ld_stream(k_tok + off[j] + half);
+      } else if (kind[j] == 2) {
+        x1[j] = ld_stream(v_tok + off[j]);
       }
     }
   };
-  // Without PDL nothing precedes this kernel's start: issue the activation
-  // loads first, then stage biases and compute cos/sin while they fly.
   if (!EARLY) {
     grid_dep_wait();
     grid_dep_launch();
     issue_loads();
   }
 
-  // Biases are small and never written by a chain kernel: stage them in
-  // shared memory (q, k, v back to back) before the dependency wait.
-  extern __shared__ __align__(16) unsigned char s_bias[];
-  const void* bq = a.bq;
-  const void* bk = a.bk;
-  const void* bv = a.bv;
+  for (int i = threadIdx.x; i < half; i += blockDim.x) s_freq[i] = a.inv_freq[i];
+  // Biases never written by a chain kernel: staged before the dependency
+  // wait, q then k then v, each head row padded to `brow` elements.
+  const TB* bq = static_cast<const TB*>(a.bq);
+  const TB* bk = static_cast<const TB*>(a.bk);
+  const TB* bv = static_cast<const TB*>(a.bv);
   if (a.stage_bias) {
-    const int qb = a.n_heads * a.head_dim * static_cast<int>(sizeof(TB));
-    const int kb = a.n_kv_heads * a.head_dim * static_cast<int>(sizeof(TB));
-    if (a.bq) { stage16(s_bias, a.bq, qb); bq = s_bias; }
-    if (a.bk) { stage16(s_bias + qb, a.bk, kb); bk = s_bias + qb; }
-    if (a.bv) { stage16(s_bias + qb + kb, a.bv, kb); bv = s_bias + qb + kb; }
-  }
-
-  int32_t pos = 0, slot = 0;
-  if (live) {
-    pos = a.positions ? __ldg(a.positions + t) : a.past_len + static_cast<int32_t>(t);
-    slot = a.slots ? __ldg(a.slots + t) : 0;
+    const int vec_per_row = D * static_cast<int>(sizeof(TB)) / 16;
+    const int row_vecs = brow * static_cast<int>(sizeof(TB)) / 16;
+    uint4* sb = reinterpret_cast<uint4*>(s_bias);
+    const TB* srcs[3] = {bq, bk, bv};
+    const int heads[3] = {a.n_heads, a.n_kv_heads, a.n_kv_heads};
+    int base = 0;
+    for (int m = 0; m < 3; ++m) {
+      const int n = heads[m] * vec_per_row;
+      if (srcs[m] != nullptr) {
+        const uint4* src = reinterpret_cast<const uint4*>(srcs[m]);
+        for (int i = threadIdx.x; i < n; i += blockDim.x) {
+          const int h = i / vec_per_row;
+          sb[base + h * row_vecs + (i - h * vec_per_row)] = ld_keep(src + i);
+        }
+      }
+      base += heads[m] * row_vecs;
+    }
+    const TB* sbase = reinterpret_cast<const TB*>(s_bias);
+    if (bq) bq = sbase;
+    if (bk) bk = sbase + a.n_heads * brow;
+    if (bv) bv = sbase + (a.n_heads + a.n_kv_heads) * brow;
   }
   __syncthreads();  // s_freq and staged biases visible; every thread reaches this point
 
-  auto fill_cs = [&]() {
+  if (live) {
     for (int d = lane; d < half; d += 32) {
       float sn, cs;
       sincosf(__fmul_rn(static_cast<float>(pos), s_freq[d]), &sn, &cs);
-      s_cs[warp][d] = make_float2(cs, sn);
+      s_cos[warp][d] = cs;
+      s_sin[warp][d] = sn;
     }
-  };
-  if (live) fill_cs();
+  }
   if (EARLY) {
     grid_dep_wait();
     grid_dep_launch();
@@ -231,59 +289,54 @@ __global__ void __launch_bounds__(kWarpThreads) qkv_rope_warp_kernel(const __gri
     }
     cache_ok = pos_ok && slot_ok;
   }
-  // element offset of [slot, head 0, pos, 0] in a [n_slots, n_kv_heads, max_seq, head_dim] plane
-  const int64_t cache_base = (static_cast<int64_t>(slot) * a.n_kv_heads * a.max_seq + pos) * a.head_dim;
-  const int64_t head_stride = a.max_seq * a.head_dim;
+  // [slot, head, pos, :] of a [n_slots, n_kv_heads, max_seq, D] plane: head h
+  // of this token starts at cache_tok + h * max_seq * D
+  const int64_t cache_tok = (static_cast<int64_t>(slot) * a.n_kv_heads * a.max_seq + pos) * D;
+  const int64_t head_stride = a.max_seq * D;
+  __half* q_out = a.q + t * a.n_heads * D;
 
 #pragma unroll
   for (int j = 0; j < UPL; ++j) {
     if (kind[j] < 0) continue;
-    const int h = head[j];
-    const int d0 = dcol[j];
     if (kind[j] < 2) {
       const bool is_q = kind[j] == 0;
       float f1[8], f2[8];
-      unpack8(x1[j], f1);
-      unpack8(x2[j], f2);
-      const void* bias = is_q ? bq : bk;
+      const TB* bias = is_q ? bq : bk;
       if (bias != nullptr) {
-        float b1[8], b2[8];
-        load_bias8<TB>(bias, static_cast<int64_t>(h) * a.head_dim + d0, b1);
-        load_bias8<TB>(bias, static_cast<int64_t>(h) * a.head_dim + d0 + half, b2);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          f1[i] = round_f16(f1[i] + b1[i]);
-          f2[i] = round_f16(f2[i] + b2[i]);
-        }
+        // the biased values rounded to fp16, as the reference's separate
+        // bias add stores them
+        const int bo = a.stage_bias ? boff[j] : off[j];  // padded rows when staged
+        unpack8(add_bias8<TB>(x1[j], bias, bo), f1);
+        unpack8(add_bias8<TB>(x2[j], bias, bo + half), f2);
+      } else {
+        unpack8(x1[j], f1);
+        unpack8(x2[j], f2);
       }
-      const float2* csr = &s_cs[warp][d0];
+      const int d0 = off[j] % D;
+      const float4* cp = reinterpret_cast<const float4*>(&s_cos[warp][d0]);
+      const float4* sp = reinterpret_cast<const float4*>(&s_sin[warp][d0]);
+      const float4 c0 = cp[0], c1 = cp[1], s0 = sp[0], s1 = sp[1];
+      const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+      const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
       float y1[8], y2[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float2 c = csr[i];
-        rotate(f1[i], f2[i], c.x, c.y, y1[i], y2[i]);
-      }
+      for (int i = 0; i < 8; ++i) rotate(f1[i], f2[i], c[i], sn[i], y1[i], y2[i]);
       __half* dst;
       if (is_q) {
-        dst = a.q + (t * a.n_heads + h) * a.head_dim + d0;
+        dst = q_out + off[j];
       } else {
         if (a.k_cache == nullptr || !cache_ok) continue;
-        dst = a.k_cache + cache_base + h * head_stride + d0;
+        const int h = off[j] / D;
+        dst = a.k_cache + cache_tok + h * head_stride + (off[j] - h * D);
       }
       st_plain(dst, pack8(y1));
       st_plain(dst + half, pack8(y2));
     } else {
       if (a.v_cache == nullptr || !cache_ok) continue;
       uint4 x = x1[j];
-      if (bv != nullptr) {
-        float xf[8], b[8];
-        unpack8(x, xf);
-        load_bias8<TB>(bv, static_cast<int64_t>(h) * a.head_dim + d0, b);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) xf[i] = xf[i] + b[i];
-        x = pack8(xf);
-      }
-      st_plain(a.v_cache + cache_base + h * head_stride + d0, x);
+      if (bv != nullptr) x = add_bias8<TB>(x, bv, a.stage_bias ? boff[j] : off[j]);
+      const int h = off[j] / D;
+      st_plain(a.v_cache + cache_tok + h * head_stride + (off[j] - h * D), x);
     }
   }
 }
@@ -368,6 +421,29 @@ void fill_inv_freq(RopeArgs& a, float theta) {
   }
 }
 
+template <int DT, int UPL>
+void (*pick_tb(bool bias16, bool pdl))(RopeArgs) {
+  if (pdl) return bias16 ? qkv_rope_warp_kernel<DT, UPL, __half, true> : qkv_rope_warp_kernel<DT, UPL, float, true>;
+  return bias16 ? qkv_rope_warp_kernel<DT, UPL, __half, false> : qkv_rope_warp_kernel<DT, UPL, float, false>;
+}
+
+template <int DT>
+void (*pick_upl(int upl, bool bias16, bool pdl))(RopeArgs) {
+  switch (upl) {
+    case 1: return pick_tb<DT, 1>(bias16, pdl);
+    case 2: return pick_tb<DT, 2>(bias16, pdl);
+    case 3: return pick_tb<DT, 3>(bias16, pdl);
+    default: return pick_tb<DT, 4>(bias16, pdl);
+  }
+}
+
+// head_dim 64 and 128 get compile-time unit geometry; others the runtime form.
+void (*pick_warp_kernel(int head_dim, int upl, bool bias16, bool pdl))(RopeArgs) {
+  if (head_dim == 64) return pick_upl<64>(upl, bias16, pdl);
+  if (head_dim == 128) return pick_upl<128>(upl, bias16, pdl);
+  return pick_upl<0>(upl, bias16, pdl);
+}
+
 int run_rope(RopeArgs& a, int act_dtype, int bias_dtype, const LaunchOpts& o, const char* what) {
   const int D = a.head_dim;
   const bool bias16 = bias_dtype == KLLM_B200_F16;
@@ -383,26 +459,11 @@ int run_rope(RopeArgs& a, int act_dtype, int bias_dtype, const LaunchOpts& o, co
     a.warps_per_token = wpt;
     const int64_t warps = a.n_tokens * wpt;
     const unsigned grid = static_cast<unsigned>((warps + kWarpsPerCta - 1) / kWarpsPerCta);
-    const size_t bias_bytes = static_cast<size_t>(a.n_heads + 2 * a.n_kv_heads) * D * (bias16 ? 2 : 4);
+    const size_t bias_bytes = static_cast<size_t>(a.n_heads + 2 * a.n_kv_heads) * (D * (bias16 ? 2 : 4) + 16);
     const bool any_bias = a.bq || a.bk || a.bv;
     a.stage_bias = any_bias && bias_bytes <= kMaxBiasStage;
     const size_t smem = a.stage_bias ? bias_bytes : 0;
-    void (*k)(RopeArgs);
-    if (o.pdl) {
-      switch (upl) {
-        case 1: k = bias16 ? qkv_rope_warp_kernel<1, __half, true> : qkv_rope_warp_kernel<1, float, true>; break;
-        case 2: k = bias16 ? qkv_rope_warp_kernel<2, __half, true> : qkv_rope_warp_kernel<2, float, true>; break;
-        case 3: k = bias16 ? qkv_rope_warp_kernel<3, __half, true> : qkv_rope_warp_kernel<3, float, true>; break;
-        default: k = bias16 ? qkv_rope_warp_kernel<4, __half, true> : qkv_rope_warp_kernel<4, float, true>; break;
-      }
-    } else {
-      switch (upl) {
-        case 1: k = bias16 ? qkv_rope_warp_kernel<1, __half, false> : qkv_rope_warp_kernel<1, float, false>; break;
-        case 2: k = bias16 ? qkv_rope_warp_kernel<2, __half, false> : qkv_rope_warp_kernel<2, float, false>; break;
-        case 3: k = bias16 ? qkv_rope_warp_kernel<3, __half, false> : qkv_rope_warp_kernel<3, float, false>; break;
-        default: k = bias16 ? qkv_rope_warp_kernel<4, __half, false> : qkv_rope_warp_kernel<4, float, false>; break;
-      }
-    }
+    void (*k)(RopeArgs) = pick_warp_kernel(D, upl, bias16, o.pdl);
     return launch_status(launch(k, grid, kWarpThreads, smem, o.stream, o.pdl, a), what);
   }
   const int per_tok = a.n_heads * (D / 2) + (a.k ? a.n_kv_heads * (D / 2) : 0) + (a.v ? a.n_kv_heads * D : 0);

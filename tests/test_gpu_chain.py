@@ -105,3 +105,23 @@ def test_chain_graph_replay_equals_eager(cuda):
     assert torch.equal(a.layers[1]["attn_norm_out"], b.layers[1]["attn_norm_out"])
     assert torch.equal(a.layers[0]["q"], b.layers[0]["q"])
     del g
+
+
+def test_chain_op_mask_launches_only_selected_ops(cuda, oracle):
+    """op_mask = SwiGLU only: one launch per layer, SwiGLU outputs right,
+    the norm outputs untouched (profiling mode of the chain executor)."""
+    from littlellm_b200 import _capi
+    from littlellm_b200.chain import ChainRunner
+    w = _tiny(False, "qwen")
+    r = ChainRunner(w, device=cuda, seed=4, use_pdl=True)
+    for L in r.layers:
+        L["attn_norm_out"].fill_(7.0)
+    r.desc.op_mask = _capi.OP_SWIGLU
+    n = r.run()
+    torch.cuda.synchronize()
+    assert n == w.model.n_layers
+    for L in r.layers:
+        assert bool((L["attn_norm_out"] == 7.0).all())
+        assert_tol(host(L["swiglu_out"]), oracle.silu_mul(host(L["gate"]), host(L["up"])))
+    r.desc.op_mask = _capi.OP_INPUT_NORM | _capi.OP_POST_NORM
+    assert r.run() == 2 * w.model.n_layers
