@@ -494,6 +494,112 @@ def per_op_chain_timing(runner, stream, reps: int) -> dict:
     return out
 
 
+def _write_llama_int8(path: str, layers: int, seed: int = 11) -> list[str]:
+    """A Llama-2-7B-shaped .kllm file with INT8 linear/embedding records
+    (int8 ~U[-127,127] + fp32 scale ~U(1e-3,1e-2)) and fp16 norm weights;
+    returns the tensor names."""
+    import struct
+
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    H, I, V = 4096, 11008, 32000
+    recs = [("model.embed_tokens.weight", (V, H), "i8")]
+    for i in range(layers):
+        p = f"model.layers.{i}."
+        recs += [(p + "input_layernorm.weight", (H,), "f16")]
+        recs += [(p + f"self_attn.{m}_proj.weight", (H, H), "i8") for m in "qkvo"]
+        recs += [(p + "post_attention_layernorm.weight", (H,), "f16"),
+                 (p + "mlp.gate_proj.weight", (I, H), "i8"), (p + "mlp.up_proj.weight", (I, H), "i8"),
+                 (p + "mlp.down_proj.weight", (H, I), "i8")]
+    recs += [("model.norm.weight", (H,), "f16"), ("lm_head.weight", (V, H), "i8")]
+    with open(path, "wb") as f:
+        f.write(b"KLLM0001" + struct.pack("<II", 1, 0))
+        f.write(struct.pack("<8i", V, H, I, layers, 32, 32, 128, 4096))
+        f.write(struct.pack("<ffBBBBI", 1e-5, 1e4, 0, 0, 0, 0, len(recs)))
+        for name, shape, dt in recs:
+            n = int(np.prod(shape))
+            enc = name.encode()
+            f.write(struct.pack("<I", len(enc)) + enc)
+            f.write(struct.pack("<II", 3 if dt == "i8" else 1, len(shape)))
+            f.write(b"".join(struct.pack("<q", d) for d in shape))
+            if dt == "i8":
+                f.write(struct.pack("<Q", n + 4))
+                f.write(rng.integers(-127, 128, n, dtype=np.int8).tobytes())
+                f.write(np.array([rng.uniform(1e-3, 1e-2)], np.float32).tobytes())
+            else:
+                f.write(struct.pack("<Q", 2 * n))
+                f.write(rng.uniform(0.5, 1.5, n).astype(np.float16).tobytes())
+    return [r[0] for r in recs]
+
+
+def _checksums(t) -> tuple[int, int]:
+    import numpy as np
+    b = t.contiguous().view(-1).cpu().numpy().view(np.uint8)
+    pad = (-b.size) % 8
+    if pad:
+        b = np.concatenate([b, np.zeros(pad, np.uint8)])
+    w = b.view(np.uint64)
+    return int(w.sum(dtype=np.uint64)), int(np.bitwise_xor.reduce(w))
+
+
+def run_load(args):
+    """.kllm checkpoint load onto the GPU: a partial Llama-2-7B INT8 file
+    (embedding, 4 decoder layers, lm_head: 1.07 B parameters) loaded by the
+    streaming loader (device-side dequant) and by the reference's own
+    ModelWeights::load (host dequant). Metric: file GB/s, wall clock (both
+    loads end synchronised, the file is in the page cache for both)."""
+    import subprocess
+    import tempfile
+
+    import torch
+
+    from littlellm_b200 import build as kbuild
+    from littlellm_b200 import loader
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA GPU")
+    device = torch.device("cuda", dist_env()[2])
+    torch.cuda.set_device(device)
+    kbuild.build()
+    layers = args.layers or 4
+    with tempfile.TemporaryDirectory() as tmp:
+        path = os.path.join(tmp, "llama_int8.kllm")
+        names = _write_llama_int8(path, layers)
+        file_bytes = os.path.getsize(path)
+        log(f"load: wrote {file_bytes / 1e9:.2f} GB")
+        idx = loader.read_index(path)
+        times = []
+        for _ in range(max(args.steps, 1)):
+            t0 = time.perf_counter()
+            _, tensors = loader.load(path, device, index=idx)
+            torch.cuda.synchronize(device)
+            times.append(time.perf_counter() - t0)
+            if len(times) < max(args.steps, 1):
+                del tensors
+        ours = min(times)
+        ref = None
+        exe = os.path.join(ROOT, "oracle", "_ref", "refcuda", "ref_load")
+        match = None
+        if os.path.exists(exe):
+            names_path = os.path.join(tmp, "names.txt")
+            with open(names_path, "w") as f:
+                f.write("\n".join(names) + "\n")
+            r = subprocess.run([exe, path, names_path], capture_output=True, text=True, timeout=1200)
+            if r.returncode == 0:
+                lines = r.stdout.splitlines()
+                ref = float(lines[0].split()[1])
+                want = {ln.split()[0]: (int(ln.split()[1]), int(ln.split()[2])) for ln in lines[1:]}
+                match = all(_checksums(tensors[n]) == want[n] for n in names)
+            else:
+                log(f"reference loader failed: {r.stderr.strip()[-300:]}")
+    emit({"metric": "int8 .kllm checkpoint load", "value": file_bytes / ours / 1e9, "unit": "GB/s",
+          "n_gpus": 1, "steps": len(times), "warmup": 0, "ms_per_step": ours * 1e3, "higher_is_better": True,
+          "scaling": "none", "vs_baseline": None, "dtype": "i8->f16", "data": "synthetic",
+          "config": {"workload": "llama_int8_load", "layers": layers, "file_bytes": file_bytes,
+                     "tensors": len(names), "staging": "2 x 32 MB pinned host, 2 x 32 MB device"},
+          "reference_loader_seconds": ref, "speedup_vs_reference_loader": (ref / ours) if ref else None,
+          "bit_exact_vs_reference_loader": match, "all_load_seconds": times})
+
+
 def run_ours(args):
     import torch
 
@@ -716,6 +822,8 @@ def main():
         run_reference(args)
     elif args.workload == "llama_int8_dequant":
         run_dequant(args)
+    elif args.workload == "llama_int8_load":
+        run_load(args)
     else:
         run_ours(args)
 

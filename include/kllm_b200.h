@@ -50,7 +50,9 @@ enum {
   KLLM_B200_ERR_ALIGN = -4,       /* pointer alignment a kernel requires is not met */
   KLLM_B200_ERR_RANGE = -5,       /* host-visible id / position out of range */
   KLLM_B200_ERR_CAPACITY = -6,    /* KV cache capacity exceeded */
-  KLLM_B200_ERR_CUDA = -7         /* CUDA runtime / launch error */
+  KLLM_B200_ERR_CUDA = -7,        /* CUDA runtime / launch error */
+  KLLM_B200_ERR_IO = -8,          /* file open / read error */
+  KLLM_B200_ERR_FORMAT = -9       /* malformed .kllm file */
 };
 
 /* ---- bits OR-ed into the optional device word `err_flags` ---- */
@@ -265,6 +267,54 @@ typedef struct kllm_b200_chain {
  * when it is 0). *n_launches (if given) receives the number of kernels
  * launched. Can be captured into a CUDA graph. */
 int kllm_b200_chain_run(const kllm_b200_chain* chain, int* n_launches, void* stream);
+
+/* ======================================================================== *
+ *  .kllm weight files: index + streaming load with device-side dequant      *
+ * ======================================================================== */
+
+/* Model config of a .kllm file header (read by src/model/weights.cpp:65-79). */
+typedef struct kllm_b200_kllm_config {
+  uint32_t model_type; /* 0 llama, 1 qwen2 */
+  int32_t vocab_size, hidden_size, intermediate_size, num_layers, num_heads, num_kv_heads;
+  int32_t head_dim, max_seq_len;
+  float rms_norm_eps, rope_theta;
+  uint8_t tie_word_embeddings, qkv_bias, o_bias, mlp_bias;
+} kllm_b200_kllm_config;
+
+/* One tensor record of a .kllm file (src/model/weights.cpp:81-118). */
+typedef struct kllm_b200_kllm_record {
+  char name[192];
+  int32_t dtype;        /* as stored: F32, F16, I32 or I8 */
+  int32_t ndim;
+  int64_t dims[8];
+  int64_t numel;
+  uint64_t data_offset; /* file offset of the record's bytes */
+  uint64_t nbytes;      /* stored bytes; I8 records: numel int8 values + one fp32 scale */
+  int32_t load_dtype;   /* dtype of the device tensor: I8 -> F16 (the reference's CUDA
+                           load type, src/model/weights.cpp:122), others as stored */
+  int32_t reserved;
+  int64_t load_bytes;   /* bytes of the device tensor */
+} kllm_b200_kllm_record;
+
+/* Parses the header and record table of a .kllm file (magic "KLLM0001",
+ * version 1) with the checks of ModelWeights::load (src/model/weights.cpp:
+ * 47-118): magic, version, byte counts per dtype. Writes up to max_records
+ * entries and the total count to *n_records (so a first call with
+ * max_records = 0 sizes the array). Host only; no CUDA calls. */
+int kllm_b200_kllm_read_index(const char* path, kllm_b200_kllm_config* config,
+                              kllm_b200_kllm_record* records, int max_records, int* n_records);
+
+/* Streams records into caller-allocated device tensors dst[i]
+ * (records[i].load_bytes each): F32/F16/I32 records are copied as stored;
+ * I8 records are copied to the device and dequantised there to fp16 with the
+ * rounding of the reference loader (src/model/weights.cpp:120-154), bit for
+ * bit. host_staging (pinned host memory, >= 64 KB) is used as two halves so
+ * file reads overlap the copies; dev_staging (device memory, needed only
+ * for I8 records, >= 64 KB) holds int8 chunks before dequant. Returns after
+ * the stream has finished all copies and kernels of the call. */
+int kllm_b200_kllm_load(const char* path, const kllm_b200_kllm_record* records, int n_records,
+                        void* const* dst, void* host_staging, size_t host_staging_bytes,
+                        void* dev_staging, size_t dev_staging_bytes, void* stream);
 
 #ifdef __cplusplus
 }

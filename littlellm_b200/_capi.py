@@ -20,6 +20,8 @@ ERR_ALIGN = -4
 ERR_RANGE = -5
 ERR_CAPACITY = -6
 ERR_CUDA = -7
+ERR_IO = -8
+ERR_FORMAT = -9
 
 FLAG_BAD_TOKEN = 1
 FLAG_BAD_POSITION = 2
@@ -90,6 +92,9 @@ SIGNATURES = {
                                           _i64, _i64, _f32, _vp, _vp, _i64, _i64, _vp, _vp],
     "kllm_b200_select_last_rows": [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _int, _vp, _vp],
     "kllm_b200_chain_run": [ctypes.POINTER(Chain), ctypes.POINTER(ctypes.c_int), _vp],
+    # argtypes of the .kllm entry points use the structures in loader.py
+    "kllm_b200_kllm_read_index": None,
+    "kllm_b200_kllm_load": None,
 }
 _RESTYPES = {
     "kllm_b200_last_error": ctypes.c_size_t,
@@ -105,7 +110,8 @@ def _load() -> ctypes.CDLL:
     lib = ctypes.CDLL(LIB_PATH)
     for name, argtypes in SIGNATURES.items():
         fn = getattr(lib, name)
-        fn.argtypes = argtypes
+        if argtypes is not None:
+            fn.argtypes = argtypes
         fn.restype = _RESTYPES.get(name, ctypes.c_int)
     return lib
 

@@ -14,7 +14,7 @@
 // always read 32 different banks: no bank conflicts whatever the data. The
 // stream itself moves 16 int8 in (one 16-byte load) and 16 fp16 out (two
 // 16-byte stores) per vector.
-#include "common.cuh"
+#include "ops.cuh"
 
 namespace kb {
 namespace {
@@ -57,13 +57,16 @@ __device__ __forceinline__ void lut16(const uint32_t* my, uint4 w, uint4& o0, ui
   o1 = make_uint4(lut2(my, w.z, 0), lut2(my, w.z, 16), lut2(my, w.w, 0), lut2(my, w.w, 16));
 }
 
+// `scale` points to the per-tensor scale in device memory; when it is null
+// the scale comes by value in `scale_value` (the weight loader reads it from
+// the file).
 __global__ void __launch_bounds__(kThreads) dequant_f16_kernel(const int8_t* __restrict__ q,
-                                                               const float* __restrict__ scale,
+                                                               const float* __restrict__ scale, float scale_value,
                                                                __half* __restrict__ out, int64_t n) {
   __shared__ uint32_t lut[256 * 32];
   grid_dep_wait();
   grid_dep_launch();
-  const float s = __ldg(scale);
+  const float s = scale != nullptr ? __ldg(scale) : scale_value;
   {
     // Thread b evaluates byte value b and writes its 32 lane copies,
     // rotating the lane so a warp's 32 stores hit 32 different banks.
@@ -106,11 +109,11 @@ __global__ void __launch_bounds__(kThreads) dequant_f16_kernel(const int8_t* __r
 }
 
 __global__ void __launch_bounds__(kThreads) dequant_f32_kernel(const int8_t* __restrict__ q,
-                                                               const float* __restrict__ scale,
+                                                               const float* __restrict__ scale, float scale_value,
                                                                float* __restrict__ out, int64_t n) {
   grid_dep_wait();
   grid_dep_launch();
-  const float s = __ldg(scale);
+  const float s = scale != nullptr ? __ldg(scale) : scale_value;
   const int64_t nvec = n >> 4;
   const uint4* src = reinterpret_cast<const uint4*>(q);
   float4* dst = reinterpret_cast<float4*>(out);
@@ -134,11 +137,11 @@ __global__ void __launch_bounds__(kThreads) dequant_f32_kernel(const int8_t* __r
 
 // Unaligned buffers: element per thread, same arithmetic.
 template <bool F16>
-__global__ void __launch_bounds__(kThreads) dequant_generic_kernel(const int8_t* q, const float* scale, void* out,
-                                                                   int64_t n) {
+__global__ void __launch_bounds__(kThreads) dequant_generic_kernel(const int8_t* q, const float* scale,
+                                                                   float scale_value, void* out, int64_t n) {
   grid_dep_wait();
   grid_dep_launch();
-  const float s = __ldg(scale);
+  const float s = scale != nullptr ? __ldg(scale) : scale_value;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
     const float val = __fmul_rn(static_cast<float>(q[i]), s);
@@ -267,32 +270,43 @@ __global__ void __launch_bounds__(kThreads) dequant_batched_kernel(const __grid_
 
 }  // namespace
 
-int dequantize_int8(const int8_t* data, const float* scale, void* out, int64_t n, int out_dtype,
-                    const LaunchOpts& o) {
+int dequantize_int8_impl(const int8_t* data, const float* scale, float scale_value, void* out, int64_t n,
+                         int out_dtype, const LaunchOpts& o) {
   if (n < 0) return fail(KLLM_B200_ERR_INVALID_ARG, "dequantize_int8: negative size");
   if (n == 0) return KLLM_B200_OK;
-  if (!data || !scale || !out) return fail(KLLM_B200_ERR_INVALID_ARG, "dequantize_int8: null pointer");
+  if (!data || !out) return fail(KLLM_B200_ERR_INVALID_ARG, "dequantize_int8: null pointer");
   if (!is_float_dtype(out_dtype)) {
     return fail(KLLM_B200_ERR_DTYPE, "dequantize_int8: output dtype %d not supported (F32/F16)", out_dtype);
   }
   const bool vec = aligned16(data) && aligned16(out);
   if (out_dtype == KLLM_B200_F16 && vec) {
     const unsigned grid = persistent_grid(dequant_f16_kernel, kThreads, 0, kThreads * 2, (n >> 4) + 1);
-    return launch_status(launch(dequant_f16_kernel, grid, kThreads, 0, o.stream, o.pdl, data, scale,
+    return launch_status(launch(dequant_f16_kernel, grid, kThreads, 0, o.stream, o.pdl, data, scale, scale_value,
                                 static_cast<__half*>(out), n),
                          "dequantize_int8");
   }
   if (out_dtype == KLLM_B200_F32 && vec) {
     const unsigned grid = persistent_grid(dequant_f32_kernel, kThreads, 0, kThreads, (n >> 4) + 1);
-    return launch_status(launch(dequant_f32_kernel, grid, kThreads, 0, o.stream, o.pdl, data, scale,
+    return launch_status(launch(dequant_f32_kernel, grid, kThreads, 0, o.stream, o.pdl, data, scale, scale_value,
                                 static_cast<float*>(out), n),
                          "dequantize_int8");
   }
   auto k = out_dtype == KLLM_B200_F16 ? dequant_generic_kernel<true> : dequant_generic_kernel<false>;
   const unsigned grid = persistent_grid(k, kThreads, 0, kThreads * 4, n);
-  return launch_status(launch(k, grid, kThreads, 0, o.stream, o.pdl, data, scale, out, n), "dequantize_int8");
+  return launch_status(launch(k, grid, kThreads, 0, o.stream, o.pdl, data, scale, scale_value, out, n),
+                       "dequantize_int8");
 }
 
+int dequantize_int8(const int8_t* data, const float* scale, void* out, int64_t n, int out_dtype,
+                    const LaunchOpts& o) {
+  if (n > 0 && !scale) return fail(KLLM_B200_ERR_INVALID_ARG, "dequantize_int8: null scale");
+  return dequantize_int8_impl(data, scale, 0.0f, out, n, out_dtype, o);
+}
+
+int dequantize_int8_value(const int8_t* data, float scale, void* out, int64_t n, int out_dtype,
+                          const LaunchOpts& o) {
+  return dequantize_int8_impl(data, nullptr, scale, out, n, out_dtype, o);
+}
 
 int dequantize_int8_batched(const int8_t* const* data, const float* const* scales, void* const* outs,
                             const int64_t* counts, int n_tensors, int out_dtype, const LaunchOpts& o) {

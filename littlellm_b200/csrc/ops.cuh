@@ -25,6 +25,13 @@ int qkv_bias_rope_kv_append(void* q, const void* k, const void* v, const void* b
                             float theta, void* k_cache, void* v_cache, int64_t n_slots, int64_t max_seq,
                             int32_t* err_flags, const LaunchOpts& o);
 
+int dequantize_int8(const int8_t* data, const float* scale, void* out, int64_t n, int out_dtype,
+                    const LaunchOpts& o);
+
+// The same with the scale passed by value (host-side scale, e.g. read from a file).
+int dequantize_int8_value(const int8_t* data, float scale, void* out, int64_t n, int out_dtype,
+                          const LaunchOpts& o);
+
 int select_last_rows(const void* x, int64_t rows, int64_t cols, const int32_t* seq_ends, int64_t seq_len,
                      int64_t n_seqs, void* out, int dtype, int32_t* err_flags, const LaunchOpts& o);
 

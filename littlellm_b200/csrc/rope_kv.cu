@@ -289,6 +289,21 @@ __global__ void __launch_bounds__(kWarpThreads) qkv_rope_warp_kernel(const __gri
     }
     cache_ok = pos_ok && slot_ok;
   }
+  // With a compile-time head_dim, 32 is a multiple of the rotation units per
+  // head, so every rotation unit of this lane covers the same 8 frequencies
+  // (lane % chunks): read their cos/sin once. At 4 units per lane the 16
+  // extra live registers would cost occupancy, so there they are re-read per
+  // unit.
+  constexpr bool kHoistCs = DT != 0 && UPL <= 3;
+  float cc[8], ss[8];
+  if (kHoistCs) {
+    const int rd0 = (lane % chunks) << 3;
+    const float4* cp = reinterpret_cast<const float4*>(&s_cos[warp][rd0]);
+    const float4* sp = reinterpret_cast<const float4*>(&s_sin[warp][rd0]);
+    const float4 c0 = cp[0], c1 = cp[1], s0 = sp[0], s1 = sp[1];
+    cc[0] = c0.x; cc[1] = c0.y; cc[2] = c0.z; cc[3] = c0.w; cc[4] = c1.x; cc[5] = c1.y; cc[6] = c1.z; cc[7] = c1.w;
+    ss[0] = s0.x; ss[1] = s0.y; ss[2] = s0.z; ss[3] = s0.w; ss[4] = s1.x; ss[5] = s1.y; ss[6] = s1.z; ss[7] = s1.w;
+  }
   // [slot, head, pos, :] of a [n_slots, n_kv_heads, max_seq, D] plane: head h
   // of this token starts at cache_tok + h * max_seq * D
   const int64_t cache_tok = (static_cast<int64_t>(slot) * a.n_kv_heads * a.max_seq + pos) * D;
@@ -312,15 +327,20 @@ __global__ void __launch_bounds__(kWarpThreads) qkv_rope_warp_kernel(const __gri
         unpack8(x1[j], f1);
         unpack8(x2[j], f2);
       }
-      const int d0 = off[j] % D;
-      const float4* cp = reinterpret_cast<const float4*>(&s_cos[warp][d0]);
-      const float4* sp = reinterpret_cast<const float4*>(&s_sin[warp][d0]);
-      const float4 c0 = cp[0], c1 = cp[1], s0 = sp[0], s1 = sp[1];
-      const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-      const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
       float y1[8], y2[8];
+      if (kHoistCs) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) rotate(f1[i], f2[i], c[i], sn[i], y1[i], y2[i]);
+        for (int i = 0; i < 8; ++i) rotate(f1[i], f2[i], cc[i], ss[i], y1[i], y2[i]);
+      } else {
+        const int d0 = off[j] % D;
+        const float4* cp = reinterpret_cast<const float4*>(&s_cos[warp][d0]);
+        const float4* sp = reinterpret_cast<const float4*>(&s_sin[warp][d0]);
+        const float4 c0 = cp[0], c1 = cp[1], s0 = sp[0], s1 = sp[1];
+        const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+        const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) rotate(f1[i], f2[i], c[i], sn[i], y1[i], y2[i]);
+      }
       __half* dst;
       if (is_q) {
         dst = q_out + off[j];

@@ -117,6 +117,8 @@ extern "C" const char* kllm_b200_status_string(int status) {
     case KLLM_B200_ERR_RANGE: return "value out of range";
     case KLLM_B200_ERR_CAPACITY: return "KV cache capacity exceeded";
     case KLLM_B200_ERR_CUDA: return "CUDA error";
+    case KLLM_B200_ERR_IO: return "I/O error";
+    case KLLM_B200_ERR_FORMAT: return "malformed model file";
     default: return "unknown status";
   }
 }

@@ -264,6 +264,13 @@ class Reference:
         lib.kref_chain_destroy.argtypes = [vp]
         lib.kref_chain_run.restype = i32
         lib.kref_chain_run.argtypes = [vp, i32]
+        lib.kref_weights_load.restype = vp
+        lib.kref_weights_load.argtypes = [ctypes.c_char_p]
+        lib.kref_weights_free.argtypes = [vp]
+        lib.kref_weights_get.restype = i64
+        lib.kref_weights_get.argtypes = [vp, ctypes.c_char_p, vp, i64]
+        lib.kref_weights_dtype.restype = i32
+        lib.kref_weights_dtype.argtypes = [vp, ctypes.c_char_p]
 
     def _check(self, rc: int) -> None:
         if rc != 0:
@@ -351,6 +358,32 @@ class Reference:
         out = np.empty(q.shape, dtype=np.uint16)
         self.lib.kref_dequantize_int8_f16(self._vp(q), q.size, scale, self._vp(out))
         return out
+
+
+class ReferenceWeights:
+    """A .kllm file loaded by the reference's own ModelWeights::load on the
+    CPU (INT8 records become fp32 float(q) * scale there)."""
+
+    def __init__(self, ref: "Reference", path: str):
+        self.lib = ref.lib
+        self.h = self.lib.kref_weights_load(path.encode())
+        if not self.h:
+            raise RuntimeError(self.lib.kref_last_error().decode())
+
+    def get(self, name: str, numel: int) -> np.ndarray:
+        out = np.empty(max(numel, 1), dtype=np.float32)
+        n = self.lib.kref_weights_get(self.h, name.encode(), ctypes.c_void_p(out.ctypes.data), out.size)
+        if n < 0:
+            raise KeyError(name)
+        return out[:n]
+
+    def dtype(self, name: str) -> int:
+        return self.lib.kref_weights_dtype(self.h, name.encode())
+
+    def close(self) -> None:
+        if self.h:
+            self.lib.kref_weights_free(self.h)
+            self.h = None
 
 
 def reference_available() -> bool:

@@ -23,6 +23,7 @@
 
 #include "kllm/base/half.h"
 #include "kllm/base/tensor.h"
+#include "kllm/model/weights.h"
 #include "kllm/op/ops.h"
 
 namespace {
@@ -207,6 +208,38 @@ void kref_dequantize_int8_f16(const std::int8_t* q, std::int64_t n, float scale,
     const float deq = static_cast<float>(q[i]) * scale;
     out[i] = kllm::float_to_half(deq);
   }
+}
+
+// ---- the reference weight loader (src/model/weights.cpp) on the CPU --------
+
+void* kref_weights_load(const char* path) {
+  try {
+    return new kllm::ModelWeights(kllm::ModelWeights::load(path, kllm::DeviceType::CPU));
+  } catch (const std::exception& e) {
+    g_error = e.what();
+    return nullptr;
+  }
+}
+
+void kref_weights_free(void* w) { delete static_cast<kllm::ModelWeights*>(w); }
+
+// Copies the named tensor as float values (its CPU dtype: F32 for F32 and
+// I8 records, F16/I32 converted exactly); returns numel or -1.
+std::int64_t kref_weights_get(void* w, const char* name, float* out, std::int64_t cap) {
+  const kllm::Tensor* t = static_cast<kllm::ModelWeights*>(w)->find(name);
+  if (t == nullptr) {
+    g_error = std::string("no tensor ") + name;
+    return -1;
+  }
+  const std::vector<float> v = t->to_float_vector();
+  if (static_cast<std::int64_t>(v.size()) > cap) return -1;
+  std::memcpy(out, v.data(), v.size() * sizeof(float));
+  return static_cast<std::int64_t>(v.size());
+}
+
+int kref_weights_dtype(void* w, const char* name) {
+  const kllm::Tensor* t = static_cast<kllm::ModelWeights*>(w)->find(name);
+  return t == nullptr ? -1 : static_cast<int>(t->dtype());
 }
 
 // ---- timing chain -------------------------------------------------------
