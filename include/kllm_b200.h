@@ -316,6 +316,27 @@ int kllm_b200_kllm_load(const char* path, const kllm_b200_kllm_record* records, 
                         void* const* dst, void* host_staging, size_t host_staging_bytes,
                         void* dev_staging, size_t dev_staging_bytes, void* stream);
 
+/* ======================================================================== *
+ *  No device allocation                                                     *
+ * ======================================================================== */
+
+/* out[i] = host_data[i] * scale for n INT8 values that live in HOST memory,
+ * with no device memory allocated anywhere: the int8 bytes are staged in a
+ * 32 MiB device array built into the library (the staged dequant of
+ * kllm_b200_kllm_load, which instead stages in device memory the caller
+ * allocates). For callers that cannot call cudaMalloc, e.g. a plugin handed
+ * only output buffers by its host application. Rounding as
+ * kllm_b200_dequantize_int8 for out_dtype (F16: the reference loader's
+ * float_to_half, bit for bit). n above 33554432 (32 MiB) fails with
+ * KLLM_B200_ERR_CAPACITY before any GPU work. The first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress) and should
+ * come before any stream capture. All calls share the array, so calls that
+ * overlap on the GPU race; run them in one stream order. host_data must not
+ * change until the stream has passed the copy (pinned memory is read
+ * asynchronously). This entry point has no counterpart in the reference. */
+int kllm_b200_dequantize_int8_host_static(const int8_t* host_data, float scale, void* out,
+                                          int64_t n, int out_dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

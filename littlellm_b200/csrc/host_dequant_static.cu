@@ -1,0 +1,85 @@
+// host_dequant_static.cu — INT8 -> fp16/fp32 dequant of a tensor held in host
+// memory, without allocating any device memory.
+//
+// kllm_b200_kllm_load stages INT8 records in device memory the caller
+// allocates before the dequant kernel reads them. Some callers cannot
+// allocate device memory: a plugin that only receives device output buffers
+// from the application hosting it, or a weight-refresh path running inside a
+// serving process whose GPU memory is owned by another allocator that forbids
+// cudaMalloc while requests are in flight. For them this entry point stages
+// the int8 bytes in a fixed device array compiled into this file instead.
+//
+// The array is kStaticStagingBytes (32 MiB) and every GPU that loads the
+// library holds it until the process exits. Host code cannot use the array's
+// name as a device address (it names a host-side stand-in), so the device
+// address is looked up with cudaGetSymbolAddress once per device, with that
+// device current, on the first call on that device; that first call should
+// come before any stream capture. Every call uses the same array: the copy
+// of a call's int8 bytes overwrites the previous contents entirely (nothing
+// needs to start at zero), and calls that overlap on the GPU (different
+// streams, or different host threads on the same device) race on it.
+#include <mutex>
+
+#include "ops.cuh"
+
+namespace kb {
+namespace {
+
+constexpr int64_t kStaticStagingBytes = int64_t{32} << 20;  // the largest tensor one call accepts
+
+// One int8 value per byte; file scope, so every device holds one copy.
+__device__ __align__(256) int8_t g_int8_staging[kStaticStagingBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_setup_mutex;
+int8_t* g_staging_address[kMaxDevices];  // per device, filled on its first call
+
+int staging_address(int8_t** out) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return launch_status(err, "dequantize_int8_host_static: cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) {
+    return fail(KLLM_B200_ERR_INVALID_ARG, "dequantize_int8_host_static: device %d out of range", dev);
+  }
+  std::lock_guard<std::mutex> lock(g_setup_mutex);
+  if (g_staging_address[dev] == nullptr) {
+    void* p = nullptr;
+    err = cudaGetSymbolAddress(&p, g_int8_staging);  // device `dev` is current
+    if (err != cudaSuccess || p == nullptr) {
+      return launch_status(err != cudaSuccess ? err : cudaErrorInvalidSymbol,
+                           "dequantize_int8_host_static: cudaGetSymbolAddress");
+    }
+    g_staging_address[dev] = static_cast<int8_t*>(p);
+  }
+  *out = g_staging_address[dev];
+  return KLLM_B200_OK;
+}
+
+}  // namespace
+}  // namespace kb
+
+extern "C" int kllm_b200_dequantize_int8_host_static(const int8_t* host_data, float scale, void* out,
+                                                     int64_t n, int out_dtype, void* stream) {
+  using namespace kb;
+  if (n < 0) return fail(KLLM_B200_ERR_INVALID_ARG, "dequantize_int8_host_static: negative size");
+  if (n == 0) return KLLM_B200_OK;
+  if (!host_data || !out) return fail(KLLM_B200_ERR_INVALID_ARG, "dequantize_int8_host_static: null pointer");
+  if (!is_float_dtype(out_dtype)) {
+    return fail(KLLM_B200_ERR_DTYPE, "dequantize_int8_host_static: output dtype %d not supported (F32/F16)",
+                out_dtype);
+  }
+  if (n > kStaticStagingBytes) {
+    return fail(KLLM_B200_ERR_CAPACITY,
+                "dequantize_int8_host_static: %lld values exceed the %lld-byte static staging area; "
+                "use kllm_b200_kllm_load or kllm_b200_dequantize_int8 with caller-allocated memory",
+                (long long)n, (long long)kStaticStagingBytes);
+  }
+  int8_t* staging = nullptr;
+  int rc = staging_address(&staging);
+  if (rc != KLLM_B200_OK) return rc;
+  LaunchOpts o;
+  o.stream = static_cast<cudaStream_t>(stream);
+  const cudaError_t err = cudaMemcpyAsync(staging, host_data, static_cast<size_t>(n), cudaMemcpyHostToDevice, o.stream);
+  if (err != cudaSuccess) return launch_status(err, "dequantize_int8_host_static: copy to the staging area");
+  return dequantize_int8_value(staging, scale, out, n, out_dtype, o);
+}
