@@ -253,11 +253,97 @@ def host_threads() -> int:
 # ---------------------------------------------------------------------------
 
 
+def run_reference_dequant(args):
+    """The reference weight loader's host INT8 -> fp16 loop body
+    (src/model/weights.cpp:139-148: float(q) * scale, float_to_half) on the
+    host cores, one slice of a 64 M-value sample per thread; metric as our
+    arm's (1 B read + 2 B written per value)."""
+    import ctypes
+    from concurrent.futures import ThreadPoolExecutor
+
+    import numpy as np
+
+    from oracle.oracle import Oracle, Reference, reference_available
+    kind = "reference" if reference_available() else "port"
+    fn = Reference().lib.kref_dequantize_int8_f16 if kind == "reference" else \
+        Oracle().lib.kllm_oracle_dequantize_int8_f16
+    threads = host_threads()
+    n = 1 << 26
+    q = np.random.default_rng(5).integers(-127, 128, n, dtype=np.int8)
+    out16 = np.empty(n, np.uint16)
+    bounds = np.linspace(0, n, threads + 1).astype(np.int64)
+
+    def one(i):
+        lo, hi = int(bounds[i]), int(bounds[i + 1])
+        fn(ctypes.c_void_p(q.ctypes.data + lo), hi - lo, ctypes.c_float(0.0047),
+           ctypes.c_void_p(out16.ctypes.data + 2 * lo))
+
+    steps = []
+    with ThreadPoolExecutor(threads) as ex:
+        for _ in range(args.warmup):
+            list(ex.map(one, range(threads)))
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            list(ex.map(one, range(threads)))
+            steps.append(time.perf_counter() - t0)
+    value = 3 * n * len(steps) / sum(steps) / 1e9
+    emit({"metric": "int8->fp16 dequant throughput", "value": value, "unit": "GB/s", "impl": "reference",
+          "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+          "ms_per_step": 1000.0 * statistics.mean(steps), "higher_is_better": True, "scaling": "none",
+          "vs_baseline": None, "dtype": "i8->f16", "data": "synthetic",
+          "config": {"workload": "llama_int8_dequant", "params_per_step": n,
+                     "impl_detail": "reference weight-loader dequant loop (src/model/weights.cpp)"},
+          "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": kind,
+                           "sample": f"{n} int8 values per step split over {threads} threads"},
+          "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
+
+
+def run_reference_load(args):
+    """The reference's own ModelWeights::load (CUDA device, host dequant,
+    src/model/weights.cpp:81-160) on the same partial Llama-2-7B INT8 file as
+    our arm; each step is one whole load, at most 3 steps (about 7 s each)."""
+    import subprocess
+    import tempfile
+    exe = os.path.join(ROOT, "oracle", "_ref", "refcuda", "ref_load")
+    if not os.path.exists(exe):
+        emit({"impl": "reference", "unavailable": "oracle/_ref/refcuda/ref_load was not built"})
+        return
+    layers = args.layers or 4
+    times = []
+    with tempfile.TemporaryDirectory() as tmp:
+        path = os.path.join(tmp, "llama_int8.kllm")
+        names = _write_llama_int8(path, layers)
+        file_bytes = os.path.getsize(path)
+        names_path = os.path.join(tmp, "names.txt")
+        with open(names_path, "w") as f:
+            f.write("\n".join(names) + "\n")
+        for _ in range(min(max(args.steps, 1), 3)):
+            r = subprocess.run([exe, path, names_path], capture_output=True, text=True, timeout=1200)
+            if r.returncode != 0:
+                emit({"impl": "reference", "unavailable": "ref_load failed: " + r.stderr.strip()[-200:]})
+                return
+            times.append(float(r.stdout.splitlines()[0].split()[1]))
+    value = file_bytes / min(times) / 1e9
+    emit({"metric": "int8 .kllm checkpoint load", "value": value, "unit": "GB/s", "impl": "reference",
+          "n_gpus": args.gpus, "steps": len(times), "warmup": 0, "ms_per_step": 1000.0 * min(times),
+          "higher_is_better": True, "scaling": "none", "vs_baseline": None, "dtype": "i8->f16",
+          "data": "synthetic",
+          "config": {"workload": "llama_int8_load", "layers": layers, "file_bytes": file_bytes,
+                     "tensors": len(names), "impl_detail": "reference ModelWeights::load(path, CUDA)"},
+          "cpu_baseline": {"value": value, "unit": "GB/s", "cores": 1, "kind": "reference",
+                           "sample": f"{len(times)} whole loads of a {file_bytes} B file"},
+          "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
+
+
 def run_reference(args):
     from littlellm_b200.chain import WORKLOADS
     world, rank, _ = dist_env()
     if rank != 0:
         return
+    if args.workload == "llama_int8_dequant":
+        return run_reference_dequant(args)
+    if args.workload == "llama_int8_load":
+        return run_reference_load(args)
     w = WORKLOADS[args.workload]
     threads = host_threads()
     tokens = 128
