@@ -202,6 +202,32 @@ int kllm_b200_select_last_rows(const void* x, int64_t rows, int64_t cols,
                                const int32_t* seq_ends, int64_t seq_len, int64_t n_seqs,
                                void* out, int dtype, int32_t* err_flags, void* stream);
 
+/* Attention over the head-major cache (replaces cuda_attention,
+ * src/op/cuda/attention.cu:224-263, for a runner that keeps the cache
+ * [n_slots, n_kv_heads, max_seq, head_dim] per layer that
+ * kllm_b200_qkv_bias_rope_kv_append fills). For token t and query head h:
+ * out[t, h, :] = sum_j p_j * v_cache[slots[t], h / G, j, :] over positions
+ * j = 0..positions[t], with p = softmax_j(q[t, h, :] . k_cache[slots[t], h / G,
+ * j, :] / sqrt(head_dim)) and G = n_heads / n_kv_heads, as cpu_attention
+ * (src/op/cpu/attention.cpp:12-67) computes it with past_len + t equal to
+ * positions[t]. q and out are [n_tokens, n_heads, head_dim]. F16 only;
+ * head_dim 64 or 128; G <= 16. seq_len: tokens arrive in runs of seq_len
+ * consecutive rows of one sequence (1 for decode); it selects the kernel,
+ * and the rows of one run must then share a slot. A token whose position
+ * or slot is out of range gets zero rows and sets KLLM_B200_FLAG_BAD_POSITION
+ * / _BAD_SLOT. workspace (device, 16-byte aligned) holds split-sequence
+ * partials; kllm_b200_attention_workspace_bytes gives the size for the best
+ * split, and a smaller (or NULL) workspace gives coarser splits with the
+ * same results. Nothing is allocated; the workspace needs no clearing. */
+int kllm_b200_attention_workspace_bytes(int64_t n_tokens, int64_t n_heads, int64_t n_kv_heads,
+                                        int64_t head_dim, int64_t max_seq, int64_t* bytes);
+int kllm_b200_attention_head_major(const void* q, const void* k_cache, const void* v_cache,
+                                   void* out, const int32_t* positions, const int32_t* slots,
+                                   int64_t n_tokens, int64_t seq_len, int64_t n_heads,
+                                   int64_t n_kv_heads, int64_t head_dim, int64_t n_slots,
+                                   int64_t max_seq, int dtype, void* workspace,
+                                   int64_t workspace_bytes, int32_t* err_flags, void* stream);
+
 /* ======================================================================== *
  *  Layer-op chain executor                                                  *
  * ======================================================================== */

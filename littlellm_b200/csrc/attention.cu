@@ -1,0 +1,490 @@
+// attention.cu — causal attention of new tokens over the head-major KV cache
+// [n_slots, kv_heads, max_seq, head_dim] (one layer) that
+// qkv_bias_rope_kv_append fills.
+//
+// Semantics follow cpu_attention (src/op/cpu/attention.cpp:12-67): for token
+// t and query head h, scores q·k * 1/sqrt(head_dim) over the cached positions
+// 0..positions[t] of sequence slot slots[t] and kv head h / (Hq / Hkv), a
+// softmax, and the probability-weighted sum of the cached values. The
+// reference reads a per-sequence cache [max_seq, kv_heads, head_dim] with a
+// scalar past_len (src/op/cuda/attention.cu:30-149); here every token carries
+// its own position and slot, so one launch serves a whole batch of sequences.
+//
+// Decode kernel (one token per sequence, or any token set): a CTA takes one
+// (token, kv head, chunk of positions) item. Its four warps stream 32-position
+// K/V tiles of the chunk through a per-warp cp.async ring and run both
+// products on mma.sync m16n8k16 (fp16 in, fp32 accumulate) with the
+// kv head's query heads as the M rows, keeping an online softmax per row.
+// The warps merge in shared memory; a sequence whose positions span several
+// chunks writes normalised partials (o, max, sum) to the caller's workspace
+// and a combine kernel merges them. The kernel is bound by HBM reads of
+// K and V: 2 * (positions[t] + 1) * head_dim * 2 bytes per (token, kv head).
+#include <math.h>
+
+#include "ops.cuh"
+
+namespace kb {
+namespace {
+
+constexpr int kAttnWarps = 4;
+constexpr int kAttnThreads = kAttnWarps * 32;
+constexpr int kTile = 32;                       // positions per warp tile
+constexpr int kStages = 3;                      // cp.async ring depth per warp
+constexpr int kChunkUnit = kAttnWarps * kTile;  // chunk sizes are multiples of this
+constexpr int kMaxGroups = 16;                  // query heads per kv head (the mma M rows)
+constexpr int kCombineWarps = 4;
+
+struct AttnArgs {
+  const __half* q;        // [T, Hq, D]
+  const __half* k_cache;  // [n_slots, Hkv, max_seq, D]
+  const __half* v_cache;
+  __half* out;            // [T, Hq, D]
+  const int32_t* positions;
+  const int32_t* slots;
+  float* part_o;          // [T, Hq, n_chunks, D] chunk outputs, normalised by their own sum
+  float* part_ml;         // [T, Hq, n_chunks, 2] chunk (max, sum), max in log2 units
+  int32_t* err_flags;
+  int64_t n_tokens;
+  int n_heads, n_kv_heads, groups;
+  int max_seq, n_slots;
+  int chunk;              // positions per CTA, a multiple of kChunkUnit
+  int n_chunks;           // ceil(max_seq / chunk)
+  float scale_log2;       // log2(e) / sqrt(D)
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// 16-byte global -> shared copy; src_bytes 0 writes zeros and reads nothing.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+// c += a * b for one m16n8k16 tile (row-major A, column-major B).
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ uint32_t ld_u32(const __half* p) { return *reinterpret_cast<const uint32_t*>(p); }
+
+// Byte offset of 16-byte chunk `chunk` of row `row` in a [rows][D] fp16 tile;
+// the chunk index is XOR-ed with row % 8 so that the eight rows one
+// ldmatrix phase reads fall in eight different bank groups.
+template <int D>
+__device__ __forceinline__ uint32_t swz(int row, int chunk) {
+  return static_cast<uint32_t>(row * (D * 2) + ((chunk ^ (row & 7)) << 4));
+}
+
+template <int D>
+__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  constexpr int kRowChunks = D / 8;        // 16-byte chunks per cached row
+  constexpr int kTileBytes = kTile * D * 2;
+  constexpr int kKS = D / 16;              // k-steps of q·k over head_dim
+  constexpr int kND = D / 8;               // n8 tiles of the output over head_dim
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gid = lane >> 2, tig = lane & 3;
+  const int64_t t = blockIdx.x / a.n_chunks;
+  const int c = static_cast<int>(blockIdx.x - t * a.n_chunks);
+  const int g = blockIdx.y;
+  const int G = a.groups;
+
+  grid_dep_wait();
+  const int pos = a.positions[t];
+  const int slot = a.slots[t];
+  __half* out_t = a.out + (t * a.n_heads + static_cast<int64_t>(g) * G) * D;
+  if (pos < 0 || pos >= a.max_seq || slot < 0 || slot >= a.n_slots) {
+    if (c == 0) {
+      if (threadIdx.x == 0 && g == 0) {
+        if (pos < 0 || pos >= a.max_seq) set_flag(a.err_flags, KLLM_B200_FLAG_BAD_POSITION);
+        if (slot < 0 || slot >= a.n_slots) set_flag(a.err_flags, KLLM_B200_FLAG_BAD_SLOT);
+      }
+      for (int i = threadIdx.x; i < G * kRowChunks; i += kAttnThreads) {
+        reinterpret_cast<uint4*>(out_t)[i] = make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+    return;
+  }
+  const int c0 = c * a.chunk;
+  if (c0 > pos) return;  // this chunk lies past the token's position
+  const int c1 = min(c0 + a.chunk, pos + 1);
+  const int n_tiles = (c1 - c0 + kTile - 1) / kTile;
+  const int my_tiles = n_tiles > warp ? (n_tiles - warp + kAttnWarps - 1) / kAttnWarps : 0;
+
+  const size_t head_off = (static_cast<size_t>(slot) * a.n_kv_heads + g) * static_cast<size_t>(a.max_seq) * D;
+  const __half* kbase = a.k_cache + head_off;
+  const __half* vbase = a.v_cache + head_off;
+  unsigned char* ring = smem + warp * (kStages * 2 * kTileBytes);
+
+  // Warp tile i covers positions c0 + (warp + 4 i) * 32 ... (+31); rows past
+  // c1 are zero-filled so that no stale bits reach the products.
+  auto issue = [&](int i) {
+    if (i < my_tiles) {
+      const int j0 = c0 + (warp + i * kAttnWarps) * kTile;
+      unsigned char* sk = ring + (i % kStages) * 2 * kTileBytes;
+      unsigned char* sv = sk + kTileBytes;
+#pragma unroll
+      for (int it = 0; it < kTile * kRowChunks / 32; ++it) {
+        const int idx = lane + it * 32;
+        const int r = idx / kRowChunks, ch = idx % kRowChunks;
+        const int j = j0 + r;
+        const bool ok = j < c1;
+        const size_t off = static_cast<size_t>(ok ? j : c0) * D + ch * 8;
+        cp_async16(smem_u32(sk + swz<D>(r, ch)), kbase + off, ok ? 16 : 0);
+        cp_async16(smem_u32(sv + swz<D>(r, ch)), vbase + off, ok ? 16 : 0);
+      }
+    }
+    cp_async_commit();  // empty groups keep the group count uniform
+  };
+
+#pragma unroll
+  for (int i = 0; i < kStages - 1; ++i) issue(i);
+
+  // A fragments of the query rows (rows >= G are zero).
+  uint32_t qa[kKS][4];
+  const __half* qg = a.q + (t * a.n_heads + static_cast<int64_t>(g) * G) * D;
+#pragma unroll
+  for (int ks = 0; ks < kKS; ++ks) {
+    const int d0 = ks * 16 + 2 * tig;
+    qa[ks][0] = gid < G ? ld_u32(qg + gid * D + d0) : 0u;
+    qa[ks][1] = gid + 8 < G ? ld_u32(qg + (gid + 8) * D + d0) : 0u;
+    qa[ks][2] = gid < G ? ld_u32(qg + gid * D + d0 + 8) : 0u;
+    qa[ks][3] = gid + 8 < G ? ld_u32(qg + (gid + 8) * D + d0 + 8) : 0u;
+  }
+
+  float o[kND][4];
+#pragma unroll
+  for (int nd = 0; nd < kND; ++nd) o[nd][0] = o[nd][1] = o[nd][2] = o[nd][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  const float sl2 = a.scale_log2;
+
+  for (int i = 0; i < my_tiles; ++i) {
+    issue(i + kStages - 1);
+    cp_async_wait<kStages - 1>();
+    __syncwarp();
+    const int j0 = c0 + (warp + i * kAttnWarps) * kTile;
+    const unsigned char* sk = ring + (i % kStages) * 2 * kTileBytes;
+    const unsigned char* sv = sk + kTileBytes;
+
+    // scores of 16 rows x 32 positions
+    float s[4][4];
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < D / 32; ++kk) {
+        uint32_t b[4];
+        ldsm_x4(b, smem_u32(sk + swz<D>(nt * 8 + (lane & 7), 4 * kk + (lane >> 3))));
+        mma16816(s[nt], qa[2 * kk], b[0], b[1]);
+        mma16816(s[nt], qa[2 * kk + 1], b[2], b[3]);
+      }
+    }
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int col = j0 + nt * 8 + 2 * tig + (e & 1);
+        const float v = col < c1 ? s[nt][e] * sl2 : -INFINITY;
+        s[nt][e] = v;
+        if (e < 2) mx0 = fmaxf(mx0, v); else mx1 = fmaxf(mx1, v);
+      }
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);  // finite: every tile has a valid column
+    const float cr0 = exp2f(m0 - mn0), cr1 = exp2f(m1 - mn1);
+    m0 = mn0;
+    m1 = mn1;
+    float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      s[nt][0] = exp2f(s[nt][0] - mn0);
+      s[nt][1] = exp2f(s[nt][1] - mn0);
+      s[nt][2] = exp2f(s[nt][2] - mn1);
+      s[nt][3] = exp2f(s[nt][3] - mn1);
+      ps0 += s[nt][0] + s[nt][1];
+      ps1 += s[nt][2] + s[nt][3];
+    }
+    l0 = l0 * cr0 + ps0;
+    l1 = l1 * cr1 + ps1;
+#pragma unroll
+    for (int nd = 0; nd < kND; ++nd) {
+      o[nd][0] *= cr0;
+      o[nd][1] *= cr0;
+      o[nd][2] *= cr1;
+      o[nd][3] *= cr1;
+    }
+    // o += p v: the score accumulators of n-tiles 2kv, 2kv+1 are the A fragment
+#pragma unroll
+    for (int kv = 0; kv < 2; ++kv) {
+      const uint32_t pa[4] = {pack_h2(s[2 * kv][0], s[2 * kv][1]), pack_h2(s[2 * kv][2], s[2 * kv][3]),
+                              pack_h2(s[2 * kv + 1][0], s[2 * kv + 1][1]),
+                              pack_h2(s[2 * kv + 1][2], s[2 * kv + 1][3])};
+      const int mtx = lane >> 3;
+#pragma unroll
+      for (int nd2 = 0; nd2 < D / 16; ++nd2) {
+        uint32_t b[4];
+        ldsm_x4_trans(b, smem_u32(sv + swz<D>(16 * kv + 8 * (mtx & 1) + (lane & 7), 2 * nd2 + (mtx >> 1))));
+        mma16816(o[2 * nd2], pa, b[0], b[1]);
+        mma16816(o[2 * nd2 + 1], pa, b[2], b[3]);
+      }
+    }
+    __syncwarp();  // the stage is refilled by the next iteration's issue
+  }
+  cp_async_wait<0>();
+
+  // merge the four warps (each row's sum is spread over its quad)
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  __syncthreads();  // all rings idle: reuse them for the merge
+  float* red_o = reinterpret_cast<float*>(smem);       // [warps][16][D]
+  float* red_ml = red_o + kAttnWarps * 16 * D;         // [warps][16][2]
+#pragma unroll
+  for (int nd = 0; nd < kND; ++nd) {
+    *reinterpret_cast<float2*>(red_o + (warp * 16 + gid) * D + nd * 8 + 2 * tig) = make_float2(o[nd][0], o[nd][1]);
+    *reinterpret_cast<float2*>(red_o + (warp * 16 + gid + 8) * D + nd * 8 + 2 * tig) =
+        make_float2(o[nd][2], o[nd][3]);
+  }
+  if (tig == 0) {
+    red_ml[(warp * 16 + gid) * 2] = m0;
+    red_ml[(warp * 16 + gid) * 2 + 1] = l0;
+    red_ml[(warp * 16 + gid + 8) * 2] = m1;
+    red_ml[(warp * 16 + gid + 8) * 2 + 1] = l1;
+  }
+  __syncthreads();
+  const int n_used = pos / a.chunk + 1;  // chunks holding positions 0..pos
+  for (int idx = threadIdx.x; idx < G * D; idx += kAttnThreads) {
+    const int row = idx / D, d = idx - row * D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, red_ml[(w * 16 + row) * 2]);
+    float L = 0.f, acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) {
+      const float f = exp2f(red_ml[(w * 16 + row) * 2] - M);  // 0 for a warp without tiles
+      L += red_ml[(w * 16 + row) * 2 + 1] * f;
+      acc += red_o[(w * 16 + row) * D + d] * f;
+    }
+    if (n_used == 1) {
+      out_t[row * D + d] = __float2half_rn(acc / L);
+    } else {
+      const int64_t prow = (t * a.n_heads + static_cast<int64_t>(g) * G + row) * a.n_chunks + c;
+      a.part_o[prow * D + d] = acc / L;
+      if (d == 0) {
+        a.part_ml[prow * 2] = M;
+        a.part_ml[prow * 2 + 1] = L;
+      }
+    }
+  }
+}
+
+// One warp per (token, query head) row whose positions span several chunks.
+template <int D>
+__global__ void __launch_bounds__(kCombineWarps * 32) attn_combine_kernel(const AttnArgs a) {
+  constexpr int kPer = D / 32;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kCombineWarps + (threadIdx.x >> 5);
+  grid_dep_wait();
+  if (row >= a.n_tokens * a.n_heads) return;
+  const int64_t t = row / a.n_heads;
+  const int pos = a.positions[t], slot = a.slots[t];
+  if (pos < 0 || pos >= a.max_seq || slot < 0 || slot >= a.n_slots) return;
+  const int n_used = pos / a.chunk + 1;
+  if (n_used <= 1) return;
+  const float* ml = a.part_ml + row * a.n_chunks * 2;
+  const float* po = a.part_o + row * a.n_chunks * D;
+  float M = -INFINITY;
+  for (int c = lane; c < n_used; c += 32) M = fmaxf(M, ml[2 * c]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+  float L = 0.f;
+  for (int c = lane; c < n_used; c += 32) L += ml[2 * c + 1] * exp2f(ml[2 * c] - M);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+  float acc[kPer];
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) acc[k] = 0.f;
+  for (int c = 0; c < n_used; ++c) {
+    const float w = ml[2 * c + 1] * exp2f(ml[2 * c] - M);
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) acc[k] += w * po[c * D + lane * kPer + k];
+  }
+  const float inv = 1.f / L;
+  __half* dst = a.out + row * D + lane * kPer;
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) dst[k] = __float2half_rn(acc[k] * inv);
+}
+
+constexpr size_t decode_smem(int head_dim) { return static_cast<size_t>(kAttnWarps) * kStages * 2 * kTile * head_dim * 2; }
+
+// Positions per decode CTA: 512, halved (down to 128) while the launch would
+// have fewer than four CTAs per SM, and never more than max_seq rounded up.
+int64_t preferred_chunk(int64_t n_tokens, int64_t n_kv_heads, int64_t max_seq) {
+  const int64_t cap = (max_seq + kChunkUnit - 1) / kChunkUnit * kChunkUnit;
+  int64_t chunk = 512;
+  const int64_t target = 4LL * sm_count();
+  while (chunk > kChunkUnit && n_tokens * n_kv_heads * ((max_seq + chunk - 1) / chunk) < target) chunk /= 2;
+  return chunk < cap ? chunk : cap;
+}
+
+int64_t workspace_for(int64_t n_tokens, int64_t n_heads, int64_t head_dim, int64_t max_seq, int64_t chunk) {
+  const int64_t n_chunks = (max_seq + chunk - 1) / chunk;
+  if (n_chunks <= 1) return 0;
+  return n_tokens * n_heads * n_chunks * (head_dim + 2) * static_cast<int64_t>(sizeof(float));
+}
+
+int check_attention_args(const void* q, const void* k_cache, const void* v_cache, const void* out,
+                         const int32_t* positions, const int32_t* slots, int64_t n_tokens, int64_t n_heads,
+                         int64_t n_kv_heads, int64_t head_dim, int64_t n_slots, int64_t max_seq, int dtype) {
+  if (n_tokens < 0 || n_heads < 0 || n_kv_heads < 0 || head_dim < 0 || n_slots < 0 || max_seq < 0) {
+    return fail(KLLM_B200_ERR_INVALID_ARG, "attention: negative size");
+  }
+  if (dtype != KLLM_B200_F16) return fail(KLLM_B200_ERR_DTYPE, "attention: dtype %d not supported (F16)", dtype);
+  if (head_dim != 64 && head_dim != 128) {
+    return fail(KLLM_B200_ERR_SHAPE, "attention: head_dim %lld not supported (64, 128)", (long long)head_dim);
+  }
+  if (n_kv_heads == 0 || n_heads % n_kv_heads != 0) {
+    return fail(KLLM_B200_ERR_SHAPE, "attention: %lld query heads not a multiple of %lld kv heads",
+                (long long)n_heads, (long long)n_kv_heads);
+  }
+  if (n_heads / n_kv_heads > kMaxGroups) {
+    return fail(KLLM_B200_ERR_SHAPE, "attention: more than %d query heads per kv head", kMaxGroups);
+  }
+  if (n_tokens == 0 || n_heads == 0) return KLLM_B200_OK;
+  if (max_seq == 0 || n_slots == 0) return fail(KLLM_B200_ERR_SHAPE, "attention: empty cache");
+  if (max_seq > (1LL << 30) || n_kv_heads > 65535) return fail(KLLM_B200_ERR_SHAPE, "attention: cache too large");
+  if (!q || !k_cache || !v_cache || !out || !positions || !slots) {
+    return fail(KLLM_B200_ERR_INVALID_ARG, "attention: null pointer");
+  }
+  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(out)) {
+    return fail(KLLM_B200_ERR_ALIGN, "attention: q, caches and out must be 16-byte aligned");
+  }
+  return KLLM_B200_OK;
+}
+
+template <int D>
+int launch_attention(AttnArgs& a, const LaunchOpts& o) {
+  const size_t smem = decode_smem(D);
+  cudaError_t err = allow_smem(reinterpret_cast<const void*>(attn_decode_kernel<D>), smem);
+  if (err != cudaSuccess) return launch_status(err, "attention: shared memory opt-in");
+  const dim3 grid(static_cast<unsigned>(a.n_tokens * a.n_chunks), static_cast<unsigned>(a.n_kv_heads));
+  err = launch(attn_decode_kernel<D>, grid, dim3(kAttnThreads), smem, o.stream, o.pdl, a);
+  if (err != cudaSuccess) return launch_status(err, "attention: decode kernel");
+  if (a.n_chunks > 1) {
+    const int64_t rows = a.n_tokens * a.n_heads;
+    const dim3 cgrid(static_cast<unsigned>((rows + kCombineWarps - 1) / kCombineWarps));
+    err = launch(attn_combine_kernel<D>, cgrid, dim3(kCombineWarps * 32), 0, o.stream, true, a);
+    if (err != cudaSuccess) return launch_status(err, "attention: combine kernel");
+  }
+  return KLLM_B200_OK;
+}
+
+}  // namespace
+
+int attention_workspace_bytes(int64_t n_tokens, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim,
+                              int64_t max_seq, int64_t* bytes) {
+  if (!bytes) return fail(KLLM_B200_ERR_INVALID_ARG, "attention_workspace_bytes: null pointer");
+  *bytes = 0;
+  if (n_tokens < 0 || n_heads < 0 || n_kv_heads < 0 || head_dim < 0 || max_seq < 0) {
+    return fail(KLLM_B200_ERR_INVALID_ARG, "attention_workspace_bytes: negative size");
+  }
+  if (n_tokens == 0 || n_heads == 0 || n_kv_heads == 0 || max_seq == 0) return KLLM_B200_OK;
+  *bytes = workspace_for(n_tokens, n_heads, head_dim, max_seq, preferred_chunk(n_tokens, n_kv_heads, max_seq));
+  return KLLM_B200_OK;
+}
+
+int attention_head_major(const void* q, const void* k_cache, const void* v_cache, void* out,
+                         const int32_t* positions, const int32_t* slots, int64_t n_tokens, int64_t seq_len,
+                         int64_t n_heads, int64_t n_kv_heads, int64_t head_dim, int64_t n_slots, int64_t max_seq,
+                         int dtype, void* workspace, int64_t workspace_bytes, int32_t* err_flags,
+                         const LaunchOpts& o) {
+  int rc = check_attention_args(q, k_cache, v_cache, out, positions, slots, n_tokens, n_heads, n_kv_heads,
+                                head_dim, n_slots, max_seq, dtype);
+  if (rc != KLLM_B200_OK || n_tokens == 0 || n_heads == 0) return rc;
+  if (seq_len < 1) return fail(KLLM_B200_ERR_SHAPE, "attention: seq_len must be >= 1");
+  if (workspace_bytes < 0) return fail(KLLM_B200_ERR_INVALID_ARG, "attention: negative workspace size");
+  if (workspace_bytes > 0 && (!workspace || !aligned16(workspace))) {
+    return fail(KLLM_B200_ERR_ALIGN, "attention: workspace must be non-null and 16-byte aligned");
+  }
+  // the preferred chunk, doubled until its partials fit the workspace (one
+  // chunk per sequence needs none)
+  int64_t chunk = preferred_chunk(n_tokens, n_kv_heads, max_seq);
+  while (workspace_for(n_tokens, n_heads, head_dim, max_seq, chunk) > (workspace ? workspace_bytes : 0)) chunk *= 2;
+  const int64_t n_chunks = (max_seq + chunk - 1) / chunk;
+  if (n_tokens * n_chunks > 0x7fffffffLL) return fail(KLLM_B200_ERR_SHAPE, "attention: too many tokens");
+
+  AttnArgs a = {};
+  a.q = static_cast<const __half*>(q);
+  a.k_cache = static_cast<const __half*>(k_cache);
+  a.v_cache = static_cast<const __half*>(v_cache);
+  a.out = static_cast<__half*>(out);
+  a.positions = positions;
+  a.slots = slots;
+  a.err_flags = err_flags;
+  a.n_tokens = n_tokens;
+  a.n_heads = static_cast<int>(n_heads);
+  a.n_kv_heads = static_cast<int>(n_kv_heads);
+  a.groups = static_cast<int>(n_heads / n_kv_heads);
+  a.max_seq = static_cast<int>(max_seq);
+  a.n_slots = static_cast<int>(n_slots > 0x7fffffffLL ? 0x7fffffffLL : n_slots);
+  a.chunk = static_cast<int>(chunk);
+  a.n_chunks = static_cast<int>(n_chunks);
+  a.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(head_dim));
+  if (n_chunks > 1) {
+    a.part_o = static_cast<float*>(workspace);
+    a.part_ml = a.part_o + n_tokens * n_heads * n_chunks * head_dim;
+  }
+  return head_dim == 64 ? launch_attention<64>(a, o) : launch_attention<128>(a, o);
+}
+
+}  // namespace kb
+
+extern "C" int kllm_b200_attention_workspace_bytes(int64_t n_tokens, int64_t n_heads, int64_t n_kv_heads,
+                                                   int64_t head_dim, int64_t max_seq, int64_t* bytes) {
+  return kb::attention_workspace_bytes(n_tokens, n_heads, n_kv_heads, head_dim, max_seq, bytes);
+}
+
+extern "C" int kllm_b200_attention_head_major(const void* q, const void* k_cache, const void* v_cache, void* out,
+                                              const int32_t* positions, const int32_t* slots, int64_t n_tokens,
+                                              int64_t seq_len, int64_t n_heads, int64_t n_kv_heads,
+                                              int64_t head_dim, int64_t n_slots, int64_t max_seq, int dtype,
+                                              void* workspace, int64_t workspace_bytes, int32_t* err_flags,
+                                              void* stream) {
+  kb::LaunchOpts o;
+  o.stream = static_cast<cudaStream_t>(stream);
+  return kb::attention_head_major(q, k_cache, v_cache, out, positions, slots, n_tokens, seq_len, n_heads,
+                                  n_kv_heads, head_dim, n_slots, max_seq, dtype, workspace, workspace_bytes,
+                                  err_flags, o);
+}

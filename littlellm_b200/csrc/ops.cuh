@@ -35,4 +35,13 @@ int dequantize_int8_value(const int8_t* data, float scale, void* out, int64_t n,
 int select_last_rows(const void* x, int64_t rows, int64_t cols, const int32_t* seq_ends, int64_t seq_len,
                      int64_t n_seqs, void* out, int dtype, int32_t* err_flags, const LaunchOpts& o);
 
+int attention_workspace_bytes(int64_t n_tokens, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim,
+                              int64_t max_seq, int64_t* bytes);
+
+int attention_head_major(const void* q, const void* k_cache, const void* v_cache, void* out,
+                         const int32_t* positions, const int32_t* slots, int64_t n_tokens, int64_t seq_len,
+                         int64_t n_heads, int64_t n_kv_heads, int64_t head_dim, int64_t n_slots, int64_t max_seq,
+                         int dtype, void* workspace, int64_t workspace_bytes, int32_t* err_flags,
+                         const LaunchOpts& o);
+
 }  // namespace kb

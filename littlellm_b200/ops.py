@@ -147,6 +147,41 @@ def select_last_rows(x: torch.Tensor, seq_len: int = 0, n_seqs: int | None = Non
     return out
 
 
+def attention_workspace_bytes(n_tokens: int, n_heads: int, n_kv_heads: int, head_dim: int,
+                              max_seq: int) -> int:
+    import ctypes
+    n = ctypes.c_int64(0)
+    check(lib.kllm_b200_attention_workspace_bytes(n_tokens, n_heads, n_kv_heads, head_dim, max_seq,
+                                                  ctypes.addressof(n)))
+    return n.value
+
+
+def attention_head_major(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                         positions: torch.Tensor, slots: torch.Tensor, seq_len: int = 1,
+                         out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+                         err_flags: torch.Tensor | None = None) -> torch.Tensor:
+    """Causal attention of q [T, Hq, D] over the head-major cache of one
+    layer [n_slots, Hkv, max_seq, D]: token t sees positions 0..positions[t]
+    of slot slots[t]. ``workspace=None`` allocates the preferred split
+    workspace here (the C entry point itself never allocates)."""
+    T, Hq, D = q.shape
+    n_slots, Hkv, max_seq, _ = k_cache.shape
+    if out is None:
+        out = torch.empty_like(q)
+    if workspace is None:
+        nbytes = attention_workspace_bytes(T, Hq, Hkv, D, max_seq)
+        workspace = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=q.device)
+    dev = _dev(q, k_cache, v_cache, positions, slots, out, workspace, err_flags)
+    if positions.dtype != torch.int32 or slots.dtype != torch.int32:
+        raise KllmError(_capi.ERR_DTYPE, "attention: positions and slots must be int32")
+    with torch.cuda.device(dev):
+        check(lib.kllm_b200_attention_head_major(
+            _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(out), _ptr(positions), _ptr(slots), T, seq_len, Hq,
+            Hkv, D, n_slots, max_seq, dtype_code(q), _ptr(workspace), workspace.numel(), _ptr(err_flags),
+            _stream(dev)))
+    return out
+
+
 def silu_mul(gate: torch.Tensor, up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     if out is None:
         out = torch.empty_like(gate)

@@ -18,6 +18,7 @@
 #include "kllm_oracle.h"
 
 #include <math.h>
+#include <stdlib.h>
 #include <string.h>
 
 /* ---------------------------------------------------------------------- */
@@ -272,4 +273,92 @@ int kllm_oracle_select_last_rows(const float* x, int64_t rows, int64_t cols,
     kllm_oracle_select_last_row(x, end, cols, out + b * cols);
   }
   return status;
+}
+
+/* ---------------------------------------------------------------------- */
+/* Attention (scope row f1)                                                */
+/* ---------------------------------------------------------------------- */
+
+/* One (token, head) of cpu_attention (src/op/cpu/attention.cpp:31-64):
+ * scores over keys 0..key_limit-1 scaled by 1/sqrt(head_dim), max, exp,
+ * the sum of exps, then out[d] = sum_pos (score[pos] / denom) * v[pos][d],
+ * every sum in key order. k_row(pos) = k + pos * pos_stride (same for v). */
+static void oracle_attend_row(const float* q_row, const float* k, const float* v,
+                              int64_t pos_stride, int64_t key_limit, int64_t head_dim,
+                              float* scores, float* out_row) {
+  const float scale = 1.0f / sqrtf((float)head_dim);
+  float max_score = -INFINITY;
+  for (int64_t pos = 0; pos < key_limit; ++pos) {
+    const float* k_row = k + pos * pos_stride;
+    float dot = 0.0f;
+    for (int64_t d = 0; d < head_dim; ++d) dot += q_row[d] * k_row[d];
+    scores[pos] = dot * scale;
+    if (scores[pos] > max_score) max_score = scores[pos];
+  }
+  float denom = 0.0f;
+  for (int64_t pos = 0; pos < key_limit; ++pos) {
+    scores[pos] = expf(scores[pos] - max_score);
+    denom += scores[pos];
+  }
+  for (int64_t d = 0; d < head_dim; ++d) {
+    float value = 0.0f;
+    for (int64_t pos = 0; pos < key_limit; ++pos) {
+      const float prob = scores[pos] / denom;
+      value += prob * v[pos * pos_stride + d];
+    }
+    out_row[d] = value;
+  }
+}
+
+/* cpu_attention (src/op/cpu/attention.cpp:12-67): q/out [seq, num_heads,
+ * head_dim], caches [max_seq, num_kv_heads, head_dim]; token t attends to
+ * keys 0..past_len+t, head h reads kv head h / (num_heads / num_kv_heads). */
+void kllm_oracle_attention(const float* q, const float* k_cache, const float* v_cache, float* out,
+                           int64_t seq, int32_t past_len, int64_t num_heads, int64_t num_kv_heads,
+                           int64_t head_dim) {
+  const int64_t groups = num_heads / num_kv_heads;
+  float* scores = (float*)malloc((size_t)(past_len + seq + 1) * sizeof(float));
+  if (!scores) return;
+  for (int64_t t = 0; t < seq; ++t) {
+    const int64_t key_limit = past_len + t + 1;
+    for (int64_t h = 0; h < num_heads; ++h) {
+      const int64_t kv_h = h / groups;
+      oracle_attend_row(q + (t * num_heads + h) * head_dim, k_cache + kv_h * head_dim,
+                        v_cache + kv_h * head_dim, num_kv_heads * head_dim, key_limit, head_dim,
+                        scores, out + (t * num_heads + h) * head_dim);
+    }
+  }
+  free(scores);
+}
+
+/* The same per-row computation over the head-major cache [n_slots,
+ * num_kv_heads, max_seq, head_dim] of one layer: token t attends to
+ * positions 0..positions[t] of sequence slot slots[t]. Rows of tokens with
+ * a position outside [0, max_seq) or a slot outside [0, n_slots) are zero.
+ * Returns the number of such tokens. */
+int64_t kllm_oracle_attention_head_major(const float* q, const float* k_cache, const float* v_cache,
+                                         float* out, const int32_t* positions, const int32_t* slots,
+                                         int64_t n_tokens, int64_t num_heads, int64_t num_kv_heads,
+                                         int64_t head_dim, int64_t n_slots, int64_t max_seq) {
+  const int64_t groups = num_heads / num_kv_heads;
+  int64_t bad = 0;
+  float* scores = (float*)malloc((size_t)(max_seq + 1) * sizeof(float));
+  if (!scores) return -1;
+  for (int64_t t = 0; t < n_tokens; ++t) {
+    const int64_t pos = positions[t], slot = slots[t];
+    float* out_t = out + t * num_heads * head_dim;
+    if (pos < 0 || pos >= max_seq || slot < 0 || slot >= n_slots) {
+      memset(out_t, 0, (size_t)(num_heads * head_dim) * sizeof(float));
+      ++bad;
+      continue;
+    }
+    for (int64_t h = 0; h < num_heads; ++h) {
+      const int64_t kv_h = h / groups;
+      const int64_t base = ((slot * num_kv_heads + kv_h) * max_seq) * head_dim;
+      oracle_attend_row(q + (t * num_heads + h) * head_dim, k_cache + base, v_cache + base, head_dim,
+                        pos + 1, head_dim, scores, out_t + h * head_dim);
+    }
+  }
+  free(scores);
+  return bad;
 }

@@ -58,6 +58,17 @@ int kllm_oracle_select_last_rows(const float* x, int64_t rows, int64_t cols,
                                  const int32_t* seq_ends, int64_t seq_len, int64_t n_seqs,
                                  float* out);
 
+/* Attention: the reference layout (caches [max_seq, kv_heads, head_dim]) and
+ * the head-major cache [n_slots, kv_heads, max_seq, head_dim] with per-token
+ * positions and slots (returns the number of tokens zeroed as invalid). */
+void kllm_oracle_attention(const float* q, const float* k_cache, const float* v_cache, float* out,
+                           int64_t seq, int32_t past_len, int64_t num_heads, int64_t num_kv_heads,
+                           int64_t head_dim);
+int64_t kllm_oracle_attention_head_major(const float* q, const float* k_cache, const float* v_cache,
+                                         float* out, const int32_t* positions, const int32_t* slots,
+                                         int64_t n_tokens, int64_t num_heads, int64_t num_kv_heads,
+                                         int64_t head_dim, int64_t n_slots, int64_t max_seq);
+
 #ifdef __cplusplus
 }
 #endif

@@ -93,6 +93,12 @@ class Oracle:
         lib.kllm_oracle_select_last_rows.restype = ctypes.c_int
         lib.kllm_oracle_select_last_rows.argtypes = [_c_f32p, _c_i64, _c_i64, _c_i32p, _c_i64,
                                                      _c_i64, _c_f32p]
+        lib.kllm_oracle_attention.argtypes = [_c_f32p, _c_f32p, _c_f32p, _c_f32p, _c_i64,
+                                              ctypes.c_int32, _c_i64, _c_i64, _c_i64]
+        lib.kllm_oracle_attention_head_major.restype = ctypes.c_int64
+        lib.kllm_oracle_attention_head_major.argtypes = [
+            _c_f32p, _c_f32p, _c_f32p, _c_f32p, _c_i32p, _c_i32p, _c_i64, _c_i64, _c_i64, _c_i64,
+            _c_i64, _c_i64]
 
     # -- fp16 conversion ----------------------------------------------------
     def float_to_half_bits(self, x) -> np.ndarray:
@@ -226,6 +232,29 @@ class Oracle:
                                                    _ptr(out, _c_f32p))
         return out, rc
 
+    def attention(self, q, k_cache, v_cache, past_len: int, n_kv_heads: int) -> np.ndarray:
+        """q [seq, Hq, D]; caches [max_seq, Hkv, D] (the reference layout)."""
+        q, kc, vc = _f32(q), _f32(k_cache), _f32(v_cache)
+        out = np.empty_like(q)
+        self.lib.kllm_oracle_attention(_ptr(q, _c_f32p), _ptr(kc, _c_f32p), _ptr(vc, _c_f32p),
+                                       _ptr(out, _c_f32p), q.shape[0], past_len, q.shape[1],
+                                       n_kv_heads, q.shape[2])
+        return out
+
+    def attention_head_major(self, q, k_cache, v_cache, positions, slots):
+        """q [T, Hq, D]; caches [n_slots, Hkv, max_seq, D]. Returns (out, n_invalid)."""
+        q, kc, vc = _f32(q), _f32(k_cache), _f32(v_cache)
+        pos = np.ascontiguousarray(positions, dtype=np.int32)
+        slo = np.ascontiguousarray(slots, dtype=np.int32)
+        out = np.empty_like(q)
+        bad = self.lib.kllm_oracle_attention_head_major(
+            _ptr(q, _c_f32p), _ptr(kc, _c_f32p), _ptr(vc, _c_f32p), _ptr(out, _c_f32p),
+            _ptr(pos, _c_i32p), _ptr(slo, _c_i32p), q.shape[0], q.shape[1], kc.shape[1], q.shape[2],
+            kc.shape[0], kc.shape[2])
+        if bad < 0:
+            raise MemoryError("oracle attention: allocation failed")
+        return out, int(bad)
+
 
 class Reference:
     """The reference's compiled CPU operators (``oracle/_ref/libkllm_ref.so``).
@@ -253,6 +282,7 @@ class Reference:
         lib.kref_silu_mul.argtypes = [vp, vp, vp, i64, i32]
         lib.kref_rope_inplace.argtypes = [vp, i64, i64, i64, i32, ctypes.c_float, i32]
         lib.kref_copy_kv_to_cache.argtypes = [vp, vp, i64, i64, i64, vp, vp, i64, i32, i32]
+        lib.kref_attention.argtypes = [vp, vp, vp, vp, i64, i64, i32, i32, i32, i32, i32]
         lib.kref_dequantize_int8.argtypes = [vp, i64, ctypes.c_float, vp]
         lib.kref_dequantize_int8_f16.argtypes = [vp, i64, ctypes.c_float, vp]
         lib.kref_table_create.restype = vp
@@ -346,6 +376,15 @@ class Reference:
             self._vp(k), self._vp(v), k.shape[0], k.shape[1], k.shape[2], self._vp(kc),
             self._vp(vc), kc.shape[0], past_len, dtype))
         return kc, vc
+
+    def attention(self, q, k_cache, v_cache, past_len: int, n_kv_heads: int, dtype: int = F32):
+        """kllm::op::attention: q [seq, Hq, D]; caches [max_seq, Hkv, D]."""
+        q, kc, vc = self._buf(q, dtype), self._buf(k_cache, dtype), self._buf(v_cache, dtype)
+        out = np.empty_like(q)
+        self._check(self.lib.kref_attention(self._vp(q), self._vp(kc), self._vp(vc), self._vp(out),
+                                            q.shape[0], kc.shape[0], past_len, q.shape[1], n_kv_heads,
+                                            q.shape[2], dtype))
+        return out
 
     def dequantize_int8_f32(self, q, scale: float):
         q = np.ascontiguousarray(q, dtype=np.int8)

@@ -190,6 +190,22 @@ int kref_copy_kv_to_cache(const void* k, const void* v, std::int64_t seq,
   });
 }
 
+// kllm::op::attention on CPU tensors: q/out [seq, heads, head_dim], caches
+// [max_seq, kv_heads, head_dim]; keys 0..past_len+t for token t.
+int kref_attention(const void* q, const void* k_cache, const void* v_cache, void* out,
+                   std::int64_t seq, std::int64_t max_seq, int past_len, int heads, int kv_heads,
+                   int head_dim, int dtype) {
+  return guarded([&] {
+    auto qt = make_tensor({seq, heads, head_dim}, dtype, q);
+    auto kc = make_tensor({max_seq, kv_heads, head_dim}, dtype, k_cache);
+    auto vc = make_tensor({max_seq, kv_heads, head_dim}, dtype, v_cache);
+    auto ot = make_tensor({seq, heads, head_dim}, dtype, nullptr);
+    kllm::op::attention(qt, kc, vc, ot, past_len, past_len + static_cast<int>(seq), heads, kv_heads,
+                        head_dim);
+    read_back(ot, out);
+  });
+}
+
 int kref_dequantize_int8(const std::int8_t* q, std::int64_t n, float scale, float* out) {
   return guarded([&] {
     auto qt = make_tensor({n}, 3, q);

@@ -1,0 +1,145 @@
+"""Attention over the head-major cache (scope row f1) against the oracle
+(cpu_attention restated, src/op/cpu/attention.cpp:12-67, pinned to the
+compiled reference in test_oracle_attention.py), run in fp32 on the same fp16
+inputs. Tolerance: |gpu - oracle| <= 1e-2 + 1e-2 * |oracle|."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import TOL, assert_tol, canary_intact, dev, f16r, host
+
+pytestmark = pytest.mark.gpu
+
+
+def _cache(rng, n_slots, hkv, max_seq, d):
+    k = f16r(rng.standard_normal((n_slots, hkv, max_seq, d)))
+    v = f16r(rng.standard_normal((n_slots, hkv, max_seq, d)))
+    return k, v
+
+
+def _run(ops, q, kc, vc, positions, slots, seq_len=1, workspace=None, err=None):
+    return ops.attention_head_major(dev(q), dev(kc), dev(vc), dev(positions, torch.int32), dev(slots, torch.int32),
+                                    seq_len=seq_len, workspace=workspace, err_flags=err)
+
+
+@pytest.mark.parametrize("hq,hkv,d,max_seq,n_tok", [
+    (14, 2, 64, 1000, 64),    # Qwen2.5-0.5B heads, ragged max_seq (not a multiple of 128)
+    (32, 32, 128, 700, 16),   # Llama-2-7B heads (one query head per kv head)
+    (16, 1, 64, 300, 9),      # 16 query heads per kv head (the largest group)
+    (8, 2, 128, 4096, 6),     # long cache, positions up to 4095 (several chunks)
+])
+def test_decode_matches_oracle(cuda, ops, oracle, hq, hkv, d, max_seq, n_tok):
+    rng = np.random.default_rng(hq * 1000 + max_seq)
+    n_slots = n_tok + 3
+    kc, vc = _cache(rng, n_slots, hkv, max_seq, d)
+    q = f16r(rng.standard_normal((n_tok, hq, d)))
+    positions = rng.integers(0, max_seq, n_tok).astype(np.int32)
+    positions[0], positions[-1] = 0, max_seq - 1  # one key; the whole cache
+    slots = rng.permutation(n_slots)[:n_tok].astype(np.int32)
+    want, bad = oracle.attention_head_major(q, kc, vc, positions, slots)
+    assert bad == 0
+    got = _run(ops, q, kc, vc, positions, slots)
+    torch.cuda.synchronize()
+    assert_tol(host(got), want, TOL, "attention decode")
+    # a single key: the output is that key's value row exactly
+    assert np.array_equal(host(got)[0], vc[slots[0], np.arange(hq) // (hq // hkv), 0])
+
+
+def test_workspace_size_does_not_change_results(cuda, ops, oracle):
+    """No workspace (one chunk per sequence), a small one (coarser split) and
+    the preferred one agree with the oracle."""
+    rng = np.random.default_rng(17)
+    hq, hkv, d, max_seq, n_tok = 14, 2, 64, 2048, 24
+    kc, vc = _cache(rng, n_tok, hkv, max_seq, d)
+    q = f16r(rng.standard_normal((n_tok, hq, d)))
+    positions = rng.integers(0, max_seq, n_tok).astype(np.int32)
+    slots = np.arange(n_tok, dtype=np.int32)
+    want, _ = oracle.attention_head_major(q, kc, vc, positions, slots)
+    full = ops.attention_workspace_bytes(n_tok, hq, hkv, d, max_seq)
+    assert full > 0
+    from littlellm_b200 import _capi
+    args = [dev(q), dev(kc), dev(vc), None, dev(positions, torch.int32), dev(slots, torch.int32)]
+    for nbytes in (0, full // 3, full):
+        ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=cuda)
+        args[3] = out = torch.empty(q.shape, dtype=torch.float16, device=cuda)
+        rc = _capi.lib.kllm_b200_attention_head_major(
+            *[a.data_ptr() for a in args], n_tok, 1, hq, hkv, d, n_tok, max_seq, _capi.F16,
+            ws.data_ptr() if nbytes else None, nbytes, None, torch.cuda.current_stream().cuda_stream)
+        assert rc == _capi.OK, _capi.last_error()
+        torch.cuda.synchronize()
+        assert_tol(host(out), want, TOL, f"workspace {nbytes}")
+
+
+def test_prefill_runs_match_oracle(cuda, ops, oracle):
+    """Three prefill sequences of 37 tokens (positions 0..36) in slots 4, 0,
+    2, plus a chunk continuing a sequence at positions 37..73."""
+    rng = np.random.default_rng(5)
+    hq, hkv, d, max_seq, n_slots, s = 14, 2, 64, 512, 5, 37
+    kc, vc = _cache(rng, n_slots, hkv, max_seq, d)
+    runs = [(4, 0), (0, 0), (2, 0), (4, s)]
+    positions = np.concatenate([np.arange(p, p + s) for _, p in runs]).astype(np.int32)
+    slots = np.concatenate([np.full(s, sl) for sl, _ in runs]).astype(np.int32)
+    q = f16r(rng.standard_normal((positions.size, hq, d)))
+    want, _ = oracle.attention_head_major(q, kc, vc, positions, slots)
+    got = _run(ops, q, kc, vc, positions, slots, seq_len=s)
+    torch.cuda.synchronize()
+    assert_tol(host(got), want, TOL, "attention prefill")
+
+
+def test_sharp_scores_are_stable(cuda, ops, oracle):
+    """Scores spread over +-200 (queries x 25): the running max keeps the
+    exponentials finite and the result matches."""
+    rng = np.random.default_rng(23)
+    hq, hkv, d, max_seq, n_tok = 4, 2, 64, 900, 8
+    kc, vc = _cache(rng, n_tok, hkv, max_seq, d)
+    q = f16r(25.0 * rng.standard_normal((n_tok, hq, d)))
+    positions = rng.integers(100, max_seq, n_tok).astype(np.int32)
+    slots = np.arange(n_tok, dtype=np.int32)
+    want, _ = oracle.attention_head_major(q, kc, vc, positions, slots)
+    got = _run(ops, q, kc, vc, positions, slots)
+    torch.cuda.synchronize()
+    out = host(got)
+    assert np.all(np.isfinite(out))
+    assert_tol(out, want, TOL, "sharp scores")
+
+
+def test_invalid_rows_zero_and_flag(cuda, ops, oracle):
+    rng = np.random.default_rng(2)
+    hq, hkv, d, max_seq = 4, 2, 64, 256
+    kc, vc = _cache(rng, 3, hkv, max_seq, d)
+    q = f16r(rng.standard_normal((5, hq, d)))
+    positions = np.array([3, max_seq, -1, 10, 200], np.int32)
+    slots = np.array([0, 1, 2, 3, -2], np.int32)
+    want, bad = oracle.attention_head_major(q, kc, vc, positions, slots)
+    assert bad == 4
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    whole = torch.full((5 * hq * d + 64,), -1234.0, dtype=torch.float16, device=cuda)
+    out = whole[:5 * hq * d].view(5, hq, d)
+    ops.attention_head_major(dev(q), dev(kc), dev(vc), dev(positions, torch.int32), dev(slots, torch.int32),
+                             out=out, err_flags=err)
+    torch.cuda.synchronize()
+    from littlellm_b200 import _capi
+    assert int(err.item()) == _capi.FLAG_BAD_POSITION | _capi.FLAG_BAD_SLOT
+    assert np.all(host(out)[1:] == 0)
+    assert_tol(host(out)[:1], want[:1], TOL, "valid row")
+    assert canary_intact(whole, 5 * hq * d)
+
+
+def test_argument_errors(cuda, ops):
+    from littlellm_b200 import _capi
+    lib = _capi.lib
+    x = torch.zeros(4096, dtype=torch.float16, device=cuda)
+    p = x.data_ptr()
+    # head_dim 96 is not supported; 3 query heads over 2 kv heads; dtype F32
+    assert lib.kllm_b200_attention_head_major(p, p, p, p, p, p, 1, 1, 2, 2, 96, 1, 8, _capi.F16, None, 0, None,
+                                              None) == _capi.ERR_SHAPE
+    assert lib.kllm_b200_attention_head_major(p, p, p, p, p, p, 1, 1, 3, 2, 64, 1, 8, _capi.F16, None, 0, None,
+                                              None) == _capi.ERR_SHAPE
+    assert lib.kllm_b200_attention_head_major(p, p, p, p, p, p, 1, 1, 2, 2, 64, 1, 8, _capi.F32, None, 0, None,
+                                              None) == _capi.ERR_DTYPE
+    assert lib.kllm_b200_attention_head_major(p + 2, p, p, p, p, p, 1, 1, 2, 2, 64, 1, 8, _capi.F16, None, 0,
+                                              None, None) == _capi.ERR_ALIGN
+    assert lib.kllm_b200_attention_head_major(None, None, None, None, None, None, 0, 1, 2, 2, 64, 1, 8, _capi.F16,
+                                              None, 0, None, None) == _capi.OK
