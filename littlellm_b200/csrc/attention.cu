@@ -19,6 +19,14 @@
 // chunks writes normalised partials (o, max, sum) to the caller's workspace
 // and a combine kernel merges them. The kernel is bound by HBM reads of
 // K and V: 2 * (positions[t] + 1) * head_dim * 2 bytes per (token, kv head).
+//
+// Prefill kernel (runs of seq_len >= 16 tokens of one sequence): a CTA takes
+// 64 consecutive tokens of a run and one query head; each warp owns 16 of
+// the tokens as mma rows. 64-position K/V tiles of the run's slot are
+// double-buffered in shared memory (cp.async, one barrier per tile) and
+// shared by the four warps; each row masks positions beyond its own. The
+// kernel is bound by the tensor pipe: 4 * head_dim FLOPs per (token, head,
+// attended position).
 #include <math.h>
 
 #include "ops.cuh"
@@ -50,6 +58,7 @@ struct AttnArgs {
   int chunk;              // positions per CTA, a multiple of kChunkUnit
   int n_chunks;           // ceil(max_seq / chunk)
   float scale_log2;       // log2(e) / sqrt(D)
+  int64_t seq_len;        // prefill: tokens per run of one sequence
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -347,6 +356,202 @@ __global__ void __launch_bounds__(kCombineWarps * 32) attn_combine_kernel(const 
   for (int k = 0; k < kPer; ++k) dst[k] = __float2half_rn(acc[k] * inv);
 }
 
+constexpr int kPfRows = kAttnWarps * 16;  // query tokens per prefill CTA
+constexpr int kPfKeys = 64;               // positions per prefill K/V tile
+
+template <int D>
+__global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(const AttnArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  constexpr int kRowChunks = D / 8;
+  constexpr int kTileBytes = kPfKeys * D * 2;
+  constexpr int kKS = D / 16;
+  constexpr int kND = D / 8;
+  __shared__ int s_max_pos;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gid = lane >> 2, tig = lane & 3;
+  const int h = blockIdx.y;
+  const int g = h / a.groups;
+  const int tiles_per_run = static_cast<int>((a.seq_len + kPfRows - 1) / kPfRows);
+  const int64_t run = blockIdx.x / tiles_per_run;
+  // the tiles late in a run attend to the most positions: schedule them first
+  const int qt = tiles_per_run - 1 - static_cast<int>(blockIdx.x - run * tiles_per_run);
+  const int64_t run_start = run * a.seq_len;
+  const int64_t run_end = min(run_start + a.seq_len, a.n_tokens);
+  const int64_t tok0 = run_start + static_cast<int64_t>(qt) * kPfRows;
+  if (tok0 >= run_end) return;  // the short last run has fewer tiles
+  const int rows = static_cast<int>(min(static_cast<int64_t>(kPfRows), run_end - tok0));
+
+  grid_dep_wait();
+  const int run_slot = a.slots[run_start];
+  const bool run_slot_ok = run_slot >= 0 && run_slot < a.n_slots;
+  if (threadIdx.x == 0) s_max_pos = -1;
+  __syncthreads();
+  if (threadIdx.x < rows) {
+    const int p = a.positions[tok0 + threadIdx.x];
+    const int sl = a.slots[tok0 + threadIdx.x];
+    const bool pos_ok = p >= 0 && p < a.max_seq;
+    const bool slot_ok = run_slot_ok && sl == run_slot;
+    if (pos_ok && slot_ok) atomicMax(&s_max_pos, p);
+    if (h == 0) {
+      if (!pos_ok) set_flag(a.err_flags, KLLM_B200_FLAG_BAD_POSITION);
+      if (!slot_ok) set_flag(a.err_flags, KLLM_B200_FLAG_BAD_SLOT);
+    }
+  }
+  __syncthreads();
+  const int max_pos = s_max_pos;
+
+  // this thread's two rows (r0, r0 + 8 of the warp's 16); -1 = not computed
+  const int r0 = warp * 16 + gid, r1 = r0 + 8;
+  auto row_pos = [&](int r) -> int {
+    if (r >= rows) return -1;
+    const int p = a.positions[tok0 + r];
+    const int sl = a.slots[tok0 + r];
+    return (p >= 0 && p < a.max_seq && run_slot_ok && sl == run_slot) ? p : -1;
+  };
+  const int p0 = row_pos(r0), p1 = row_pos(r1);
+  __half* out0 = a.out + ((tok0 + r0) * a.n_heads + h) * D;
+  __half* out1 = a.out + ((tok0 + r1) * a.n_heads + h) * D;
+  if (max_pos < 0) {  // no valid row in the tile: zero the rows that exist
+#pragma unroll
+    for (int nd = 0; nd < kND; ++nd) {
+      if (r0 < rows) *reinterpret_cast<uint32_t*>(out0 + nd * 8 + 2 * tig) = 0u;
+      if (r1 < rows) *reinterpret_cast<uint32_t*>(out1 + nd * 8 + 2 * tig) = 0u;
+    }
+    return;
+  }
+
+  const size_t head_off = (static_cast<size_t>(run_slot) * a.n_kv_heads + g) * static_cast<size_t>(a.max_seq) * D;
+  const __half* kbase = a.k_cache + head_off;
+  const __half* vbase = a.v_cache + head_off;
+  const int n_kt = max_pos / kPfKeys + 1;
+
+  auto issue = [&](int kt) {
+    unsigned char* sk = smem + (kt & 1) * 2 * kTileBytes;
+    unsigned char* sv = sk + kTileBytes;
+    const int j0 = kt * kPfKeys;
+#pragma unroll
+    for (int it = 0; it < kPfKeys * kRowChunks / kAttnThreads; ++it) {
+      const int idx = threadIdx.x + it * kAttnThreads;
+      const int r = idx / kRowChunks, ch = idx % kRowChunks;
+      const int j = j0 + r;
+      const bool ok = j <= max_pos;
+      const size_t off = static_cast<size_t>(ok ? j : 0) * D + ch * 8;
+      cp_async16(smem_u32(sk + swz<D>(r, ch)), kbase + off, ok ? 16 : 0);
+      cp_async16(smem_u32(sv + swz<D>(r, ch)), vbase + off, ok ? 16 : 0);
+    }
+    cp_async_commit();
+  };
+  issue(0);
+
+  uint32_t qa[kKS][4];
+  const __half* q0 = a.q + ((tok0 + r0) * a.n_heads + h) * D;
+  const __half* q1 = a.q + ((tok0 + r1) * a.n_heads + h) * D;
+#pragma unroll
+  for (int ks = 0; ks < kKS; ++ks) {
+    const int d0 = ks * 16 + 2 * tig;
+    qa[ks][0] = r0 < rows ? ld_u32(q0 + d0) : 0u;
+    qa[ks][1] = r1 < rows ? ld_u32(q1 + d0) : 0u;
+    qa[ks][2] = r0 < rows ? ld_u32(q0 + d0 + 8) : 0u;
+    qa[ks][3] = r1 < rows ? ld_u32(q1 + d0 + 8) : 0u;
+  }
+
+  float o[kND][4];
+#pragma unroll
+  for (int nd = 0; nd < kND; ++nd) o[nd][0] = o[nd][1] = o[nd][2] = o[nd][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  const float sl2 = a.scale_log2;
+
+  for (int kt = 0; kt < n_kt; ++kt) {
+    cp_async_wait<0>();
+    __syncthreads();  // tile kt landed; every warp is done with tile kt - 1
+    if (kt + 1 < n_kt) issue(kt + 1);  // into the buffer tile kt - 1 used
+    const unsigned char* sk = smem + (kt & 1) * 2 * kTileBytes;
+    const unsigned char* sv = sk + kTileBytes;
+    const int j0 = kt * kPfKeys;
+
+    float s[8][4];
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < D / 32; ++kk) {
+        uint32_t b[4];
+        ldsm_x4(b, smem_u32(sk + swz<D>(nt * 8 + (lane & 7), 4 * kk + (lane >> 3))));
+        mma16816(s[nt], qa[2 * kk], b[0], b[1]);
+        mma16816(s[nt], qa[2 * kk + 1], b[2], b[3]);
+      }
+    }
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int col = j0 + nt * 8 + 2 * tig + (e & 1);
+        const bool keep = col <= (e < 2 ? p0 : p1);
+        const float v = keep ? s[nt][e] * sl2 : -INFINITY;
+        s[nt][e] = v;
+        if (e < 2) mx0 = fmaxf(mx0, v); else mx1 = fmaxf(mx1, v);
+      }
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    // a row with nothing unmasked yet (a row not computed) keeps exponent base 0
+    const float b0 = mn0 == -INFINITY ? 0.f : mn0, b1 = mn1 == -INFINITY ? 0.f : mn1;
+    const float cr0 = exp2f(m0 - b0), cr1 = exp2f(m1 - b1);
+    m0 = mn0;
+    m1 = mn1;
+    float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      s[nt][0] = exp2f(s[nt][0] - b0);
+      s[nt][1] = exp2f(s[nt][1] - b0);
+      s[nt][2] = exp2f(s[nt][2] - b1);
+      s[nt][3] = exp2f(s[nt][3] - b1);
+      ps0 += s[nt][0] + s[nt][1];
+      ps1 += s[nt][2] + s[nt][3];
+    }
+    l0 = l0 * cr0 + ps0;
+    l1 = l1 * cr1 + ps1;
+#pragma unroll
+    for (int nd = 0; nd < kND; ++nd) {
+      o[nd][0] *= cr0;
+      o[nd][1] *= cr0;
+      o[nd][2] *= cr1;
+      o[nd][3] *= cr1;
+    }
+    const int mtx = lane >> 3;
+#pragma unroll
+    for (int kv = 0; kv < 4; ++kv) {
+      const uint32_t pa[4] = {pack_h2(s[2 * kv][0], s[2 * kv][1]), pack_h2(s[2 * kv][2], s[2 * kv][3]),
+                              pack_h2(s[2 * kv + 1][0], s[2 * kv + 1][1]),
+                              pack_h2(s[2 * kv + 1][2], s[2 * kv + 1][3])};
+#pragma unroll
+      for (int nd2 = 0; nd2 < D / 16; ++nd2) {
+        uint32_t b[4];
+        ldsm_x4_trans(b, smem_u32(sv + swz<D>(16 * kv + 8 * (mtx & 1) + (lane & 7), 2 * nd2 + (mtx >> 1))));
+        mma16816(o[2 * nd2], pa, b[0], b[1]);
+        mma16816(o[2 * nd2 + 1], pa, b[2], b[3]);
+      }
+    }
+  }
+
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  const float inv0 = p0 >= 0 ? 1.f / l0 : 0.f, inv1 = p1 >= 0 ? 1.f / l1 : 0.f;
+#pragma unroll
+  for (int nd = 0; nd < kND; ++nd) {
+    if (r0 < rows) *reinterpret_cast<uint32_t*>(out0 + nd * 8 + 2 * tig) = pack_h2(o[nd][0] * inv0, o[nd][1] * inv0);
+    if (r1 < rows) *reinterpret_cast<uint32_t*>(out1 + nd * 8 + 2 * tig) = pack_h2(o[nd][2] * inv1, o[nd][3] * inv1);
+  }
+}
+
+constexpr size_t prefill_smem(int head_dim) { return static_cast<size_t>(2) * 2 * kPfKeys * head_dim * 2; }
+
 constexpr size_t decode_smem(int head_dim) { return static_cast<size_t>(kAttnWarps) * kStages * 2 * kTile * head_dim * 2; }
 
 // Positions per decode CTA: 512, halved (down to 128) while the launch would
@@ -394,8 +599,25 @@ int check_attention_args(const void* q, const void* k_cache, const void* v_cache
   return KLLM_B200_OK;
 }
 
+constexpr int64_t kPrefillMinRun = 16;  // runs this long take the prefill kernel
+
+template <int D>
+int launch_prefill(AttnArgs& a, const LaunchOpts& o) {
+  const size_t smem = prefill_smem(D);
+  cudaError_t err = allow_smem(reinterpret_cast<const void*>(attn_prefill_kernel<D>), smem);
+  if (err != cudaSuccess) return launch_status(err, "attention: shared memory opt-in");
+  const int64_t tiles_per_run = (a.seq_len + kPfRows - 1) / kPfRows;
+  const int64_t runs = (a.n_tokens + a.seq_len - 1) / a.seq_len;
+  if (runs * tiles_per_run > 0x7fffffffLL) return fail(KLLM_B200_ERR_SHAPE, "attention: too many tokens");
+  const dim3 grid(static_cast<unsigned>(runs * tiles_per_run), static_cast<unsigned>(a.n_heads));
+  err = launch(attn_prefill_kernel<D>, grid, dim3(kAttnThreads), smem, o.stream, o.pdl, a);
+  if (err != cudaSuccess) return launch_status(err, "attention: prefill kernel");
+  return KLLM_B200_OK;
+}
+
 template <int D>
 int launch_attention(AttnArgs& a, const LaunchOpts& o) {
+  if (a.seq_len >= kPrefillMinRun) return launch_prefill<D>(a, o);
   const size_t smem = decode_smem(D);
   cudaError_t err = allow_smem(reinterpret_cast<const void*>(attn_decode_kernel<D>), smem);
   if (err != cudaSuccess) return launch_status(err, "attention: shared memory opt-in");
@@ -438,9 +660,10 @@ int attention_head_major(const void* q, const void* k_cache, const void* v_cache
   if (workspace_bytes > 0 && (!workspace || !aligned16(workspace))) {
     return fail(KLLM_B200_ERR_ALIGN, "attention: workspace must be non-null and 16-byte aligned");
   }
+  if (n_heads > 65535) return fail(KLLM_B200_ERR_SHAPE, "attention: too many heads");
   // the preferred chunk, doubled until its partials fit the workspace (one
-  // chunk per sequence needs none)
-  int64_t chunk = preferred_chunk(n_tokens, n_kv_heads, max_seq);
+  // chunk per sequence needs none); the prefill kernel does not split
+  int64_t chunk = seq_len >= kPrefillMinRun ? max_seq : preferred_chunk(n_tokens, n_kv_heads, max_seq);
   while (workspace_for(n_tokens, n_heads, head_dim, max_seq, chunk) > (workspace ? workspace_bytes : 0)) chunk *= 2;
   const int64_t n_chunks = (max_seq + chunk - 1) / chunk;
   if (n_tokens * n_chunks > 0x7fffffffLL) return fail(KLLM_B200_ERR_SHAPE, "attention: too many tokens");
@@ -462,6 +685,7 @@ int attention_head_major(const void* q, const void* k_cache, const void* v_cache
   a.chunk = static_cast<int>(chunk);
   a.n_chunks = static_cast<int>(n_chunks);
   a.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(head_dim));
+  a.seq_len = seq_len;
   if (n_chunks > 1) {
     a.part_o = static_cast<float*>(workspace);
     a.part_ml = a.part_o + n_tokens * n_heads * n_chunks * head_dim;

@@ -20,6 +20,7 @@ def _cache(rng, n_slots, hkv, max_seq, d):
 
 
 def _run(ops, q, kc, vc, positions, slots, seq_len=1, workspace=None, err=None):
+    # seq_len 1 takes the decode kernel; runs of 16 or more tokens the prefill kernel
     return ops.attention_head_major(dev(q), dev(kc), dev(vc), dev(positions, torch.int32), dev(slots, torch.int32),
                                     seq_len=seq_len, workspace=workspace, err_flags=err)
 
@@ -143,3 +144,49 @@ def test_argument_errors(cuda, ops):
                                               None, None) == _capi.ERR_ALIGN
     assert lib.kllm_b200_attention_head_major(None, None, None, None, None, None, 0, 1, 2, 2, 64, 1, 8, _capi.F16,
                                               None, 0, None, None) == _capi.OK
+
+
+@pytest.mark.parametrize("hq,hkv,d,max_seq,seq_len,n_runs,start", [
+    (14, 2, 64, 4096, 512, 2, 0),      # Qwen prefill shape
+    (32, 32, 128, 512, 200, 3, 0),     # Llama heads, runs not a multiple of 64 tokens
+    (8, 2, 128, 2048, 64, 2, 1000),    # a chunk continuing at position 1000
+    (4, 4, 64, 300, 16, 5, 7),         # the shortest run the prefill kernel takes
+])
+def test_prefill_kernel_matches_oracle(cuda, ops, oracle, hq, hkv, d, max_seq, seq_len, n_runs, start):
+    rng = np.random.default_rng(seq_len * 7 + hq)
+    n_slots = n_runs + 1
+    kc, vc = _cache(rng, n_slots, hkv, max_seq, d)
+    slot_of_run = rng.permutation(n_slots)[:n_runs]
+    positions = np.tile(np.arange(start, start + seq_len), n_runs).astype(np.int32)
+    slots = np.repeat(slot_of_run, seq_len).astype(np.int32)
+    q = f16r(rng.standard_normal((positions.size, hq, d)))
+    want, _ = oracle.attention_head_major(q, kc, vc, positions, slots)
+    got = _run(ops, q, kc, vc, positions, slots, seq_len=seq_len)
+    per_token = _run(ops, q, kc, vc, positions, slots, seq_len=1)  # the decode kernel on the same rows
+    torch.cuda.synchronize()
+    assert_tol(host(got), want, TOL, "prefill kernel")
+    assert_tol(host(got), host(per_token), TOL, "prefill vs decode kernel")
+
+
+def test_prefill_short_last_run_and_bad_rows(cuda, ops, oracle):
+    """100 tokens in runs of 40 (the last run has 20); in the second run one
+    row names another slot and one an out-of-range position: those rows are
+    zero and flagged, the others still match."""
+    rng = np.random.default_rng(41)
+    hq, hkv, d, max_seq, seq_len = 6, 2, 64, 256, 40
+    kc, vc = _cache(rng, 4, hkv, max_seq, d)
+    positions = np.concatenate([np.arange(40), np.arange(40), np.arange(50, 70)]).astype(np.int32)
+    slots = np.repeat([2, 0, 3], [40, 40, 20]).astype(np.int32)
+    slots[45] = 1
+    positions[47] = max_seq + 5
+    q = f16r(rng.standard_normal((positions.size, hq, d)))
+    want, bad = oracle.attention_head_major(q, kc, vc, positions, slots)
+    assert bad == 1  # the oracle attends row 45 to slot 1; the prefill kernel refuses it
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    got = host(_run(ops, q, kc, vc, positions, slots, seq_len=seq_len, err=err))
+    torch.cuda.synchronize()
+    from littlellm_b200 import _capi
+    assert int(err.item()) == _capi.FLAG_BAD_POSITION | _capi.FLAG_BAD_SLOT
+    assert np.all(got[[45, 47]] == 0)
+    keep = np.setdiff1d(np.arange(positions.size), [45, 47])
+    assert_tol(got[keep], want[keep], TOL, "prefill rows")
