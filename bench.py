@@ -22,6 +22,7 @@ CPU operators (compiled from its sources, oracle/_ref) on a bounded sample.
 from __future__ import annotations
 
 import argparse
+from dataclasses import replace
 import json
 import os
 import statistics
@@ -50,6 +51,8 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample length")
     ap.add_argument("--layers", type=int, default=None,
                     help="run only this many decoder layers (small profiling cases; not a bench line)")
+    ap.add_argument("--sequences", type=int, default=None,
+                    help="attention workloads: run this many sequences (small profiling cases; not a bench line)")
     ap.add_argument("--settle-seconds", type=float, default=1.5,
                     help="untimed graph replays before timing so clocks settle under load")
     return ap.parse_args()
@@ -780,6 +783,8 @@ def run_attention(args):
         kd.init("nccl", device, timeout_s=300)
 
     base = WORKLOADS[ATTENTION_WORKLOADS[args.workload]]
+    if args.sequences:
+        base = replace(base, n_seqs=args.sequences)
     weak = base.name == "qwen_prefill"
     w = base if weak else shard(base, rank, world)
     m = w.model
