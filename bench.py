@@ -861,7 +861,8 @@ def run_attention(args):
                     "timing": f"{L} layers per CUDA graph replay (decode + split combine per layer), CUDA events"}
     else:
         tc_peak = load_tc_peak()
-        roofline = {"bound": "tensor", "kernel": "attn_decode_kernel", "achieved": tflops, "peak": tc_peak["tflops"],
+        kernel = "attn_prefill_tc_kernel (tcgen05)" if m.head_dim == 128 else "attn_prefill_kernel (mma.sync)"
+        roofline = {"bound": "tensor", "kernel": kernel, "achieved": tflops, "peak": tc_peak["tflops"],
                     "unit": "TFLOP/s", "frac": tflops / tc_peak["tflops"], "traffic": None,
                     "peak_source": tc_peak["source"],
                     "timing": f"{L} layers per CUDA graph replay, CUDA events"}
@@ -927,7 +928,7 @@ def run_attention(args):
                        "kv_cache": [L, 2, B, m.n_kv_heads, S, m.head_dim],
                        "positions": "U[0, %d)" % (S - 1) if w.decode else "0..%d per sequence" % (w.seq_len - 1),
                        "parallelism": f"dp{world} (sequences split, no collective on the path)",
-                       "math": "fp16 operands, fp32 accumulate (mma.sync m16n8k16), fp32 online softmax",
+                       "math": "fp16 operands, fp32 accumulate, fp32 online softmax",
                        "l2": "no flush: each step reads %.2f GB of distinct per-layer K/V (>> 126 MB L2)"
                              % (work["bytes"] / 1e9) if w.decode else
                              "per-sequence K/V is L2-resident within a layer; layers use distinct caches",

@@ -60,7 +60,9 @@ enum {
   KLLM_B200_FLAG_BAD_TOKEN = 1,    /* embedding id outside [0, vocab) */
   KLLM_B200_FLAG_BAD_POSITION = 2, /* RoPE/KV position outside [0, max_seq) */
   KLLM_B200_FLAG_BAD_SLOT = 4,     /* KV cache slot outside [0, n_slots) */
-  KLLM_B200_FLAG_BAD_SEQ_END = 8   /* select_last_rows end index outside [1, rows] */
+  KLLM_B200_FLAG_BAD_SEQ_END = 8,  /* select_last_rows end index outside [1, rows] */
+  KLLM_B200_FLAG_TIMEOUT = 16      /* a kernel's bounded wait on its tensor-core work ran out;
+                                      that launch's outputs are incomplete */
 };
 
 /* Copies the calling thread's most recent error message into buf (always

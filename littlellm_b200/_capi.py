@@ -27,6 +27,7 @@ FLAG_BAD_TOKEN = 1
 FLAG_BAD_POSITION = 2
 FLAG_BAD_SLOT = 4
 FLAG_BAD_SEQ_END = 8
+FLAG_TIMEOUT = 16
 
 OP_EMBEDDING, OP_INPUT_NORM, OP_QKV_ROPE, OP_POST_NORM, OP_SWIGLU, OP_FINAL_NORM, OP_SELECT = (
     1, 2, 4, 8, 16, 32, 64)

@@ -20,13 +20,14 @@
 // and a combine kernel merges them. The kernel is bound by HBM reads of
 // K and V: 2 * (positions[t] + 1) * head_dim * 2 bytes per (token, kv head).
 //
-// Prefill kernel (runs of seq_len >= 16 tokens of one sequence): a CTA takes
-// 64 consecutive tokens of a run and one query head; each warp owns 16 of
-// the tokens as mma rows. 64-position K/V tiles of the run's slot are
-// double-buffered in shared memory (cp.async, one barrier per tile) and
-// shared by the four warps; each row masks positions beyond its own. The
-// kernel is bound by the tensor pipe: 4 * head_dim FLOPs per (token, head,
-// attended position).
+// Prefill kernels (runs of seq_len >= 16 tokens of one sequence), bound by
+// the tensor pipe: 4 * head_dim FLOPs per (token, head, attended position).
+// head_dim 128 runs on tcgen05 (attn_prefill_tc_kernel, below). head_dim 64
+// runs on mma.sync (attn_prefill_kernel): a CTA takes 64 consecutive tokens
+// of a run and one query head; each warp owns 16 of the tokens as mma rows.
+// 64-position K/V tiles of the run's slot are double-buffered in shared
+// memory (cp.async, one barrier per tile) and shared by the four warps; each
+// row masks positions beyond its own.
 #include <math.h>
 
 #include "ops.cuh"
@@ -550,6 +551,503 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(const AttnAr
   }
 }
 
+// ---------------------------------------------------------------------------
+// Prefill on tcgen05: q.k and p.v are single-thread-issued UMMAs (M = 128 query
+// rows) whose fp32 accumulators live in tensor memory; one thread per row
+// reads its scores back (tcgen05.ld), runs the online softmax and writes its
+// row of P to shared memory for the p.v product.
+//
+// Shared-memory operands use the 128-byte-swizzle canonical layouts: a tile
+// is stored as 64-element (128-byte) wide panels, row r of a panel at r * 128
+// bytes with 16-byte chunk c at ((c ^ (r % 8)) * 16), panels and 8-row atoms
+// 1024-byte aligned. Q, K and P are K-major operands (rows = M or N, the
+// reduction dimension contiguous); V is the N-major B operand of p.v (rows =
+// positions = the reduction dimension, head_dim contiguous).
+// ---------------------------------------------------------------------------
+
+constexpr int kTcKeys = 128;                      // positions per K/V tile: the UMMA N of q.k
+constexpr long long kWaitCycles = 4000000000LL;   // bound on one mbarrier wait (about 2 s)
+
+// Shared-memory matrix descriptor: start address, leading / stride byte
+// offsets (16-byte units), descriptor version 1, 128-byte swizzle.
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(2) << 61;
+  return d;
+}
+
+// Instruction descriptor of kind::f16: fp16 A and B, fp32 accumulator, A
+// K-major, B K-major or N-major, shape M x N.
+__host__ __device__ constexpr uint32_t umma_idesc(int m, int n, bool b_n_major) {
+  return (1u << 4) | (b_n_major ? (1u << 16) : 0u) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  const uint32_t z = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z));
+}
+
+// Arrive once on `bar` when every tcgen05.mma this thread issued has completed.
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// 32 consecutive fp32 columns of this thread's tensor-memory lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 2^x with the hardware approximation (ex2.approx, flush to zero); used for
+// softmax probabilities that are rounded to fp16 right after.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Wait for phase `parity` of an mbarrier, giving up after kWaitCycles.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  const long long t0 = clock64();
+  while (true) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if (clock64() - t0 > kWaitCycles) return false;
+  }
+}
+
+// Byte offset of 16-byte chunk c (of D / 8) of row r in a 128-byte-swizzled
+// tile of `rows` rows stored as 64-element panels.
+__device__ __forceinline__ uint32_t sw128(int rows, int r, int c) {
+  return static_cast<uint32_t>((c >> 3) * rows * 128 + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+}
+
+// 32 consecutive fp32 columns written to this thread's tensor-memory lane.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+// Arrive on `bar` once this thread's cp.async copies issued so far have landed.
+__device__ __forceinline__ void cp_async_mbar_arrive(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// p.v with A = P from tensor memory (16-bit pairs packed per 32-bit column).
+__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  const uint32_t z = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z));
+}
+
+// 16 consecutive 32-bit columns written to this thread's tensor-memory lane.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+
+// Warp roles of the tcgen05 prefill CTA: two softmax warpgroups (one per
+// 128-row query tile; thread t of a warpgroup owns row t and tensor-memory
+// lane t), one warp whose lane 0 issues every tcgen05.mma, one load warp.
+constexpr int kTcQTiles = 2;
+constexpr int kMmaWarp = 4 * kTcQTiles;
+constexpr int kLoadWarp = kMmaWarp + 1;
+constexpr int kTcThreads = (kLoadWarp + 1) * 32;
+constexpr float kRescaleLog2 = 8.f;  // rescale O only when a row max grows by more than 2^8
+constexpr int kTcMaxStages = 4;
+__host__ __device__ constexpr int tc_stages(int head_dim) { return head_dim > 64 ? 2 : 4; }  // K/V tiles in flight
+
+// mbarriers: Q loaded; K/V stage full / empty; S_i complete; P_i written; p.v of tile i complete
+enum TcBar {
+  kQFull = 0,
+  kKvFull = 1,
+  kKvEmpty = kKvFull + kTcMaxStages,
+  kSFull = kKvEmpty + kTcMaxStages,
+  kPFull = kSFull + kTcQTiles,
+  kODone = kPFull + kTcQTiles,
+  kNumTcBars = kODone + kTcQTiles
+};
+
+// Tensor memory (512 columns): S_i (fp32, 128 columns) at i * 128, with P_i
+// (fp16 pairs, 64 columns) written over its first half; O_i (fp32, D
+// columns) at 256 + i * D.
+template <int D>
+__global__ void __launch_bounds__(kTcThreads, 1) attn_prefill_tc_kernel(const AttnArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  constexpr int kStages = tc_stages(D);
+  constexpr int kChunks = D / 8;
+  constexpr int kRowsCta = 128 * kTcQTiles;
+  constexpr int kQBytes = 128 * D * 2;        // one query tile
+  constexpr int kKVBytes = kTcKeys * D * 2;   // one K or V tile
+  constexpr uint32_t kOCol = kTcQTiles * kTcKeys;
+  constexpr uint32_t kCols = 512;
+  constexpr uint32_t kIdescS = umma_idesc(128, kTcKeys, false);
+  constexpr uint32_t kIdescO = umma_idesc(128, D, true);
+  static_assert(kOCol + kTcQTiles * D <= kCols, "tensor memory overflow");
+  __shared__ __align__(8) uint64_t s_bar[kNumTcBars];
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_max_pos[kTcQTiles];
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int h = blockIdx.y;
+  const int g = h / a.groups;
+  const int tiles_per_run = static_cast<int>((a.seq_len + kRowsCta - 1) / kRowsCta);
+  const int64_t run = blockIdx.x / tiles_per_run;
+  const int qt = tiles_per_run - 1 - static_cast<int>(blockIdx.x - run * tiles_per_run);
+  const int64_t run_start = run * a.seq_len;
+  const int64_t run_end = min(run_start + a.seq_len, a.n_tokens);
+  const int64_t tok0 = run_start + static_cast<int64_t>(qt) * kRowsCta;
+  if (tok0 >= run_end) return;
+  const int rows = static_cast<int>(min(static_cast<int64_t>(kRowsCta), run_end - tok0));
+
+  grid_dep_wait();
+  const int run_slot = a.slots[run_start];
+  const bool run_slot_ok = run_slot >= 0 && run_slot < a.n_slots;
+  if (tid < kTcQTiles) s_max_pos[tid] = -1;
+  __syncthreads();
+  int my_pos = -1;  // softmax threads: row tid of the CTA's 256
+  if (tid < rows) {
+    const int p = a.positions[tok0 + tid];
+    const int sl = a.slots[tok0 + tid];
+    const bool pos_ok = p >= 0 && p < a.max_seq;
+    const bool slot_ok = run_slot_ok && sl == run_slot;
+    if (pos_ok && slot_ok) {
+      my_pos = p;
+      atomicMax(&s_max_pos[tid >> 7], p);
+    }
+    if (h == 0) {
+      if (!pos_ok) set_flag(a.err_flags, KLLM_B200_FLAG_BAD_POSITION);
+      if (!slot_ok) set_flag(a.err_flags, KLLM_B200_FLAG_BAD_SLOT);
+    }
+  }
+  __syncthreads();
+  // K/V tiles each query tile needs (0: no valid row), and the CTA's maximum
+  int n_kt_q[kTcQTiles];
+  int max_pos = -1;
+#pragma unroll
+  for (int i = 0; i < kTcQTiles; ++i) {
+    n_kt_q[i] = s_max_pos[i] < 0 ? 0 : s_max_pos[i] / kTcKeys + 1;
+    max_pos = max(max_pos, s_max_pos[i]);
+  }
+  __half* out_row = a.out + ((tok0 + tid) * a.n_heads + h) * D;
+  if (max_pos < 0) {
+    if (tid < rows) {
+#pragma unroll
+      for (int c = 0; c < kChunks; ++c) reinterpret_cast<uint4*>(out_row)[c] = make_uint4(0u, 0u, 0u, 0u);
+    }
+    return;
+  }
+  const int n_kt = max_pos / kTcKeys + 1;
+
+  // 1024-byte aligned carve-out: Q_0 Q_1 | (K V) x stages
+  const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  const uint32_t q_s = base;
+  const uint32_t kv_s = q_s + kTcQTiles * kQBytes;
+  auto bar = [&](int i) { return smem_u32(&s_bar[i]); };
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                 "r"(kCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (tid == 0) {
+    mbar_init(bar(kQFull), 32);
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(bar(kKvFull + i), 32);
+      mbar_init(bar(kKvEmpty + i), 1);
+    }
+    for (int i = 0; i < kTcQTiles; ++i) {
+      mbar_init(bar(kSFull + i), 1);
+      mbar_init(bar(kPFull + i), 128);
+      mbar_init(bar(kODone + i), 1);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+  bool ok = true;
+
+  if (warp < kMmaWarp) {
+    // ---------------- softmax warpgroup i: row tid of the CTA ----------------
+    const int wg = warp >> 2;
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t t_s = tmem + lane_base + wg * kTcKeys;  // S_i, then P_i over its first 64 columns
+    const uint32_t t_o = tmem + lane_base + kOCol + wg * D;
+    float m_used = -INFINITY, l = 0.f;
+    const float sl2 = a.scale_log2;
+    const int my_n_kt = n_kt_q[wg];
+    for (int kt = 0; kt < my_n_kt && ok; ++kt) {
+      // waits and tensor-memory accesses stay warp-uniform (tcgen05.ld/st are .sync.aligned)
+      ok = __all_sync(0xffffffffu, mbar_wait(bar(kSFull + wg), kt & 1));
+      if (!ok) break;
+      tc_fence_after();
+      // pass 1 over the row's 128 scores in tensor memory: the max of the raw
+      // scores (the scale is positive, so it is applied to the max alone);
+      // masks only where the tile crosses a row's position
+      const int j0 = kt * kTcKeys;
+      const bool warp_full = __all_sync(0xffffffffu, j0 + kTcKeys - 1 <= my_pos);
+      float mxp[8];  // eight independent chains instead of one 128-long one
+#pragma unroll
+      for (int q = 0; q < 8; ++q) mxp[q] = -INFINITY;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        float t[2][32];
+        tmem_ld32(t_s + hh * 64, t[0]);
+        tmem_ld32(t_s + hh * 64 + 32, t[1]);
+        tc_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          const float v = (warp_full || j0 + hh * 64 + i <= my_pos) ? t[i >> 5][i & 31] : -INFINITY;
+          mxp[i & 7] = fmaxf(mxp[i & 7], v);
+        }
+      }
+      const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                             fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7]))) * sl2;
+      if (kt > 0) {  // p.v of the previous tile done: P_i is read and O_i stable
+        ok = __all_sync(0xffffffffu, mbar_wait(bar(kODone + wg), (kt - 1) & 1));
+        if (!ok) break;
+        tc_fence_after();
+      }
+      // lazy rescale: the exponent base m_used moves only when the row max
+      // grows by more than 2^8, so P stays <= 256 and O is rarely rewritten
+      const bool grow = mx > m_used + kRescaleLog2;
+      const float f = !grow ? 1.f : (m_used == -INFINITY ? 0.f : exp2f(m_used - mx));
+      if (kt > 0 && __any_sync(0xffffffffu, f != 1.f)) {
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          float t[32];
+          tmem_ld32(t_o + c * 32, t);
+          tc_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) t[i] *= f;
+          tmem_st32(t_o + c * 32, t);
+        }
+        tc_wait_st();
+      }
+      l *= f;
+      if (grow) m_used = mx;
+      // pass 2: p = 2^(s * scale - base), one FMA and one ex2 per score,
+      // written back as P (fp16 pairs) over score columns already read
+      const float nb = m_used == -INFINITY ? 0.f : -m_used;
+      float psp[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) psp[q] = 0.f;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        float t[2][32];
+        tmem_ld32(t_s + hh * 64, t[0]);
+        tmem_ld32(t_s + hh * 64 + 32, t[1]);
+        tc_wait_ld();
+#pragma unroll
+        for (int c2 = 0; c2 < 2; ++c2) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int j = j0 + hh * 64 + c2 * 32 + 2 * i;
+            float e0 = ex2_approx(__fmaf_rn(t[c2][2 * i], sl2, nb));
+            float e1 = ex2_approx(__fmaf_rn(t[c2][2 * i + 1], sl2, nb));
+            if (!warp_full) {
+              e0 = j <= my_pos ? e0 : 0.f;
+              e1 = j + 1 <= my_pos ? e1 : 0.f;
+            }
+            psp[(2 * i) & 7] += e0;
+            psp[(2 * i + 1) & 7] += e1;
+            pk[i] = pack_h2(e0, e1);
+          }
+          tmem_st16(t_s + hh * 32 + c2 * 16, pk);  // P columns for positions 64 hh + 32 c2 ...
+        }
+      }
+      l += ((psp[0] + psp[1]) + (psp[2] + psp[3])) + ((psp[4] + psp[5]) + (psp[6] + psp[7]));
+      tc_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar(kPFull + wg));
+    }
+    if (ok && my_n_kt > 0) ok = __all_sync(0xffffffffu, mbar_wait(bar(kODone + wg), (my_n_kt - 1) & 1));
+    if (ok && my_n_kt == 0) {  // no valid row in this query tile
+      if (tid < rows) {
+#pragma unroll
+        for (int c = 0; c < kChunks; ++c) reinterpret_cast<uint4*>(out_row)[c] = make_uint4(0u, 0u, 0u, 0u);
+      }
+    } else if (ok) {
+      tc_fence_after();
+      const float inv = my_pos >= 0 ? 1.f / l : 0.f;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        float t[32];
+        tmem_ld32(t_o + c * 32, t);
+        tc_wait_ld();
+        if (tid < rows) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 w;
+            w.x = pack_h2(t[q * 8 + 0] * inv, t[q * 8 + 1] * inv);
+            w.y = pack_h2(t[q * 8 + 2] * inv, t[q * 8 + 3] * inv);
+            w.z = pack_h2(t[q * 8 + 4] * inv, t[q * 8 + 5] * inv);
+            w.w = pack_h2(t[q * 8 + 6] * inv, t[q * 8 + 7] * inv);
+            reinterpret_cast<uint4*>(out_row)[c * 4 + q] = w;
+          }
+        }
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ---------------- MMA issue: lane 0 ----------------
+    if (lane == 0) {
+      // descriptors of stage 0 / query tile 0; other stages and tiles add a
+      // byte offset / 16 to the start-address field
+      const uint64_t q_desc = umma_desc(q_s, 16, 1024);
+      const uint64_t k_desc = umma_desc(kv_s, 16, 1024);
+      const uint64_t v_desc = umma_desc(kv_s + kKVBytes, kTcKeys * 128, 1024);
+      auto issue_s = [&](int i, int kt) {
+        const uint64_t qd = q_desc + static_cast<uint64_t>((i * kQBytes) >> 4);
+        const uint64_t kd = k_desc + static_cast<uint64_t>(((kt % kStages) * 2 * kKVBytes) >> 4);
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const uint32_t qo = ((k >> 2) * (128 * 128) + (k & 3) * 32) >> 4;
+          const uint32_t ko = ((k >> 2) * (kTcKeys * 128) + (k & 3) * 32) >> 4;
+          umma_f16(tmem + i * kTcKeys, qd + qo, kd + ko, kIdescS, k > 0 ? 1u : 0u);
+        }
+        umma_commit(bar(kSFull + i));
+      };
+      auto issue_pv = [&](int i, int kt) {
+        const uint64_t vd = v_desc + static_cast<uint64_t>(((kt % kStages) * 2 * kKVBytes) >> 4);
+#pragma unroll
+        for (int k = 0; k < kTcKeys / 16; ++k) {
+          umma_f16_ts(tmem + kOCol + i * D, tmem + i * kTcKeys + k * 8, vd + static_cast<uint64_t>((k * 2048) >> 4),
+                      kIdescO, (kt > 0 || k > 0) ? 1u : 0u);
+        }
+        umma_commit(bar(kODone + i));
+      };
+      // step kt: p.v of tile kt - 1 and q.k of tile kt for each query tile that
+      // reaches them, then release the stage of tile kt - 1
+      ok = mbar_wait(bar(kQFull), 0);
+      for (int kt = 0; kt <= n_kt && ok; ++kt) {
+        bool kv_ready = false;
+        for (int i = 0; i < kTcQTiles && ok; ++i) {
+          if (kt > 0 && kt - 1 < n_kt_q[i]) {  // softmax i wrote P_i of tile kt - 1
+            ok = mbar_wait(bar(kPFull + i), (kt - 1) & 1);
+            if (!ok) break;
+            tc_fence_after();
+            issue_pv(i, kt - 1);
+          }
+          if (kt < n_kt_q[i]) {  // S_i is free: p.v above was issued before it
+            if (!kv_ready) {
+              ok = mbar_wait(bar(kKvFull + kt % kStages), (kt / kStages) & 1);
+              if (!ok) break;
+              fence_async_smem();
+              tc_fence_after();
+              kv_ready = true;
+            }
+            issue_s(i, kt);
+          }
+        }
+        if (ok && kt > 0) umma_commit(bar(kKvEmpty + (kt - 1) % kStages));
+      }
+    }
+  } else {
+    // ---------------- loads: the load warp, cp.async with zero fill ----------------
+    const __half* qrow0 = a.q + (tok0 * a.n_heads + h) * D;
+    const int64_t q_stride = static_cast<int64_t>(a.n_heads) * D;
+    for (int idx = lane; idx < kRowsCta * kChunks; idx += 32) {
+      const int r = idx / kChunks, c = idx % kChunks;
+      const bool in = r < rows;
+      cp_async16(q_s + (r >> 7) * kQBytes + sw128(128, r & 127, c), qrow0 + (in ? r : 0) * q_stride + c * 8,
+                 in ? 16 : 0);
+    }
+    cp_async_mbar_arrive(bar(kQFull));
+    const size_t head_off =
+        (static_cast<size_t>(run_slot) * a.n_kv_heads + g) * static_cast<size_t>(a.max_seq) * D;
+    const __half* kbase = a.k_cache + head_off;
+    const __half* vbase = a.v_cache + head_off;
+    for (int kt = 0; kt < n_kt; ++kt) {
+      if (kt >= kStages) {  // the stage's previous tile (kt - stages) has been consumed
+        ok = __all_sync(0xffffffffu, mbar_wait(bar(kKvEmpty + kt % kStages), ((kt / kStages) - 1) & 1));
+        if (!ok) break;
+      }
+      const uint32_t ks = kv_s + (kt % kStages) * 2 * kKVBytes, vs = ks + kKVBytes;
+      for (int idx = lane; idx < kTcKeys * kChunks; idx += 32) {
+        const int r = idx / kChunks, c = idx % kChunks;
+        const int j = kt * kTcKeys + r;
+        const bool in = j <= max_pos;
+        const size_t off = static_cast<size_t>(in ? j : 0) * D + c * 8;
+        cp_async16(ks + sw128(kTcKeys, r, c), kbase + off, in ? 16 : 0);
+        cp_async16(vs + sw128(kTcKeys, r, c), vbase + off, in ? 16 : 0);
+      }
+      cp_async_mbar_arrive(bar(kKvFull + kt % kStages));
+    }
+    cp_async_wait<0>();
+  }
+
+  if (!ok) set_flag(a.err_flags, KLLM_B200_FLAG_TIMEOUT);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols));
+  }
+}
+
+constexpr size_t prefill_tc_smem(int head_dim) {
+  return static_cast<size_t>(kTcQTiles) * 128 * head_dim * 2 +
+         2 * static_cast<size_t>(tc_stages(head_dim)) * kTcKeys * head_dim * 2 + 1024;
+}
+
 constexpr size_t prefill_smem(int head_dim) { return static_cast<size_t>(2) * 2 * kPfKeys * head_dim * 2; }
 
 constexpr size_t decode_smem(int head_dim) { return static_cast<size_t>(kAttnWarps) * kStages * 2 * kTile * head_dim * 2; }
@@ -602,6 +1100,20 @@ int check_attention_args(const void* q, const void* k_cache, const void* v_cache
 constexpr int64_t kPrefillMinRun = 16;  // runs this long take the prefill kernel
 
 template <int D>
+int launch_prefill_tc(AttnArgs& a, const LaunchOpts& o) {
+  const size_t smem = prefill_tc_smem(D);
+  cudaError_t err = allow_smem(reinterpret_cast<const void*>(attn_prefill_tc_kernel<D>), smem);
+  if (err != cudaSuccess) return launch_status(err, "attention: shared memory opt-in");
+  const int64_t tiles_per_run = (a.seq_len + 128 * kTcQTiles - 1) / (128 * kTcQTiles);
+  const int64_t runs = (a.n_tokens + a.seq_len - 1) / a.seq_len;
+  if (runs * tiles_per_run > 0x7fffffffLL) return fail(KLLM_B200_ERR_SHAPE, "attention: too many tokens");
+  const dim3 grid(static_cast<unsigned>(runs * tiles_per_run), static_cast<unsigned>(a.n_heads));
+  err = launch(attn_prefill_tc_kernel<D>, grid, dim3(kTcThreads), smem, o.stream, o.pdl, a);
+  if (err != cudaSuccess) return launch_status(err, "attention: prefill kernel");
+  return KLLM_B200_OK;
+}
+
+template <int D>
 int launch_prefill(AttnArgs& a, const LaunchOpts& o) {
   const size_t smem = prefill_smem(D);
   cudaError_t err = allow_smem(reinterpret_cast<const void*>(attn_prefill_kernel<D>), smem);
@@ -617,7 +1129,15 @@ int launch_prefill(AttnArgs& a, const LaunchOpts& o) {
 
 template <int D>
 int launch_attention(AttnArgs& a, const LaunchOpts& o) {
-  if (a.seq_len >= kPrefillMinRun) return launch_prefill<D>(a, o);
+  // prefill: tcgen05 at head_dim 128; at head_dim 64 the mma.sync kernel is
+  // faster (half the tensor work per score, and 64-row tiles give 4x the CTAs)
+  if (a.seq_len >= kPrefillMinRun) {
+    if constexpr (D == 128) {
+      return launch_prefill_tc<D>(a, o);
+    } else {
+      return launch_prefill<D>(a, o);
+    }
+  }
   const size_t smem = decode_smem(D);
   cudaError_t err = allow_smem(reinterpret_cast<const void*>(attn_decode_kernel<D>), smem);
   if (err != cudaSuccess) return launch_status(err, "attention: shared memory opt-in");
