@@ -803,7 +803,7 @@ def run_attention(args):
         t = torch.arange(T, device=device, dtype=torch.int32)
         positions, slots = t % w.seq_len, t // w.seq_len
     ws_bytes = ops.attention_workspace_bytes(T, m.n_heads, m.n_kv_heads, m.head_dim, S)
-    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=device)
+    ws = torch.zeros(max(ws_bytes, 16), dtype=torch.uint8, device=device)
     err = torch.zeros(1, dtype=torch.int32, device=device)
     work = attention_work(w, positions.cpu().numpy(), L)
     log(f"attention: {args.workload}, {L} layers, cache {cache.numel() * 2 / 1e9:.1f} GB, "
@@ -814,7 +814,7 @@ def run_attention(args):
             ops.attention_head_major(q[layer], cache[layer, 0], cache[layer, 1], positions, slots,
                                      seq_len=w.seq_len, out=out[layer], workspace=ws, err_flags=err)
 
-    launches = L * (2 if ws_bytes > 0 else 1)
+    launches = L * (2 if ws_bytes > 0 else 1)  # decode + split combine per layer
     stream = torch.cuda.Stream(device)
     torch.cuda.synchronize(device)
     with torch.cuda.stream(stream):

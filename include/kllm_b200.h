@@ -220,7 +220,8 @@ int kllm_b200_select_last_rows(const void* x, int64_t rows, int64_t cols,
  * / _BAD_SLOT. workspace (device, 16-byte aligned) holds split-sequence
  * partials; kllm_b200_attention_workspace_bytes gives the size for the best
  * split, and a smaller (or NULL) workspace gives coarser splits with the
- * same results. Nothing is allocated; the workspace needs no clearing. */
+ * same results. Nothing is allocated; the workspace needs no clearing, and
+ * calls sharing one workspace must not overlap on the GPU. */
 int kllm_b200_attention_workspace_bytes(int64_t n_tokens, int64_t n_heads, int64_t n_kv_heads,
                                         int64_t head_dim, int64_t max_seq, int64_t* bytes);
 int kllm_b200_attention_head_major(const void* q, const void* k_cache, const void* v_cache,

@@ -279,12 +279,14 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
   l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
   __syncthreads();  // all rings idle: reuse them for the merge
-  float* red_o = reinterpret_cast<float*>(smem);       // [warps][16][D]
-  float* red_ml = red_o + kAttnWarps * 16 * D;         // [warps][16][2]
+  constexpr int kRedRow = D + 8;  // padded rows: the float2 stores of 8 rows spread over the banks
+  float* red_o = reinterpret_cast<float*>(smem);       // [warps][16][kRedRow]
+  float* red_ml = red_o + kAttnWarps * 16 * kRedRow;   // [warps][16][2]
 #pragma unroll
   for (int nd = 0; nd < kND; ++nd) {
-    *reinterpret_cast<float2*>(red_o + (warp * 16 + gid) * D + nd * 8 + 2 * tig) = make_float2(o[nd][0], o[nd][1]);
-    *reinterpret_cast<float2*>(red_o + (warp * 16 + gid + 8) * D + nd * 8 + 2 * tig) =
+    *reinterpret_cast<float2*>(red_o + (warp * 16 + gid) * kRedRow + nd * 8 + 2 * tig) =
+        make_float2(o[nd][0], o[nd][1]);
+    *reinterpret_cast<float2*>(red_o + (warp * 16 + gid + 8) * kRedRow + nd * 8 + 2 * tig) =
         make_float2(o[nd][2], o[nd][3]);
   }
   if (tig == 0) {
@@ -305,7 +307,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
     for (int w = 0; w < kAttnWarps; ++w) {
       const float f = exp2f(red_ml[(w * 16 + row) * 2] - M);  // 0 for a warp without tiles
       L += red_ml[(w * 16 + row) * 2 + 1] * f;
-      acc += red_o[(w * 16 + row) * D + d] * f;
+      acc += red_o[(w * 16 + row) * kRedRow + d] * f;
     }
     if (n_used == 1) {
       out_t[row * D + d] = __float2half_rn(acc / L);
@@ -703,11 +705,13 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16
 
 // Warp roles of the tcgen05 prefill CTA: two softmax warpgroups (one per
 // 128-row query tile; thread t of a warpgroup owns row t and tensor-memory
-// lane t), one warp whose lane 0 issues every tcgen05.mma, one load warp.
+// lane t; they also load their query tile), one warp whose lane 0 issues
+// every tcgen05.mma, two K/V load warps.
 constexpr int kTcQTiles = 2;
 constexpr int kMmaWarp = 4 * kTcQTiles;
 constexpr int kLoadWarp = kMmaWarp + 1;
-constexpr int kTcThreads = (kLoadWarp + 1) * 32;
+constexpr int kLoadWarps = 2;
+constexpr int kTcThreads = (kLoadWarp + kLoadWarps) * 32;
 constexpr float kRescaleLog2 = 8.f;  // rescale O only when a row max grows by more than 2^8
 constexpr int kTcMaxStages = 4;
 __host__ __device__ constexpr int tc_stages(int head_dim) { return head_dim > 64 ? 2 : 4; }  // K/V tiles in flight
@@ -806,9 +810,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_prefill_tc_kernel(const At
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   if (tid == 0) {
-    mbar_init(bar(kQFull), 32);
+    mbar_init(bar(kQFull), 128 * kTcQTiles);
     for (int i = 0; i < kStages; ++i) {
-      mbar_init(bar(kKvFull + i), 32);
+      mbar_init(bar(kKvFull + i), 32 * kLoadWarps);
       mbar_init(bar(kKvEmpty + i), 1);
     }
     for (int i = 0; i < kTcQTiles; ++i) {
@@ -830,6 +834,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_prefill_tc_kernel(const At
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t t_s = tmem + lane_base + wg * kTcKeys;  // S_i, then P_i over its first 64 columns
     const uint32_t t_o = tmem + lane_base + kOCol + wg * D;
+    {  // this warpgroup's query tile (rows past `rows` zero-filled)
+      const __half* qrow0 = a.q + (tok0 * a.n_heads + h) * D;
+      const int64_t q_stride = static_cast<int64_t>(a.n_heads) * D;
+      const int r0 = tid & 127;
+#pragma unroll 4
+      for (int idx = r0; idx < 128 * kChunks; idx += 128) {
+        const int r = idx / kChunks, c = idx % kChunks;
+        const int row = wg * 128 + r;
+        const bool in = row < rows;
+        cp_async16(q_s + wg * kQBytes + sw128(128, r, c), qrow0 + (in ? row : 0) * q_stride + c * 8, in ? 16 : 0);
+      }
+      cp_async_mbar_arrive(bar(kQFull));
+    }
     float m_used = -INFINITY, l = 0.f;
     const float sl2 = a.scale_log2;
     const int my_n_kt = n_kt_q[wg];
@@ -1001,16 +1018,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_prefill_tc_kernel(const At
       }
     }
   } else {
-    // ---------------- loads: the load warp, cp.async with zero fill ----------------
-    const __half* qrow0 = a.q + (tok0 * a.n_heads + h) * D;
-    const int64_t q_stride = static_cast<int64_t>(a.n_heads) * D;
-    for (int idx = lane; idx < kRowsCta * kChunks; idx += 32) {
-      const int r = idx / kChunks, c = idx % kChunks;
-      const bool in = r < rows;
-      cp_async16(q_s + (r >> 7) * kQBytes + sw128(128, r & 127, c), qrow0 + (in ? r : 0) * q_stride + c * 8,
-                 in ? 16 : 0);
-    }
-    cp_async_mbar_arrive(bar(kQFull));
+    // ---------------- K/V loads: the load warps, cp.async with zero fill ----------------
+    const int lt = (warp - kLoadWarp) * 32 + lane;  // 0 .. 32 * kLoadWarps - 1
     const size_t head_off =
         (static_cast<size_t>(run_slot) * a.n_kv_heads + g) * static_cast<size_t>(a.max_seq) * D;
     const __half* kbase = a.k_cache + head_off;
@@ -1021,7 +1030,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_prefill_tc_kernel(const At
         if (!ok) break;
       }
       const uint32_t ks = kv_s + (kt % kStages) * 2 * kKVBytes, vs = ks + kKVBytes;
-      for (int idx = lane; idx < kTcKeys * kChunks; idx += 32) {
+#pragma unroll 4
+      for (int idx = lt; idx < kTcKeys * kChunks; idx += 32 * kLoadWarps) {
         const int r = idx / kChunks, c = idx % kChunks;
         const int j = kt * kTcKeys + r;
         const bool in = j <= max_pos;
@@ -1035,6 +1045,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_prefill_tc_kernel(const At
   }
 
   if (!ok) set_flag(a.err_flags, KLLM_B200_FLAG_TIMEOUT);
+  cp_async_wait<0>();  // no copy of this thread is still in flight
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -1062,6 +1073,8 @@ int64_t preferred_chunk(int64_t n_tokens, int64_t n_kv_heads, int64_t max_seq) {
   return chunk < cap ? chunk : cap;
 }
 
+// Split workspace: chunk partials (o, then max/sum); none when every
+// sequence fits one chunk.
 int64_t workspace_for(int64_t n_tokens, int64_t n_heads, int64_t head_dim, int64_t max_seq, int64_t chunk) {
   const int64_t n_chunks = (max_seq + chunk - 1) / chunk;
   if (n_chunks <= 1) return 0;

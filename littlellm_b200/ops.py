@@ -163,14 +163,15 @@ def attention_head_major(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.
     """Causal attention of q [T, Hq, D] over the head-major cache of one
     layer [n_slots, Hkv, max_seq, D]: token t sees positions 0..positions[t]
     of slot slots[t]. ``workspace=None`` allocates the preferred split
-    workspace here (the C entry point itself never allocates)."""
+    workspace here, zero-filled (the C entry point itself never allocates; a
+    caller-provided workspace must be zeroed once before its first use)."""
     T, Hq, D = q.shape
     n_slots, Hkv, max_seq, _ = k_cache.shape
     if out is None:
         out = torch.empty_like(q)
     if workspace is None:
         nbytes = attention_workspace_bytes(T, Hq, Hkv, D, max_seq)
-        workspace = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=q.device)
+        workspace = torch.zeros(max(nbytes, 16), dtype=torch.uint8, device=q.device)
     dev = _dev(q, k_cache, v_cache, positions, slots, out, workspace, err_flags)
     if positions.dtype != torch.int32 or slots.dtype != torch.int32:
         raise KllmError(_capi.ERR_DTYPE, "attention: positions and slots must be int32")

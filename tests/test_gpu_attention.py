@@ -63,7 +63,7 @@ def test_workspace_size_does_not_change_results(cuda, ops, oracle):
     from littlellm_b200 import _capi
     args = [dev(q), dev(kc), dev(vc), None, dev(positions, torch.int32), dev(slots, torch.int32)]
     for nbytes in (0, full // 3, full):
-        ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=cuda)
+        ws = torch.zeros(max(nbytes, 16), dtype=torch.uint8, device=cuda)
         args[3] = out = torch.empty(q.shape, dtype=torch.float16, device=cuda)
         rc = _capi.lib.kllm_b200_attention_head_major(
             *[a.data_ptr() for a in args], n_tok, 1, hq, hkv, d, n_tok, max_seq, _capi.F16,
@@ -71,6 +71,15 @@ def test_workspace_size_does_not_change_results(cuda, ops, oracle):
         assert rc == _capi.OK, _capi.last_error()
         torch.cuda.synchronize()
         assert_tol(host(out), want, TOL, f"workspace {nbytes}")
+        if nbytes == full:
+            # a second call on the same (now dirty) workspace gives the same result
+            first = out.clone()
+            rc = _capi.lib.kllm_b200_attention_head_major(
+                *[a.data_ptr() for a in args], n_tok, 1, hq, hkv, d, n_tok, max_seq, _capi.F16, ws.data_ptr(),
+                nbytes, None, torch.cuda.current_stream().cuda_stream)
+            assert rc == _capi.OK
+            torch.cuda.synchronize()
+            assert torch.equal(out, first)
 
 
 def test_prefill_runs_match_oracle(cuda, ops, oracle):
