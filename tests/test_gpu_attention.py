@@ -199,3 +199,22 @@ def test_prefill_short_last_run_and_bad_rows(cuda, ops, oracle):
     assert np.all(got[[45, 47]] == 0)
     keep = np.setdiff1d(np.arange(positions.size), [45, 47])
     assert_tol(got[keep], want[keep], TOL, "prefill rows")
+
+
+def test_prefill_more_items_than_sms(cuda, ops, oracle):
+    """head_dim 128 prefill with 12 runs x 2 blocks of 256 tokens x 8 heads =
+    192 CTAs (more than one per SM, so SMs take a second CTA that allocates
+    the tensor memory the first released), runs at random start positions."""
+    rng = np.random.default_rng(61)
+    hq, hkv, d, max_seq, seq_len, n_runs = 8, 8, 128, 1024, 512, 12
+    kc, vc = _cache(rng, n_runs, hkv, max_seq, d)
+    starts = rng.integers(0, max_seq - seq_len, n_runs)
+    positions = np.concatenate([np.arange(s0, s0 + seq_len) for s0 in starts]).astype(np.int32)
+    slots = np.repeat(rng.permutation(n_runs), seq_len).astype(np.int32)
+    q = f16r(rng.standard_normal((positions.size, hq, d)))
+    want, _ = oracle.attention_head_major(q, kc, vc, positions, slots)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    got = _run(ops, q, kc, vc, positions, slots, seq_len=seq_len, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert_tol(host(got), want, TOL, "persistent prefill")
