@@ -51,6 +51,8 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample length")
     ap.add_argument("--layers", type=int, default=None,
                     help="run only this many decoder layers (small profiling cases; not a bench line)")
+    ap.add_argument("--attention", action="store_true",
+                    help="chain workloads: run attention over the cache in every layer as part of the chain")
     ap.add_argument("--sequences", type=int, default=None,
                     help="attention workloads: run this many sequences (small profiling cases; not a bench line)")
     ap.add_argument("--settle-seconds", type=float, default=1.5,
@@ -562,6 +564,12 @@ def per_op_chain_timing(runner, stream, reps: int) -> dict:
         "qkv_bias_rope_kv_append": (_capi.OP_QKV_ROPE, qkv_bytes),
         "silu_mul": (_capi.OP_SWIGLU, 3 * T * m.intermediate * 2),
     }
+    if runner.attention:
+        # per layer (a decode layer launches the attention kernel and the split
+        # combine); bytes as chain_bytes counts them
+        from littlellm_b200.chain import chain_bytes
+        att = chain_bytes(w, L, positions=runner.positions.cpu().numpy())["attention"] / L
+        kinds["attention"] = (_capi.OP_ATTENTION, att)
     out = {}
     with torch.cuda.stream(stream):
         for name, (mask, nbytes) in kinds.items():
@@ -569,11 +577,15 @@ def per_op_chain_timing(runner, stream, reps: int) -> dict:
             n = runner.run(stream)
             g = capture(lambda: runner.run(stream), stream)
             g.replay()
-            ms = time_graph(g, stream, reps) / n
+            per = L if name == "attention" else n
+            ms = time_graph(g, stream, reps) / per
             out[name] = {"us_per_launch": ms * 1000.0, "bytes_per_launch": int(nbytes),
-                         "gbs": nbytes / (ms * 1e-3) / 1e9, "launches_per_replay": n}
+                         "gbs": nbytes / (ms * 1e-3) / 1e9, "launches_per_replay": per}
+            if name == "attention":
+                out[name]["kernel_launches_per_replay"] = n
+                out[name]["note"] = "per layer, not per kernel launch"
             del g
-        runner.desc.op_mask = 0
+        runner.desc.op_mask = runner.full_mask
     return out
 
 
@@ -994,7 +1006,8 @@ def run_ours(args):
     base = WORKLOADS[args.workload]
     weak = args.workload == "qwen_prefill"
     w = base if weak else shard(base, rank, world)
-    runner = ChainRunner(w, device=device, seed=1000 + rank, use_pdl=not args.no_pdl, n_layers=args.layers)
+    runner = ChainRunner(w, device=device, seed=1000 + rank, use_pdl=not args.no_pdl, n_layers=args.layers,
+                         attention=args.attention)
     stream = torch.cuda.Stream(device)
     torch.cuda.synchronize(device)
 
@@ -1048,7 +1061,8 @@ def run_ours(args):
     ms_per_step = max_ms / args.steps
     tokens_total = w.n_tokens * world
     value = tokens_total / (ms_per_step * 1e-3)
-    bytes_step = chain_bytes(w, runner.n_layers)
+    bytes_step = chain_bytes(w, runner.n_layers,
+                             positions=runner.positions.cpu().numpy() if args.attention else None)
     chain_gbs = bytes_step["total"] / (ms_per_step * 1e-3) / 1e9
     peaks = load_peaks()
 
@@ -1065,8 +1079,17 @@ def run_ours(args):
         "unit": "GB/s", "frac": silu["gbs"] / peaks["hbm_gbs"],
         "traffic": ncu_traffic("silu_mul", w.name), "peak_source": peaks["source"],
         "bytes_per_launch": silu["bytes_per_launch"], "us_per_launch": silu["us_per_launch"],
-        "timing": "24 PDL launches per CUDA graph (chain executor, op mask), CUDA events on the launch stream",
+        "timing": f"{runner.n_layers} PDL launches per CUDA graph (chain executor, op mask), CUDA events on the "
+                  "launch stream",
     }
+    if args.attention and w.decode:  # the attention dominates a decode step: HBM-bound K/V reads
+        att = op_chain["attention"]
+        roofline = {
+            "bound": "hbm", "kernel": "attn_decode_kernel + attn_combine_kernel", "achieved": att["gbs"],
+            "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": att["gbs"] / peaks["hbm_gbs"], "traffic": None,
+            "peak_source": peaks["source"], "bytes_per_layer": att["bytes_per_launch"],
+            "us_per_layer": att["us_per_launch"],
+            "timing": f"attention of {runner.n_layers} layers per CUDA graph (chain executor, op mask, PDL)"}
 
     # end to end through the C ABI with host buffers
     e2e = None
@@ -1074,7 +1097,7 @@ def run_ours(args):
         e2e = run_e2e(runner, stream, args.steps, device, dist, world)
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.attention:
         threads = 1
         tokens = 128
         v, steps, kind = time_reference_cpu(w.model, tokens, threads, args.cpu_seconds)
@@ -1086,7 +1109,8 @@ def run_ours(args):
     del graph
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "metric": METRIC + (" (chain with attention)" if args.attention else ""), "value": value, "unit": UNIT,
+            "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
             "scaling": "weak" if weak else "strong", "vs_baseline": None, "dtype": "f16",
             "data": "synthetic",
@@ -1098,7 +1122,7 @@ def run_ours(args):
                 "math": "fp16 storage, fp32 arithmetic",
                 "l2": "no flush: each step streams %.2f GB of distinct per-layer buffers (>> 126 MB L2)"
                       % (bytes_step["total"] / 1e9),
-                "pdl": not args.no_pdl, "cuda_graph": True,
+                "pdl": not args.no_pdl, "cuda_graph": True, "attention": bool(args.attention),
             },
             "hbm_gbs_chain": chain_gbs,
             "hbm_frac_chain": chain_gbs / peaks["hbm_gbs"],

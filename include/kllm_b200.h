@@ -256,6 +256,7 @@ typedef struct kllm_b200_layer_buffers {
   void* swiglu_out;          /* [T, intermediate] */
   void* k_cache;             /* [n_slots, n_kv_heads, max_seq, head_dim] */
   void* v_cache;             /* [n_slots, n_kv_heads, max_seq, head_dim] */
+  void* attn_ctx;            /* [T, n_heads*head_dim] attention output (KLLM_B200_OP_ATTENTION) or NULL */
 } kllm_b200_layer_buffers;
 
 /* op_mask bits of kllm_b200_chain */
@@ -266,7 +267,12 @@ enum {
   KLLM_B200_OP_POST_NORM = 8,   /* per layer: residual add + RMSNorm */
   KLLM_B200_OP_SWIGLU = 16,     /* per layer */
   KLLM_B200_OP_FINAL_NORM = 32,
-  KLLM_B200_OP_SELECT = 64
+  KLLM_B200_OP_SELECT = 64,
+  /* per layer, after the RoPE/KV append: attention of q over the layer's
+   * cache into attn_ctx (kllm_b200_attention_head_major; runs of seq_len
+   * tokens, or single tokens when seq_ends is given). Not in op_mask 0:
+   * the GEMM-free chain of the seven ops above stays the default. */
+  KLLM_B200_OP_ATTENTION = 128
 };
 
 typedef struct kllm_b200_chain {
@@ -288,13 +294,16 @@ typedef struct kllm_b200_chain {
   void* last_rows;                /* [n_seqs, hidden] */
   const kllm_b200_layer_buffers* layers; /* host array of n_layers entries */
   int32_t* err_flags;             /* device word or NULL */
+  void* attn_workspace;           /* attention split workspace (KLLM_B200_OP_ATTENTION), or NULL */
+  int64_t attn_workspace_bytes;
 } kllm_b200_chain;
 
 /* Launches the whole non-GEMM chain on `stream`: embedding, then per layer
- * add+RMSNorm, fused bias+RoPE+KV append, add+RMSNorm, SwiGLU, then the final
- * add+RMSNorm and select_last_rows (the op kinds selected by op_mask, all
- * when it is 0). *n_launches (if given) receives the number of kernels
- * launched. Can be captured into a CUDA graph. */
+ * add+RMSNorm, fused bias+RoPE+KV append, (attention, when its bit is set),
+ * add+RMSNorm, SwiGLU, then the final add+RMSNorm and select_last_rows (the
+ * op kinds selected by op_mask; 0 selects the seven ops without attention).
+ * *n_launches (if given) receives the number of kernels launched. Can be
+ * captured into a CUDA graph. */
 int kllm_b200_chain_run(const kllm_b200_chain* chain, int* n_launches, void* stream);
 
 /* ======================================================================== *

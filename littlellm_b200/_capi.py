@@ -31,6 +31,8 @@ FLAG_TIMEOUT = 16
 
 OP_EMBEDDING, OP_INPUT_NORM, OP_QKV_ROPE, OP_POST_NORM, OP_SWIGLU, OP_FINAL_NORM, OP_SELECT = (
     1, 2, 4, 8, 16, 32, 64)
+OP_ATTENTION = 128
+OP_CHAIN = 0x7f  # the seven ops of op_mask 0
 
 
 class KllmError(RuntimeError):
@@ -45,7 +47,7 @@ class LayerBuffers(ctypes.Structure):
     _fields_ = [(name, ctypes.c_void_p) for name in (
         "q", "k", "v", "q_bias", "k_bias", "v_bias", "attn_out", "ffn_out", "gate", "up",
         "input_norm_w", "post_norm_w", "attn_norm_out", "ffn_norm_out", "swiglu_out",
-        "k_cache", "v_cache")]
+        "k_cache", "v_cache", "attn_ctx")]
 
 
 class Chain(ctypes.Structure):
@@ -63,6 +65,7 @@ class Chain(ctypes.Structure):
         ("final_norm_w", ctypes.c_void_p), ("final_norm_out", ctypes.c_void_p),
         ("last_rows", ctypes.c_void_p), ("layers", ctypes.POINTER(LayerBuffers)),
         ("err_flags", ctypes.c_void_p),
+        ("attn_workspace", ctypes.c_void_p), ("attn_workspace_bytes", ctypes.c_int64),
     ]
 
 

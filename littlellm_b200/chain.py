@@ -74,10 +74,13 @@ def shard(workload: Workload, rank: int, world: int) -> Workload:
     return replace(workload, n_seqs=workload.n_seqs // world)
 
 
-def chain_bytes(w: Workload, n_layers: int | None = None) -> dict:
+def chain_bytes(w: Workload, n_layers: int | None = None, positions=None) -> dict:
     """Algorithmic HBM bytes of one chain step: every logical fp16 tensor read
     once and written once; norm weights and biases are negligible and not
-    counted; ids/positions/slots are int32."""
+    counted; ids/positions/slots are int32. With ``positions`` (host array of
+    the step's token positions) the attention of every layer is included:
+    each sequence's cached K and V rows 0..position read once (decode: per
+    token), q read and the context written."""
     m, T = w.model, w.n_tokens
     H, I, L = m.hidden, m.intermediate, n_layers or m.n_layers
     qkv_elems = T * (m.n_heads + 2 * m.n_kv_heads) * m.head_dim
@@ -88,6 +91,9 @@ def chain_bytes(w: Workload, n_layers: int | None = None) -> dict:
         "silu_mul": L * 3 * T * I * 2,
         "select_last_rows": 2 * w.n_seqs * H * 2,
     }
+    if positions is not None:
+        kv_rows = int((positions.astype("int64") + 1).sum()) if w.decode else T
+        per["attention"] = L * (kv_rows * m.n_kv_heads * m.head_dim * 2 * 2 + 2 * T * m.n_heads * m.head_dim * 2)
     per["total"] = sum(per.values())
     return per
 
@@ -110,7 +116,8 @@ class ChainRunner:
 
     def __init__(self, workload: Workload, device: torch.device | str = "cuda:0", seed: int = 0,
                  use_pdl: bool = True, n_layers: int | None = None,
-                 weight_dtype: torch.dtype = torch.float16, shard: tuple[int, int] | None = None):
+                 weight_dtype: torch.dtype = torch.float16, shard: tuple[int, int] | None = None,
+                 attention: bool = False):
         m = workload.model
         self.device = torch.device(device)
         self.n_layers = n_layers or m.n_layers
@@ -173,7 +180,18 @@ class ChainRunner:
                     "v_cache": torch.empty((s1 - s0, m.n_kv_heads, workload.max_seq, m.head_dim),
                                            dtype=f16, device=dev),
                 }
+                if attention:
+                    # the step attends to the whole cache up to each position:
+                    # earlier positions hold values from previous steps
+                    L["k_cache"].normal_(generator=gen)
+                    L["v_cache"].normal_(generator=gen)
+                    L["attn_ctx"] = torch.empty((Tl, qd), dtype=f16, device=dev)
                 self.layers.append(L)
+            self.attention = attention
+            if attention:
+                from . import ops
+                nbytes = ops.attention_workspace_bytes(Tl, m.n_heads, m.n_kv_heads, m.head_dim, workload.max_seq)
+                self.attn_workspace = torch.zeros(max(nbytes, 16), dtype=torch.uint8, device=dev)
         self.weight_dtype = weight_dtype
         self._build_desc(use_pdl)
 
@@ -197,7 +215,12 @@ class ChainRunner:
         c.final_norm_out, c.last_rows = self.final_norm_out.data_ptr(), self.last_rows.data_ptr()
         c.layers = ctypes.cast(arr, ctypes.POINTER(_capi.LayerBuffers))
         c.err_flags = self.err_flags.data_ptr()
+        if self.attention:
+            c.op_mask = _capi.OP_CHAIN | _capi.OP_ATTENTION
+            c.attn_workspace = self.attn_workspace.data_ptr()
+            c.attn_workspace_bytes = self.attn_workspace.numel()
         self.desc = c
+        self.full_mask = c.op_mask
 
     def set_pdl(self, use_pdl: bool) -> None:
         self.desc.use_pdl = int(use_pdl)

@@ -1184,7 +1184,8 @@ int attention_head_major(const void* q, const void* k_cache, const void* v_cache
                          const int32_t* positions, const int32_t* slots, int64_t n_tokens, int64_t seq_len,
                          int64_t n_heads, int64_t n_kv_heads, int64_t head_dim, int64_t n_slots, int64_t max_seq,
                          int dtype, void* workspace, int64_t workspace_bytes, int32_t* err_flags,
-                         const LaunchOpts& o) {
+                         const LaunchOpts& o, int* n_launched) {
+  if (n_launched) *n_launched = 0;
   int rc = check_attention_args(q, k_cache, v_cache, out, positions, slots, n_tokens, n_heads, n_kv_heads,
                                 head_dim, n_slots, max_seq, dtype);
   if (rc != KLLM_B200_OK || n_tokens == 0 || n_heads == 0) return rc;
@@ -1223,7 +1224,9 @@ int attention_head_major(const void* q, const void* k_cache, const void* v_cache
     a.part_o = static_cast<float*>(workspace);
     a.part_ml = a.part_o + n_tokens * n_heads * n_chunks * head_dim;
   }
-  return head_dim == 64 ? launch_attention<64>(a, o) : launch_attention<128>(a, o);
+  rc = head_dim == 64 ? launch_attention<64>(a, o) : launch_attention<128>(a, o);
+  if (rc == KLLM_B200_OK && n_launched) *n_launched = (seq_len < kPrefillMinRun && n_chunks > 1) ? 2 : 1;
+  return rc;
 }
 
 }  // namespace kb

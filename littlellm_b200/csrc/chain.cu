@@ -6,6 +6,7 @@
 //   per layer l:
 //     add+RMSNorm  r += ffn_out[l-1]; attn_norm = norm(r)   (l=0: norm only; :83-87, :166)
 //     bias+RoPE+KV q/k/v -> q rotated, cache[l] appended    (:89-114)
+//     [attention   ctx = attn(q, cache[l]), when requested]  (:116-126)
 //     add+RMSNorm  r += attn_out[l]; ffn_norm = norm(r)      (:135-143)
 //     SwiGLU       swiglu = silu(gate) * up                  (:158)
 //   add+RMSNorm  r += ffn_out[L-1]; normed = norm(r)         (:166, :171)
@@ -33,6 +34,11 @@ extern "C" int kllm_b200_chain_run(const kllm_b200_chain* c, int* n_launches, vo
   const int64_t T = c->n_tokens, H = c->hidden;
   const int wdt = c->weight_dtype;
   const int mask = c->op_mask == 0 ? 0x7f : c->op_mask;
+  if ((mask & KLLM_B200_OP_ATTENTION) != 0) {
+    for (int64_t l = 0; l < c->n_layers; ++l) {
+      if (c->layers[l].attn_ctx == nullptr) return fail(KLLM_B200_ERR_INVALID_ARG, "chain_run: layer %lld has no attn_ctx", (long long)l);
+    }
+  }
   auto on = [mask](int bit) { return (mask & bit) != 0; };
   int launched = 0;
   int rc = KLLM_B200_OK;
@@ -56,6 +62,16 @@ extern "C" int kllm_b200_chain_run(const kllm_b200_chain* c, int* n_launches, vo
                                    c->n_slots, c->max_seq, c->err_flags, o);
       if (rc != KLLM_B200_OK) return rc;
       ++launched;
+    }
+    if (on(KLLM_B200_OP_ATTENTION)) {
+      // runs of seq_len tokens of one sequence; single tokens for ragged batches
+      const int64_t run = c->seq_ends == nullptr && c->seq_len >= 1 ? c->seq_len : 1;
+      int n = 0;
+      rc = attention_head_major(L.q, L.k_cache, L.v_cache, L.attn_ctx, c->positions, c->slots, T, run, c->n_heads,
+                                c->n_kv_heads, c->head_dim, c->n_slots, c->max_seq, KLLM_B200_F16, c->attn_workspace,
+                                c->attn_workspace_bytes, c->err_flags, o, &n);
+      if (rc != KLLM_B200_OK) return rc;
+      launched += n;
     }
     if (on(KLLM_B200_OP_POST_NORM)) {
       rc = add_rms_norm(c->residual, L.attn_out, L.post_norm_w, L.ffn_norm_out, T, H, c->eps, KLLM_B200_F16, wdt,

@@ -42,6 +42,6 @@ int attention_head_major(const void* q, const void* k_cache, const void* v_cache
                          const int32_t* positions, const int32_t* slots, int64_t n_tokens, int64_t seq_len,
                          int64_t n_heads, int64_t n_kv_heads, int64_t head_dim, int64_t n_slots, int64_t max_seq,
                          int dtype, void* workspace, int64_t workspace_bytes, int32_t* err_flags,
-                         const LaunchOpts& o);
+                         const LaunchOpts& o, int* n_launched = nullptr);
 
 }  // namespace kb

@@ -115,7 +115,9 @@ def test_last_error_is_per_thread(capi):
 
 def test_chain_struct_layout(capi):
     # the ctypes mirror of kllm_b200_chain must match the C layout: 12 int64,
-    # 2 floats, 3 ints (+4 bytes padding), 9 pointers, the layers pointer and err_flags
-    assert ctypes.sizeof(capi.Chain) == 12 * 8 + 2 * 4 + 3 * 4 + 4 + 11 * 8
+    # 2 floats, 3 ints (+4 bytes padding), 9 pointers, the layers pointer,
+    # err_flags, the attention workspace pointer and its size
+    assert ctypes.sizeof(capi.Chain) == 12 * 8 + 2 * 4 + 3 * 4 + 4 + 11 * 8 + 2 * 8
     assert capi.Chain.embed_table.offset == 12 * 8 + 2 * 4 + 3 * 4 + 4
-    assert ctypes.sizeof(capi.LayerBuffers) == 17 * 8
+    assert capi.Chain.attn_workspace.offset == 12 * 8 + 2 * 4 + 3 * 4 + 4 + 11 * 8
+    assert ctypes.sizeof(capi.LayerBuffers) == 18 * 8

@@ -125,3 +125,27 @@ def test_chain_op_mask_launches_only_selected_ops(cuda, oracle):
         assert_tol(host(L["swiglu_out"]), oracle.silu_mul(host(L["gate"]), host(L["up"])))
     r.desc.op_mask = _capi.OP_INPUT_NORM | _capi.OP_POST_NORM
     assert r.run() == 2 * w.model.n_layers
+
+
+@pytest.mark.parametrize("shape", ["qwen", "llama"])
+@pytest.mark.parametrize("decode", [False, True])
+def test_chain_with_attention(cuda, oracle, shape, decode):
+    """KLLM_B200_OP_ATTENTION in the chain (PDL on): every layer's context
+    equals the oracle attention of that layer's rotated q over its cache as
+    the step left it (prefill: runs of 17 tokens take the prefill kernel,
+    tcgen05 at head_dim 128; decode: single tokens over a filled cache)."""
+    from littlellm_b200.chain import ChainRunner
+    w = _tiny(decode, shape)
+    m = w.model
+    r = ChainRunner(w, device=cuda, seed=7, use_pdl=True, attention=True)
+    launches = r.run()
+    torch.cuda.synchronize()
+    assert launches == 1 + 5 * m.n_layers + 2
+    assert int(r.err_flags.item()) == 0
+    pos, slots = r.positions.cpu().numpy(), r.slots.cpu().numpy()
+    T, D = w.n_tokens, m.head_dim
+    for l, L in enumerate(r.layers):
+        want, bad = oracle.attention_head_major(host(L["q"]).reshape(T, m.n_heads, D), host(L["k_cache"]),
+                                                host(L["v_cache"]), pos, slots)
+        assert bad == 0
+        assert_tol(host(L["attn_ctx"]).reshape(T, m.n_heads, D), want, what=f"attention layer {l}")
