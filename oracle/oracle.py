@@ -35,12 +35,18 @@ _c_i8p = ctypes.POINTER(ctypes.c_int8)
 _c_i64 = ctypes.c_int64
 
 
+def reference_sources_present() -> bool:
+    """Whether the reference source tree the Makefile compiles is here (it is
+    not on machines that only run the prebuilt checkers)."""
+    return os.path.isdir("/root/reference")
+
+
 def build(force: bool = False) -> None:
     """Runs oracle/Makefile (C restatement, plus the compiled reference when
     its source tree is present)."""
     if force or not os.path.exists(ORACLE_SO):
         subprocess.run(["make", "-C", HERE, "-s"], check=True)
-    elif os.path.isdir("/root/reference"):
+    elif reference_sources_present():
         subprocess.run(["make", "-C", HERE, "-s"], check=True)
 
 
