@@ -1063,14 +1063,17 @@ constexpr size_t prefill_smem(int head_dim) { return static_cast<size_t>(2) * 2 
 
 constexpr size_t decode_smem(int head_dim) { return static_cast<size_t>(kAttnWarps) * kStages * 2 * kTile * head_dim * 2; }
 
-// Positions per decode CTA: 512, halved (down to 128) while the launch would
-// have fewer than four CTAs per SM, and never more than max_seq rounded up.
+// Positions per decode CTA. Splitting a (token, kv head) item costs partial
+// writes, a combine pass and per-CTA prologues, so items are split only as far
+// as needed for load balance: a chunk is about an eighth of one resident CTA
+// slot's share of the work, counting half of max_seq per item (positions are
+// on the device), in multiples of 128, at most max_seq (no split).
 int64_t preferred_chunk(int64_t n_tokens, int64_t n_kv_heads, int64_t max_seq) {
   const int64_t cap = (max_seq + kChunkUnit - 1) / kChunkUnit * kChunkUnit;
-  int64_t chunk = 512;
-  const int64_t target = 4LL * sm_count();
-  while (chunk > kChunkUnit && n_tokens * n_kv_heads * ((max_seq + chunk - 1) / chunk) < target) chunk /= 2;
-  return chunk < cap ? chunk : cap;
+  const int64_t slots = 2LL * sm_count();  // decode CTAs resident per SM at head_dim 64
+  const int64_t share = n_tokens * n_kv_heads * ((max_seq + 1) / 2) / (8 * slots);
+  const int64_t chunk = (share + kChunkUnit - 1) / kChunkUnit * kChunkUnit;
+  return chunk < kChunkUnit ? kChunkUnit : (chunk < cap ? chunk : cap);
 }
 
 // Split workspace: chunk partials (o, then max/sum); none when every
