@@ -182,9 +182,13 @@ class ChainRunner:
                 }
                 if attention:
                     # the step attends to the whole cache up to each position:
-                    # earlier positions hold values from previous steps
-                    L["k_cache"].normal_(generator=gen)
-                    L["v_cache"].normal_(generator=gen)
+                    # earlier positions hold values from previous steps (the
+                    # whole batch's values drawn, this shard's slots kept, so a
+                    # sharded run sees the same cache rows as an unsharded one)
+                    for name in ("k_cache", "v_cache"):
+                        full = normal((workload.n_seqs, m.n_kv_heads, workload.max_seq, m.head_dim))
+                        L[name].copy_(full[s0:s1] if (s0, s1) != (0, workload.n_seqs) else full)
+                        del full
                     L["attn_ctx"] = torch.empty((Tl, qd), dtype=f16, device=dev)
                 self.layers.append(L)
             self.attention = attention
