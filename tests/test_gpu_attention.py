@@ -177,12 +177,14 @@ def test_prefill_kernel_matches_oracle(cuda, ops, oracle, hq, hkv, d, max_seq, s
     assert_tol(host(got), host(per_token), TOL, "prefill vs decode kernel")
 
 
-def test_prefill_short_last_run_and_bad_rows(cuda, ops, oracle):
+@pytest.mark.parametrize("d", [64, 128])  # the mma.sync and the tcgen05 prefill kernels
+def test_prefill_short_last_run_and_bad_rows(cuda, ops, oracle, d):
     """100 tokens in runs of 40 (the last run has 20); in the second run one
     row names another slot and one an out-of-range position: those rows are
-    zero and flagged, the others still match."""
+    zero and flagged, the others still match. At head_dim 128 every CTA's
+    second 128-row query tile is empty."""
     rng = np.random.default_rng(41)
-    hq, hkv, d, max_seq, seq_len = 6, 2, 64, 256, 40
+    hq, hkv, max_seq, seq_len = 6, 2, 256, 40
     kc, vc = _cache(rng, 4, hkv, max_seq, d)
     positions = np.concatenate([np.arange(40), np.arange(40), np.arange(50, 70)]).astype(np.int32)
     slots = np.repeat([2, 0, 3], [40, 40, 20]).astype(np.int32)
