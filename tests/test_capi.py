@@ -121,3 +121,47 @@ def test_chain_struct_layout(capi):
     assert capi.Chain.embed_table.offset == 12 * 8 + 2 * 4 + 3 * 4 + 4
     assert capi.Chain.attn_workspace.offset == 12 * 8 + 2 * 4 + 3 * 4 + 4 + 11 * 8
     assert ctypes.sizeof(capi.LayerBuffers) == 18 * 8
+
+
+def test_attention_validation_without_gpu(capi):
+    """kllm_b200_attention_head_major rejects bad shapes, dtypes and pointers
+    on the host, before any CUDA call; the workspace query needs no GPU."""
+    lib = capi.lib
+    n = ctypes.c_int64(-1)
+    assert lib.kllm_b200_attention_workspace_bytes(2048, 14, 2, 64, 4096, ctypes.addressof(n)) == capi.OK
+    assert n.value >= 0
+    assert lib.kllm_b200_attention_workspace_bytes(0, 14, 2, 64, 4096, ctypes.addressof(n)) == capi.OK
+    assert n.value == 0
+    assert lib.kllm_b200_attention_workspace_bytes(1, 1, 1, 64, 8, None) == capi.ERR_INVALID_ARG
+    p = 16  # any non-null, 16-byte aligned value: nothing is dereferenced before validation fails
+    cases = [
+        ((p,) * 6 + (1, 1, 2, 2, 96, 1, 8, capi.F16), capi.ERR_SHAPE, "head_dim"),      # head_dim 96
+        ((p,) * 6 + (1, 1, 3, 2, 64, 1, 8, capi.F16), capi.ERR_SHAPE, "multiple"),      # 3 heads over 2
+        ((p,) * 6 + (1, 1, 40, 2, 64, 1, 8, capi.F16), capi.ERR_SHAPE, "16"),           # 20 per kv head
+        ((p,) * 6 + (1, 1, 2, 2, 64, 1, 8, capi.F32), capi.ERR_DTYPE, "dtype"),
+        ((None,) * 6 + (4, 1, 2, 2, 64, 1, 8, capi.F16), capi.ERR_INVALID_ARG, "null"),
+        ((p + 2,) + (p,) * 5 + (4, 1, 2, 2, 64, 1, 8, capi.F16), capi.ERR_ALIGN, "aligned"),
+        ((p,) * 6 + (4, 0, 2, 2, 64, 1, 8, capi.F16), capi.ERR_SHAPE, "seq_len"),
+        ((p,) * 6 + (4, 1, 2, 2, 64, 0, 8, capi.F16), capi.ERR_SHAPE, "empty cache"),
+    ]
+    for args, status, word in cases:
+        rc = lib.kllm_b200_attention_head_major(*args, None, 0, None, None)
+        assert rc == status, (args, rc, capi.last_error())
+        assert word in capi.last_error()
+    # nothing to do: no tokens
+    assert lib.kllm_b200_attention_head_major(*(None,) * 6, 0, 1, 2, 2, 64, 1, 8, capi.F16, None, 0, None,
+                                              None) == capi.OK
+
+
+def test_chain_attention_needs_context_buffers(capi):
+    """KLLM_B200_OP_ATTENTION with a layer lacking attn_ctx is refused before
+    any launch."""
+    layers = (capi.LayerBuffers * 2)()
+    c = capi.Chain()
+    c.n_tokens, c.hidden, c.n_heads, c.n_kv_heads, c.head_dim = 4, 64, 2, 2, 64
+    c.intermediate, c.vocab, c.n_layers, c.n_slots, c.max_seq, c.n_seqs, c.seq_len = 128, 10, 2, 1, 8, 1, 4
+    c.weight_dtype = capi.F16
+    c.op_mask = capi.OP_CHAIN | capi.OP_ATTENTION
+    c.layers = ctypes.cast(layers, ctypes.POINTER(capi.LayerBuffers))
+    assert capi.lib.kllm_b200_chain_run(ctypes.byref(c), None, None) == capi.ERR_INVALID_ARG
+    assert "attn_ctx" in capi.last_error()
