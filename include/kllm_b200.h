@@ -142,6 +142,16 @@ int kllm_b200_copy_kv_to_cache(const void* k, const void* v, int64_t seq, int64_
 int kllm_b200_dequantize_int8(const int8_t* data, const float* scale, void* out, int64_t n,
                               int out_dtype, void* stream);
 
+/* Opt-in IEEE rounding of the INT8 -> fp16 dequant: out[i] is
+ * float(data[i]) * scale[0] rounded to nearest even (__float2half_rn)
+ * instead of by the reference loader's float_to_half (src/base/half.cpp:
+ * 38-61, which rounds ties away from zero and drops a carry into an odd
+ * exponent). If `mismatches` (a device uint64) is given, the number of
+ * elements where the two roundings differ is ADDED to it; zero it first.
+ * Same alignment rules and fast path as kllm_b200_dequantize_int8. */
+int kllm_b200_dequantize_int8_rne(const int8_t* data, const float* scale, void* out, int64_t n,
+                                  unsigned long long* mismatches, void* stream);
+
 /* ======================================================================== *
  *  Fused / batched operators (additive to include/kllm/op/ops.h)           *
  * ======================================================================== */

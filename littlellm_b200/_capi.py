@@ -95,6 +95,7 @@ SIGNATURES = {
     "kllm_b200_qkv_bias_rope_kv_append": [_vp, _vp, _vp, _vp, _vp, _vp, _int, _vp, _vp, _i64, _i64,
                                           _i64, _i64, _f32, _vp, _vp, _i64, _i64, _vp, _vp],
     "kllm_b200_select_last_rows": [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _int, _vp, _vp],
+    "kllm_b200_dequantize_int8_rne": [_vp, _vp, _vp, _i64, _vp, _vp],
     "kllm_b200_attention_workspace_bytes": [_i64, _i64, _i64, _i64, _i64, _vp],
     "kllm_b200_attention_head_major": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64,
                                        _i64, _int, _vp, _i64, _vp, _vp],

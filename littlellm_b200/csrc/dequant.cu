@@ -6,6 +6,8 @@
 // out_dtype F16: the reference weight loader's result
 //   (src/model/weights.cpp:139-148): the fp32 product rounded by the
 //   project's own float_to_half (src/base/half.cpp:38-61), bit for bit.
+// Opt-in: fp16 rounded to nearest even (IEEE), with a count of the values
+//   where that differs from the reference rounding.
 //
 // With one scale per tensor the fp16 result is a function of the int8 byte
 // alone, so each CTA evaluates the reference rounding for all 256 byte
@@ -150,6 +152,94 @@ __global__ void __launch_bounds__(kThreads) dequant_generic_kernel(const int8_t*
     } else {
       static_cast<float*>(out)[i] = val;
     }
+  }
+}
+
+// ---- opt-in IEEE rounding --------------------------------------------------
+//
+// The same dequant with round-to-nearest-even fp16 (__float2half_rn) in place
+// of the reference loader's rounding, for callers that want IEEE results.
+// Each table entry holds the RNE half in its low 16 bits and, in bit 16,
+// whether it differs from the reference rounding of the same byte, so one
+// lookup gives both the output and that element's contribution to the count
+// of values the two roundings disagree on.
+
+__device__ __forceinline__ uint32_t rne_entry(uint32_t b, float s) {
+  const float v = dequant_value(b, s);
+  const uint32_t rne = static_cast<uint32_t>(__half_as_ushort(__float2half_rn(v)));
+  return rne | ((rne != ref_float_to_half(v)) ? 0x10000u : 0u);
+}
+
+// Two fp16 results (bytes 0/1 or 2/3 of w) packed low-first; their mismatch
+// flags are added to `count`.
+__device__ __forceinline__ uint32_t rne2(const uint32_t* my, uint32_t w, int shift, uint32_t& count) {
+  const uint32_t lo = my[((w >> shift) & 0xffu) << 5];
+  const uint32_t hi = my[((w >> (shift + 8)) & 0xffu) << 5];
+  count += (lo >> 16) + (hi >> 16);
+  return (lo & 0xffffu) | (hi << 16);
+}
+
+__global__ void __launch_bounds__(kThreads) dequant_f16_rne_kernel(const int8_t* __restrict__ q,
+                                                                   const float* __restrict__ scale,
+                                                                   __half* __restrict__ out, int64_t n,
+                                                                   unsigned long long* mismatches) {
+  __shared__ uint32_t lut[256 * 32];
+  grid_dep_wait();
+  grid_dep_launch();
+  const float s = __ldg(scale);
+  {
+    const uint32_t b = threadIdx.x;
+    const uint32_t e = rne_entry(b, s);
+#pragma unroll 8
+    for (int l = 0; l < 32; ++l) lut[b * 32 + ((l + b) & 31)] = e;
+  }
+  __syncthreads();
+  const uint32_t* my = lut + (threadIdx.x & 31);
+  uint32_t count = 0;
+  const int64_t nvec = n >> 4;
+  const uint4* src = reinterpret_cast<const uint4*>(q);
+  uint4* dst = reinterpret_cast<uint4*>(out);
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < nvec; i += stride) {
+    const uint4 w = ld_stream(src + i);
+    st_plain(dst + 2 * i, make_uint4(rne2(my, w.x, 0, count), rne2(my, w.x, 16, count), rne2(my, w.y, 0, count),
+                                     rne2(my, w.y, 16, count)));
+    st_plain(dst + 2 * i + 1, make_uint4(rne2(my, w.z, 0, count), rne2(my, w.z, 16, count),
+                                         rne2(my, w.w, 0, count), rne2(my, w.w, 16, count)));
+  }
+  if (blockIdx.x == 0) {
+    unsigned short* o16 = reinterpret_cast<unsigned short*>(out);
+    for (int64_t j = (nvec << 4) + threadIdx.x; j < n; j += blockDim.x) {
+      const uint32_t e = my[(static_cast<uint32_t>(static_cast<uint8_t>(q[j]))) << 5];
+      o16[j] = static_cast<unsigned short>(e & 0xffffu);
+      count += e >> 16;
+    }
+  }
+  if (mismatches != nullptr) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) count += __shfl_xor_sync(0xffffffffu, count, off);
+    if ((threadIdx.x & 31) == 0 && count != 0) atomicAdd(mismatches, static_cast<unsigned long long>(count));
+  }
+}
+
+// Unaligned buffers: element per thread, same rounding and count.
+__global__ void __launch_bounds__(kThreads) dequant_f16_rne_generic_kernel(const int8_t* q, const float* scale,
+                                                                           unsigned short* out, int64_t n,
+                                                                           unsigned long long* mismatches) {
+  grid_dep_wait();
+  grid_dep_launch();
+  const float s = __ldg(scale);
+  uint32_t count = 0;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const uint32_t e = rne_entry(static_cast<uint32_t>(static_cast<uint8_t>(q[i])), s);
+    out[i] = static_cast<unsigned short>(e & 0xffffu);
+    count += e >> 16;
+  }
+  if (mismatches != nullptr) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) count += __shfl_xor_sync(0xffffffffu, count, off);
+    if ((threadIdx.x & 31) == 0 && count != 0) atomicAdd(mismatches, static_cast<unsigned long long>(count));
   }
 }
 
@@ -308,6 +398,23 @@ int dequantize_int8_value(const int8_t* data, float scale, void* out, int64_t n,
   return dequantize_int8_impl(data, nullptr, scale, out, n, out_dtype, o);
 }
 
+int dequantize_int8_rne(const int8_t* data, const float* scale, void* out, int64_t n,
+                        unsigned long long* mismatches, const LaunchOpts& o) {
+  if (n < 0) return fail(KLLM_B200_ERR_INVALID_ARG, "dequantize_int8_rne: negative size");
+  if (n == 0) return KLLM_B200_OK;
+  if (!data || !scale || !out) return fail(KLLM_B200_ERR_INVALID_ARG, "dequantize_int8_rne: null pointer");
+  if (aligned16(data) && aligned16(out)) {
+    const unsigned grid = persistent_grid(dequant_f16_rne_kernel, kThreads, 0, kThreads * 2, (n >> 4) + 1);
+    return launch_status(launch(dequant_f16_rne_kernel, grid, kThreads, 0, o.stream, o.pdl, data, scale,
+                                static_cast<__half*>(out), n, mismatches),
+                         "dequantize_int8_rne");
+  }
+  const unsigned grid = persistent_grid(dequant_f16_rne_generic_kernel, kThreads, 0, kThreads * 4, n);
+  return launch_status(launch(dequant_f16_rne_generic_kernel, grid, kThreads, 0, o.stream, o.pdl, data, scale,
+                              static_cast<unsigned short*>(out), n, mismatches),
+                       "dequantize_int8_rne");
+}
+
 int dequantize_int8_batched(const int8_t* const* data, const float* const* scales, void* const* outs,
                             const int64_t* counts, int n_tensors, int out_dtype, const LaunchOpts& o) {
   if (n_tensors < 0) return fail(KLLM_B200_ERR_INVALID_ARG, "dequantize_int8_batched: negative tensor count");
@@ -362,6 +469,13 @@ extern "C" int kllm_b200_dequantize_int8(const int8_t* data, const float* scale,
   kb::LaunchOpts o;
   o.stream = static_cast<cudaStream_t>(stream);
   return kb::dequantize_int8(data, scale, out, n, out_dtype, o);
+}
+
+extern "C" int kllm_b200_dequantize_int8_rne(const int8_t* data, const float* scale, void* out, int64_t n,
+                                             unsigned long long* mismatches, void* stream) {
+  kb::LaunchOpts o;
+  o.stream = static_cast<cudaStream_t>(stream);
+  return kb::dequantize_int8_rne(data, scale, out, n, mismatches, o);
 }
 
 extern "C" int kllm_b200_dequantize_int8_batched(const int8_t* const* data, const float* const* scales,

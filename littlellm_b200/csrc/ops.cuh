@@ -32,6 +32,9 @@ int dequantize_int8(const int8_t* data, const float* scale, void* out, int64_t n
 int dequantize_int8_value(const int8_t* data, float scale, void* out, int64_t n, int out_dtype,
                           const LaunchOpts& o);
 
+int dequantize_int8_rne(const int8_t* data, const float* scale, void* out, int64_t n,
+                        unsigned long long* mismatches, const LaunchOpts& o);
+
 int select_last_rows(const void* x, int64_t rows, int64_t cols, const int32_t* seq_ends, int64_t seq_len,
                      int64_t n_seqs, void* out, int dtype, int32_t* err_flags, const LaunchOpts& o);
 

@@ -254,6 +254,25 @@ def dequantize_int8(data: torch.Tensor, scale: torch.Tensor,
     return out
 
 
+def dequantize_int8_rne(data: torch.Tensor, scale: torch.Tensor, out: torch.Tensor | None = None,
+                        mismatches: torch.Tensor | None = None) -> torch.Tensor:
+    """out = data * scale[0] in fp16 rounded to nearest even (IEEE), not by
+    the reference loader's rounding; when given, ``mismatches`` (a CUDA int64
+    tensor of one element) is increased by the number of elements where the
+    two roundings differ."""
+    if out is None:
+        out = torch.empty(data.shape, dtype=torch.float16, device=data.device)
+    dev = _dev(data, scale, out, mismatches)
+    if data.dtype != torch.int8 or scale.dtype != torch.float32 or out.dtype != torch.float16:
+        raise KllmError(_capi.ERR_DTYPE, "dequantize_int8_rne expects int8 data, an fp32 scale and fp16 out")
+    if mismatches is not None and (mismatches.dtype != torch.int64 or mismatches.numel() != 1):
+        raise KllmError(_capi.ERR_DTYPE, "dequantize_int8_rne: mismatches must be one int64")
+    with torch.cuda.device(dev):
+        check(lib.kllm_b200_dequantize_int8_rne(_ptr(data), _ptr(scale), _ptr(out), data.numel(), _ptr(mismatches),
+                                                _stream(dev)))
+    return out
+
+
 def dequantize_int8_batched(data: list[torch.Tensor], scales: list[torch.Tensor],
                             outs: list[torch.Tensor]) -> list[torch.Tensor]:
     """outs[i] = data[i] * scales[i][0] for every i in one launch (rounding

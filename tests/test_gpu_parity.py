@@ -317,3 +317,33 @@ def test_dequant_batched_many_tensors(ops, oracle):
     ops.dequantize_int8_batched(data, sc, outs)
     for q, s, o in zip(qs, scales, outs):
         assert np.array_equal(bits16(o), oracle.dequantize_int8_f16_bits(q, float(s)))
+
+
+@pytest.mark.parametrize("n,offset", [(1_000_003, 0), (70_001, 1)])  # vector path with a ragged tail; unaligned
+def test_dequant_rne_and_mismatch_count(cuda, ops, oracle, n, offset):
+    """Opt-in IEEE rounding: the fp16 output equals numpy's round-to-nearest-even
+    conversion of the same fp32 product, bit for bit, and the count equals the
+    number of elements where that differs from the reference loader's
+    rounding (ties away from zero, the dropped carry). Two calls add up."""
+    rng = np.random.default_rng(n)
+    q = rng.integers(-128, 128, n, dtype=np.int8)
+    # 0.0061: no disagreement; (1 + 2^-11) * 2^-8 puts 15 of the 256 byte values on exact ties;
+    # 0.0062498804 has 6 byte values where the two roundings differ
+    for scale in (np.float32(0.0061), np.float32((1 + 2.0 ** -11) * 2.0 ** -8), np.float32(0.006249880418181419)):
+        prod = q.astype(np.float32) * scale
+        want = prod.astype(np.float16).view(np.uint16)
+        ref = oracle.dequantize_int8_f16_bits(q, float(scale))
+        expect = int(np.count_nonzero(want != ref))
+        qbuf = torch.empty(n + offset, dtype=torch.int8, device=cuda)
+        qbuf[offset:] = torch.from_numpy(q).to(cuda)
+        obuf = torch.empty(n + offset, dtype=torch.float16, device=cuda)
+        count = torch.zeros(1, dtype=torch.int64, device=cuda)
+        sc = torch.tensor([scale], dtype=torch.float32, device=cuda)
+        for _ in range(2):
+            ops.dequantize_int8_rne(qbuf[offset:], sc, out=obuf[offset:], mismatches=count)
+        torch.cuda.synchronize()
+        got = obuf[offset:].cpu().view(torch.int16).numpy().view(np.uint16)
+        assert np.array_equal(got, want)
+        assert int(count.item()) == 2 * expect
+        if scale != np.float32(0.0061):
+            assert expect > 0  # the case exercises the count
