@@ -242,6 +242,34 @@ int kllm_b200_attention_head_major(const void* q, const void* k_cache, const voi
                                    int64_t workspace_bytes, int32_t* err_flags, void* stream);
 
 /* ======================================================================== *
+ *  GEMM with fused epilogues (tcgen05)                                      *
+ * ======================================================================== */
+
+/* linear() of src/model/llama.cpp:12-24, i.e. matmul (cuda_matmul,
+ * src/op/cuda/matmul.cu:130-160; cpu_matmul, src/op/cpu/matmul.cpp:9-33)
+ * followed by add_bias_inplace (src/op/cuda/add.cu:59-69), in one kernel:
+ * out[i, j] = fp16(fp16(sum_c x[i, c] * w[j, c]) + bias[j]), fp32
+ * accumulation, both roundings to nearest even. x [m, k], w [n, k] and
+ * out [m, n] are fp16, row-major, 16-byte aligned; k must be a positive
+ * multiple of 8. bias (F16 or F32, 4-byte aligned) may be NULL (plain
+ * matmul). out must not overlap x or w. A bounded wait that runs out inside
+ * the kernel sets KLLM_B200_FLAG_TIMEOUT in err_flags (optional). */
+int kllm_b200_linear(const void* x, const void* w, const void* bias, int bias_dtype, void* out,
+                     int64_t m, int64_t n, int64_t k, int32_t* err_flags, void* stream);
+
+/* The MLP's gate and up linears and silu_mul (src/model/llama.cpp:145-158)
+ * in one kernel: out = silu_mul(linear(x, w_gate, b_gate),
+ * linear(x, w_up, b_up)), with the gate and up values rounded to fp16
+ * (plus bias, rounded again) exactly as the separate ops store them, then
+ * silu(g) * u in fp32 rounded to fp16 as kllm_b200_silu_mul computes it.
+ * w_gate and w_up are [n, k] (n = intermediate size); out is [m, n]; the
+ * biases share bias_dtype and may each be NULL. Gate and up never reach
+ * memory. Same requirements and error flag as kllm_b200_linear. */
+int kllm_b200_linear_swiglu(const void* x, const void* w_gate, const void* w_up,
+                            const void* b_gate, const void* b_up, int bias_dtype, void* out,
+                            int64_t m, int64_t n, int64_t k, int32_t* err_flags, void* stream);
+
+/* ======================================================================== *
  *  Layer-op chain executor                                                  *
  * ======================================================================== */
 

@@ -101,6 +101,8 @@ SIGNATURES = {
                                        _i64, _int, _vp, _i64, _vp, _vp],
     "kllm_b200_chain_run": [ctypes.POINTER(Chain), ctypes.POINTER(ctypes.c_int), _vp],
     "kllm_b200_dequantize_int8_host_static": [_vp, _f32, _vp, _i64, _int, _vp],
+    "kllm_b200_linear": [_vp, _vp, _vp, _int, _vp, _i64, _i64, _i64, _vp, _vp],
+    "kllm_b200_linear_swiglu": [_vp, _vp, _vp, _vp, _vp, _int, _vp, _i64, _i64, _i64, _vp, _vp],
     # argtypes of the .kllm entry points use the structures in loader.py
     "kllm_b200_kllm_read_index": None,
     "kllm_b200_kllm_load": None,

@@ -149,6 +149,14 @@ __device__ __forceinline__ uint32_t f2_to_h2(float lo, float hi) {
 
 __device__ __forceinline__ float round_f16(float x) { return __half2float(__float2half_rn(x)); }
 
+// silu(g) = g * sigmoid(g) = g / (1 + e^-g). The exponent argument is capped
+// at 80 so 1 + e^-g stays finite; below g = -80 the result is ~1e-33, zero
+// in fp16 either way.
+__device__ __forceinline__ float silu(float g) {
+  const float e = __expf(fminf(-g, 80.0f));
+  return __fdividef(g, 1.0f + e);
+}
+
 template <int WIDTH>
 __device__ __forceinline__ float group_sum(float v) {
 #pragma unroll

@@ -1,0 +1,476 @@
+// gemm.cu — fp16 GEMM on the Blackwell tensor cores (tcgen05, TMA) with the
+// epilogues that follow it in a decoder layer fused in:
+//
+//   linear        out = fp16(fp16(x . w^T) + bias)   replaces linear() =
+//                 matmul + add_bias_inplace (src/model/llama.cpp:12-24;
+//                 cuda_matmul src/op/cuda/matmul.cu:130-160 and
+//                 cuda_add_bias_inplace src/op/cuda/add.cu:59-69)
+//   linear_swiglu out = silu_mul(linear(x, w_gate, b_gate), linear(x, w_up, b_up))
+//                 replaces the MLP's gate and up linears and silu_mul
+//                 (src/model/llama.cpp:145-158); gate and up never reach HBM.
+//
+// Layout: x [m, k] and w [n, k] row-major, both contiguous along k (the
+// reference's out[m, n] = a[m, k] * b[n, k]^T, src/op/cpu/matmul.cpp:9-33).
+// The epilogue rounds the fp32 accumulator to fp16 (round to nearest even,
+// as cuBLAS's fp16 output does), then adds the bias and rounds again, the
+// two roundings of matmul followed by add_bias_inplace; silu_mul then runs on
+// those fp16 values with the same arithmetic as kllm_b200_silu_mul, so the
+// fused op equals linear + linear + silu_mul of this library bit for bit.
+//
+// Kernel: persistent, one CTA per SM, 128 x 256 accumulator tiles (a SwiGLU
+// tile is 128 output columns: 128 gate rows and 128 up rows of w stacked as
+// the UMMA's N = 256). Warp 0 issues TMA loads of 64-wide k slices (128-byte
+// swizzle) into a 4-stage ring; warp 1 issues tcgen05.mma (M 128, N 256, K 16)
+// into one of two fp32 accumulators in tensor memory (2 x 256 columns); warps
+// 2-5 read the other accumulator back (tcgen05.ld, one row per thread), apply
+// the epilogue and store, so the epilogue of tile i overlaps the main loop of
+// tile i + 1. Tiles are visited in groups of 16 row tiles (all column tiles
+// of a group before the next group) so the CTAs in flight share x and w in L2.
+// Every mbarrier wait is bounded; a wait that runs out sets
+// KLLM_B200_FLAG_TIMEOUT and the CTA drains its copies and MMAs and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstring>
+#include <type_traits>
+
+#include "ops.cuh"
+#include "tcgen05.cuh"
+
+namespace kb {
+namespace {
+
+constexpr int kBM = 128;                      // tile rows: the UMMA M
+constexpr int kBN = 256;                      // the UMMA N: accumulator columns per tile
+constexpr int kBK = 64;                       // k per stage: one 128-byte swizzle panel of fp16
+constexpr int kStages = 4;
+constexpr int kABytes = kBM * kBK * 2;        // 16 KB
+constexpr int kBBytes = kBN * kBK * 2;        // 32 KB
+constexpr int kStageBytes = kABytes + kBBytes;
+constexpr uint32_t kTmemCols = 2 * kBN;       // two accumulators: all 512 columns
+constexpr int kEpiWarps = 4;
+constexpr int kThreads = (2 + kEpiWarps) * 32;
+constexpr int kGroupM = 16;                   // row tiles per raster group
+constexpr size_t kSmemBytes = static_cast<size_t>(kStages) * kStageBytes + 1024;  // + alignment slack
+
+// mbarriers: stage full (TMA bytes landed) / empty (MMAs that read it done);
+// accumulator full (tile's MMAs done) / empty (epilogue read it); final drain
+enum GemmBar {
+  kFull = 0,
+  kEmpty = kFull + kStages,
+  kAccFull = kEmpty + kStages,
+  kAccEmpty = kAccFull + 2,
+  kMmaDone = kAccEmpty + 2,
+  kNumBars = kMmaDone + 1
+};
+
+struct alignas(64) GemmArgs {
+  CUtensorMap map_a;   // x [m, k], box 64 x 128
+  CUtensorMap map_b;   // w [n, k] (SwiGLU: w_gate), box 64 x 256 (SwiGLU: 64 x 128)
+  CUtensorMap map_b2;  // SwiGLU: w_up, box 64 x 128
+  __half* out;         // [m, n]
+  const void* bias;    // [n] or NULL (SwiGLU: gate bias)
+  const void* bias2;   // SwiGLU: up bias or NULL
+  int32_t* err_flags;
+  int64_t m, n;        // output rows and columns
+  int m_tiles, n_tiles, k_blocks;
+  int vec_out;         // n % 8 == 0: 16-byte stores
+};
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+// 2-D tiled TMA load of the box at (x = k element, y = row) into shared
+// memory, completing `bytes` of the transaction count of `bar`.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_map(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// Row tile and column tile of persistent tile index `tile`: groups of kGroupM
+// row tiles, column-major inside a group.
+__device__ __forceinline__ void tile_coords(int tile, int m_tiles, int n_tiles, int& mt, int& nt) {
+  const int per_group = kGroupM * n_tiles;
+  const int g = tile / per_group;
+  const int first = g * kGroupM;
+  const int rows = min(kGroupM, m_tiles - first);
+  const int local = tile - g * per_group;
+  mt = first + local % rows;
+  nt = local / rows;
+}
+
+// Bias value of column c as float (fp16 or fp32 bias vector).
+template <typename TB>
+__device__ __forceinline__ float bias_at(const void* b, int64_t c) {
+  return to_f<TB>(static_cast<const TB*>(b)[c]);
+}
+
+// fp16(acc) and, with a bias, fp16(float(fp16(acc)) + bias): matmul's output
+// rounding followed by add_bias_inplace's.
+template <typename TB>
+__device__ __forceinline__ __half2 round_bias2(float lo, float hi, const void* bias, int64_t c) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  if (bias != nullptr) {
+    if constexpr (std::is_same<TB, __half>::value) {
+      // fp16 + fp16 summed in fp32 and rounded once to fp16 equals the packed
+      // fp16 add (fp32 carries >= 2 * 11 + 2 significand bits)
+      h = __hadd2(h, *reinterpret_cast<const __half2*>(static_cast<const __half*>(bias) + c));
+    } else {
+      const float2 f = __half22float2(h);
+      h = __floats2half2_rn(f.x + bias_at<TB>(bias, c), f.y + bias_at<TB>(bias, c + 1));
+    }
+  }
+  return h;
+}
+
+template <typename TB>
+__device__ __forceinline__ __half round_bias1(float v, const void* bias, int64_t c) {
+  __half h = __float2half_rn(v);
+  if (bias != nullptr) h = __float2half_rn(__half2float(h) + bias_at<TB>(bias, c));
+  return h;
+}
+
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+
+// 32 accumulator columns of one row -> out[row, c0 .. c0 + 31] (linear).
+template <typename TB>
+__device__ __forceinline__ void store_linear(const GemmArgs& a, int64_t row, int64_t c0, const float (&v)[32]) {
+  __half* orow = a.out + row * a.n;
+  if (a.vec_out && c0 + 32 <= a.n) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 w;
+      w.x = h2_bits(round_bias2<TB>(v[q * 8 + 0], v[q * 8 + 1], a.bias, c0 + q * 8 + 0));
+      w.y = h2_bits(round_bias2<TB>(v[q * 8 + 2], v[q * 8 + 3], a.bias, c0 + q * 8 + 2));
+      w.z = h2_bits(round_bias2<TB>(v[q * 8 + 4], v[q * 8 + 5], a.bias, c0 + q * 8 + 4));
+      w.w = h2_bits(round_bias2<TB>(v[q * 8 + 6], v[q * 8 + 7], a.bias, c0 + q * 8 + 6));
+      st_plain(orow + c0 + q * 8, w);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (c0 + j < a.n) orow[c0 + j] = round_bias1<TB>(v[j], a.bias, c0 + j);
+    }
+  }
+}
+
+// silu(fp16 gate) * fp16 up, rounded to fp16: the arithmetic of silu_mul.
+__device__ __forceinline__ __half2 swiglu2(__half2 g, __half2 u) {
+  const float2 gf = __half22float2(g), uf = __half22float2(u);
+  return __floats2half2_rn(silu(gf.x) * uf.x, silu(gf.y) * uf.y);
+}
+
+// 32 gate and 32 up accumulator columns of one row -> out[row, c0 .. c0 + 31].
+template <typename TB>
+__device__ __forceinline__ void store_swiglu(const GemmArgs& a, int64_t row, int64_t c0, const float (&g)[32],
+                                             const float (&u)[32]) {
+  __half* orow = a.out + row * a.n;
+  if (a.vec_out && c0 + 32 <= a.n) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint32_t w[4];
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        const int j = q * 8 + p * 2;
+        w[p] = h2_bits(swiglu2(round_bias2<TB>(g[j], g[j + 1], a.bias, c0 + j),
+                               round_bias2<TB>(u[j], u[j + 1], a.bias2, c0 + j)));
+      }
+      st_plain(orow + c0 + q * 8, make_uint4(w[0], w[1], w[2], w[3]));
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (c0 + j < a.n) {
+        const float gh = __half2float(round_bias1<TB>(g[j], a.bias, c0 + j));
+        const float uh = __half2float(round_bias1<TB>(u[j], a.bias2, c0 + j));
+        orow[c0 + j] = __float2half_rn(silu(gh) * uh);
+      }
+    }
+  }
+}
+
+template <bool kSwiGLU, typename TB>
+__global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_constant__ GemmArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  __shared__ __align__(8) uint64_t s_bar[kNumBars];
+  __shared__ uint32_t s_tmem;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;  // stage s: A at base + s * kStageBytes, then B
+  const int n_tiles_total = a.m_tiles * a.n_tiles;
+  constexpr int kOutCols = kSwiGLU ? kBN / 2 : kBN;  // output columns per tile
+  auto bar = [&](int i) { return smem_u32(&s_bar[i]); };
+
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(bar(kFull + s), 1);
+      mbar_init(bar(kEmpty + s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(bar(kAccFull + b), 1);
+      mbar_init(bar(kAccEmpty + b), kEpiWarps);
+    }
+    mbar_init(bar(kMmaDone), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    tma_prefetch_map(&a.map_a);
+    tma_prefetch_map(&a.map_b);
+    if (kSwiGLU) tma_prefetch_map(&a.map_b2);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+  // x may come from the previous kernel on the stream and out may be read by it
+  grid_dep_wait();
+  bool ok = true;
+
+  if (warp == 0) {
+    // ---------------- TMA producer: lane 0 ----------------
+    if (lane == 0) {
+      int it = 0;  // k slices issued by this CTA
+      for (int tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x) {
+        int mt, nt;
+        tile_coords(tile, a.m_tiles, a.n_tiles, mt, nt);
+        const int m0 = mt * kBM, n0 = nt * kOutCols;
+        for (int kb = 0; kb < a.k_blocks; ++kb, ++it) {
+          const int s = it % kStages;
+          if (it >= kStages) {  // the slice issued kStages ago into this stage has been consumed
+            ok = mbar_wait(bar(kEmpty + s), ((it / kStages) - 1) & 1);
+            if (!ok) break;
+          }
+          const uint32_t sa = base + s * kStageBytes, sb = sa + kABytes;
+          mbar_expect_tx(bar(kFull + s), kStageBytes);
+          tma_load_2d(sa, &a.map_a, kb * kBK, m0, bar(kFull + s));
+          if (kSwiGLU) {
+            tma_load_2d(sb, &a.map_b, kb * kBK, n0, bar(kFull + s));
+            tma_load_2d(sb + kBBytes / 2, &a.map_b2, kb * kBK, n0, bar(kFull + s));
+          } else {
+            tma_load_2d(sb, &a.map_b, kb * kBK, n0, bar(kFull + s));
+          }
+        }
+      }
+      // every copy issued has landed before the CTA may exit (on the normal
+      // path these phases completed long ago)
+      for (int j = it > kStages ? it - kStages : 0; j < it; ++j) {
+        if (!mbar_wait(bar(kFull + j % kStages), (j / kStages) & 1)) ok = false;
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issue: lane 0 ----------------
+    if (lane == 0) {
+      constexpr uint32_t kIdesc = umma_idesc(kBM, kBN, false);
+      const uint64_t adesc = umma_desc(base, 16, 1024);
+      const uint64_t bdesc = umma_desc(base + kABytes, 16, 1024);
+      int it = 0, i = 0;
+      for (int tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x, ++i) {
+        const int b = i & 1;
+        if (i >= 2) {  // the epilogue has read this accumulator's previous tile
+          ok = mbar_wait(bar(kAccEmpty + b), ((i >> 1) - 1) & 1);
+          if (!ok) break;
+          tc_fence_after();
+        }
+        const uint32_t d = tmem + b * kBN;
+        for (int kb = 0; kb < a.k_blocks; ++kb, ++it) {
+          const int s = it % kStages;
+          ok = mbar_wait(bar(kFull + s), (it / kStages) & 1);
+          if (!ok) break;
+          tc_fence_after();
+          const uint64_t so = static_cast<uint64_t>((s * kStageBytes) >> 4);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            // k step: 16 elements = 32 bytes along the swizzled 128-byte row
+            umma_f16(d, adesc + so + 2 * k, bdesc + so + 2 * k, kIdesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(bar(kEmpty + s));
+        }
+        if (!ok) break;
+        umma_commit(bar(kAccFull + b));
+      }
+      // no MMA is in flight when tensor memory is released
+      umma_commit(bar(kMmaDone));
+      if (!mbar_wait(bar(kMmaDone), 0)) ok = false;
+    }
+  } else {
+    // ---------------- epilogue: warps 2-5, one accumulator row per thread ----------------
+    const int quad = warp & 3;  // tensor-memory lanes 32 * quad .. + 31 are this warp's
+    const int r = quad * 32 + lane;
+    int i = 0;
+    for (int tile = blockIdx.x; tile < n_tiles_total; tile += gridDim.x, ++i) {
+      int mt, nt;
+      tile_coords(tile, a.m_tiles, a.n_tiles, mt, nt);
+      const int b = i & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(bar(kAccFull + b), (i >> 1) & 1));
+      if (!ok) break;
+      tc_fence_after();
+      const int64_t row = static_cast<int64_t>(mt) * kBM + r;
+      const int64_t n0 = static_cast<int64_t>(nt) * kOutCols;
+      const uint32_t t = tmem + (static_cast<uint32_t>(quad * 32) << 16) + b * kBN;
+      if constexpr (!kSwiGLU) {
+#pragma unroll 1
+        for (int c = 0; c < kBN / 32; ++c) {
+          float v[32];
+          tmem_ld32(t + c * 32, v);
+          tc_wait_ld();
+          if (row < a.m) store_linear<TB>(a, row, n0 + c * 32, v);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < kBN / 64; ++c) {
+          float g[32], u[32];
+          tmem_ld32(t + c * 32, g);
+          tmem_ld32(t + kBN / 2 + c * 32, u);
+          tc_wait_ld();
+          if (row < a.m) store_swiglu<TB>(a, row, n0 + c * 32, g, u);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kAccEmpty + b));
+    }
+  }
+
+  if (!ok) set_flag(a.err_flags, KLLM_B200_FLAG_TIMEOUT);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
+// cuTensorMapEncodeTiled from the driver, through the runtime (no libcuda link).
+PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      p = nullptr;
+    }
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+
+// Tensor map of a row-major fp16 [rows, k] matrix read in boxes of 64 (k) x
+// box_rows, 128-byte swizzled; reads past the edges return zeros.
+int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t k, int box_rows, const char* what) {
+  auto fn = encode_tiled();
+  if (fn == nullptr) return fail(KLLM_B200_ERR_CUDA, "%s: cuTensorMapEncodeTiled unavailable", what);
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(k) * 2};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t elem[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, elem,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(KLLM_B200_ERR_INVALID_ARG, "%s: tensor map rejected (CUresult %d)", what, (int)r);
+  return KLLM_B200_OK;
+}
+
+int check_gemm_args(const char* what, const void* x, const void* w, const void* w2, const void* bias,
+                    const void* bias2, int bias_dtype, const void* out, int64_t m, int64_t n, int64_t k,
+                    bool swiglu) {
+  if (m < 0 || n < 0 || k < 0) return fail(KLLM_B200_ERR_INVALID_ARG, "%s: negative size", what);
+  if ((bias || bias2) && bias_dtype != KLLM_B200_F16 && bias_dtype != KLLM_B200_F32) {
+    return fail(KLLM_B200_ERR_DTYPE, "%s: bias dtype %d not supported (F32, F16)", what, bias_dtype);
+  }
+  if (m == 0 || n == 0) return KLLM_B200_OK;
+  if (k == 0) return fail(KLLM_B200_ERR_SHAPE, "%s: k must be positive", what);
+  if (k % 8 != 0) return fail(KLLM_B200_ERR_SHAPE, "%s: k = %lld is not a multiple of 8", what, (long long)k);
+  if (k > (1LL << 31) || m > (1LL << 31) || n > (1LL << 31)) {
+    return fail(KLLM_B200_ERR_SHAPE, "%s: dimension too large", what);
+  }
+  if (!x || !w || !out || (swiglu && !w2)) return fail(KLLM_B200_ERR_INVALID_ARG, "%s: null pointer", what);
+  if (!aligned16(x) || !aligned16(w) || !aligned16(out) || (swiglu && !aligned16(w2))) {
+    return fail(KLLM_B200_ERR_ALIGN, "%s: x, weights and out must be 16-byte aligned", what);
+  }
+  if ((bias && (reinterpret_cast<uintptr_t>(bias) & 3u)) || (bias2 && (reinterpret_cast<uintptr_t>(bias2) & 3u))) {
+    return fail(KLLM_B200_ERR_ALIGN, "%s: biases must be 4-byte aligned", what);
+  }
+  return KLLM_B200_OK;
+}
+
+template <bool kSwiGLU, typename TB>
+int launch_gemm(GemmArgs& a, const LaunchOpts& o, const char* what) {
+  auto kernel = gemm_tc_kernel<kSwiGLU, TB>;
+  cudaError_t err = allow_smem(reinterpret_cast<const void*>(kernel), kSmemBytes);
+  if (err != cudaSuccess) return launch_status(err, what);
+  const int64_t tiles = static_cast<int64_t>(a.m_tiles) * a.n_tiles;
+  const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
+  err = launch(kernel, dim3(grid), dim3(kThreads), kSmemBytes, o.stream, o.pdl, a);
+  return launch_status(err, what);
+}
+
+int run_gemm(const void* x, const void* w, const void* w2, const void* bias, const void* bias2, int bias_dtype,
+             void* out, int64_t m, int64_t n, int64_t k, int32_t* err_flags, bool swiglu, const LaunchOpts& o) {
+  const char* what = swiglu ? "linear_swiglu" : "linear";
+  int rc = check_gemm_args(what, x, w, w2, bias, bias2, bias_dtype, out, m, n, k, swiglu);
+  if (rc != KLLM_B200_OK || m == 0 || n == 0) return rc;
+  const int out_cols = swiglu ? kBN / 2 : kBN;
+  const int64_t m_tiles = (m + kBM - 1) / kBM, n_tiles = (n + out_cols - 1) / out_cols;
+  if (m_tiles * n_tiles > 0x7fffffffLL) return fail(KLLM_B200_ERR_SHAPE, "%s: too many tiles", what);
+  GemmArgs a;
+  memset(&a, 0, sizeof(a));
+  if ((rc = make_map(&a.map_a, x, m, k, kBM, what)) != KLLM_B200_OK) return rc;
+  if ((rc = make_map(&a.map_b, w, n, k, swiglu ? kBN / 2 : kBN, what)) != KLLM_B200_OK) return rc;
+  if (swiglu && (rc = make_map(&a.map_b2, w2, n, k, kBN / 2, what)) != KLLM_B200_OK) return rc;
+  a.out = static_cast<__half*>(out);
+  a.bias = bias;
+  a.bias2 = bias2;
+  a.err_flags = err_flags;
+  a.m = m;
+  a.n = n;
+  a.m_tiles = static_cast<int>(m_tiles);
+  a.n_tiles = static_cast<int>(n_tiles);
+  a.k_blocks = static_cast<int>((k + kBK - 1) / kBK);
+  a.vec_out = n % 8 == 0;
+  const bool f32_bias = (bias || bias2) && bias_dtype == KLLM_B200_F32;
+  if (swiglu) {
+    return f32_bias ? launch_gemm<true, float>(a, o, what) : launch_gemm<true, __half>(a, o, what);
+  }
+  return f32_bias ? launch_gemm<false, float>(a, o, what) : launch_gemm<false, __half>(a, o, what);
+}
+
+}  // namespace
+
+int linear(const void* x, const void* w, const void* bias, int bias_dtype, void* out, int64_t m, int64_t n,
+           int64_t k, int32_t* err_flags, const LaunchOpts& o) {
+  return run_gemm(x, w, nullptr, bias, nullptr, bias_dtype, out, m, n, k, err_flags, false, o);
+}
+
+int linear_swiglu(const void* x, const void* w_gate, const void* w_up, const void* b_gate, const void* b_up,
+                  int bias_dtype, void* out, int64_t m, int64_t n, int64_t k, int32_t* err_flags,
+                  const LaunchOpts& o) {
+  return run_gemm(x, w_gate, w_up, b_gate, b_up, bias_dtype, out, m, n, k, err_flags, true, o);
+}
+
+}  // namespace kb
+
+extern "C" int kllm_b200_linear(const void* x, const void* w, const void* bias, int bias_dtype, void* out,
+                                int64_t m, int64_t n, int64_t k, int32_t* err_flags, void* stream) {
+  kb::LaunchOpts o;
+  o.stream = static_cast<cudaStream_t>(stream);
+  return kb::linear(x, w, bias, bias_dtype, out, m, n, k, err_flags, o);
+}
+
+extern "C" int kllm_b200_linear_swiglu(const void* x, const void* w_gate, const void* w_up, const void* b_gate,
+                                       const void* b_up, int bias_dtype, void* out, int64_t m, int64_t n,
+                                       int64_t k, int32_t* err_flags, void* stream) {
+  kb::LaunchOpts o;
+  o.stream = static_cast<cudaStream_t>(stream);
+  return kb::linear_swiglu(x, w_gate, w_up, b_gate, b_up, bias_dtype, out, m, n, k, err_flags, o);
+}

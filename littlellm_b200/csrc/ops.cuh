@@ -38,6 +38,15 @@ int dequantize_int8_rne(const int8_t* data, const float* scale, void* out, int64
 int select_last_rows(const void* x, int64_t rows, int64_t cols, const int32_t* seq_ends, int64_t seq_len,
                      int64_t n_seqs, void* out, int dtype, int32_t* err_flags, const LaunchOpts& o);
 
+// out = fp16(fp16(x . w^T) + bias) on tcgen05 (gemm.cu).
+int linear(const void* x, const void* w, const void* bias, int bias_dtype, void* out, int64_t m, int64_t n,
+           int64_t k, int32_t* err_flags, const LaunchOpts& o);
+
+// out = silu_mul(linear(x, w_gate, b_gate), linear(x, w_up, b_up)) in one kernel (gemm.cu).
+int linear_swiglu(const void* x, const void* w_gate, const void* w_up, const void* b_gate, const void* b_up,
+                  int bias_dtype, void* out, int64_t m, int64_t n, int64_t k, int32_t* err_flags,
+                  const LaunchOpts& o);
+
 int attention_workspace_bytes(int64_t n_tokens, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim,
                               int64_t max_seq, int64_t* bytes);
 

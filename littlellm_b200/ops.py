@@ -4,7 +4,8 @@ One function per operator of the reference interface
 (``include/kllm/op/ops.h:10-35``: embedding, rms_norm, add_bias_inplace,
 add_inplace, select_last_row, silu_mul, rope_inplace, copy_kv_to_cache,
 dequantize_int8) plus the fused/batched entry points (add_rms_norm,
-qkv_bias_rope_kv_append, select_last_rows). Each takes CUDA tensors, passes
+qkv_bias_rope_kv_append, select_last_rows, attention_head_major, linear,
+linear_swiglu). Each takes CUDA tensors, passes
 their device pointers to ``libkllm_b200.so`` on the tensor's current stream
 and raises ``KllmError`` with the library's message on a non-zero status,
 the way the reference throws ``std::runtime_error``.
@@ -194,6 +195,52 @@ def silu_mul(gate: torch.Tensor, up: torch.Tensor, out: torch.Tensor | None = No
     with torch.cuda.device(dev):
         check(lib.kllm_b200_silu_mul(_ptr(gate), _ptr(up), _ptr(out), gate.numel(),
                                      dtype_code(gate), _stream(dev)))
+    return out
+
+
+def _gemm_checks(x: torch.Tensor, weights, out: torch.Tensor, biases):
+    if x.dim() != 2 or any(w.dim() != 2 for w in weights):
+        raise KllmError(_capi.ERR_SHAPE, "linear: x and weights must be 2-D")
+    if any(t.dtype != torch.float16 for t in (x, out, *weights)):
+        raise KllmError(_capi.ERR_DTYPE, "linear: x, weights and out must be float16")
+    n, k = weights[0].shape
+    if x.shape[1] != k or any(w.shape != (n, k) for w in weights) or out.shape != (x.shape[0], n):
+        raise KllmError(_capi.ERR_SHAPE, "linear shape mismatch")
+    present = [b for b in biases if b is not None]
+    if any(b.numel() != n for b in present):
+        raise KllmError(_capi.ERR_SHAPE, "linear: bias length must equal the output columns")
+    if len({b.dtype for b in present}) > 1:
+        raise KllmError(_capi.ERR_DTYPE, "linear_swiglu: biases must share a dtype")
+    return dtype_code(present[0]) if present else F16
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
+           out: torch.Tensor | None = None, err_flags: torch.Tensor | None = None) -> torch.Tensor:
+    """out = fp16(fp16(x @ w.T) + bias): the reference linear() (matmul +
+    add_bias_inplace) as one tcgen05 GEMM. x [m, k], w [n, k] fp16."""
+    if out is None:
+        out = torch.empty(x.shape[0], w.shape[0], dtype=torch.float16, device=x.device)
+    dev = _dev(x, w, bias, out, err_flags)
+    bias_dtype = _gemm_checks(x, [w], out, [bias])
+    with torch.cuda.device(dev):
+        check(lib.kllm_b200_linear(_ptr(x), _ptr(w), _ptr(bias), bias_dtype, _ptr(out), x.shape[0],
+                                   w.shape[0], x.shape[1], _ptr(err_flags), _stream(dev)))
+    return out
+
+
+def linear_swiglu(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor,
+                  b_gate: torch.Tensor | None = None, b_up: torch.Tensor | None = None,
+                  out: torch.Tensor | None = None, err_flags: torch.Tensor | None = None) -> torch.Tensor:
+    """out = silu_mul(linear(x, w_gate, b_gate), linear(x, w_up, b_up)) in one
+    kernel; w_gate and w_up [n, k] fp16."""
+    if out is None:
+        out = torch.empty(x.shape[0], w_gate.shape[0], dtype=torch.float16, device=x.device)
+    dev = _dev(x, w_gate, w_up, b_gate, b_up, out, err_flags)
+    bias_dtype = _gemm_checks(x, [w_gate, w_up], out, [b_gate, b_up])
+    with torch.cuda.device(dev):
+        check(lib.kllm_b200_linear_swiglu(_ptr(x), _ptr(w_gate), _ptr(w_up), _ptr(b_gate), _ptr(b_up),
+                                          bias_dtype, _ptr(out), x.shape[0], w_gate.shape[0], x.shape[1],
+                                          _ptr(err_flags), _stream(dev)))
     return out
 
 

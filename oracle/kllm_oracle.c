@@ -141,6 +141,21 @@ void kllm_oracle_select_last_row(const float* x, int64_t rows, int64_t cols, flo
   memcpy(out, x + (rows - 1) * cols, (size_t)cols * sizeof(float));
 }
 
+/* cpu_matmul (src/op/cpu/matmul.cpp:9-33): out[r, c] = sum over i = 0..k-1,
+ * in that order, of a[r, i] * b[c, i], accumulated in one fp32 variable
+ * (b is [n, k]: the weight layout linear() passes, src/model/llama.cpp:12-24). */
+void kllm_oracle_matmul(const float* a, const float* b, float* out, int64_t m, int64_t n, int64_t k) {
+  for (int64_t r = 0; r < m; ++r) {
+    const float* ar = a + r * k;
+    for (int64_t c = 0; c < n; ++c) {
+      const float* bc = b + c * k;
+      float sum = 0.0f;
+      for (int64_t i = 0; i < k; ++i) sum += ar[i] * bc[i];
+      out[r * n + c] = sum;
+    }
+  }
+}
+
 /* cpu_silu_mul (src/op/cpu/silu.cpp:9-20) with sigmoid from
  * include/kllm/op/detail/cpu_helpers.h:19-21: (g * (1 / (1 + exp(-g)))) * u. */
 void kllm_oracle_silu_mul(const float* gate, const float* up, float* out, int64_t n) {

@@ -34,6 +34,7 @@ void kllm_oracle_rms_norm(const float* x, const float* weight, float* out, int64
 void kllm_oracle_add_inplace(float* x, const float* y, int64_t n);
 void kllm_oracle_add_bias_inplace(float* x, const float* bias, int64_t rows, int64_t cols);
 void kllm_oracle_select_last_row(const float* x, int64_t rows, int64_t cols, float* out);
+void kllm_oracle_matmul(const float* a, const float* b, float* out, int64_t m, int64_t n, int64_t k);
 void kllm_oracle_silu_mul(const float* gate, const float* up, float* out, int64_t n);
 void kllm_oracle_rope_inplace(float* x, int64_t seq, int64_t heads, int64_t head_dim,
                               int32_t past_len, float theta);

@@ -99,6 +99,7 @@ class Oracle:
         lib.kllm_oracle_select_last_rows.restype = ctypes.c_int
         lib.kllm_oracle_select_last_rows.argtypes = [_c_f32p, _c_i64, _c_i64, _c_i32p, _c_i64,
                                                      _c_i64, _c_f32p]
+        lib.kllm_oracle_matmul.argtypes = [_c_f32p, _c_f32p, _c_f32p, _c_i64, _c_i64, _c_i64]
         lib.kllm_oracle_attention.argtypes = [_c_f32p, _c_f32p, _c_f32p, _c_f32p, _c_i64,
                                               ctypes.c_int32, _c_i64, _c_i64, _c_i64]
         lib.kllm_oracle_attention_head_major.restype = ctypes.c_int64
@@ -157,6 +158,24 @@ class Oracle:
         out = np.empty((1, x.shape[1]), dtype=np.float32)
         self.lib.kllm_oracle_select_last_row(_ptr(x, _c_f32p), x.shape[0], x.shape[1],
                                              _ptr(out, _c_f32p))
+        return out
+
+    def matmul(self, a, b) -> np.ndarray:
+        """a [m, k] times b [n, k] transposed, fp32 (cpu_matmul)."""
+        a, b = _f32(a), _f32(b)
+        if a.shape[1] != b.shape[1]:
+            raise ValueError("matmul shape mismatch")
+        out = np.empty((a.shape[0], b.shape[0]), dtype=np.float32)
+        self.lib.kllm_oracle_matmul(_ptr(a, _c_f32p), _ptr(b, _c_f32p), _ptr(out, _c_f32p), a.shape[0],
+                                    b.shape[0], a.shape[1])
+        return out
+
+    def linear(self, x, w, bias=None) -> np.ndarray:
+        """linear() of src/model/llama.cpp:12-24 in fp32: matmul, then
+        add_bias_inplace."""
+        out = self.matmul(x, w)
+        if bias is not None:
+            out = self.add_bias(out, bias)
         return out
 
     def silu_mul(self, g, u) -> np.ndarray:
@@ -286,6 +305,7 @@ class Reference:
         lib.kref_add_bias_inplace.argtypes = [vp, vp, i64, i64, i32]
         lib.kref_select_last_row.argtypes = [vp, i64, i64, vp, i32]
         lib.kref_silu_mul.argtypes = [vp, vp, vp, i64, i32]
+        lib.kref_matmul.argtypes = [vp, vp, vp, i64, i64, i64, i32]
         lib.kref_rope_inplace.argtypes = [vp, i64, i64, i64, i32, ctypes.c_float, i32]
         lib.kref_copy_kv_to_cache.argtypes = [vp, vp, i64, i64, i64, vp, vp, i64, i32, i32]
         lib.kref_attention.argtypes = [vp, vp, vp, vp, i64, i64, i32, i32, i32, i32, i32]
@@ -360,6 +380,14 @@ class Reference:
         out = np.empty((1, x.shape[1]), dtype=x.dtype)
         self._check(self.lib.kref_select_last_row(self._vp(x), x.shape[0], x.shape[1],
                                                   self._vp(out), dtype))
+        return out
+
+    def matmul(self, a, b, dtype: int = F32):
+        """kllm::op::matmul: a [m, k] times b [n, k] transposed."""
+        a, b = self._buf(a, dtype), self._buf(b, dtype)
+        out = np.empty((a.shape[0], b.shape[0]), dtype=a.dtype)
+        self._check(self.lib.kref_matmul(self._vp(a), self._vp(b), self._vp(out), a.shape[0], b.shape[0],
+                                         a.shape[1], dtype))
         return out
 
     def silu_mul(self, g, u, dtype: int = F32):

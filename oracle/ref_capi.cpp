@@ -157,6 +157,19 @@ int kref_select_last_row(const void* x, std::int64_t rows, std::int64_t cols, vo
   });
 }
 
+// kllm::op::matmul on the CPU (cpu_matmul, src/op/cpu/matmul.cpp:9-33):
+// out [m, n] = a [m, k] * b [n, k]^T.
+int kref_matmul(const void* a, const void* b, void* out, std::int64_t m, std::int64_t n, std::int64_t k,
+                int dtype) {
+  return guarded([&] {
+    auto at = make_tensor({m, k}, dtype, a);
+    auto bt = make_tensor({n, k}, dtype, b);
+    auto ot = make_tensor({m, n}, dtype, nullptr);
+    kllm::op::matmul(at, bt, ot);
+    read_back(ot, out);
+  });
+}
+
 int kref_silu_mul(const void* g, const void* u, void* out, std::int64_t n, int dtype) {
   return guarded([&] {
     auto gt = make_tensor({n}, dtype, g);

@@ -147,6 +147,29 @@ def main(out_path: str = os.path.join(HERE, "golden.npz")) -> None:
     g["f2h_in"] = vals
     g["f2h_out"] = ref.float_to_half_bits(vals)
 
+    # linear() = matmul + add_bias_inplace (src/model/llama.cpp:12-24) and the
+    # MLP's gate/up linears + silu_mul (src/model/llama.cpp:145-158), F32. A
+    # separate stream keeps the fixtures above unchanged. k = 72 and 96 are not
+    # multiples of the kernel's 64-wide k slices; m and n are partial tiles.
+    rng2 = np.random.default_rng(SEED + 1)
+    m, n, k = 24, 40, 72
+    x = f16r(rng2.normal(0, 1, (m, k)))
+    w = f16r(rng2.normal(0, 1, (n, k)) / np.sqrt(k))
+    b = f16r(rng2.normal(0, 0.1, n))
+    g["mm_x"], g["mm_w"], g["mm_b"] = x, w, b
+    g["mm_out"] = ref.matmul(x, w, F32)
+    g["lin_out"] = ref.add_bias(g["mm_out"], b, F32)
+    m, n, k = 20, 48, 96
+    x = f16r(rng2.normal(0, 1, (m, k)))
+    wg = f16r(rng2.normal(0, 1, (n, k)) / np.sqrt(k))
+    wu = f16r(rng2.normal(0, 1, (n, k)) / np.sqrt(k))
+    bg = f16r(rng2.normal(0, 0.1, n))
+    bu = f16r(rng2.normal(0, 0.1, n))
+    g.update(mlp_x=x, mlp_wg=wg, mlp_wu=wu, mlp_bg=bg, mlp_bu=bu)
+    gate = ref.add_bias(ref.matmul(x, wg, F32), bg, F32)
+    up = ref.add_bias(ref.matmul(x, wu, F32), bu, F32)
+    g["mlp_out"] = ref.silu_mul(gate, up, F32)
+
     np.savez_compressed(out_path, **g)
     print(f"wrote {out_path}: {len(g)} arrays, {os.path.getsize(out_path)} bytes")
 

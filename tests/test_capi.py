@@ -165,3 +165,32 @@ def test_chain_attention_needs_context_buffers(capi):
     c.layers = ctypes.cast(layers, ctypes.POINTER(capi.LayerBuffers))
     assert capi.lib.kllm_b200_chain_run(ctypes.byref(c), None, None) == capi.ERR_INVALID_ARG
     assert "attn_ctx" in capi.last_error()
+
+
+def test_gemm_validation_without_gpu(capi):
+    """kllm_b200_linear / kllm_b200_linear_swiglu reject bad sizes, pointers,
+    alignment and bias dtypes on the host, before any CUDA call; an empty
+    output is a successful no-op."""
+    lib = capi.lib
+    p = 16  # non-null and 16-byte aligned; nothing is dereferenced before validation fails
+    cases = [  # (x, w, bias, bias_dtype, out, m, n, k)
+        ((p, p, None, capi.F16, p, -1, 8, 8), capi.ERR_INVALID_ARG, "negative"),
+        ((p, p, None, capi.F16, p, 4, 8, 0), capi.ERR_SHAPE, "positive"),
+        ((p, p, None, capi.F16, p, 4, 8, 12), capi.ERR_SHAPE, "multiple of 8"),
+        ((None, p, None, capi.F16, p, 4, 8, 8), capi.ERR_INVALID_ARG, "null"),
+        ((p + 8, p, None, capi.F16, p, 4, 8, 8), capi.ERR_ALIGN, "aligned"),
+        ((p, p, p + 2, capi.F16, p, 4, 8, 8), capi.ERR_ALIGN, "bias"),
+        ((p, p, p, capi.I32, p, 4, 8, 8), capi.ERR_DTYPE, "bias dtype"),
+    ]
+    for args, status, word in cases:
+        rc = lib.kllm_b200_linear(*args, None, None)
+        assert rc == status, (args, rc, capi.last_error())
+        assert word in capi.last_error()
+    assert lib.kllm_b200_linear(p, p, None, capi.F16, p, 0, 8, 8, None, None) == capi.OK
+    assert lib.kllm_b200_linear(p, p, None, capi.F16, p, 4, 0, 8, None, None) == capi.OK
+    # the SwiGLU form also needs the up weight
+    rc = lib.kllm_b200_linear_swiglu(p, p, None, None, None, capi.F16, p, 4, 8, 8, None, None)
+    assert rc == capi.ERR_INVALID_ARG and "null" in capi.last_error()
+    rc = lib.kllm_b200_linear_swiglu(p, p, p + 8, None, None, capi.F16, p, 4, 8, 8, None, None)
+    assert rc == capi.ERR_ALIGN
+    assert lib.kllm_b200_linear_swiglu(p, p, p, None, None, capi.F16, p, 0, 8, 8, None, None) == capi.OK

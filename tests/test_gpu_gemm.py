@@ -1,0 +1,136 @@
+"""tcgen05 GEMM with fused epilogues (scope row f4) against the oracle:
+linear() = matmul + add_bias_inplace and the MLP's gate/up linears +
+silu_mul, on the reference's known-answer test, the golden fixtures of the
+compiled reference, seeded shapes against the C oracle (ragged m, n and k,
+fp16 and fp32 biases), model shapes against a torch fp32 reference, and the
+fused SwiGLU against this library's own linear + linear + silu_mul bit for
+bit."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import TOL, assert_tol, bits16, dev, f16r, host
+
+pytestmark = pytest.mark.gpu
+
+
+def _inputs(rng, m, n, k, n_weights=1):
+    x = f16r(rng.standard_normal((m, k)))
+    ws = [f16r(rng.standard_normal((n, k)) / np.sqrt(k)) for _ in range(n_weights)]
+    return x, ws
+
+
+def test_reference_kat(cuda, ops):
+    # tests/test_matmul.cpp:7-13 and tests/test_ops.cpp:59-68; k is padded from
+    # 3 to 8 with zeros (the kernel takes k in multiples of 8), which leaves
+    # every dot product unchanged
+    a = np.zeros((2, 8), np.float32)
+    b = np.zeros((2, 8), np.float32)
+    a[:, :3] = [[1, 2, 3], [4, 5, 6]]
+    b[:, :3] = [[1, 0, 1], [0, 1, 1]]
+    out = ops.linear(dev(a), dev(b))
+    assert np.array_equal(host(out), [[4, 5], [10, 11]])
+    out = ops.linear(dev(a), dev(b), dev([1, -1]))
+    assert np.array_equal(host(out), [[5, 4], [11, 10]])
+    out = ops.linear(dev(a), dev(b), dev([1, -1], torch.float32))
+    assert np.array_equal(host(out), [[5, 4], [11, 10]])
+
+
+def test_golden_linear_and_mlp(cuda, ops, golden):
+    g = golden
+    assert_tol(host(ops.linear(dev(g["mm_x"]), dev(g["mm_w"]))), g["mm_out"], what="matmul")
+    assert_tol(host(ops.linear(dev(g["mm_x"]), dev(g["mm_w"]), dev(g["mm_b"]))), g["lin_out"], what="linear")
+    out = ops.linear_swiglu(dev(g["mlp_x"]), dev(g["mlp_wg"]), dev(g["mlp_wu"]), dev(g["mlp_bg"]),
+                            dev(g["mlp_bu"]))
+    assert_tol(host(out), g["mlp_out"], what="linear_swiglu")
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 256, 64), (128, 256, 64), (130, 300, 136), (256, 512, 896),
+                                   (513, 1152, 896), (77, 203, 200)])
+@pytest.mark.parametrize("bias", [None, torch.float16, torch.float32])
+def test_linear_vs_oracle(cuda, ops, oracle, m, n, k, bias):
+    rng = np.random.default_rng(m * 7 + n * 3 + k)
+    x, (w,) = _inputs(rng, m, n, k)
+    b = f16r(rng.normal(0, 0.1, n)) if bias is not None else None
+    out = ops.linear(dev(x), dev(w), dev(b, bias) if bias is not None else None)
+    want = oracle.linear(x, w, b)
+    assert_tol(host(out), want, what=f"linear {m}x{n}x{k}")
+
+
+@pytest.mark.parametrize("m,n,k", [(5, 128, 64), (300, 640, 896), (129, 203, 136), (1, 4864, 896)])
+@pytest.mark.parametrize("bias", [None, torch.float16, torch.float32])
+def test_swiglu_vs_oracle_and_unfused(cuda, ops, oracle, m, n, k, bias):
+    rng = np.random.default_rng(m * 11 + n + k * 5)
+    x, (wg, wu) = _inputs(rng, m, n, k, 2)
+    bg = f16r(rng.normal(0, 0.1, n)) if bias is not None else None
+    bu = f16r(rng.normal(0, 0.1, n)) if bias is not None else None
+    tb = (lambda a: dev(a, bias)) if bias is not None else (lambda a: None)
+    xd, wgd, wud, bgd, bud = dev(x), dev(wg), dev(wu), tb(bg), tb(bu)
+    fused = ops.linear_swiglu(xd, wgd, wud, bgd, bud)
+    want = oracle.silu_mul(oracle.linear(x, wg, bg), oracle.linear(x, wu, bu))
+    assert_tol(host(fused), want, what=f"linear_swiglu {m}x{n}x{k}")
+    # the same values as the separate ops of this library, bit for bit
+    unfused = ops.silu_mul(ops.linear(xd, wgd, bgd), ops.linear(xd, wud, bud))
+    torch.cuda.synchronize()
+    assert np.array_equal(bits16(fused), bits16(unfused))
+
+
+@pytest.mark.parametrize("what,m,n,k", [
+    ("qwen qkv linear", 4096, 1152, 896),
+    ("qwen gate/up + silu", 4096, 4864, 896),
+    ("llama gate/up + silu", 512, 11008, 4096),
+    ("llama down linear", 300, 4096, 11008),
+])
+def test_model_shapes_vs_torch_fp32(cuda, ops, what, m, n, k):
+    g = torch.Generator(device=cuda).manual_seed(m + n + k)
+    x = torch.randn(m, k, device=cuda, generator=g).half()
+    w = (torch.randn(n, k, device=cuda, generator=g) / k ** 0.5).half()
+    b = (torch.randn(n, device=cuda, generator=g) * 0.1).half()
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    ref = x.float() @ w.float().T + b.float()
+    if "silu" in what:
+        w2 = (torch.randn(n, k, device=cuda, generator=g) / k ** 0.5).half()
+        b2 = (torch.randn(n, device=cuda, generator=g) * 0.1).half()
+        out = ops.linear_swiglu(x, w, w2, b, b2, err_flags=err)
+        up = x.float() @ w2.float().T + b2.float()
+        ref = ref * torch.sigmoid(ref) * up
+    else:
+        out = ops.linear(x, w, b, err_flags=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    diff = (out.float() - ref).abs()
+    bad = diff > TOL + TOL * ref.abs()
+    assert not bool(bad.any()), f"{what}: {int(bad.sum())} outside tolerance, max abs err {float(diff.max()):.3g}"
+
+
+def test_output_bounds_and_ragged_columns(cuda, ops, oracle):
+    """Only out[m, n] is written: rows past m (a partial 128-row tile) and, for
+    n not a multiple of 8, the element-wise edge path stay in bounds."""
+    rng = np.random.default_rng(3)
+    m, n, k = 130, 203, 72
+    x, (wg, wu) = _inputs(rng, m, n, k, 2)
+    whole = torch.full(((m + 2) * n,), -1234.0, dtype=torch.float16, device=cuda)
+    out = whole[: m * n].view(m, n)
+    ops.linear(dev(x), dev(wg), out=out)
+    torch.cuda.synchronize()
+    assert bool((whole[m * n:] == -1234.0).all())
+    assert_tol(host(out), oracle.matmul(x, wg), what="ragged linear")
+    whole.fill_(-1234.0)
+    ops.linear_swiglu(dev(x), dev(wg), dev(wu), out=out)
+    torch.cuda.synchronize()
+    assert bool((whole[m * n:] == -1234.0).all())
+    assert_tol(host(out), oracle.silu_mul(oracle.matmul(x, wg), oracle.matmul(x, wu)), what="ragged swiglu")
+
+
+def test_repeated_calls_are_deterministic(cuda, ops):
+    g = torch.Generator(device=cuda).manual_seed(9)
+    x = torch.randn(1000, 896, device=cuda, generator=g).half()
+    wg = (torch.randn(4864, 896, device=cuda, generator=g) / 30).half()
+    wu = (torch.randn(4864, 896, device=cuda, generator=g) / 30).half()
+    first = ops.linear_swiglu(x, wg, wu)
+    for _ in range(3):
+        again = ops.linear_swiglu(x, wg, wu)
+        torch.cuda.synchronize()
+        assert torch.equal(first, again)
