@@ -349,6 +349,8 @@ def run_reference(args):
         return run_reference_dequant(args)
     if args.workload in ATTENTION_WORKLOADS:
         return run_reference_attention(args)
+    if args.workload in GEMM_WORKLOADS:
+        return run_reference_gemm(args)
     if args.workload == "llama_int8_load":
         return run_reference_load(args)
     w = WORKLOADS[args.workload]
@@ -973,12 +975,304 @@ def run_reference_attention(args):
           "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
 
 
-def load_tc_peak() -> dict:
+def load_tc_peak(sustained: bool = False) -> dict:
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
         with open(path) as f:
-            return {"tflops": float(json.load(f)["bf16_tflops"]), "source": "measured (cuBLAS bf16 burst)"}
-    return {"tflops": 1590.0, "source": "fallback"}
+            p = json.load(f)
+        if sustained and "bf16_tflops_sustained" in p:
+            return {"tflops": float(p["bf16_tflops_sustained"]), "source": "measured (cuBLAS bf16 sustained)"}
+        return {"tflops": float(p["bf16_tflops"]), "source": "measured (cuBLAS bf16 burst)"}
+    return {"tflops": 1400.0 if sustained else 1590.0, "source": "fallback"}
+
+
+# ---------------------------------------------------------------------------
+# scope row f4: the MLP's gate/up GEMM with the SwiGLU epilogue fused
+# ---------------------------------------------------------------------------
+
+GEMM_WORKLOADS = {
+    # Qwen2.5-0.5B, 8 x 512 tokens: x [4096, 896] @ [w_gate; w_up] [2 x 4864, 896]^T -> silu_mul, 24 layers
+    "qwen_mlp_gemm": "qwen_prefill",
+    # Llama-2-7B, 32 x 512 tokens: x [16384, 4096] @ [2 x 11008, 4096]^T -> silu_mul, 32 layers
+    "llama_mlp_gemm": "llama_prefill",
+}
+GEMM_METRIC = "MLP gate/up+SwiGLU tokens/s"
+
+
+def time_reference_mlp(m, n_layers: int, threads: int, seconds: float, rows: int, steps: int | None = None,
+                       warmup: int = 0):
+    """The reference's linear() + silu_mul on the CPU (kllm::op::matmul, CPU
+    F32 tensors; no MLP bias in either model) for `rows` token rows per
+    thread through every layer, one layer's weights reused for all layers (at
+    these sizes the weights stream from DRAM either way). Returns (tokens/s,
+    per-step seconds, kind)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    import numpy as np
+
+    from oracle.oracle import Reference, reference_available
+    if not reference_available():
+        raise RuntimeError("compiled reference (oracle/_ref) not available")
+    ref = Reference()
+    rng = np.random.default_rng(0)
+    wg = (rng.standard_normal((m.intermediate, m.hidden)) / np.sqrt(m.hidden)).astype(np.float32)
+    wu = (rng.standard_normal((m.intermediate, m.hidden)) / np.sqrt(m.hidden)).astype(np.float32)
+    xs = [rng.standard_normal((rows, m.hidden)).astype(np.float32) for _ in range(threads)]
+
+    def one(i):
+        for _ in range(n_layers):
+            ref.silu_mul(ref.matmul(xs[i], wg), ref.matmul(xs[i], wu))
+
+    step_times = []
+    with ThreadPoolExecutor(threads) as ex:
+        for _ in range(warmup):
+            list(ex.map(one, range(threads)))
+        t_start = time.perf_counter()
+        while True:
+            t0 = time.perf_counter()
+            list(ex.map(one, range(threads)))
+            step_times.append(time.perf_counter() - t0)
+            if steps is not None and len(step_times) >= steps:
+                break
+            if steps is None and time.perf_counter() - t_start >= seconds:
+                break
+    return threads * rows * len(step_times) / sum(step_times), step_times, "reference"
+
+
+def run_gemm(args):
+    """One step = kllm_b200_linear_swiglu of every layer (x [T, H] of the layer
+    times its own w_gate and w_up [I, H], SwiGLU in the epilogue), replayed as
+    one CUDA graph; every layer has distinct x, weights and output (several
+    GB, far beyond L2). The same step with cuBLAS (torch.matmul over the
+    stacked [w_gate; w_up]) plus this library's silu_mul is timed beside it
+    as the unfused baseline."""
+    import torch
+
+    from littlellm_b200 import build as kbuild
+    from littlellm_b200 import ops
+    from littlellm_b200.chain import WORKLOADS, shard
+
+    world, rank, local = dist_env()
+    if world == 1 and args.gpus > 1:
+        raise SystemExit("--gpus N > 1 must be launched with torchrun (one rank per GPU)")
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA GPU")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    kbuild.build()
+    from littlellm_b200 import dist as kd
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        kd.init("nccl", device, timeout_s=300)
+
+    base = WORKLOADS[GEMM_WORKLOADS[args.workload]]
+    if args.sequences:
+        base = replace(base, n_seqs=args.sequences)
+    weak = base.name == "qwen_prefill"
+    w = base if weak else shard(base, rank, world)
+    m = w.model
+    L = args.layers or m.n_layers
+    T, H, I = w.n_tokens, m.hidden, m.intermediate
+    gen = torch.Generator(device=device)
+    gen.manual_seed(5000 + rank)
+    x = torch.empty((L, T, H), dtype=torch.float16, device=device).normal_(generator=gen)
+    # [w_gate; w_up] stacked per layer: the fused kernel reads the two halves,
+    # cuBLAS the whole
+    wgu = torch.empty((L, 2 * I, H), dtype=torch.float16, device=device).normal_(std=H ** -0.5, generator=gen)
+    out = torch.empty((L, T, I), dtype=torch.float16, device=device)
+    err = torch.zeros(1, dtype=torch.int32, device=device)
+    flops_per_layer = 2 * T * H * 2 * I
+    flops = flops_per_layer * L
+    log(f"gemm: {args.workload}, {L} layers, x {x.numel() * 2 / 1e9:.2f} GB, weights {wgu.numel() * 2 / 1e9:.2f} GB,"
+        f" out {out.numel() * 2 / 1e9:.2f} GB, {flops / 1e12:.2f} TFLOP per step")
+
+    def step():
+        for layer in range(L):
+            ops.linear_swiglu(x[layer], wgu[layer, :I], wgu[layer, I:], out=out[layer], err_flags=err)
+
+    gu = torch.empty((T, 2 * I), dtype=torch.float16, device=device)
+    g_buf = torch.empty((T, I), dtype=torch.float16, device=device)
+    u_buf = torch.empty((T, I), dtype=torch.float16, device=device)
+
+    def step_unfused():
+        # the reference's structure: linear(gate), linear(up), silu_mul
+        for layer in range(L):
+            torch.matmul(x[layer], wgu[layer, :I].T, out=g_buf)
+            torch.matmul(x[layer], wgu[layer, I:].T, out=u_buf)
+            ops.silu_mul(g_buf, u_buf, out=out[layer])
+
+    def step_gemm_only():
+        for layer in range(L):
+            torch.matmul(x[layer], wgu[layer].T, out=gu)
+
+    stream = torch.cuda.Stream(device)
+    torch.cuda.synchronize(device)
+
+    def timed(graph, reps):
+        for _ in range(max(args.warmup, 3)):
+            graph.replay()
+        stream.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e.record(stream)
+        e.synchronize()
+        return s.elapsed_time(e) / reps
+
+    with torch.cuda.stream(stream):
+        step()
+        stream.synchronize()
+        graph = capture(step, stream)
+        for _ in range(max(args.warmup, 3)):
+            graph.replay()
+        stream.synchronize()
+        sampler = ClockSampler(device)
+        sampler.start()
+        t_end = time.perf_counter() + args.settle_seconds
+        while time.perf_counter() < t_end:
+            graph.replay()
+            stream.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        end.record(stream)
+        end.synchronize()
+        torch.cuda.synchronize(device)
+    if dist is not None:
+        dist.barrier()
+    tt = torch.tensor([start.elapsed_time(end)], dtype=torch.float64, device=device)
+    if dist is not None:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    max_ms = float(tt.item())
+    clocks = sampler.stop()
+    flags = kd.or_over_ranks(int(err.item()), device)
+    finite = bool(torch.isfinite(out[-1]).all().item())
+    # spot check against a torch fp32 reference on a few rows of the last layer
+    rows = torch.arange(0, T, max(1, T // 16), device=device)
+    xs = x[-1, rows].float()
+    gref = xs @ wgu[-1, :I].float().T
+    uref = xs @ wgu[-1, I:].float().T
+    yref = gref * torch.sigmoid(gref) * uref
+    spot_ok = bool(((out[-1, rows].float() - yref).abs() <= 1e-2 + 1e-2 * yref.abs()).all().item())
+
+    comparison = None
+    if rank == 0:
+        with torch.cuda.stream(stream):
+            g_unf = capture(step_unfused, stream)
+            unf_ms = timed(g_unf, args.steps)
+            g_cb = capture(step_gemm_only, stream)
+            cb_ms = timed(g_cb, args.steps)
+        del g_unf, g_cb
+        comparison = {"unfused_ms_per_step": unf_ms, "cublas_gemm_only_ms_per_step": cb_ms,
+                      "fused_speedup_vs_unfused": unf_ms / (max_ms / args.steps),
+                      "unfused": "per layer torch.matmul (cuBLAS, fp16, fp32 accumulate) for gate and for up, "
+                                 "then kllm_b200_silu_mul; CUDA graph",
+                      "cublas_gemm_only": "one torch.matmul per layer over the stacked [w_gate; w_up] (N = 2I), "
+                                          "no SwiGLU: the GEMM work alone"}
+
+    ms = max_ms / args.steps
+    value = T * world / (ms * 1e-3)
+    tflops = flops / (ms * 1e-3) / 1e12
+    # the clocks are settled under this load before timing (power-capped steady
+    # state), so the sustained GEMM peak is the denominator; burst beside it
+    tc = load_tc_peak(sustained=True)
+    burst = load_tc_peak(sustained=False)
+    roofline = {"bound": "tensor", "kernel": "gemm_tc_kernel<SwiGLU> (tcgen05)", "achieved": tflops,
+                "peak": tc["tflops"], "unit": "TFLOP/s", "frac": tflops / tc["tflops"],
+                "frac_of_burst_peak": tflops / burst["tflops"],
+                "traffic": ncu_traffic("gemm_tc_swiglu", args.workload), "peak_source": tc["source"],
+                "flops_per_launch": flops_per_layer,
+                "timing": f"{L} launches per CUDA graph replay, {args.steps} replays, CUDA events"}
+
+    e2e = None
+    if not args.no_e2e:
+        xh = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
+        xh.copy_(x.cpu())
+        last = torch.arange(w.seq_len - 1, T, w.seq_len, device=device)
+        oh = torch.empty((last.numel(), I), dtype=out.dtype, pin_memory=True)
+
+        def e2e_step():
+            x.copy_(xh, non_blocking=True)
+            step()
+            oh.copy_(out[-1].index_select(0, last), non_blocking=True)
+
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                e2e_step()
+            stream.synchronize()
+            if dist is not None:
+                dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(args.steps):
+                e2e_step()
+            e1.record(stream)
+            e1.synchronize()
+        et = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=device)
+        if dist is not None:
+            dist.all_reduce(et, op=dist.ReduceOp.MAX)
+        e_ms = float(et.item()) / args.steps
+        e2e = {"value": T * world / (e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e_ms,
+               "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": oh.numel() * 2,
+               "path": "every layer's x copied from pinned host memory, kllm_b200_linear_swiglu per layer "
+                       "(eager), the last layer's last-token rows copied back"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            sample_rows = 8 if m.hidden <= 1024 else 1
+            v, st, kind = time_reference_mlp(m, L, 1, args.cpu_seconds, sample_rows)
+            cpu = {"value": v, "unit": "tokens/s", "cores": 1, "kind": kind,
+                   "sample": f"{sample_rows} token row(s) through the gate/up linears + silu_mul of all {L} layers "
+                             f"(reference CPU matmul, fp32), repeated {len(st)}x ({sum(st):.1f} s), single thread"}
+        except RuntimeError as e:
+            log(f"cpu baseline skipped: {e}")
+
+    del graph
+    if rank == 0:
+        emit({
+            "metric": GEMM_METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak" if weak else "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": args.workload, "model": m.name, "layers": L, "tokens_per_gpu": T,
+                       "gemm": [T, 2 * I, H], "parallelism": f"dp{world} (token rows split, no collective)",
+                       "math": "fp16 operands, fp32 accumulate (tcgen05 TMEM), fp16 gate/up rounding then SwiGLU "
+                               "in fp32, fp16 out",
+                       "l2": "no flush: each step reads %.2f GB of distinct per-layer x and weights and writes "
+                             "%.2f GB (>> 126 MB L2)" % ((x.numel() + wgu.numel()) * 2 / 1e9, out.numel() * 2 / 1e9),
+                       "cuda_graph": True},
+            "tflops": tflops, "flops_per_step": flops, "roofline": roofline, "clocks": clocks,
+            "gpu_launches": L * args.steps, "launches_per_step": L, "comparison": comparison, "e2e": e2e,
+            "cpu_baseline": cpu,
+            "verification": {"ranks": world, "finite": finite, "err_flags": flags,
+                             "torch_fp32_spot_check": spot_ok},
+        })
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_reference_gemm(args):
+    from littlellm_b200.chain import WORKLOADS
+    m = WORKLOADS[GEMM_WORKLOADS[args.workload]].model
+    L = args.layers or m.n_layers
+    threads = host_threads()
+    rows = 4 if m.hidden <= 1024 else 1
+    value, st, kind = time_reference_mlp(m, L, threads, 0.0, rows, steps=args.steps, warmup=args.warmup)
+    emit({"metric": GEMM_METRIC, "value": value, "unit": "tokens/s", "impl": "reference", "n_gpus": args.gpus,
+          "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * statistics.mean(st),
+          "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+          "config": {"workload": args.workload, "model": m.name, "layers": L, "tokens_per_step": threads * rows,
+                     "impl_detail": "reference linear() (kllm::op::matmul, CPU) x2 + silu_mul on CPU F32 tensors"},
+          "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": kind,
+                           "sample": f"{threads} threads x {rows} token row(s) each through {L} layers per step"},
+          "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
 
 
 def run_ours(args):
@@ -1219,6 +1513,8 @@ def main():
         run_load(args)
     elif args.workload in ATTENTION_WORKLOADS:
         run_attention(args)
+    elif args.workload in GEMM_WORKLOADS:
+        run_gemm(args)
     else:
         run_ours(args)
 

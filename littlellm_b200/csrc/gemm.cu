@@ -17,15 +17,17 @@
 // those fp16 values with the same arithmetic as kllm_b200_silu_mul, so the
 // fused op equals linear + linear + silu_mul of this library bit for bit.
 //
-// Kernel: persistent, one CTA per SM, 128 x 256 accumulator tiles (a SwiGLU
-// tile is 128 output columns: 128 gate rows and 128 up rows of w stacked as
-// the UMMA's N = 256). Warp 0 issues TMA loads of 64-wide k slices (128-byte
-// swizzle) into a 4-stage ring; warp 1 issues tcgen05.mma (M 128, N 256, K 16)
-// into one of two fp32 accumulators in tensor memory (2 x 256 columns); warps
+// Kernel: persistent, one CTA per SM, 128 x BN accumulator tiles, BN = 256
+// (or 128 when 256-wide tiles would leave the last wave of SMs mostly idle);
+// a SwiGLU tile is BN / 2 output columns: BN / 2 gate rows and BN / 2 up rows
+// of the weights stacked as the UMMA's N. Warp 0 issues TMA loads of 64-wide
+// k slices (128-byte swizzle) into a ring of 4 (BN 256) or 6 (BN 128) stages;
+// warp 1 issues tcgen05.mma (M 128, N BN, K 16) into one of two fp32
+// accumulators in tensor memory (2 x BN columns); warps
 // 2-5 read the other accumulator back (tcgen05.ld, one row per thread), apply
 // the epilogue and store, so the epilogue of tile i overlaps the main loop of
-// tile i + 1. Tiles are visited in groups of 16 row tiles (all column tiles
-// of a group before the next group) so the CTAs in flight share x and w in L2.
+// tile i + 1. Tiles are visited in groups of 4096 rows (all column tiles of
+// a group before the next group) so the CTAs in flight share x and w in L2.
 // Every mbarrier wait is bounded; a wait that runs out sets
 // KLLM_B200_FLAG_TIMEOUT and the CTA drains its copies and MMAs and returns.
 #include <cuda.h>
@@ -41,24 +43,28 @@ namespace kb {
 namespace {
 
 constexpr int kBM = 128;                      // tile rows: the UMMA M
-constexpr int kBN = 256;                      // the UMMA N: accumulator columns per tile
 constexpr int kBK = 64;                       // k per stage: one 128-byte swizzle panel of fp16
-constexpr int kStages = 4;
 constexpr int kABytes = kBM * kBK * 2;        // 16 KB
-constexpr int kBBytes = kBN * kBK * 2;        // 32 KB
-constexpr int kStageBytes = kABytes + kBBytes;
-constexpr uint32_t kTmemCols = 2 * kBN;       // two accumulators: all 512 columns
 constexpr int kEpiWarps = 4;
 constexpr int kThreads = (2 + kEpiWarps) * 32;
-constexpr int kGroupM = 16;                   // row tiles per raster group
-constexpr size_t kSmemBytes = static_cast<size_t>(kStages) * kStageBytes + 1024;  // + alignment slack
+constexpr int kGroupRows = 4096;              // rows of x per raster group (x slab resident in L2)
+constexpr int kMaxStages = 6;
+
+// Tile width BN (the UMMA N, accumulator columns per tile): 256, or 128 for
+// problems whose 256-wide tiles would leave the last wave of SMs mostly idle.
+// The ring holds as many stages as fit in 192 KB.
+__host__ __device__ constexpr int gemm_stages(int bn) { return bn == 256 ? 4 : 6; }
+__host__ __device__ constexpr int gemm_stage_bytes(int bn) { return kABytes + bn * kBK * 2; }
+constexpr size_t gemm_smem(int bn) {
+  return static_cast<size_t>(gemm_stages(bn)) * gemm_stage_bytes(bn) + 1024;  // + alignment slack
+}
 
 // mbarriers: stage full (TMA bytes landed) / empty (MMAs that read it done);
 // accumulator full (tile's MMAs done) / empty (epilogue read it); final drain
 enum GemmBar {
   kFull = 0,
-  kEmpty = kFull + kStages,
-  kAccFull = kEmpty + kStages,
+  kEmpty = kFull + kMaxStages,
+  kAccFull = kEmpty + kMaxStages,
   kAccEmpty = kAccFull + 2,
   kMmaDone = kAccEmpty + 2,
   kNumBars = kMmaDone + 1
@@ -66,14 +72,15 @@ enum GemmBar {
 
 struct alignas(64) GemmArgs {
   CUtensorMap map_a;   // x [m, k], box 64 x 128
-  CUtensorMap map_b;   // w [n, k] (SwiGLU: w_gate), box 64 x 256 (SwiGLU: 64 x 128)
-  CUtensorMap map_b2;  // SwiGLU: w_up, box 64 x 128
+  CUtensorMap map_b;   // w [n, k] (SwiGLU: w_gate), box 64 x BN (SwiGLU: 64 x BN / 2)
+  CUtensorMap map_b2;  // SwiGLU: w_up, box 64 x BN / 2
   __half* out;         // [m, n]
   const void* bias;    // [n] or NULL (SwiGLU: gate bias)
   const void* bias2;   // SwiGLU: up bias or NULL
   int32_t* err_flags;
   int64_t m, n;        // output rows and columns
   int m_tiles, n_tiles, k_blocks;
+  int group;           // row tiles per raster group
   int vec_out;         // n % 8 == 0: 16-byte stores
 };
 
@@ -95,13 +102,15 @@ __device__ __forceinline__ void tma_prefetch_map(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// Row tile and column tile of persistent tile index `tile`: groups of kGroupM
-// row tiles, column-major inside a group.
-__device__ __forceinline__ void tile_coords(int tile, int m_tiles, int n_tiles, int& mt, int& nt) {
-  const int per_group = kGroupM * n_tiles;
+// Row tile and column tile of persistent tile index `tile`: groups of
+// `group` row tiles (kGroupRows rows of x), column-major inside a group, so
+// the CTAs in flight share one slab of x and a few column tiles of w in L2
+// and w is read from HBM once per group.
+__device__ __forceinline__ void tile_coords(int tile, int m_tiles, int n_tiles, int group, int& mt, int& nt) {
+  const int per_group = group * n_tiles;
   const int g = tile / per_group;
-  const int first = g * kGroupM;
-  const int rows = min(kGroupM, m_tiles - first);
+  const int first = g * group;
+  const int rows = min(group, m_tiles - first);
   const int local = tile - g * per_group;
   mt = first + local % rows;
   nt = local / rows;
@@ -197,8 +206,12 @@ __device__ __forceinline__ void store_swiglu(const GemmArgs& a, int64_t row, int
   }
 }
 
-template <bool kSwiGLU, typename TB>
+template <int kBN, bool kSwiGLU, typename TB>
 __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_constant__ GemmArgs a) {
+  constexpr int kStages = gemm_stages(kBN);
+  constexpr int kStageBytes = gemm_stage_bytes(kBN);
+  constexpr int kBBytes = kBN * kBK * 2;
+  constexpr uint32_t kTmemCols = 2 * kBN;  // two accumulators
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   __shared__ __align__(8) uint64_t s_bar[kNumBars];
   __shared__ uint32_t s_tmem;
@@ -243,7 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
       int it = 0;  // k slices issued by this CTA
       for (int tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x) {
         int mt, nt;
-        tile_coords(tile, a.m_tiles, a.n_tiles, mt, nt);
+        tile_coords(tile, a.m_tiles, a.n_tiles, a.group, mt, nt);
         const int m0 = mt * kBM, n0 = nt * kOutCols;
         for (int kb = 0; kb < a.k_blocks; ++kb, ++it) {
           const int s = it % kStages;
@@ -310,7 +323,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     int i = 0;
     for (int tile = blockIdx.x; tile < n_tiles_total; tile += gridDim.x, ++i) {
       int mt, nt;
-      tile_coords(tile, a.m_tiles, a.n_tiles, mt, nt);
+      tile_coords(tile, a.m_tiles, a.n_tiles, a.group, mt, nt);
       const int b = i & 1;
       ok = __all_sync(0xffffffffu, mbar_wait(bar(kAccFull + b), (i >> 1) & 1));
       if (!ok) break;
@@ -404,15 +417,46 @@ int check_gemm_args(const char* what, const void* x, const void* w, const void* 
   return KLLM_B200_OK;
 }
 
-template <bool kSwiGLU, typename TB>
+template <int kBN, bool kSwiGLU, typename TB>
 int launch_gemm(GemmArgs& a, const LaunchOpts& o, const char* what) {
-  auto kernel = gemm_tc_kernel<kSwiGLU, TB>;
-  cudaError_t err = allow_smem(reinterpret_cast<const void*>(kernel), kSmemBytes);
+  auto kernel = gemm_tc_kernel<kBN, kSwiGLU, TB>;
+  constexpr size_t smem = gemm_smem(kBN);
+  cudaError_t err = allow_smem(reinterpret_cast<const void*>(kernel), smem);
   if (err != cudaSuccess) return launch_status(err, what);
   const int64_t tiles = static_cast<int64_t>(a.m_tiles) * a.n_tiles;
   const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
-  err = launch(kernel, dim3(grid), dim3(kThreads), kSmemBytes, o.stream, o.pdl, a);
+  err = launch(kernel, dim3(grid), dim3(kThreads), smem, o.stream, o.pdl, a);
   return launch_status(err, what);
+}
+
+// Tile width for an m x n problem: 256, or 128 when the 256-wide tiling
+// leaves the last wave of SMs mostly idle. Cost = tiles per CTA x width, with
+// 128-wide tiles charged 45% extra per column (measured on B200: an N = 128
+// UMMA reads 4/3 the shared-memory bytes per FLOP and each x tile is fetched
+// twice as often; 832 against 1190 TFLOP/s on the Qwen2.5-0.5B MLP).
+int pick_tile_width(int64_t m, int64_t n, bool swiglu) {
+  const int64_t sms = sm_count();
+  const int64_t m_tiles = (m + kBM - 1) / kBM;
+  int64_t best_cost = -1;
+  int best = 256;
+  for (int bn : {256, 128}) {
+    const int64_t cols = swiglu ? bn / 2 : bn;
+    const int64_t tiles = m_tiles * ((n + cols - 1) / cols);
+    const int64_t cost = (tiles + sms - 1) / sms * bn * (bn == 256 ? 20 : 29);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = bn;
+    }
+  }
+  return best;
+}
+
+template <int kBN>
+int dispatch_gemm(GemmArgs& a, bool swiglu, bool f32_bias, const LaunchOpts& o, const char* what) {
+  if (swiglu) {
+    return f32_bias ? launch_gemm<kBN, true, float>(a, o, what) : launch_gemm<kBN, true, __half>(a, o, what);
+  }
+  return f32_bias ? launch_gemm<kBN, false, float>(a, o, what) : launch_gemm<kBN, false, __half>(a, o, what);
 }
 
 int run_gemm(const void* x, const void* w, const void* w2, const void* bias, const void* bias2, int bias_dtype,
@@ -420,14 +464,15 @@ int run_gemm(const void* x, const void* w, const void* w2, const void* bias, con
   const char* what = swiglu ? "linear_swiglu" : "linear";
   int rc = check_gemm_args(what, x, w, w2, bias, bias2, bias_dtype, out, m, n, k, swiglu);
   if (rc != KLLM_B200_OK || m == 0 || n == 0) return rc;
-  const int out_cols = swiglu ? kBN / 2 : kBN;
+  const int bn = pick_tile_width(m, n, swiglu);
+  const int out_cols = swiglu ? bn / 2 : bn;  // output columns per tile
   const int64_t m_tiles = (m + kBM - 1) / kBM, n_tiles = (n + out_cols - 1) / out_cols;
   if (m_tiles * n_tiles > 0x7fffffffLL) return fail(KLLM_B200_ERR_SHAPE, "%s: too many tiles", what);
   GemmArgs a;
   memset(&a, 0, sizeof(a));
   if ((rc = make_map(&a.map_a, x, m, k, kBM, what)) != KLLM_B200_OK) return rc;
-  if ((rc = make_map(&a.map_b, w, n, k, swiglu ? kBN / 2 : kBN, what)) != KLLM_B200_OK) return rc;
-  if (swiglu && (rc = make_map(&a.map_b2, w2, n, k, kBN / 2, what)) != KLLM_B200_OK) return rc;
+  if ((rc = make_map(&a.map_b, w, n, k, out_cols, what)) != KLLM_B200_OK) return rc;
+  if (swiglu && (rc = make_map(&a.map_b2, w2, n, k, out_cols, what)) != KLLM_B200_OK) return rc;
   a.out = static_cast<__half*>(out);
   a.bias = bias;
   a.bias2 = bias2;
@@ -437,12 +482,10 @@ int run_gemm(const void* x, const void* w, const void* w2, const void* bias, con
   a.m_tiles = static_cast<int>(m_tiles);
   a.n_tiles = static_cast<int>(n_tiles);
   a.k_blocks = static_cast<int>((k + kBK - 1) / kBK);
+  a.group = kGroupRows / kBM;
   a.vec_out = n % 8 == 0;
   const bool f32_bias = (bias || bias2) && bias_dtype == KLLM_B200_F32;
-  if (swiglu) {
-    return f32_bias ? launch_gemm<true, float>(a, o, what) : launch_gemm<true, __half>(a, o, what);
-  }
-  return f32_bias ? launch_gemm<false, float>(a, o, what) : launch_gemm<false, __half>(a, o, what);
+  return bn == 256 ? dispatch_gemm<256>(a, swiglu, f32_bias, o, what) : dispatch_gemm<128>(a, swiglu, f32_bias, o, what);
 }
 
 }  // namespace

@@ -134,3 +134,36 @@ def test_repeated_calls_are_deterministic(cuda, ops):
         again = ops.linear_swiglu(x, wg, wu)
         torch.cuda.synchronize()
         assert torch.equal(first, again)
+
+
+@pytest.mark.parametrize("what,m,n,k,bias", [
+    ("linear, ragged m, n and k", 4100, 4100, 200, torch.float16),
+    ("linear, square", 8192, 8192, 256, None),
+    ("swiglu, ragged n and k, fp32 bias", 8192, 3000, 136, torch.float32),
+])
+def test_large_tilings_vs_torch_fp32(cuda, ops, what, m, n, k, bias):
+    """Problems of many waves (several raster groups of 4096 rows), with
+    partial row and column tiles and a k tail, against torch fp32."""
+    g = torch.Generator(device=cuda).manual_seed(m ^ n ^ k)
+    x = torch.randn(m, k, device=cuda, generator=g).half()
+    w = (torch.randn(n, k, device=cuda, generator=g) / k ** 0.5).half()
+    b = (torch.randn(n, device=cuda, generator=g) * 0.1).to(bias) if bias is not None else None
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    ref = x.float() @ w.float().T + (b.float() if b is not None else 0)
+    if "swiglu" in what:
+        w2 = (torch.randn(n, k, device=cuda, generator=g) / k ** 0.5).half()
+        b2 = (torch.randn(n, device=cuda, generator=g) * 0.1).to(bias)
+        out = ops.linear_swiglu(x, w, w2, b, b2, err_flags=err)
+        up = x.float() @ w2.float().T + b2.float()
+        ref = ref * torch.sigmoid(ref) * up
+        # the fused op equals this library's separate ops bit for bit here too
+        unfused = ops.silu_mul(ops.linear(x, w, b), ops.linear(x, w2, b2))
+        torch.cuda.synchronize()
+        assert torch.equal(out, unfused)
+    else:
+        out = ops.linear(x, w, b, err_flags=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    diff = (out.float() - ref).abs()
+    bad = diff > TOL + TOL * ref.abs()
+    assert not bool(bad.any()), f"{what}: {int(bad.sum())} outside tolerance, max abs err {float(diff.max()):.3g}"
