@@ -51,6 +51,8 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample length")
     ap.add_argument("--layers", type=int, default=None,
                     help="run only this many decoder layers (small profiling cases; not a bench line)")
+    ap.add_argument("--forward", action="store_true",
+                    help="time the whole forward step (chain + attention + tcgen05 GEMMs + lm_head)")
     ap.add_argument("--attention", action="store_true",
                     help="chain workloads: run attention over the cache in every layer as part of the chain")
     ap.add_argument("--sequences", type=int, default=None,
@@ -1437,6 +1439,233 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+FORWARD_METRIC = "forward tokens/s"
+
+
+def forward_flops(w, n_layers: int, positions) -> dict:
+    """Tensor work of one forward step: the GEMMs (q/k/v, o, gate/up, down per
+    layer; lm_head on the last rows) and attention (4 * D FLOPs per token,
+    query head and attended position)."""
+    import numpy as np
+    m = w.model
+    T, H, I = w.n_tokens, m.hidden, m.intermediate
+    qd, kvd = m.n_heads * m.head_dim, m.n_kv_heads * m.head_dim
+    per_layer = 2 * T * (H * (qd + 2 * kvd) + qd * H + H * 2 * I + I * H)
+    gemm = per_layer * n_layers + 2 * w.n_seqs * H * m.vocab
+    attn = int((np.asarray(positions, dtype=np.int64) + 1).sum()) * m.n_heads * m.head_dim * 4 * n_layers
+    return {"gemm": gemm, "gemm_per_layer": per_layer, "attention": attn, "total": gemm + attn}
+
+
+def run_forward(args):
+    """One step = the whole forward of a decoder step (KLLM_B200_OP_GEMM: the
+    chain with its GEMMs; LlamaRunner::forward, src/model/llama.cpp:78-184)
+    for the workload's tokens, one CUDA graph replay. Random weights of the
+    model's shapes; the roofline is the GEMM work, timed alone on the same
+    buffers (tcgen05, tensor-bound)."""
+    import torch
+
+    from littlellm_b200 import build as kbuild
+    from littlellm_b200 import ops
+    from littlellm_b200.chain import WORKLOADS, ChainRunner, shard
+
+    world, rank, local = dist_env()
+    if world == 1 and args.gpus > 1:
+        raise SystemExit("--gpus N > 1 must be launched with torchrun (one rank per GPU)")
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA GPU")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    kbuild.build()
+    from littlellm_b200 import dist as kd
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        kd.init("nccl", device, timeout_s=300)
+
+    base = WORKLOADS[args.workload]
+    weak = args.workload == "qwen_prefill"
+    w = base if weak else shard(base, rank, world)
+    r = ChainRunner(w, device=device, seed=1000 + rank, use_pdl=not args.no_pdl, n_layers=args.layers,
+                    attention=True, gemm=True)
+    m, L = w.model, r.n_layers
+    work = forward_flops(w, L, r.positions.cpu().numpy())
+    stream = torch.cuda.Stream(device)
+    torch.cuda.synchronize(device)
+
+    def timed(graph, reps):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e.record(stream)
+        e.synchronize()
+        return s.elapsed_time(e) / reps
+
+    with torch.cuda.stream(stream):
+        launches = r.run(stream)
+        stream.synchronize()
+        graph = capture(lambda: r.run(stream), stream)
+        for _ in range(max(args.warmup, 3)):
+            graph.replay()
+        stream.synchronize()
+        sampler = ClockSampler(device)
+        sampler.start()
+        t_end = time.perf_counter() + args.settle_seconds
+        while time.perf_counter() < t_end:
+            graph.replay()
+            stream.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        end.record(stream)
+        end.synchronize()
+        torch.cuda.synchronize(device)
+    if dist is not None:
+        dist.barrier()
+    tt = torch.tensor([start.elapsed_time(end)], dtype=torch.float64, device=device)
+    if dist is not None:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    max_ms = float(tt.item())
+    clocks = sampler.stop()
+    flags = kd.or_over_ranks(int(r.err_flags.item()), device)
+    logits_ok = bool(torch.isfinite(r.logits.float()).all().item())
+
+    # the GEMMs of the step alone (same kernels, shapes and buffers), for the roofline
+    T, H, I = w.n_tokens, m.hidden, m.intermediate
+
+    def gemms():
+        for Lb, W in zip(r.layers, r.weights):
+            ops.linear(Lb["attn_norm_out"], W["wq"], out=Lb["q"])
+            ops.linear(Lb["attn_norm_out"], W["wk"], out=Lb["k"])
+            ops.linear(Lb["attn_norm_out"], W["wv"], out=Lb["v"])
+            ops.linear(Lb["attn_ctx"], W["wo"], out=Lb["attn_out"])
+            ops.linear_swiglu(Lb["ffn_norm_out"], W["w_gate"], W["w_up"], out=Lb["swiglu_out"])
+            ops.linear(Lb["swiglu_out"], W["w_down"], out=Lb["ffn_out"])
+        ops.linear(r.last_rows, r.lm_head, out=r.logits)
+
+    with torch.cuda.stream(stream):
+        g2 = capture(gemms, stream)
+        for _ in range(2):
+            g2.replay()
+        gemm_ms = timed(g2, max(args.steps, 5))
+    del g2
+
+    ms = max_ms / args.steps
+    value = T * world / (ms * 1e-3)
+    gemm_tflops = work["gemm"] / (gemm_ms * 1e-3) / 1e12
+    tc = load_tc_peak(sustained=True)
+    roofline = {"bound": "tensor", "kernel": "gemm_tc_kernel (q/k/v, o, gate/up+SwiGLU, down, lm_head)",
+                "achieved": gemm_tflops, "peak": tc["tflops"], "unit": "TFLOP/s", "frac": gemm_tflops / tc["tflops"],
+                "traffic": None, "peak_source": tc["source"], "flops_per_step": work["gemm"],
+                "ms_per_step": gemm_ms, "share_of_step": gemm_ms / ms,
+                "timing": f"the step's {6 * L + 1} GEMM launches alone in one CUDA graph, CUDA events"}
+
+    e2e = None
+    if not args.no_e2e:
+        ins = [r.ids, r.positions, r.slots]
+        hosts = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in ins]
+        for h, t in zip(hosts, ins):
+            h.copy_(t.cpu())
+        lh = torch.empty(r.logits.shape, dtype=r.logits.dtype, pin_memory=True)
+
+        def e2e_step():
+            for h, t in zip(hosts, ins):
+                t.copy_(h, non_blocking=True)
+            r.run(stream)
+            lh.copy_(r.logits, non_blocking=True)
+
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                e2e_step()
+            stream.synchronize()
+            if dist is not None:
+                dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(args.steps):
+                e2e_step()
+            e1.record(stream)
+            e1.synchronize()
+        et = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=device)
+        if dist is not None:
+            dist.all_reduce(et, op=dist.ReduceOp.MAX)
+        e_ms = float(et.item()) / args.steps
+        e2e = {"value": T * world / (e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e_ms,
+               "h2d_bytes_per_step": sum(t.numel() * 4 for t in ins), "d2h_bytes_per_step": r.logits.numel() * 2,
+               "path": "ids, positions, slots from pinned host memory; kllm_b200_chain_run (whole forward, eager "
+                       "launches); logits of the last tokens to pinned host memory"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        if m.hidden <= 1024:
+            cpu = time_oracle_forward(r, args.cpu_seconds)
+        else:  # a 7B model's weights as fp32 numpy (27 GB) and ~1 minute per token on one core
+            log("cpu baseline skipped for the forward of a model this size")
+
+    del graph
+    if rank == 0:
+        emit({
+            "metric": FORWARD_METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak" if weak else "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": w.name, "model": m.name, "layers": L, "tokens_per_gpu": T,
+                       "sequences_per_gpu": w.n_seqs, "seq_len": w.seq_len,
+                       "kv_cache": [L, 2, w.n_seqs, m.n_kv_heads, w.max_seq, m.head_dim],
+                       "weights": "random, N(0, 1/fan_in), fp16", "parallelism": f"dp{world} (sequences split)",
+                       "math": "fp16 storage, fp32 accumulation (tcgen05 GEMMs, attention), fp32 elementwise",
+                       "pdl": not args.no_pdl, "cuda_graph": True},
+            "tflops_step": work["total"] / (ms * 1e-3) / 1e12, "flops_per_step": work["total"],
+            "roofline": roofline, "clocks": clocks, "gpu_launches": launches * args.steps,
+            "launches_per_step": launches, "e2e": e2e, "cpu_baseline": cpu,
+            "verification": {"ranks": world, "logits_finite": logits_ok, "err_flags": flags},
+        })
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def time_oracle_forward(r, seconds: float) -> dict:
+    """The oracle forward (the reference forward restated on the C oracle's
+    operators, single thread, fp32) on a bounded sample: one 8-token sequence
+    of the runner's model and weights through every layer and the lm_head."""
+    import numpy as np
+
+    from oracle.oracle import Oracle
+    o = Oracle()
+    m = r.w.model
+    tokens = 8
+
+    def npf(t):
+        return t.detach().float().cpu().numpy()
+
+    shape = (1, m.n_kv_heads, tokens, m.head_dim)
+    layers = []
+    for Lb, W in zip(r.layers, r.weights):
+        d = {k: npf(Lb[k]) for k in ("input_norm_w", "post_norm_w", "q_bias", "k_bias", "v_bias")}
+        d.update({k: npf(t) for k, t in W.items()})
+        d["k_cache"], d["v_cache"] = np.zeros(shape, np.float32), np.zeros(shape, np.float32)
+        layers.append(d)
+    p = {"table": npf(r.table), "ids": npf(r.ids)[:tokens].astype(np.int32),
+         "positions": np.arange(tokens, dtype=np.int32), "slots": np.zeros(tokens, np.int32),
+         "final_norm_w": npf(r.final_norm_w), "lm_head": npf(r.lm_head), "layers": layers,
+         "n_heads": m.n_heads, "n_kv_heads": m.n_kv_heads, "head_dim": m.head_dim, "eps": m.eps, "theta": m.theta,
+         "seq_len": tokens, "n_seqs": 1}
+    times = []
+    t_start = time.perf_counter()
+    while not times or time.perf_counter() - t_start < seconds:
+        t0 = time.perf_counter()
+        o.forward(p, fp16_storage=False)
+        times.append(time.perf_counter() - t0)
+    return {"value": tokens * len(times) / sum(times), "unit": "tokens/s", "cores": 1, "kind": "port",
+            "sample": f"one {tokens}-token sequence through all {len(layers)} layers and the lm_head "
+                      f"(oracle forward pinned to the reference LlamaRunner), repeated {len(times)}x "
+                      f"({sum(times):.1f} s), fp32, single thread"}
+
+
 def run_e2e(runner, stream, steps: int, device, dist, world: int) -> dict:
     """tokens/s through the C ABI with host buffers: every step copies its
     inputs (ids, positions, slots, each layer's GEMM outputs) from pinned host
@@ -1515,6 +1744,8 @@ def main():
         run_attention(args)
     elif args.workload in GEMM_WORKLOADS:
         run_gemm(args)
+    elif args.forward:
+        run_forward(args)
     else:
         run_ours(args)
 

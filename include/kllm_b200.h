@@ -297,6 +297,24 @@ typedef struct kllm_b200_layer_buffers {
   void* attn_ctx;            /* [T, n_heads*head_dim] attention output (KLLM_B200_OP_ATTENTION) or NULL */
 } kllm_b200_layer_buffers;
 
+/* Per-layer weights of the GEMMs (KLLM_B200_OP_GEMM): fp16, [out, in]
+ * row-major as linear() takes them (src/model/llama.cpp:12-24). Biases are
+ * of the chain's weight_dtype and may be NULL; the q/k/v biases stay in
+ * kllm_b200_layer_buffers (the fused RoPE op adds them). */
+typedef struct kllm_b200_layer_weights {
+  const void* wq;        /* [n_heads*head_dim, hidden] */
+  const void* wk;        /* [n_kv_heads*head_dim, hidden] */
+  const void* wv;        /* [n_kv_heads*head_dim, hidden] */
+  const void* wo;        /* [hidden, n_heads*head_dim] */
+  const void* w_gate;    /* [intermediate, hidden] */
+  const void* w_up;      /* [intermediate, hidden] */
+  const void* w_down;    /* [hidden, intermediate] */
+  const void* o_bias;    /* [hidden] or NULL */
+  const void* gate_bias; /* [intermediate] or NULL */
+  const void* up_bias;   /* [intermediate] or NULL */
+  const void* down_bias; /* [hidden] or NULL */
+} kllm_b200_layer_weights;
+
 /* op_mask bits of kllm_b200_chain */
 enum {
   KLLM_B200_OP_EMBEDDING = 1,
@@ -310,7 +328,15 @@ enum {
    * cache into attn_ctx (kllm_b200_attention_head_major; runs of seq_len
    * tokens, or single tokens when seq_ends is given). Not in op_mask 0:
    * the GEMM-free chain of the seven ops above stays the default. */
-  KLLM_B200_OP_ATTENTION = 128
+  KLLM_B200_OP_ATTENTION = 128,
+  /* the GEMMs too, making the chain the whole forward step of
+   * LlamaRunner::forward (src/model/llama.cpp:78-184): per layer the q, k
+   * and v linears after the input norm (into q, k, v), the o linear after
+   * attention (into attn_out), the gate/up linears with SwiGLU fused (into
+   * swiglu_out; replaces KLLM_B200_OP_SWIGLU's silu_mul), the down linear
+   * (into ffn_out); after select, logits = last_rows . lm_head^T when
+   * lm_head and logits are given. Needs KLLM_B200_OP_ATTENTION and weights. */
+  KLLM_B200_OP_GEMM = 256
 };
 
 typedef struct kllm_b200_chain {
@@ -334,12 +360,17 @@ typedef struct kllm_b200_chain {
   int32_t* err_flags;             /* device word or NULL */
   void* attn_workspace;           /* attention split workspace (KLLM_B200_OP_ATTENTION), or NULL */
   int64_t attn_workspace_bytes;
+  const kllm_b200_layer_weights* weights; /* host array of n_layers entries (KLLM_B200_OP_GEMM) */
+  const void* lm_head;            /* [vocab, hidden] fp16, or NULL */
+  void* logits;                   /* [n_seqs, vocab] fp16, or NULL */
 } kllm_b200_chain;
 
 /* Launches the whole non-GEMM chain on `stream`: embedding, then per layer
  * add+RMSNorm, fused bias+RoPE+KV append, (attention, when its bit is set),
  * add+RMSNorm, SwiGLU, then the final add+RMSNorm and select_last_rows (the
  * op kinds selected by op_mask; 0 selects the seven ops without attention).
+ * With KLLM_B200_OP_GEMM the layer's GEMMs run in between and the step is
+ * the whole forward: q, k, v, attn_out and ffn_out are then written.
  * *n_launches (if given) receives the number of kernels launched. Can be
  * captured into a CUDA graph. */
 int kllm_b200_chain_run(const kllm_b200_chain* chain, int* n_launches, void* stream);

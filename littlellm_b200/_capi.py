@@ -32,7 +32,9 @@ FLAG_TIMEOUT = 16
 OP_EMBEDDING, OP_INPUT_NORM, OP_QKV_ROPE, OP_POST_NORM, OP_SWIGLU, OP_FINAL_NORM, OP_SELECT = (
     1, 2, 4, 8, 16, 32, 64)
 OP_ATTENTION = 128
+OP_GEMM = 256
 OP_CHAIN = 0x7f  # the seven ops of op_mask 0
+OP_FORWARD = OP_CHAIN | OP_ATTENTION | OP_GEMM  # the whole forward step
 
 
 class KllmError(RuntimeError):
@@ -48,6 +50,11 @@ class LayerBuffers(ctypes.Structure):
         "q", "k", "v", "q_bias", "k_bias", "v_bias", "attn_out", "ffn_out", "gate", "up",
         "input_norm_w", "post_norm_w", "attn_norm_out", "ffn_norm_out", "swiglu_out",
         "k_cache", "v_cache", "attn_ctx")]
+
+
+class LayerWeights(ctypes.Structure):
+    _fields_ = [(name, ctypes.c_void_p) for name in (
+        "wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down", "o_bias", "gate_bias", "up_bias", "down_bias")]
 
 
 class Chain(ctypes.Structure):
@@ -66,6 +73,7 @@ class Chain(ctypes.Structure):
         ("last_rows", ctypes.c_void_p), ("layers", ctypes.POINTER(LayerBuffers)),
         ("err_flags", ctypes.c_void_p),
         ("attn_workspace", ctypes.c_void_p), ("attn_workspace_bytes", ctypes.c_int64),
+        ("weights", ctypes.POINTER(LayerWeights)), ("lm_head", ctypes.c_void_p), ("logits", ctypes.c_void_p),
     ]
 
 

@@ -117,7 +117,7 @@ class ChainRunner:
     def __init__(self, workload: Workload, device: torch.device | str = "cuda:0", seed: int = 0,
                  use_pdl: bool = True, n_layers: int | None = None,
                  weight_dtype: torch.dtype = torch.float16, shard: tuple[int, int] | None = None,
-                 attention: bool = False):
+                 attention: bool = False, gemm: bool = False):
         m = workload.model
         self.device = torch.device(device)
         self.n_layers = n_layers or m.n_layers
@@ -146,6 +146,8 @@ class ChainRunner:
             return t if (t0, t1) == (0, T) else t[t0:t1].contiguous()
 
         Tl = t1 - t0
+        if gemm and not attention:
+            raise ValueError("the GEMM ops need attention (o_proj reads the attention output)")
         with torch.cuda.device(dev):
             self.table = normal((m.vocab, H), 0.02)
             self.ids = rows(torch.randint(0, m.vocab, (T,), generator=gen, device=dev, dtype=torch.int32))
@@ -164,12 +166,20 @@ class ChainRunner:
             self.err_flags = torch.zeros((1,), dtype=torch.int32, device=dev)
             self.layers = []
             for _ in range(self.n_layers):
+                if gemm:  # GEMM outputs are produced in the step; weights scaled by 1/sqrt(fan_in)
+                    out = {"q": torch.empty((Tl, qd), dtype=f16, device=dev),
+                           "k": torch.empty((Tl, kvd), dtype=f16, device=dev),
+                           "v": torch.empty((Tl, kvd), dtype=f16, device=dev),
+                           "attn_out": torch.empty((Tl, H), dtype=f16, device=dev),
+                           "ffn_out": torch.empty((Tl, H), dtype=f16, device=dev)}
+                else:
+                    out = {"q": rows(normal((T, qd))), "k": rows(normal((T, kvd))), "v": rows(normal((T, kvd))),
+                           "attn_out": rows(normal((T, H))), "ffn_out": rows(normal((T, H))),
+                           "gate": rows(normal((T, I))), "up": rows(normal((T, I)))}
                 L = {
-                    "q": rows(normal((T, qd))), "k": rows(normal((T, kvd))), "v": rows(normal((T, kvd))),
+                    **out,
                     "q_bias": normal((qd,), 0.02, weight_dtype), "k_bias": normal((kvd,), 0.02, weight_dtype),
                     "v_bias": normal((kvd,), 0.02, weight_dtype),
-                    "attn_out": rows(normal((T, H))), "ffn_out": rows(normal((T, H))),
-                    "gate": rows(normal((T, I))), "up": rows(normal((T, I))),
                     "input_norm_w": uniform((H,), 0.5, 1.5, weight_dtype),
                     "post_norm_w": uniform((H,), 0.5, 1.5, weight_dtype),
                     "attn_norm_out": torch.empty((Tl, H), dtype=f16, device=dev),
@@ -192,6 +202,17 @@ class ChainRunner:
                     L["attn_ctx"] = torch.empty((Tl, qd), dtype=f16, device=dev)
                 self.layers.append(L)
             self.attention = attention
+            self.gemm = gemm
+            self.weights = []
+            if gemm:
+                for _ in range(self.n_layers):
+                    self.weights.append({
+                        "wq": normal((qd, H), H ** -0.5), "wk": normal((kvd, H), H ** -0.5),
+                        "wv": normal((kvd, H), H ** -0.5), "wo": normal((H, qd), qd ** -0.5),
+                        "w_gate": normal((I, H), H ** -0.5), "w_up": normal((I, H), H ** -0.5),
+                        "w_down": normal((H, I), I ** -0.5)})
+                self.lm_head = normal((m.vocab, H), H ** -0.5)
+                self.logits = torch.empty((s1 - s0, m.vocab), dtype=f16, device=dev)
             if attention:
                 from . import ops
                 nbytes = ops.attention_workspace_bytes(Tl, m.n_heads, m.n_kv_heads, m.head_dim, workload.max_seq)
@@ -223,6 +244,15 @@ class ChainRunner:
             c.op_mask = _capi.OP_CHAIN | _capi.OP_ATTENTION
             c.attn_workspace = self.attn_workspace.data_ptr()
             c.attn_workspace_bytes = self.attn_workspace.numel()
+        if self.gemm:
+            warr = (_capi.LayerWeights * self.n_layers)()
+            for i, W in enumerate(self.weights):
+                for name, t in W.items():
+                    setattr(warr[i], name, t.data_ptr())
+            self._weight_arr = warr
+            c.weights = ctypes.cast(warr, ctypes.POINTER(_capi.LayerWeights))
+            c.lm_head, c.logits = self.lm_head.data_ptr(), self.logits.data_ptr()
+            c.op_mask = _capi.OP_FORWARD
         self.desc = c
         self.full_mask = c.op_mask
 
@@ -241,6 +271,8 @@ class ChainRunner:
         """Tensors a step consumes that a real forward would produce afresh
         each step (ids, positions, slots and the GEMM outputs)."""
         out = [self.ids, self.positions, self.slots]
+        if self.gemm:  # the whole forward: every other tensor is produced in the step
+            return out
         for L in self.layers:
             out += [L[k] for k in ("q", "k", "v", "attn_out", "ffn_out", "gate", "up")]
         return out

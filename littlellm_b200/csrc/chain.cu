@@ -11,6 +11,14 @@
 //     SwiGLU       swiglu = silu(gate) * up                  (:158)
 //   add+RMSNorm  r += ffn_out[L-1]; normed = norm(r)         (:166, :171)
 //   select_last_rows                                          (:173)
+// With KLLM_B200_OP_GEMM the GEMMs run in between (tcgen05, gemm.cu), and the
+// step is the whole forward of llama.cpp:78-184:
+//   after the input norm   q, k, v = linear(attn_norm, wq / wk / wv)   (:89-106)
+//   after attention        attn_out = linear(ctx, wo, o_bias)          (:129-134)
+//   instead of SwiGLU      swiglu = silu_mul(linear(ffn_norm, w_gate), linear(ffn_norm, w_up)),
+//                          one kernel                                   (:145-158)
+//   then                   ffn_out = linear(swiglu, w_down, down_bias)  (:160-165)
+//   after select           logits = linear(last_rows, lm_head)          (:175-183)
 // Everything goes to one stream; with use_pdl every launch carries the
 // programmatic-dependent-launch attribute so a kernel's CTAs are scheduled
 // while its predecessor drains. The sequence contains no host sync and no
@@ -39,7 +47,21 @@ extern "C" int kllm_b200_chain_run(const kllm_b200_chain* c, int* n_launches, vo
       if (c->layers[l].attn_ctx == nullptr) return fail(KLLM_B200_ERR_INVALID_ARG, "chain_run: layer %lld has no attn_ctx", (long long)l);
     }
   }
+  const bool gemm = (mask & KLLM_B200_OP_GEMM) != 0;
+  if (gemm) {
+    if ((mask & KLLM_B200_OP_ATTENTION) == 0) {
+      return fail(KLLM_B200_ERR_INVALID_ARG, "chain_run: the GEMM op needs the attention op (o_proj reads attn_ctx)");
+    }
+    if (c->weights == nullptr) return fail(KLLM_B200_ERR_INVALID_ARG, "chain_run: the GEMM op needs weights");
+    for (int64_t l = 0; l < c->n_layers; ++l) {
+      const kllm_b200_layer_weights& W = c->weights[l];
+      if (!W.wq || !W.wk || !W.wv || !W.wo || !W.w_gate || !W.w_up || !W.w_down) {
+        return fail(KLLM_B200_ERR_INVALID_ARG, "chain_run: layer %lld is missing a GEMM weight", (long long)l);
+      }
+    }
+  }
   auto on = [mask](int bit) { return (mask & bit) != 0; };
+  const int64_t qd = c->n_heads * c->head_dim, kvd = c->n_kv_heads * c->head_dim, I = c->intermediate;
   int launched = 0;
   int rc = KLLM_B200_OK;
   if (on(KLLM_B200_OP_EMBEDDING)) {
@@ -55,6 +77,14 @@ extern "C" int kllm_b200_chain_run(const kllm_b200_chain* c, int* n_launches, vo
       rc = add_rms_norm(c->residual, delta, L.input_norm_w, L.attn_norm_out, T, H, c->eps, KLLM_B200_F16, wdt, o);
       if (rc != KLLM_B200_OK) return rc;
       ++launched;
+    }
+    if (gemm) {  // q, k and v projections of the normed residual (biases go with RoPE)
+      const kllm_b200_layer_weights& W = c->weights[l];
+      rc = linear(L.attn_norm_out, W.wq, nullptr, wdt, L.q, T, qd, H, c->err_flags, o);
+      if (rc == KLLM_B200_OK) rc = linear(L.attn_norm_out, W.wk, nullptr, wdt, const_cast<void*>(L.k), T, kvd, H, c->err_flags, o);
+      if (rc == KLLM_B200_OK) rc = linear(L.attn_norm_out, W.wv, nullptr, wdt, const_cast<void*>(L.v), T, kvd, H, c->err_flags, o);
+      if (rc != KLLM_B200_OK) return rc;
+      launched += 3;
     }
     if (on(KLLM_B200_OP_QKV_ROPE)) {
       rc = qkv_bias_rope_kv_append(L.q, L.k, L.v, L.q_bias, L.k_bias, L.v_bias, wdt, c->positions, c->slots, T,
@@ -73,16 +103,32 @@ extern "C" int kllm_b200_chain_run(const kllm_b200_chain* c, int* n_launches, vo
       if (rc != KLLM_B200_OK) return rc;
       launched += n;
     }
+    if (gemm) {  // o projection of the attention output
+      const kllm_b200_layer_weights& W = c->weights[l];
+      rc = linear(L.attn_ctx, W.wo, W.o_bias, wdt, const_cast<void*>(L.attn_out), T, H, qd, c->err_flags, o);
+      if (rc != KLLM_B200_OK) return rc;
+      ++launched;
+    }
     if (on(KLLM_B200_OP_POST_NORM)) {
       rc = add_rms_norm(c->residual, L.attn_out, L.post_norm_w, L.ffn_norm_out, T, H, c->eps, KLLM_B200_F16, wdt,
                         o);
       if (rc != KLLM_B200_OK) return rc;
       ++launched;
     }
-    if (on(KLLM_B200_OP_SWIGLU)) {
+    if (on(KLLM_B200_OP_SWIGLU) && !gemm) {
       rc = silu_mul(L.gate, L.up, L.swiglu_out, T * c->intermediate, KLLM_B200_F16, o);
       if (rc != KLLM_B200_OK) return rc;
       ++launched;
+    }
+    if (gemm) {  // gate/up projections with SwiGLU fused, then the down projection
+      const kllm_b200_layer_weights& W = c->weights[l];
+      rc = linear_swiglu(L.ffn_norm_out, W.w_gate, W.w_up, W.gate_bias, W.up_bias, wdt, L.swiglu_out, T, I, H,
+                         c->err_flags, o);
+      if (rc == KLLM_B200_OK) {
+        rc = linear(L.swiglu_out, W.w_down, W.down_bias, wdt, const_cast<void*>(L.ffn_out), T, H, I, c->err_flags, o);
+      }
+      if (rc != KLLM_B200_OK) return rc;
+      launched += 2;
     }
   }
   if (on(KLLM_B200_OP_FINAL_NORM)) {
@@ -94,6 +140,11 @@ extern "C" int kllm_b200_chain_run(const kllm_b200_chain* c, int* n_launches, vo
   if (on(KLLM_B200_OP_SELECT)) {
     rc = select_last_rows(c->final_norm_out, T, H, c->seq_ends, c->seq_len, c->n_seqs, c->last_rows,
                           KLLM_B200_F16, c->err_flags, o);
+    if (rc != KLLM_B200_OK) return rc;
+    ++launched;
+  }
+  if (gemm && c->lm_head != nullptr && c->logits != nullptr) {
+    rc = linear(c->last_rows, c->lm_head, nullptr, wdt, c->logits, c->n_seqs, c->vocab, H, c->err_flags, o);
     if (rc != KLLM_B200_OK) return rc;
     ++launched;
   }

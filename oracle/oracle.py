@@ -257,6 +257,55 @@ class Oracle:
                                                    _ptr(out, _c_f32p))
         return out, rc
 
+    def forward(self, p: dict, fp16_storage: bool = True):
+        """LlamaRunner::forward (src/model/llama.cpp:78-184) composed of this
+        module's operators, for a batch of sequences with per-token positions
+        and slots over head-major caches [n_slots, Hkv, max_seq, D].
+
+        `p` holds numpy arrays: table, ids, positions, slots, final_norm_w,
+        lm_head, and `layers`, a list of dicts with input_norm_w, post_norm_w,
+        q_bias, k_bias, v_bias (or None), wq, wk, wv, wo, w_gate, w_up, w_down
+        ([out, in]) and the layer's k_cache, v_cache before the step; plus the
+        shape scalars n_heads, n_kv_heads, head_dim, eps, theta, seq_len,
+        n_seqs. With fp16_storage every op output (and the cache) is rounded
+        to fp16, the storage points of the fp16 device path. Returns
+        (last rows, logits, [(k_cache, v_cache) per layer])."""
+        rnd = (lambda a: np.asarray(a, np.float32).astype(np.float16).astype(np.float32)) if fp16_storage \
+            else (lambda a: np.asarray(a, np.float32))
+        Hq, Hkv, D = p["n_heads"], p["n_kv_heads"], p["head_dim"]
+        pos = np.ascontiguousarray(p["positions"], np.int32)
+        slots = np.ascontiguousarray(p["slots"], np.int32)
+        T = pos.size
+        x = self.embedding(p["table"], p["ids"])
+        d = None
+        caches = []
+        for L in p["layers"]:
+            if d is not None:
+                x = rnd(x + d)                                            # add_inplace(ffn_out, x)
+            h = rnd(self.rms_norm(x, L["input_norm_w"], p["eps"]))
+            q = rnd(self.matmul(h, L["wq"]))
+            k = rnd(self.matmul(h, L["wk"]))
+            v = rnd(self.matmul(h, L["wv"]))
+            q, kc, vc, bad = self.qkv_bias_rope_kv_append(
+                q.reshape(T, Hq, D), k.reshape(T, Hkv, D), v.reshape(T, Hkv, D), L["q_bias"], L["k_bias"],
+                L["v_bias"], pos, slots, p["theta"], L["k_cache"], L["v_cache"])
+            if bad:
+                raise ValueError(f"{bad} tokens with an out-of-range position or slot")
+            q, kc, vc = rnd(q), rnd(kc), rnd(vc)
+            caches.append((kc, vc))
+            ctx, bad = self.attention_head_major(q, kc, vc, pos, slots)
+            a = rnd(self.matmul(rnd(ctx).reshape(T, Hq * D), L["wo"]))
+            x = rnd(x + a)                                                # add_inplace(attn_out, x)
+            h2 = rnd(self.rms_norm(x, L["post_norm_w"], p["eps"]))
+            s = rnd(self.silu_mul(rnd(self.matmul(h2, L["w_gate"])), rnd(self.matmul(h2, L["w_up"]))))
+            d = rnd(self.matmul(s, L["w_down"]))
+        x = rnd(x + d)
+        normed = rnd(self.rms_norm(x, p["final_norm_w"], p["eps"]))
+        last, rc = self.select_last_rows(normed, seq_len=p["seq_len"], n_seqs=p["n_seqs"])
+        if rc != 0:
+            raise ValueError("select_last_rows: bad sequence end")
+        return last, self.matmul(last, p["lm_head"]), caches
+
     def attention(self, q, k_cache, v_cache, past_len: int, n_kv_heads: int) -> np.ndarray:
         """q [seq, Hq, D]; caches [max_seq, Hkv, D] (the reference layout)."""
         q, kc, vc = _f32(q), _f32(k_cache), _f32(v_cache)
@@ -311,6 +360,10 @@ class Reference:
         lib.kref_attention.argtypes = [vp, vp, vp, vp, i64, i64, i32, i32, i32, i32, i32]
         lib.kref_dequantize_int8.argtypes = [vp, i64, ctypes.c_float, vp]
         lib.kref_dequantize_int8_f16.argtypes = [vp, i64, ctypes.c_float, vp]
+        lib.kref_runner_create.restype = vp
+        lib.kref_runner_create.argtypes = [ctypes.c_char_p, i32]
+        lib.kref_runner_destroy.argtypes = [vp]
+        lib.kref_runner_forward.argtypes = [vp, vp, i32, i32, vp, i64]
         lib.kref_table_create.restype = vp
         lib.kref_table_create.argtypes = [i64, i64, ctypes.c_uint64]
         lib.kref_table_destroy.argtypes = [vp]
@@ -431,6 +484,31 @@ class Reference:
         out = np.empty(q.shape, dtype=np.uint16)
         self.lib.kref_dequantize_int8_f16(self._vp(q), q.size, scale, self._vp(out))
         return out
+
+
+class ReferenceRunner:
+    """The reference's LlamaRunner (src/model/llama.cpp) over a .kllm file on
+    the CPU, F32 activations; one KV cache of max_seq positions."""
+
+    def __init__(self, ref: "Reference", path: str, max_seq: int, vocab: int):
+        self.lib, self.vocab = ref.lib, vocab
+        self.h = self.lib.kref_runner_create(path.encode(), max_seq)
+        if not self.h:
+            raise RuntimeError(self.lib.kref_last_error().decode())
+
+    def forward(self, ids, past_len: int) -> np.ndarray:
+        """LlamaRunner::forward: the last token's logits."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        out = np.empty(self.vocab, dtype=np.float32)
+        if self.lib.kref_runner_forward(self.h, ctypes.c_void_p(ids.ctypes.data), ids.size, past_len,
+                                        ctypes.c_void_p(out.ctypes.data), self.vocab) != 0:
+            raise RuntimeError(self.lib.kref_last_error().decode())
+        return out
+
+    def close(self) -> None:
+        if self.h:
+            self.lib.kref_runner_destroy(self.h)
+            self.h = None
 
 
 class ReferenceWeights:

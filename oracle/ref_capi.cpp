@@ -23,6 +23,7 @@
 
 #include "kllm/base/half.h"
 #include "kllm/base/tensor.h"
+#include "kllm/model/llama.h"
 #include "kllm/model/weights.h"
 #include "kllm/op/ops.h"
 
@@ -269,6 +270,34 @@ std::int64_t kref_weights_get(void* w, const char* name, float* out, std::int64_
 int kref_weights_dtype(void* w, const char* name) {
   const kllm::Tensor* t = static_cast<kllm::ModelWeights*>(w)->find(name);
   return t == nullptr ? -1 : static_cast<int>(t->dtype());
+}
+
+// ---- the reference model runner (src/model/llama.cpp) on the CPU ----------
+
+// LlamaRunner over a .kllm file loaded on the CPU (F32 activations).
+void* kref_runner_create(const char* path, int max_seq) {
+  try {
+    return new kllm::LlamaRunner(kllm::ModelWeights::load(path, kllm::DeviceType::CPU), kllm::DeviceType::CPU,
+                                 max_seq);
+  } catch (const std::exception& e) {
+    g_error = e.what();
+    return nullptr;
+  }
+}
+
+void kref_runner_destroy(void* r) { delete static_cast<kllm::LlamaRunner*>(r); }
+
+// One LlamaRunner::forward (src/model/llama.cpp:68-184) of n tokens at
+// past_len; the last token's logits (vocab floats) go to `logits`.
+int kref_runner_forward(void* r, const std::int32_t* ids, int n, int past_len, float* logits,
+                        std::int64_t vocab) {
+  return guarded([&] {
+    std::vector<int> in(ids, ids + n);
+    const kllm::Tensor out = static_cast<kllm::LlamaRunner*>(r)->forward(in, past_len);
+    const std::vector<float> v = out.to_float_vector();
+    if (static_cast<std::int64_t>(v.size()) != vocab) throw std::runtime_error("logits size mismatch");
+    std::memcpy(logits, v.data(), v.size() * sizeof(float));
+  });
 }
 
 // ---- timing chain -------------------------------------------------------

@@ -113,14 +113,36 @@ def test_last_error_is_per_thread(capi):
     assert "even" in capi.last_error()
 
 
-def test_chain_struct_layout(capi):
-    # the ctypes mirror of kllm_b200_chain must match the C layout: 12 int64,
-    # 2 floats, 3 ints (+4 bytes padding), 9 pointers, the layers pointer,
-    # err_flags, the attention workspace pointer and its size
-    assert ctypes.sizeof(capi.Chain) == 12 * 8 + 2 * 4 + 3 * 4 + 4 + 11 * 8 + 2 * 8
-    assert capi.Chain.embed_table.offset == 12 * 8 + 2 * 4 + 3 * 4 + 4
-    assert capi.Chain.attn_workspace.offset == 12 * 8 + 2 * 4 + 3 * 4 + 4 + 11 * 8
-    assert ctypes.sizeof(capi.LayerBuffers) == 18 * 8
+def test_chain_struct_layout(capi, tmp_path):
+    # the ctypes mirrors of kllm_b200_chain, kllm_b200_layer_buffers and
+    # kllm_b200_layer_weights must match the C layout the header declares:
+    # compile a probe against include/kllm_b200.h and compare every offset
+    import shutil
+    import subprocess
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    structs = {"kllm_b200_chain": capi.Chain, "kllm_b200_layer_buffers": capi.LayerBuffers,
+               "kllm_b200_layer_weights": capi.LayerWeights}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "kllm_b200.h"', 'int main(void) {']
+    for cname, cls in structs.items():
+        lines.append(f'  printf("{cname} sizeof %zu\\n", sizeof({cname}));')
+        for fname, _ in cls._fields_:
+            lines.append(f'  printf("{cname} {fname} %zu\\n", offsetof({cname}, {fname}));')
+    lines += ['  return 0;', '}']
+    src = tmp_path / "probe.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "probe"
+    subprocess.run([cc, "-std=c11", "-I", os.path.join(root, "include"), str(src), "-o", str(exe)], check=True)
+    got = {}
+    for line in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.splitlines():
+        cname, fname, value = line.split()
+        got[(cname, fname)] = int(value)
+    for cname, cls in structs.items():
+        assert got[(cname, "sizeof")] == ctypes.sizeof(cls), cname
+        for fname, _ in cls._fields_:
+            assert got[(cname, fname)] == getattr(cls, fname).offset, (cname, fname)
 
 
 def test_attention_validation_without_gpu(capi):
@@ -165,6 +187,34 @@ def test_chain_attention_needs_context_buffers(capi):
     c.layers = ctypes.cast(layers, ctypes.POINTER(capi.LayerBuffers))
     assert capi.lib.kllm_b200_chain_run(ctypes.byref(c), None, None) == capi.ERR_INVALID_ARG
     assert "attn_ctx" in capi.last_error()
+
+
+def test_chain_gemm_needs_attention_and_weights(capi):
+    """KLLM_B200_OP_GEMM without the attention op, without weights, or with a
+    layer missing a weight is refused before any launch."""
+    p = 256
+    layers = (capi.LayerBuffers * 2)()
+    for L in layers:
+        L.attn_ctx = p
+    weights = (capi.LayerWeights * 2)()
+    c = capi.Chain()
+    c.n_tokens, c.hidden, c.n_heads, c.n_kv_heads, c.head_dim = 4, 64, 2, 2, 64
+    c.intermediate, c.vocab, c.n_layers, c.n_slots, c.max_seq, c.n_seqs, c.seq_len = 128, 10, 2, 1, 8, 1, 4
+    c.weight_dtype = capi.F16
+    c.layers = ctypes.cast(layers, ctypes.POINTER(capi.LayerBuffers))
+    c.op_mask = capi.OP_CHAIN | capi.OP_GEMM
+    assert capi.lib.kllm_b200_chain_run(ctypes.byref(c), None, None) == capi.ERR_INVALID_ARG
+    assert "attention" in capi.last_error()
+    c.op_mask = capi.OP_FORWARD
+    assert capi.lib.kllm_b200_chain_run(ctypes.byref(c), None, None) == capi.ERR_INVALID_ARG
+    assert "weights" in capi.last_error()
+    c.weights = ctypes.cast(weights, ctypes.POINTER(capi.LayerWeights))
+    for W in weights:
+        for name in ("wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down"):
+            setattr(W, name, p)
+    weights[1].w_down = None
+    assert capi.lib.kllm_b200_chain_run(ctypes.byref(c), None, None) == capi.ERR_INVALID_ARG
+    assert "layer 1" in capi.last_error()
 
 
 def test_gemm_validation_without_gpu(capi):
