@@ -1539,9 +1539,9 @@ def run_forward(args):
 
     def gemms():
         for Lb, W in zip(r.layers, r.weights):
-            ops.linear(Lb["attn_norm_out"], W["wq"], out=Lb["q"])
-            ops.linear(Lb["attn_norm_out"], W["wk"], out=Lb["k"])
-            ops.linear(Lb["attn_norm_out"], W["wv"], out=Lb["v"])
+            ops.qkv_linear_rope_kv_append(Lb["attn_norm_out"], W["wq"], W["wk"], W["wv"], Lb["q_bias"],
+                                          Lb["k_bias"], Lb["v_bias"], r.positions, r.slots, m.theta,
+                                          Lb["k_cache"], Lb["v_cache"], q_out=Lb["q"])
             ops.linear(Lb["attn_ctx"], W["wo"], out=Lb["attn_out"])
             ops.linear_swiglu(Lb["ffn_norm_out"], W["w_gate"], W["w_up"], out=Lb["swiglu_out"])
             ops.linear(Lb["swiglu_out"], W["w_down"], out=Lb["ffn_out"])
@@ -1558,11 +1558,12 @@ def run_forward(args):
     value = T * world / (ms * 1e-3)
     gemm_tflops = work["gemm"] / (gemm_ms * 1e-3) / 1e12
     tc = load_tc_peak(sustained=True)
-    roofline = {"bound": "tensor", "kernel": "gemm_tc_kernel (q/k/v, o, gate/up+SwiGLU, down, lm_head)",
+    roofline = {"bound": "tensor",
+                "kernel": "gemm_tc_kernel (q/k/v with RoPE/KV append, o, gate/up+SwiGLU, down, lm_head)",
                 "achieved": gemm_tflops, "peak": tc["tflops"], "unit": "TFLOP/s", "frac": gemm_tflops / tc["tflops"],
                 "traffic": None, "peak_source": tc["source"], "flops_per_step": work["gemm"],
                 "ms_per_step": gemm_ms, "share_of_step": gemm_ms / ms,
-                "timing": f"the step's {6 * L + 1} GEMM launches alone in one CUDA graph, CUDA events"}
+                "timing": f"the step's {4 * L + 1} GEMM launches alone in one CUDA graph, CUDA events"}
 
     e2e = None
     if not args.no_e2e:

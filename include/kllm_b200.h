@@ -269,6 +269,25 @@ int kllm_b200_linear_swiglu(const void* x, const void* w_gate, const void* w_up,
                             const void* b_gate, const void* b_up, int bias_dtype, void* out,
                             int64_t m, int64_t n, int64_t k, int32_t* err_flags, void* stream);
 
+/* The attention block's projections and their epilogue in one kernel: q, k,
+ * v = x . wq^T, x . wk^T, x . wv^T (linear() x3, src/model/llama.cpp:89-106),
+ * then the work of kllm_b200_qkv_bias_rope_kv_append on them (bias, RoPE of
+ * q and k at positions[t], k and v appended to the head-major caches
+ * [n_slots, n_kv_heads, max_seq, head_dim] at slot slots[t]), bit for bit
+ * as those separate calls compute it. q_out is [n_tokens, n_heads*head_dim];
+ * k and v are never written elsewhere. x [n_tokens, hidden], wq
+ * [n_heads*head_dim, hidden], wk and wv [n_kv_heads*head_dim, hidden], fp16,
+ * 16-byte aligned; hidden a multiple of 8; head_dim 64 or 128. Out-of-range
+ * positions or slots skip the token's cache rows and set
+ * KLLM_B200_FLAG_BAD_POSITION / _BAD_SLOT. */
+int kllm_b200_qkv_linear_rope_kv_append(const void* x, const void* wq, const void* wk, const void* wv,
+                                        const void* bq, const void* bk, const void* bv, int bias_dtype,
+                                        const int32_t* positions, const int32_t* slots, int64_t n_tokens,
+                                        int64_t hidden, int64_t n_heads, int64_t n_kv_heads,
+                                        int64_t head_dim, float theta, void* q_out, void* k_cache,
+                                        void* v_cache, int64_t n_slots, int64_t max_seq,
+                                        int32_t* err_flags, void* stream);
+
 /* ======================================================================== *
  *  Layer-op chain executor                                                  *
  * ======================================================================== */
@@ -331,7 +350,9 @@ enum {
   KLLM_B200_OP_ATTENTION = 128,
   /* the GEMMs too, making the chain the whole forward step of
    * LlamaRunner::forward (src/model/llama.cpp:78-184): per layer the q, k
-   * and v linears after the input norm (into q, k, v), the o linear after
+   * and v linears after the input norm with the bias + RoPE + KV append in
+   * their epilogue (kllm_b200_qkv_linear_rope_kv_append: q rotated into q,
+   * k and v straight into the caches), the o linear after
    * attention (into attn_out), the gate/up linears with SwiGLU fused (into
    * swiglu_out; replaces KLLM_B200_OP_SWIGLU's silu_mul), the down linear
    * (into ffn_out); after select, logits = last_rows . lm_head^T when
@@ -370,7 +391,8 @@ typedef struct kllm_b200_chain {
  * add+RMSNorm, SwiGLU, then the final add+RMSNorm and select_last_rows (the
  * op kinds selected by op_mask; 0 selects the seven ops without attention).
  * With KLLM_B200_OP_GEMM the layer's GEMMs run in between and the step is
- * the whole forward: q, k, v, attn_out and ffn_out are then written.
+ * the whole forward: q, attn_out and ffn_out are then written (k and v go
+ * straight into the caches).
  * *n_launches (if given) receives the number of kernels launched. Can be
  * captured into a CUDA graph. */
 int kllm_b200_chain_run(const kllm_b200_chain* chain, int* n_launches, void* stream);

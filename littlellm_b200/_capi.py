@@ -111,6 +111,8 @@ SIGNATURES = {
     "kllm_b200_dequantize_int8_host_static": [_vp, _f32, _vp, _i64, _int, _vp],
     "kllm_b200_linear": [_vp, _vp, _vp, _int, _vp, _i64, _i64, _i64, _vp, _vp],
     "kllm_b200_linear_swiglu": [_vp, _vp, _vp, _vp, _vp, _int, _vp, _i64, _i64, _i64, _vp, _vp],
+    "kllm_b200_qkv_linear_rope_kv_append": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _int, _vp, _vp, _i64, _i64, _i64,
+                                            _i64, _i64, _f32, _vp, _vp, _vp, _i64, _i64, _vp, _vp],
     # argtypes of the .kllm entry points use the structures in loader.py
     "kllm_b200_kllm_read_index": None,
     "kllm_b200_kllm_load": None,

@@ -13,7 +13,8 @@
 //   select_last_rows                                          (:173)
 // With KLLM_B200_OP_GEMM the GEMMs run in between (tcgen05, gemm.cu), and the
 // step is the whole forward of llama.cpp:78-184:
-//   after the input norm   q, k, v = linear(attn_norm, wq / wk / wv)   (:89-106)
+//   after the input norm   q, k, v = linear(attn_norm, wq / wk / wv)   (:89-106), with
+//                          bias + RoPE + KV append in the same kernel   (:108-114)
 //   after attention        attn_out = linear(ctx, wo, o_bias)          (:129-134)
 //   instead of SwiGLU      swiglu = silu_mul(linear(ffn_norm, w_gate), linear(ffn_norm, w_up)),
 //                          one kernel                                   (:145-158)
@@ -61,7 +62,7 @@ extern "C" int kllm_b200_chain_run(const kllm_b200_chain* c, int* n_launches, vo
     }
   }
   auto on = [mask](int bit) { return (mask & bit) != 0; };
-  const int64_t qd = c->n_heads * c->head_dim, kvd = c->n_kv_heads * c->head_dim, I = c->intermediate;
+  const int64_t qd = c->n_heads * c->head_dim, I = c->intermediate;
   int launched = 0;
   int rc = KLLM_B200_OK;
   if (on(KLLM_B200_OP_EMBEDDING)) {
@@ -78,15 +79,14 @@ extern "C" int kllm_b200_chain_run(const kllm_b200_chain* c, int* n_launches, vo
       if (rc != KLLM_B200_OK) return rc;
       ++launched;
     }
-    if (gemm) {  // q, k and v projections of the normed residual (biases go with RoPE)
+    if (gemm) {  // q/k/v projections with bias + RoPE + KV append in the GEMM's epilogue
       const kllm_b200_layer_weights& W = c->weights[l];
-      rc = linear(L.attn_norm_out, W.wq, nullptr, wdt, L.q, T, qd, H, c->err_flags, o);
-      if (rc == KLLM_B200_OK) rc = linear(L.attn_norm_out, W.wk, nullptr, wdt, const_cast<void*>(L.k), T, kvd, H, c->err_flags, o);
-      if (rc == KLLM_B200_OK) rc = linear(L.attn_norm_out, W.wv, nullptr, wdt, const_cast<void*>(L.v), T, kvd, H, c->err_flags, o);
+      rc = qkv_linear_rope_kv_append(L.attn_norm_out, W.wq, W.wk, W.wv, L.q_bias, L.k_bias, L.v_bias, wdt,
+                                     c->positions, c->slots, T, H, c->n_heads, c->n_kv_heads, c->head_dim,
+                                     c->theta, L.q, L.k_cache, L.v_cache, c->n_slots, c->max_seq, c->err_flags, o);
       if (rc != KLLM_B200_OK) return rc;
-      launched += 3;
-    }
-    if (on(KLLM_B200_OP_QKV_ROPE)) {
+      ++launched;
+    } else if (on(KLLM_B200_OP_QKV_ROPE)) {
       rc = qkv_bias_rope_kv_append(L.q, L.k, L.v, L.q_bias, L.k_bias, L.v_bias, wdt, c->positions, c->slots, T,
                                    c->n_heads, c->n_kv_heads, c->head_dim, c->theta, L.k_cache, L.v_cache,
                                    c->n_slots, c->max_seq, c->err_flags, o);

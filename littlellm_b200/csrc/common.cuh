@@ -149,6 +149,22 @@ __device__ __forceinline__ uint32_t f2_to_h2(float lo, float hi) {
 
 __device__ __forceinline__ float round_f16(float x) { return __half2float(__float2half_rn(x)); }
 
+// RoPE pair rotation shared by every RoPE path (the fused bias+RoPE+KV
+// kernel, rope_inplace, the QKV GEMM epilogue) so that they agree bit for bit:
+// y1 = x1*c - x2*s, y2 = x2*c + x1*s, each as one fp32 product and one FMA.
+__device__ __forceinline__ void rope_rotate(float x1, float x2, float c, float s, float& y1, float& y2) {
+  y1 = __fmaf_rn(x1, c, -__fmul_rn(x2, s));
+  y2 = __fmaf_rn(x2, c, __fmul_rn(x1, s));
+}
+
+// (cos, sin) of the RoPE angle pos * inv_freq, the angle as one fp32 product
+// and the accurate sincosf.
+__device__ __forceinline__ float2 rope_angle_cs(int32_t pos, float inv_freq) {
+  float s, c;
+  sincosf(__fmul_rn(static_cast<float>(pos), inv_freq), &s, &c);
+  return make_float2(c, s);
+}
+
 // silu(g) = g * sigmoid(g) = g / (1 + e^-g). The exponent argument is capped
 // at 80 so 1 + e^-g stays finite; below g = -80 the result is ~1e-33, zero
 // in fp16 either way.

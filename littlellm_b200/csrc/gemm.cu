@@ -70,18 +70,37 @@ enum GemmBar {
   kNumBars = kMmaDone + 1
 };
 
+// Epilogue kinds: linear (bias), SwiGLU over stacked gate/up rows, and the
+// q/k/v projections with bias + RoPE + KV-cache append.
+enum GemmEpi { kEpiLinear = 0, kEpiSwiGLU = 1, kEpiQkvRope = 2 };
+
+constexpr int kMaxHalfDim = 64;  // RoPE frequencies: head_dim <= 128
+
 struct alignas(64) GemmArgs {
   CUtensorMap map_a;   // x [m, k], box 64 x 128
-  CUtensorMap map_b;   // w [n, k] (SwiGLU: w_gate), box 64 x BN (SwiGLU: 64 x BN / 2)
-  CUtensorMap map_b2;  // SwiGLU: w_up, box 64 x BN / 2
-  __half* out;         // [m, n]
-  const void* bias;    // [n] or NULL (SwiGLU: gate bias)
-  const void* bias2;   // SwiGLU: up bias or NULL
+  CUtensorMap map_b;   // w [n, k] (SwiGLU: w_gate; QKV: wq), box 64 x BN (SwiGLU: 64 x BN / 2)
+  CUtensorMap map_b2;  // SwiGLU: w_up, box 64 x BN / 2; QKV: wk
+  CUtensorMap map_b3;  // QKV: wv
+  __half* out;         // [m, n] (QKV: q out, [m, n_heads * head_dim])
+  const void* bias;    // [n] or NULL (SwiGLU: gate bias; QKV: q bias)
+  const void* bias2;   // SwiGLU: up bias; QKV: k bias; or NULL
+  const void* bias3;   // QKV: v bias or NULL
   int32_t* err_flags;
   int64_t m, n;        // output rows and columns
   int m_tiles, n_tiles, k_blocks;
   int group;           // row tiles per raster group
   int vec_out;         // n % 8 == 0: 16-byte stores
+  // QKV + RoPE epilogue: the column tiles are q_tiles of wq, k_tiles of wk,
+  // then those of wv; k and v go to the head-major caches
+  // [n_slots, n_kv_heads, max_seq, head_dim] at (slots[row], positions[row])
+  int q_tiles, k_tiles;
+  int head_dim, n_heads, n_kv_heads;
+  __half* k_cache;
+  __half* v_cache;
+  const int32_t* positions;
+  const int32_t* slots;
+  int64_t n_slots, max_seq;
+  float inv_freq[kMaxHalfDim];
 };
 
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
@@ -206,8 +225,111 @@ __device__ __forceinline__ void store_swiglu(const GemmArgs& a, int64_t row, int
   }
 }
 
-template <int kBN, bool kSwiGLU, typename TB>
+// The q/k/v tile's epilogue (kEpiQkvRope; a tile of kBN columns holds whole
+// heads of 64 or 128 columns, all of one segment). Bias and rounding as linear() + add_bias_inplace store
+// them, then for q and k the rotate-half RoPE of pairs (d, d + D/2) at the
+// row's position with the same arithmetic as the fused RoPE kernel; q to its
+// buffer, k and v into the caches (rows whose position or slot is out of
+// range write no cache row and set the error flag).
+template <int kBN, typename TB>
+__device__ __forceinline__ void qkv_rope_epilogue(const GemmArgs& a, uint32_t t, int64_t row, int nt) {
+  const int D = a.head_dim;
+  int seg, ct;
+  if (nt < a.q_tiles) {
+    seg = 0;
+    ct = nt;
+  } else if (nt < a.q_tiles + a.k_tiles) {
+    seg = 1;
+    ct = nt - a.q_tiles;
+  } else {
+    seg = 2;
+    ct = nt - a.q_tiles - a.k_tiles;
+  }
+  const int col0 = ct * kBN;  // first column of the tile within its segment
+  const int seg_cols = (seg == 0 ? a.n_heads : a.n_kv_heads) * D;
+  const void* bias = seg == 0 ? a.bias : (seg == 1 ? a.bias2 : a.bias3);
+  const bool live = row < a.m;
+  int32_t pos = 0, slot = 0;
+  bool cache_ok = false;
+  if (live) {
+    pos = a.positions[row];
+    slot = a.slots[row];
+    cache_ok = pos >= 0 && pos < a.max_seq && slot >= 0 && slot < a.n_slots;
+    if (seg == 1 && ct == 0) {  // one tile per row reports a bad position or slot
+      if (pos < 0 || pos >= a.max_seq) set_flag(a.err_flags, KLLM_B200_FLAG_BAD_POSITION);
+      if (slot < 0 || slot >= a.n_slots) set_flag(a.err_flags, KLLM_B200_FLAG_BAD_SLOT);
+    }
+  }
+  auto cache_row = [&](__half* cache, int head) {
+    return cache + ((static_cast<int64_t>(slot) * a.n_kv_heads + head) * a.max_seq + pos) * D;
+  };
+  if (seg == 2) {  // v: bias only, straight into the cache
+#pragma unroll 1
+    for (int c = 0; c < kBN / 32; ++c) {
+      float v[32];
+      tmem_ld32(t + c * 32, v);
+      tc_wait_ld();
+      const int col = col0 + c * 32;
+      if (live && cache_ok && col < seg_cols) {
+        __half* dst = cache_row(a.v_cache, col / D) + col % D;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 w;
+          w.x = h2_bits(round_bias2<TB>(v[q * 8 + 0], v[q * 8 + 1], bias, col + q * 8 + 0));
+          w.y = h2_bits(round_bias2<TB>(v[q * 8 + 2], v[q * 8 + 3], bias, col + q * 8 + 2));
+          w.z = h2_bits(round_bias2<TB>(v[q * 8 + 4], v[q * 8 + 5], bias, col + q * 8 + 4));
+          w.w = h2_bits(round_bias2<TB>(v[q * 8 + 6], v[q * 8 + 7], bias, col + q * 8 + 6));
+          st_plain(dst + q * 8, w);
+        }
+      }
+    }
+    return;
+  }
+  const int half = D / 2;
+  // 32 frequencies at a time (d = j*32 .. j*32+31), shared by the tile's heads
+#pragma unroll 1
+  for (int j = 0; j < half / 32; ++j) {
+    float cs[32], sn[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float2 e = rope_angle_cs(pos, a.inv_freq[j * 32 + i]);
+      cs[i] = e.x;
+      sn[i] = e.y;
+    }
+#pragma unroll 1
+    for (int hc = 0; hc < kBN; hc += D) {  // heads of this tile
+      const int col = col0 + hc;
+      if (col >= seg_cols) break;  // a segment that ends inside the tile (uniform)
+      float x1[32], x2[32];
+      tmem_ld32(t + hc + j * 32, x1);
+      tmem_ld32(t + hc + half + j * 32, x2);
+      tc_wait_ld();
+      if (!live || (seg == 1 && !cache_ok)) continue;
+      uint32_t p1[16], p2[16];
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        // fp16 rounding of the linear, the bias add, then the rotation in fp32
+        const float2 a1 = __half22float2(round_bias2<TB>(x1[i], x1[i + 1], bias, col + j * 32 + i));
+        const float2 a2 = __half22float2(round_bias2<TB>(x2[i], x2[i + 1], bias, col + half + j * 32 + i));
+        float y1a, y2a, y1b, y2b;
+        rope_rotate(a1.x, a2.x, cs[i], sn[i], y1a, y2a);
+        rope_rotate(a1.y, a2.y, cs[i + 1], sn[i + 1], y1b, y2b);
+        p1[i / 2] = h2_bits(__floats2half2_rn(y1a, y1b));
+        p2[i / 2] = h2_bits(__floats2half2_rn(y2a, y2b));
+      }
+      __half* dst = seg == 0 ? a.out + row * a.n + col : cache_row(a.k_cache, col / D);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        st_plain(dst + j * 32 + q * 8, make_uint4(p1[q * 4], p1[q * 4 + 1], p1[q * 4 + 2], p1[q * 4 + 3]));
+        st_plain(dst + half + j * 32 + q * 8, make_uint4(p2[q * 4], p2[q * 4 + 1], p2[q * 4 + 2], p2[q * 4 + 3]));
+      }
+    }
+  }
+}
+
+template <int kBN, int kEpi, typename TB>
 __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_constant__ GemmArgs a) {
+  constexpr bool kSwiGLU = kEpi == kEpiSwiGLU;
   constexpr int kStages = gemm_stages(kBN);
   constexpr int kStageBytes = gemm_stage_bytes(kBN);
   constexpr int kBBytes = kBN * kBK * 2;
@@ -240,7 +362,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     tma_prefetch_map(&a.map_a);
     tma_prefetch_map(&a.map_b);
-    if (kSwiGLU) tma_prefetch_map(&a.map_b2);
+    if (kEpi != kEpiLinear) tma_prefetch_map(&a.map_b2);
+    if (kEpi == kEpiQkvRope) tma_prefetch_map(&a.map_b3);
   }
   tc_fence_before();
   __syncthreads();
@@ -257,7 +380,18 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
       for (int tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x) {
         int mt, nt;
         tile_coords(tile, a.m_tiles, a.n_tiles, a.group, mt, nt);
-        const int m0 = mt * kBM, n0 = nt * kOutCols;
+        const int m0 = mt * kBM;
+        int n0 = nt * kOutCols;
+        const CUtensorMap* bmap = &a.map_b;
+        if (kEpi == kEpiQkvRope) {  // the tile's weight: wq, wk or wv
+          if (nt >= a.q_tiles + a.k_tiles) {
+            bmap = &a.map_b3;
+            n0 = (nt - a.q_tiles - a.k_tiles) * kOutCols;
+          } else if (nt >= a.q_tiles) {
+            bmap = &a.map_b2;
+            n0 = (nt - a.q_tiles) * kOutCols;
+          }
+        }
         for (int kb = 0; kb < a.k_blocks; ++kb, ++it) {
           const int s = it % kStages;
           if (it >= kStages) {  // the slice issued kStages ago into this stage has been consumed
@@ -271,7 +405,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
             tma_load_2d(sb, &a.map_b, kb * kBK, n0, bar(kFull + s));
             tma_load_2d(sb + kBBytes / 2, &a.map_b2, kb * kBK, n0, bar(kFull + s));
           } else {
-            tma_load_2d(sb, &a.map_b, kb * kBK, n0, bar(kFull + s));
+            tma_load_2d(sb, bmap, kb * kBK, n0, bar(kFull + s));
           }
         }
       }
@@ -331,7 +465,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
       const int64_t row = static_cast<int64_t>(mt) * kBM + r;
       const int64_t n0 = static_cast<int64_t>(nt) * kOutCols;
       const uint32_t t = tmem + (static_cast<uint32_t>(quad * 32) << 16) + b * kBN;
-      if constexpr (!kSwiGLU) {
+      if constexpr (kEpi == kEpiQkvRope) {
+        qkv_rope_epilogue<kBN, TB>(a, t, row, nt);
+      } else if constexpr (!kSwiGLU) {
 #pragma unroll 1
         for (int c = 0; c < kBN / 32; ++c) {
           float v[32];
@@ -417,9 +553,9 @@ int check_gemm_args(const char* what, const void* x, const void* w, const void* 
   return KLLM_B200_OK;
 }
 
-template <int kBN, bool kSwiGLU, typename TB>
+template <int kBN, int kEpi, typename TB>
 int launch_gemm(GemmArgs& a, const LaunchOpts& o, const char* what) {
-  auto kernel = gemm_tc_kernel<kBN, kSwiGLU, TB>;
+  auto kernel = gemm_tc_kernel<kBN, kEpi, TB>;
   constexpr size_t smem = gemm_smem(kBN);
   cudaError_t err = allow_smem(reinterpret_cast<const void*>(kernel), smem);
   if (err != cudaSuccess) return launch_status(err, what);
@@ -454,9 +590,10 @@ int pick_tile_width(int64_t m, int64_t n, bool swiglu) {
 template <int kBN>
 int dispatch_gemm(GemmArgs& a, bool swiglu, bool f32_bias, const LaunchOpts& o, const char* what) {
   if (swiglu) {
-    return f32_bias ? launch_gemm<kBN, true, float>(a, o, what) : launch_gemm<kBN, true, __half>(a, o, what);
+    return f32_bias ? launch_gemm<kBN, kEpiSwiGLU, float>(a, o, what)
+                    : launch_gemm<kBN, kEpiSwiGLU, __half>(a, o, what);
   }
-  return f32_bias ? launch_gemm<kBN, false, float>(a, o, what) : launch_gemm<kBN, false, __half>(a, o, what);
+  return f32_bias ? launch_gemm<kBN, kEpiLinear, float>(a, o, what) : launch_gemm<kBN, kEpiLinear, __half>(a, o, what);
 }
 
 int run_gemm(const void* x, const void* w, const void* w2, const void* bias, const void* bias2, int bias_dtype,
@@ -488,7 +625,87 @@ int run_gemm(const void* x, const void* w, const void* w2, const void* bias, con
   return bn == 256 ? dispatch_gemm<256>(a, swiglu, f32_bias, o, what) : dispatch_gemm<128>(a, swiglu, f32_bias, o, what);
 }
 
+template <typename TB>
+int launch_qkv(GemmArgs& a, int bn, const LaunchOpts& o, const char* what) {
+  return bn == 256 ? launch_gemm<256, kEpiQkvRope, TB>(a, o, what) : launch_gemm<128, kEpiQkvRope, TB>(a, o, what);
+}
+
 }  // namespace
+
+int qkv_linear_rope_kv_append(const void* x, const void* wq, const void* wk, const void* wv, const void* bq,
+                              const void* bk, const void* bv, int bias_dtype, const int32_t* positions,
+                              const int32_t* slots, int64_t n_tokens, int64_t hidden, int64_t n_heads,
+                              int64_t n_kv_heads, int64_t head_dim, float theta, void* q_out, void* k_cache,
+                              void* v_cache, int64_t n_slots, int64_t max_seq, int32_t* err_flags,
+                              const LaunchOpts& o) {
+  const char* what = "qkv_linear_rope_kv_append";
+  if (n_tokens < 0 || hidden < 0 || n_heads < 0 || n_kv_heads < 0 || n_slots < 0 || max_seq < 0) {
+    return fail(KLLM_B200_ERR_INVALID_ARG, "%s: negative size", what);
+  }
+  if (head_dim != 64 && head_dim != 128) {
+    return fail(KLLM_B200_ERR_SHAPE, "%s: head_dim %lld not supported (64, 128)", what, (long long)head_dim);
+  }
+  if ((bq || bk || bv) && bias_dtype != KLLM_B200_F16 && bias_dtype != KLLM_B200_F32) {
+    return fail(KLLM_B200_ERR_DTYPE, "%s: bias dtype %d not supported (F32, F16)", what, bias_dtype);
+  }
+  if (n_tokens == 0) return KLLM_B200_OK;
+  if (n_heads == 0 || n_kv_heads == 0) return fail(KLLM_B200_ERR_SHAPE, "%s: no heads", what);
+  if (hidden == 0 || hidden % 8 != 0) {
+    return fail(KLLM_B200_ERR_SHAPE, "%s: hidden = %lld is not a positive multiple of 8", what, (long long)hidden);
+  }
+  if (n_slots == 0 || max_seq == 0) return fail(KLLM_B200_ERR_SHAPE, "%s: empty cache", what);
+  if (n_tokens > (1LL << 31) || hidden > (1LL << 31) || n_heads * head_dim > (1LL << 24) ||
+      n_kv_heads * head_dim > (1LL << 24)) {
+    return fail(KLLM_B200_ERR_SHAPE, "%s: dimension too large", what);
+  }
+  if (!x || !wq || !wk || !wv || !positions || !slots || !q_out || !k_cache || !v_cache) {
+    return fail(KLLM_B200_ERR_INVALID_ARG, "%s: null pointer", what);
+  }
+  if (!aligned16(x) || !aligned16(wq) || !aligned16(wk) || !aligned16(wv) || !aligned16(q_out) ||
+      !aligned16(k_cache) || !aligned16(v_cache)) {
+    return fail(KLLM_B200_ERR_ALIGN, "%s: x, weights, q and the caches must be 16-byte aligned", what);
+  }
+  for (const void* b : {bq, bk, bv}) {
+    if (b && (reinterpret_cast<uintptr_t>(b) & 3u)) return fail(KLLM_B200_ERR_ALIGN, "%s: biases must be 4-byte aligned", what);
+  }
+  const int64_t qd = n_heads * head_dim, kvd = n_kv_heads * head_dim;
+  // a tile never spans two segments: 256-wide tiles only when both segment
+  // widths are multiples of 256, and then only where the tile model prefers them
+  const int bn = (qd % 256 == 0 && kvd % 256 == 0) ? pick_tile_width(n_tokens, qd + 2 * kvd, false) : 128;
+  GemmArgs a;
+  memset(&a, 0, sizeof(a));
+  int rc;
+  if ((rc = make_map(&a.map_a, x, n_tokens, hidden, kBM, what)) != KLLM_B200_OK) return rc;
+  if ((rc = make_map(&a.map_b, wq, qd, hidden, bn, what)) != KLLM_B200_OK) return rc;
+  if ((rc = make_map(&a.map_b2, wk, kvd, hidden, bn, what)) != KLLM_B200_OK) return rc;
+  if ((rc = make_map(&a.map_b3, wv, kvd, hidden, bn, what)) != KLLM_B200_OK) return rc;
+  a.out = static_cast<__half*>(q_out);
+  a.bias = bq;
+  a.bias2 = bk;
+  a.bias3 = bv;
+  a.err_flags = err_flags;
+  a.m = n_tokens;
+  a.n = qd;
+  a.q_tiles = static_cast<int>((qd + bn - 1) / bn);
+  a.k_tiles = static_cast<int>((kvd + bn - 1) / bn);
+  a.m_tiles = static_cast<int>((n_tokens + kBM - 1) / kBM);
+  a.n_tiles = a.q_tiles + 2 * a.k_tiles;
+  a.k_blocks = static_cast<int>((hidden + kBK - 1) / kBK);
+  a.group = kGroupRows / kBM;
+  a.vec_out = 1;
+  a.head_dim = static_cast<int>(head_dim);
+  a.n_heads = static_cast<int>(n_heads);
+  a.n_kv_heads = static_cast<int>(n_kv_heads);
+  a.k_cache = static_cast<__half*>(k_cache);
+  a.v_cache = static_cast<__half*>(v_cache);
+  a.positions = positions;
+  a.slots = slots;
+  a.n_slots = n_slots;
+  a.max_seq = max_seq;
+  rope_inv_freq(a.inv_freq, static_cast<int>(head_dim), theta);
+  const bool f32_bias = (bq || bk || bv) && bias_dtype == KLLM_B200_F32;
+  return f32_bias ? launch_qkv<float>(a, bn, o, what) : launch_qkv<__half>(a, bn, o, what);
+}
 
 int linear(const void* x, const void* w, const void* bias, int bias_dtype, void* out, int64_t m, int64_t n,
            int64_t k, int32_t* err_flags, const LaunchOpts& o) {
@@ -516,4 +733,16 @@ extern "C" int kllm_b200_linear_swiglu(const void* x, const void* w_gate, const 
   kb::LaunchOpts o;
   o.stream = static_cast<cudaStream_t>(stream);
   return kb::linear_swiglu(x, w_gate, w_up, b_gate, b_up, bias_dtype, out, m, n, k, err_flags, o);
+}
+
+extern "C" int kllm_b200_qkv_linear_rope_kv_append(
+    const void* x, const void* wq, const void* wk, const void* wv, const void* bq, const void* bk, const void* bv,
+    int bias_dtype, const int32_t* positions, const int32_t* slots, int64_t n_tokens, int64_t hidden,
+    int64_t n_heads, int64_t n_kv_heads, int64_t head_dim, float theta, void* q_out, void* k_cache, void* v_cache,
+    int64_t n_slots, int64_t max_seq, int32_t* err_flags, void* stream) {
+  kb::LaunchOpts o;
+  o.stream = static_cast<cudaStream_t>(stream);
+  return kb::qkv_linear_rope_kv_append(x, wq, wk, wv, bq, bk, bv, bias_dtype, positions, slots, n_tokens, hidden,
+                                       n_heads, n_kv_heads, head_dim, theta, q_out, k_cache, v_cache, n_slots,
+                                       max_seq, err_flags, o);
 }

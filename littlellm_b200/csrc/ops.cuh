@@ -25,6 +25,10 @@ int qkv_bias_rope_kv_append(void* q, const void* k, const void* v, const void* b
                             float theta, void* k_cache, void* v_cache, int64_t n_slots, int64_t max_seq,
                             int32_t* err_flags, const LaunchOpts& o);
 
+// RoPE frequency table inv_freq[d] = theta^(-2d / head_dim), d < head_dim / 2
+// (host, fp32; shared by every RoPE path).
+void rope_inv_freq(float* inv_freq, int head_dim, float theta);
+
 int dequantize_int8(const int8_t* data, const float* scale, void* out, int64_t n, int out_dtype,
                     const LaunchOpts& o);
 
@@ -46,6 +50,16 @@ int linear(const void* x, const void* w, const void* bias, int bias_dtype, void*
 int linear_swiglu(const void* x, const void* w_gate, const void* w_up, const void* b_gate, const void* b_up,
                   int bias_dtype, void* out, int64_t m, int64_t n, int64_t k, int32_t* err_flags,
                   const LaunchOpts& o);
+
+// q, k, v = x . wq^T, wk^T, wv^T as one tcgen05 GEMM whose epilogue adds the
+// biases, applies RoPE to q and k and appends k and v to the head-major
+// caches: linear x3 + qkv_bias_rope_kv_append in one kernel (gemm.cu).
+int qkv_linear_rope_kv_append(const void* x, const void* wq, const void* wk, const void* wv, const void* bq,
+                              const void* bk, const void* bv, int bias_dtype, const int32_t* positions,
+                              const int32_t* slots, int64_t n_tokens, int64_t hidden, int64_t n_heads,
+                              int64_t n_kv_heads, int64_t head_dim, float theta, void* q_out, void* k_cache,
+                              void* v_cache, int64_t n_slots, int64_t max_seq, int32_t* err_flags,
+                              const LaunchOpts& o);
 
 int attention_workspace_bytes(int64_t n_tokens, int64_t n_heads, int64_t n_kv_heads, int64_t head_dim,
                               int64_t max_seq, int64_t* bytes);

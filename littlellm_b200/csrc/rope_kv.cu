@@ -120,19 +120,6 @@ __device__ __forceinline__ uint4 add_bias8<float>(uint4 x, const float* bias, in
                     f2_to_h2(a2.x + b[4], a2.y + b[5]), f2_to_h2(a3.x + b[6], a3.y + b[7]));
 }
 
-// The per-pair rotation shared by every path (fused, legacy, generic) so that
-// the fused op equals the composition of the separate ops bit for bit:
-// y1 = x1*c - x2*s, y2 = x2*c + x1*s, each as one fp32 product and one FMA.
-__device__ __forceinline__ void rotate(float x1, float x2, float c, float s, float& y1, float& y2) {
-  y1 = __fmaf_rn(x1, c, -__fmul_rn(x2, s));
-  y2 = __fmaf_rn(x2, c, __fmul_rn(x1, s));
-}
-
-__device__ __forceinline__ float2 angle_cs(int32_t pos, float inv_freq) {
-  float s, c;
-  sincosf(__fmul_rn(static_cast<float>(pos), inv_freq), &s, &c);
-  return make_float2(c, s);
-}
 
 // One token is owned by `warps_per_token` warps; the token's work units are
 // dealt to its warps' lanes round-robin (consecutive units on consecutive
@@ -330,7 +317,7 @@ __global__ void __launch_bounds__(kWarpThreads) qkv_rope_warp_kernel(const __gri
       float y1[8], y2[8];
       if (kHoistCs) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) rotate(f1[i], f2[i], cc[i], ss[i], y1[i], y2[i]);
+        for (int i = 0; i < 8; ++i) rope_rotate(f1[i], f2[i], cc[i], ss[i], y1[i], y2[i]);
       } else {
         const int d0 = off[j] % D;
         const float4* cp = reinterpret_cast<const float4*>(&s_cos[warp][d0]);
@@ -339,7 +326,7 @@ __global__ void __launch_bounds__(kWarpThreads) qkv_rope_warp_kernel(const __gri
         const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
         const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
 #pragma unroll
-        for (int i = 0; i < 8; ++i) rotate(f1[i], f2[i], c[i], sn[i], y1[i], y2[i]);
+        for (int i = 0; i < 8; ++i) rope_rotate(f1[i], f2[i], c[i], sn[i], y1[i], y2[i]);
       }
       __half* dst;
       if (is_q) {
@@ -410,9 +397,9 @@ __global__ void __launch_bounds__(kThreads) qkv_rope_generic_kernel(const __grid
         x1 = to_f(from_f<TA>(x1 + to_f(b[h * D + d])));
         x2 = to_f(from_f<TA>(x2 + to_f(b[h * D + d + half])));
       }
-      const float2 c = angle_cs(pos, a.inv_freq[d]);
+      const float2 c = rope_angle_cs(pos, a.inv_freq[d]);
       float y1, y2;
-      rotate(x1, x2, c.x, c.y, y1, y2);
+      rope_rotate(x1, x2, c.x, c.y, y1, y2);
       if (is_q) {
         q[(t * a.n_heads + h) * D + d] = from_f<TA>(y1);
         q[(t * a.n_heads + h) * D + d + half] = from_f<TA>(y2);
@@ -434,12 +421,7 @@ __global__ void __launch_bounds__(kThreads) qkv_rope_generic_kernel(const __grid
   }
 }
 
-void fill_inv_freq(RopeArgs& a, float theta) {
-  const int half = a.head_dim / 2;
-  for (int d = 0; d < half; ++d) {
-    a.inv_freq[d] = std::pow(theta, -2.0f * static_cast<float>(d) / static_cast<float>(a.head_dim));
-  }
-}
+void fill_inv_freq(RopeArgs& a, float theta) { rope_inv_freq(a.inv_freq, a.head_dim, theta); }
 
 template <int DT, int UPL>
 void (*pick_tb(bool bias16, bool pdl))(RopeArgs) {
@@ -584,6 +566,15 @@ int qkv_bias_rope_kv_append(void* q, const void* k, const void* v, const void* b
   a.err_flags = err_flags;
   fill_inv_freq(a, theta);
   return run_rope(a, KLLM_B200_F16, bias_dtype, o, "qkv_bias_rope_kv_append");
+}
+
+// inv_freq[d] = theta^((-2d) / head_dim) for d < head_dim / 2, in fp32 on the
+// host: the expression of src/op/cpu/rope.cpp:24 (also how the reference CUDA
+// path builds its table, src/op/cuda/rope.cu:51-55).
+void rope_inv_freq(float* inv_freq, int head_dim, float theta) {
+  for (int d = 0; d < head_dim / 2; ++d) {
+    inv_freq[d] = std::pow(theta, -2.0f * static_cast<float>(d) / static_cast<float>(head_dim));
+  }
 }
 
 }  // namespace kb

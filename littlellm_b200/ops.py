@@ -244,6 +244,29 @@ def linear_swiglu(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor,
     return out
 
 
+def qkv_linear_rope_kv_append(x: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor, wv: torch.Tensor,
+                              bq: torch.Tensor | None, bk: torch.Tensor | None, bv: torch.Tensor | None,
+                              positions: torch.Tensor, slots: torch.Tensor, theta: float,
+                              k_cache: torch.Tensor, v_cache: torch.Tensor, q_out: torch.Tensor | None = None,
+                              err_flags: torch.Tensor | None = None) -> torch.Tensor:
+    """q = rope(x @ wq.T + bq) into q_out [T, Hq*D]; k = rope(x @ wk.T + bk) and
+    v = x @ wv.T + bv appended to the caches [n_slots, Hkv, max_seq, D] (one
+    tcgen05 GEMM with the bias + RoPE + KV append in its epilogue)."""
+    n_slots, Hkv, max_seq, D = k_cache.shape
+    Hq = wq.shape[0] // D
+    if q_out is None:
+        q_out = torch.empty(x.shape[0], wq.shape[0], dtype=torch.float16, device=x.device)
+    dev = _dev(x, wq, wk, wv, bq, bk, bv, positions, slots, k_cache, v_cache, q_out, err_flags)
+    bias = next((b for b in (bq, bk, bv) if b is not None), None)
+    bias_dtype = dtype_code(bias) if bias is not None else F16
+    with torch.cuda.device(dev):
+        check(lib.kllm_b200_qkv_linear_rope_kv_append(
+            _ptr(x), _ptr(wq), _ptr(wk), _ptr(wv), _ptr(bq), _ptr(bk), _ptr(bv), bias_dtype, _ptr(positions),
+            _ptr(slots), x.shape[0], x.shape[1], Hq, Hkv, D, theta, _ptr(q_out), _ptr(k_cache), _ptr(v_cache),
+            n_slots, max_seq, _ptr(err_flags), _stream(dev)))
+    return q_out
+
+
 def rope_inplace(x: torch.Tensor, past_len: int, theta: float) -> torch.Tensor:
     """x [seq, heads, head_dim] rotated in place at positions past_len + t."""
     dev = _dev(x)

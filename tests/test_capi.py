@@ -244,3 +244,25 @@ def test_gemm_validation_without_gpu(capi):
     rc = lib.kllm_b200_linear_swiglu(p, p, p + 8, None, None, capi.F16, p, 4, 8, 8, None, None)
     assert rc == capi.ERR_ALIGN
     assert lib.kllm_b200_linear_swiglu(p, p, p, None, None, capi.F16, p, 0, 8, 8, None, None) == capi.OK
+
+
+def test_qkv_rope_linear_validation_without_gpu(capi):
+    """kllm_b200_qkv_linear_rope_kv_append rejects bad shapes, pointers and
+    alignment before any CUDA call; no tokens is a successful no-op."""
+    lib = capi.lib
+    p = 16
+
+    def call(x=p, wq=p, n_tokens=4, hidden=64, hq=2, hkv=2, d=64, n_slots=1, max_seq=8, bias=None,
+             bias_dtype=capi.F16):
+        return lib.kllm_b200_qkv_linear_rope_kv_append(x, wq, p, p, bias, None, None, bias_dtype, p, p, n_tokens,
+                                                       hidden, hq, hkv, d, 1e4, p, p, p, n_slots, max_seq, None, None)
+
+    assert call(d=96) == capi.ERR_SHAPE and "head_dim" in capi.last_error()
+    assert call(hidden=60) == capi.ERR_SHAPE and "multiple of 8" in capi.last_error()
+    assert call(max_seq=0) == capi.ERR_SHAPE and "empty cache" in capi.last_error()
+    assert call(hq=0) == capi.ERR_SHAPE
+    assert call(x=None) == capi.ERR_INVALID_ARG and "null" in capi.last_error()
+    assert call(wq=p + 8) == capi.ERR_ALIGN
+    assert call(bias=p, bias_dtype=capi.I8) == capi.ERR_DTYPE
+    assert call(n_tokens=-1) == capi.ERR_INVALID_ARG
+    assert call(n_tokens=0) == capi.OK

@@ -167,3 +167,43 @@ def test_large_tilings_vs_torch_fp32(cuda, ops, what, m, n, k, bias):
     diff = (out.float() - ref).abs()
     bad = diff > TOL + TOL * ref.abs()
     assert not bool(bad.any()), f"{what}: {int(bad.sum())} outside tolerance, max abs err {float(diff.max()):.3g}"
+
+
+@pytest.mark.parametrize("T,hidden,hq,hkv,d,bias", [
+    (300, 896, 14, 2, 64, torch.float16),   # Qwen2.5-0.5B heads, fp16 biases
+    (130, 512, 8, 8, 128, None),            # Llama-style heads, no bias
+    (77, 256, 7, 1, 64, torch.float32),     # odd q heads: the last q tile is half full; fp32 biases
+    (4096, 512, 16, 16, 128, torch.float16),  # large enough for 256-wide tiles (two heads per tile)
+    (4096, 512, 16, 4, 64, None),             # 256-wide tiles of four 64-column heads
+])
+def test_qkv_rope_fused_equals_separate_ops(cuda, ops, T, hidden, hq, hkv, d, bias):
+    """kllm_b200_qkv_linear_rope_kv_append equals linear x3 followed by
+    kllm_b200_qkv_bias_rope_kv_append bit for bit: q, both caches (rows not
+    written stay as they were) and the error flags, with one token at an
+    out-of-range position and one at an out-of-range slot."""
+    g = torch.Generator(device=cuda).manual_seed(T * 31 + hidden)
+    x = torch.randn(T, hidden, device=cuda, generator=g).half()
+    wq, wk, wv = ((torch.randn(h * d, hidden, device=cuda, generator=g) / hidden ** 0.5).half()
+                  for h in (hq, hkv, hkv))
+    bq, bk, bv = ((torch.randn(h * d, device=cuda, generator=g) * 0.1).to(bias) if bias is not None else None
+                  for h in (hq, hkv, hkv))
+    n_slots, max_seq, theta = (64 if T > 500 else 5), 96, 1e6
+    t = torch.arange(T, device=cuda, dtype=torch.int32)
+    slots, positions = t % n_slots, t // n_slots  # distinct (slot, position) per token
+    positions[3] = max_seq
+    slots[5] = -1
+    kc0 = torch.randn(n_slots, hkv, max_seq, d, device=cuda, generator=g).half()
+    vc0 = torch.randn(n_slots, hkv, max_seq, d, device=cuda, generator=g).half()
+
+    kc1, vc1, err1 = kc0.clone(), vc0.clone(), torch.zeros(1, dtype=torch.int32, device=cuda)
+    q1 = ops.qkv_linear_rope_kv_append(x, wq, wk, wv, bq, bk, bv, positions, slots, theta, kc1, vc1, err_flags=err1)
+
+    kc2, vc2, err2 = kc0.clone(), vc0.clone(), torch.zeros(1, dtype=torch.int32, device=cuda)
+    q, k, v = ops.linear(x, wq), ops.linear(x, wk), ops.linear(x, wv)
+    ops.qkv_bias_rope_kv_append(q.view(T, hq, d), k.view(T, hkv, d), v.view(T, hkv, d), bq, bk, bv, positions,
+                                slots, theta, kc2, vc2, err_flags=err2)
+    torch.cuda.synchronize()
+    assert torch.equal(q1, q)
+    assert torch.equal(kc1, kc2)
+    assert torch.equal(vc1, vc2)
+    assert int(err1.item()) == int(err2.item()) != 0
