@@ -1,6 +1,7 @@
 """Sequence-sharded chain on 2 GPUs (one process each, NCCL only for the
 verification gather) reproduces the single-GPU chain bit for bit, with and
-without attention in the chain. Skipped when fewer than 2 GPUs are visible."""
+without attention in the chain, and the whole forward step (GEMMs and
+lm_head included). Skipped when fewer than 2 GPUs are visible."""
 from __future__ import annotations
 
 import os
@@ -22,7 +23,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, out_dir, decode, attention):
+def _worker(rank, world, port, out_dir, decode, attention, gemm=False):
     try:
         sys.path.insert(0, ROOT)
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
@@ -35,22 +36,26 @@ def _worker(rank, world, port, out_dir, decode, attention):
         shape = ModelShape("qwen-2l", 896, 14, 2, 64, 4864, 4096, 2, 1e-6, 1e6)
         w = (Workload("d", shape, n_seqs=16, seq_len=1, max_seq=256, decode=True) if decode
              else Workload("p", shape, n_seqs=4, seq_len=64, max_seq=128, decode=False))
-        part = ChainRunner(w, device=dev, seed=77, use_pdl=True, shard=(rank, world), attention=attention)
+        part = ChainRunner(w, device=dev, seed=77, use_pdl=True, shard=(rank, world), attention=attention,
+                           gemm=gemm)
         part.run()
         torch.cuda.synchronize(dev)
         last = kd.gather_rows(part.last_rows)
         normed = kd.gather_rows(part.final_norm_out)
         swiglu = kd.gather_rows(part.layers[-1]["swiglu_out"])
         ctx = kd.gather_rows(part.layers[-1]["attn_ctx"]) if attention else None
+        logits = kd.gather_rows(part.logits) if gemm else None
         flags = kd.or_over_ranks(int(part.err_flags.item()), dev)
         if rank == 0:
-            full = ChainRunner(w, device=dev, seed=77, use_pdl=True, attention=attention)
+            full = ChainRunner(w, device=dev, seed=77, use_pdl=True, attention=attention, gemm=gemm)
             full.run()
             torch.cuda.synchronize(dev)
             ok = (torch.equal(last, full.last_rows) and torch.equal(normed, full.final_norm_out)
                   and torch.equal(swiglu, full.layers[-1]["swiglu_out"]) and flags == 0)
             if attention:
                 ok = ok and torch.equal(ctx, full.layers[-1]["attn_ctx"])
+            if gemm:
+                ok = ok and torch.equal(logits, full.logits)
             with open(os.path.join(out_dir, "result"), "w") as f:
                 f.write("ok" if ok else "mismatch")
         torch.distributed.barrier()
@@ -61,14 +66,15 @@ def _worker(rank, world, port, out_dir, decode, attention):
         raise
 
 
-@pytest.mark.parametrize("attention", [False, True])
+@pytest.mark.parametrize("attention,gemm", [(False, False), (True, False), (True, True)])
 @pytest.mark.parametrize("decode", [False, True])
-def test_two_gpu_shards_equal_single_gpu(tmp_path, decode, attention):
+def test_two_gpu_shards_equal_single_gpu(tmp_path, decode, attention, gemm):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     ctx = mp.get_context("spawn")
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, str(tmp_path), decode, attention)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, str(tmp_path), decode, attention, gemm))
+             for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
