@@ -55,8 +55,12 @@ constexpr int kMaxStages = 6;
 // The ring holds as many stages as fit in 192 KB.
 __host__ __device__ constexpr int gemm_stages(int bn) { return bn == 256 ? 4 : 6; }
 __host__ __device__ constexpr int gemm_stage_bytes(int bn) { return kABytes + bn * kBK * 2; }
+// Output staging of the epilogue: per epilogue warp two 2 KB buffers, each
+// one 32-row x 32-column fp16 chunk on its way to a TMA store.
+constexpr int kEpiChunkBytes = 32 * 32 * 2;
+constexpr int kEpiStageBytes = kEpiWarps * 2 * kEpiChunkBytes;
 constexpr size_t gemm_smem(int bn) {
-  return static_cast<size_t>(gemm_stages(bn)) * gemm_stage_bytes(bn) + 1024;  // + alignment slack
+  return static_cast<size_t>(gemm_stages(bn)) * gemm_stage_bytes(bn) + kEpiStageBytes + 1024;  // + alignment
 }
 
 // mbarriers: stage full (TMA bytes landed) / empty (MMAs that read it done);
@@ -81,6 +85,7 @@ struct alignas(64) GemmArgs {
   CUtensorMap map_b;   // w [n, k] (SwiGLU: w_gate; QKV: wq), box 64 x BN (SwiGLU: 64 x BN / 2)
   CUtensorMap map_b2;  // SwiGLU: w_up, box 64 x BN / 2; QKV: wk
   CUtensorMap map_b3;  // QKV: wv
+  CUtensorMap map_out; // out [m, n], box 32 x 32, 64-byte swizzle (when tma_out)
   __half* out;         // [m, n] (QKV: q out, [m, n_heads * head_dim])
   const void* bias;    // [n] or NULL (SwiGLU: gate bias; QKV: q bias)
   const void* bias2;   // SwiGLU: up bias; QKV: k bias; or NULL
@@ -90,6 +95,7 @@ struct alignas(64) GemmArgs {
   int m_tiles, n_tiles, k_blocks;
   int group;           // row tiles per raster group
   int vec_out;         // n % 8 == 0: 16-byte stores
+  int tma_out;         // linear / SwiGLU output written by TMA stores from shared memory
   // QKV + RoPE epilogue: the column tiles are q_tiles of wq, k_tiles of wk,
   // then those of wv; k and v go to the head-major caches
   // [n_slots, n_kv_heads, max_seq, head_dim] at (slots[row], positions[row])
@@ -115,6 +121,28 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       "[%4];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
       : "memory");
+}
+
+// 2-D tiled TMA store of the box at (x = column, y = row) from shared memory,
+// tracked in this thread's bulk async-group.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int x, int y, uint32_t src) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(src)
+               : "memory");
+}
+__device__ __forceinline__ void tma_store_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until at most N of this thread's bulk groups still read their shared memory.
+template <int N>
+__device__ __forceinline__ void tma_store_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Wait until this thread's bulk groups have completed (writes performed).
+__device__ __forceinline__ void tma_store_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ void st_shared16(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
 }
 
 __device__ __forceinline__ void tma_prefetch_map(const CUtensorMap* map) {
@@ -168,6 +196,19 @@ __device__ __forceinline__ __half round_bias1(float v, const void* bias, int64_t
 
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
+// The 32 fp16 outputs of one row's 32 accumulator columns starting at output
+// column c0 (bias added when given), as four 16-byte vectors (linear).
+template <typename TB>
+__device__ __forceinline__ void linear_chunk(const GemmArgs& a, int64_t c0, const float (&v)[32], uint4 (&w)[4]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    w[q].x = h2_bits(round_bias2<TB>(v[q * 8 + 0], v[q * 8 + 1], a.bias, c0 + q * 8 + 0));
+    w[q].y = h2_bits(round_bias2<TB>(v[q * 8 + 2], v[q * 8 + 3], a.bias, c0 + q * 8 + 2));
+    w[q].z = h2_bits(round_bias2<TB>(v[q * 8 + 4], v[q * 8 + 5], a.bias, c0 + q * 8 + 4));
+    w[q].w = h2_bits(round_bias2<TB>(v[q * 8 + 6], v[q * 8 + 7], a.bias, c0 + q * 8 + 6));
+  }
+}
+
 // 32 accumulator columns of one row -> out[row, c0 .. c0 + 31] (linear).
 template <typename TB>
 __device__ __forceinline__ void store_linear(const GemmArgs& a, int64_t row, int64_t c0, const float (&v)[32]) {
@@ -194,6 +235,43 @@ __device__ __forceinline__ void store_linear(const GemmArgs& a, int64_t row, int
 __device__ __forceinline__ __half2 swiglu2(__half2 g, __half2 u) {
   const float2 gf = __half22float2(g), uf = __half22float2(u);
   return __floats2half2_rn(silu(gf.x) * uf.x, silu(gf.y) * uf.y);
+}
+
+// SwiGLU outputs of 32 gate and 32 up accumulator columns, as four 16-byte vectors.
+template <typename TB>
+__device__ __forceinline__ void swiglu_chunk(const GemmArgs& a, int64_t c0, const float (&g)[32],
+                                             const float (&u)[32], uint4 (&w)[4]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint32_t p[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int j = q * 8 + e * 2;
+      p[e] = h2_bits(swiglu2(round_bias2<TB>(g[j], g[j + 1], a.bias, c0 + j),
+                             round_bias2<TB>(u[j], u[j + 1], a.bias2, c0 + j)));
+    }
+    w[q] = make_uint4(p[0], p[1], p[2], p[3]);
+  }
+}
+
+// One warp's 32 rows x 32 columns of output through shared memory and a TMA
+// store: lane r writes its row's four 16-byte vectors into the 2 KB buffer
+// `sbuf` in the 64-byte-swizzled layout the output tensor map reads (16-byte
+// chunk q of row r at r * 64 + (q ^ ((r >> 1) & 3)) * 16), then lane 0 stores
+// the box at (column c0, row r0). The buffer alternates per chunk; a buffer is
+// rewritten only after the store issued from it two chunks earlier has read it.
+__device__ __forceinline__ void stage_and_store(const GemmArgs& a, uint32_t sbuf, int lane, int64_t c0, int64_t r0,
+                                                const uint4 (&w)[4]) {
+  if (lane == 0) tma_store_wait_read<1>();
+  __syncwarp();
+#pragma unroll
+  for (int q = 0; q < 4; ++q) st_shared16(sbuf + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4), w[q]);
+  fence_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(&a.map_out, static_cast<int>(c0), static_cast<int>(r0), sbuf);
+    tma_store_commit();
+  }
 }
 
 // 32 gate and 32 up accumulator columns of one row -> out[row, c0 .. c0 + 31].
@@ -454,6 +532,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     // ---------------- epilogue: warps 2-5, one accumulator row per thread ----------------
     const int quad = warp & 3;  // tensor-memory lanes 32 * quad .. + 31 are this warp's
     const int r = quad * 32 + lane;
+    const uint32_t ebuf0 = base + kStages * kStageBytes + quad * 2 * kEpiChunkBytes;  // this warp's buffers
+    int ebuf = 0;
     int i = 0;
     for (int tile = blockIdx.x; tile < n_tiles_total; tile += gridDim.x, ++i) {
       int mt, nt;
@@ -473,7 +553,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
           float v[32];
           tmem_ld32(t + c * 32, v);
           tc_wait_ld();
-          if (row < a.m) store_linear<TB>(a, row, n0 + c * 32, v);
+          if (a.tma_out) {
+            uint4 w[4];
+            linear_chunk<TB>(a, n0 + c * 32, v, w);
+            stage_and_store(a, ebuf0 + ebuf * kEpiChunkBytes, lane, n0 + c * 32, row - lane, w);
+            ebuf ^= 1;
+          } else if (row < a.m) {
+            store_linear<TB>(a, row, n0 + c * 32, v);
+          }
         }
       } else {
 #pragma unroll 1
@@ -482,13 +569,21 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
           tmem_ld32(t + c * 32, g);
           tmem_ld32(t + kBN / 2 + c * 32, u);
           tc_wait_ld();
-          if (row < a.m) store_swiglu<TB>(a, row, n0 + c * 32, g, u);
+          if (a.tma_out) {
+            uint4 w[4];
+            swiglu_chunk<TB>(a, n0 + c * 32, g, u, w);
+            stage_and_store(a, ebuf0 + ebuf * kEpiChunkBytes, lane, n0 + c * 32, row - lane, w);
+            ebuf ^= 1;
+          } else if (row < a.m) {
+            store_swiglu<TB>(a, row, n0 + c * 32, g, u);
+          }
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(kAccEmpty + b));
     }
+    if (lane == 0) tma_store_wait_all();  // the TMA stores have read their buffers and written the output
   }
 
   if (!ok) set_flag(a.err_flags, KLLM_B200_FLAG_TIMEOUT);
@@ -516,18 +611,27 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
 
 // Tensor map of a row-major fp16 [rows, k] matrix read in boxes of 64 (k) x
 // box_rows, 128-byte swizzled; reads past the edges return zeros.
-int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t k, int box_rows, const char* what) {
+// Tensor map of a row-major fp16 [rows, cols] matrix moved in boxes of
+// box_cols x box_rows with the given swizzle; loads past the edges read
+// zeros, stores past them are dropped.
+int make_map2d(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int box_cols, int box_rows,
+               CUtensorMapSwizzle swizzle, const char* what) {
   auto fn = encode_tiled();
   if (fn == nullptr) return fail(KLLM_B200_ERR_CUDA, "%s: cuTensorMapEncodeTiled unavailable", what);
-  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
-  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(k) * 2};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
   const cuuint32_t elem[2] = {1, 1};
   const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, elem,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(KLLM_B200_ERR_INVALID_ARG, "%s: tensor map rejected (CUresult %d)", what, (int)r);
   return KLLM_B200_OK;
+}
+
+// Operand map: [rows, k] read in 64 (k) x box_rows boxes, 128-byte swizzle.
+int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t k, int box_rows, const char* what) {
+  return make_map2d(map, ptr, rows, k, kBK, box_rows, CU_TENSOR_MAP_SWIZZLE_128B, what);
 }
 
 int check_gemm_args(const char* what, const void* x, const void* w, const void* w2, const void* bias,
@@ -621,6 +725,10 @@ int run_gemm(const void* x, const void* w, const void* w2, const void* bias, con
   a.k_blocks = static_cast<int>((k + kBK - 1) / kBK);
   a.group = kGroupRows / kBM;
   a.vec_out = n % 8 == 0;
+  if (a.vec_out) {  // TMA stores: the output row pitch (n * 2 bytes) is a multiple of 16
+    if ((rc = make_map2d(&a.map_out, out, m, n, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B, what)) != KLLM_B200_OK) return rc;
+    a.tma_out = 1;
+  }
   const bool f32_bias = (bias || bias2) && bias_dtype == KLLM_B200_F32;
   return bn == 256 ? dispatch_gemm<256>(a, swiglu, f32_bias, o, what) : dispatch_gemm<128>(a, swiglu, f32_bias, o, what);
 }
