@@ -31,7 +31,6 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kMaxHalf = 128;   // head_dim <= 256
 constexpr int kWarpsPerCta = 4;
-constexpr size_t kMaxBiasStage = 16 * 1024;  // bytes of q/k/v bias staged per CTA
 constexpr int kWarpThreads = 32 * kWarpsPerCta;
 
 struct RopeArgs {
@@ -51,7 +50,6 @@ struct RopeArgs {
   int64_t n_slots, max_seq;
   int32_t* err_flags;
   int warps_per_token;
-  int stage_bias;  // biases fit the shared-memory staging area
   float inv_freq[kMaxHalf];
 };
 
@@ -125,31 +123,29 @@ __device__ __forceinline__ uint4 add_bias8<float>(uint4 x, const float* bias, in
 // dealt to its warps' lanes round-robin (consecutive units on consecutive
 // lanes, so loads and stores coalesce), UPL units per lane. The cos/sin of
 // the token's frequencies go into the warp's slice of shared memory (one or
-// a few sincosf per lane); the q/k/v biases are staged in shared memory with
-// each head's row padded by 16 bytes, so the lanes of one instruction, which
-// read the same column of different heads, hit different banks.
+// a few sincosf per lane). The q/k/v biases are read through L1 (every token
+// reads the same few KB); staging them in shared memory measured slower in
+// the chain (an L2 round trip and a CTA barrier ahead of the loads).
 //
 // DT is the head_dim when it is a compile-time constant (64, 128: unit
 // geometry becomes shifts), 0 for a runtime head_dim.
 //
-// Positions, slots, biases and the frequency table are never written by a
-// kernel of the chain, so with EARLY (the PDL launch of the chain executor)
-// the bias staging, position load and sincos run before the grid-dependency
-// wait, overlapping the previous kernel's tail, and only the activation loads
-// wait. Without PDL the activation loads are issued first and the staging
-// and sincos run while they are in flight.
+// Positions, slots and the frequency table are never written by a kernel of
+// the chain, so with EARLY (the PDL launch of the chain executor) the
+// position load and sincos run before the grid-dependency wait, overlapping
+// the previous kernel's tail, and only the activation loads wait. Without
+// PDL the activation loads are issued first and the sincos runs while they
+// are in flight.
 template <int DT, int UPL, typename TB, bool EARLY>
 __global__ void __launch_bounds__(kWarpThreads) qkv_rope_warp_kernel(const __grid_constant__ RopeArgs a) {
   __shared__ float s_freq[kMaxHalf];
   __shared__ __align__(16) float s_cos[kWarpsPerCta][kMaxHalf];
   __shared__ __align__(16) float s_sin[kWarpsPerCta][kMaxHalf];
-  extern __shared__ __align__(16) unsigned char s_bias[];
 
   const int D = DT != 0 ? DT : a.head_dim;
   const int half = D >> 1;
   const int chunks = D >> 4;   // rotation units per head (8 pairs each)
   const int vchunks = D >> 3;  // copy units per v head (16 bytes each)
-  const int brow = D + 16 / static_cast<int>(sizeof(TB));  // padded bias row, elements
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -172,7 +168,7 @@ __global__ void __launch_bounds__(kWarpThreads) qkv_rope_warp_kernel(const __gri
 
   // unit j of this lane: kind 0 = q rotation, 1 = k rotation, 2 = v copy, -1 none;
   // `off` = element offset of the unit inside its token row (head * D + d0)
-  int kind[UPL], off[UPL], boff[UPL];
+  int kind[UPL], off[UPL];
 #pragma unroll
   for (int j = 0; j < UPL; ++j) {
     const int u = (part * UPL + j) * 32 + lane;
@@ -192,7 +188,6 @@ __global__ void __launch_bounds__(kWarpThreads) qkv_rope_warp_kernel(const __gri
       d0 = (w - h * vchunks) << 3;
     }
     off[j] = h * D + d0;
-    boff[j] = h * brow + d0;
   }
 
   const __half* q_tok = a.q + t * a.n_heads * D;
@@ -220,35 +215,10 @@ __global__ void __launch_bounds__(kWarpThreads) qkv_rope_warp_kernel(const __gri
   }
 
   for (int i = threadIdx.x; i < half; i += blockDim.x) s_freq[i] = a.inv_freq[i];
-  // Biases never written by a chain kernel: staged before the dependency
-  // wait, q then k then v, each head row padded to `brow` elements.
   const TB* bq = static_cast<const TB*>(a.bq);
   const TB* bk = static_cast<const TB*>(a.bk);
   const TB* bv = static_cast<const TB*>(a.bv);
-  if (a.stage_bias) {
-    const int vec_per_row = D * static_cast<int>(sizeof(TB)) / 16;
-    const int row_vecs = brow * static_cast<int>(sizeof(TB)) / 16;
-    uint4* sb = reinterpret_cast<uint4*>(s_bias);
-    const TB* srcs[3] = {bq, bk, bv};
-    const int heads[3] = {a.n_heads, a.n_kv_heads, a.n_kv_heads};
-    int base = 0;
-    for (int m = 0; m < 3; ++m) {
-      const int n = heads[m] * vec_per_row;
-      if (srcs[m] != nullptr) {
-        const uint4* src = reinterpret_cast<const uint4*>(srcs[m]);
-        for (int i = threadIdx.x; i < n; i += blockDim.x) {
-          const int h = i / vec_per_row;
-          sb[base + h * row_vecs + (i - h * vec_per_row)] = ld_keep(src + i);
-        }
-      }
-      base += heads[m] * row_vecs;
-    }
-    const TB* sbase = reinterpret_cast<const TB*>(s_bias);
-    if (bq) bq = sbase;
-    if (bk) bk = sbase + a.n_heads * brow;
-    if (bv) bv = sbase + (a.n_heads + a.n_kv_heads) * brow;
-  }
-  __syncthreads();  // s_freq and staged biases visible; every thread reaches this point
+  __syncthreads();  // s_freq visible; every thread reaches this point
 
   if (live) {
     for (int d = lane; d < half; d += 32) {
@@ -307,7 +277,7 @@ __global__ void __launch_bounds__(kWarpThreads) qkv_rope_warp_kernel(const __gri
       if (bias != nullptr) {
         // the biased values rounded to fp16, as the reference's separate
         // bias add stores them
-        const int bo = a.stage_bias ? boff[j] : off[j];  // padded rows when staged
+        const int bo = off[j];
         unpack8(add_bias8<TB>(x1[j], bias, bo), f1);
         unpack8(add_bias8<TB>(x2[j], bias, bo + half), f2);
       } else {
@@ -341,7 +311,7 @@ __global__ void __launch_bounds__(kWarpThreads) qkv_rope_warp_kernel(const __gri
     } else {
       if (a.v_cache == nullptr || !cache_ok) continue;
       uint4 x = x1[j];
-      if (bv != nullptr) x = add_bias8<TB>(x, bv, a.stage_bias ? boff[j] : off[j]);
+      if (bv != nullptr) x = add_bias8<TB>(x, bv, off[j]);
       const int h = off[j] / D;
       st_plain(a.v_cache + cache_tok + h * head_stride + (off[j] - h * D), x);
     }
@@ -461,12 +431,8 @@ int run_rope(RopeArgs& a, int act_dtype, int bias_dtype, const LaunchOpts& o, co
     a.warps_per_token = wpt;
     const int64_t warps = a.n_tokens * wpt;
     const unsigned grid = static_cast<unsigned>((warps + kWarpsPerCta - 1) / kWarpsPerCta);
-    const size_t bias_bytes = static_cast<size_t>(a.n_heads + 2 * a.n_kv_heads) * (D * (bias16 ? 2 : 4) + 16);
-    const bool any_bias = a.bq || a.bk || a.bv;
-    a.stage_bias = any_bias && bias_bytes <= kMaxBiasStage;
-    const size_t smem = a.stage_bias ? bias_bytes : 0;
     void (*k)(RopeArgs) = pick_warp_kernel(D, upl, bias16, o.pdl);
-    return launch_status(launch(k, grid, kWarpThreads, smem, o.stream, o.pdl, a), what);
+    return launch_status(launch(k, grid, kWarpThreads, 0, o.stream, o.pdl, a), what);
   }
   const int per_tok = a.n_heads * (D / 2) + (a.k ? a.n_kv_heads * (D / 2) : 0) + (a.v ? a.n_kv_heads * D : 0);
   const int64_t total = a.n_tokens * per_tok;
