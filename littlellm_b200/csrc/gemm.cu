@@ -17,17 +17,18 @@
 // those fp16 values with the same arithmetic as kllm_b200_silu_mul, so the
 // fused op equals linear + linear + silu_mul of this library bit for bit.
 //
-// Kernel: persistent, one CTA per SM, 128 x BN accumulator tiles, BN = 256
-// (or 128 when 256-wide tiles would leave the last wave of SMs mostly idle);
-// a SwiGLU tile is BN / 2 output columns: BN / 2 gate rows and BN / 2 up rows
-// of the weights stacked as the UMMA's N. Warp 0 issues TMA loads of 64-wide
-// k slices (128-byte swizzle) into a ring of 4 (BN 256) or 6 (BN 128) stages;
-// warp 1 issues tcgen05.mma (M 128, N BN, K 16) into one of two fp32
-// accumulators in tensor memory (2 x BN columns); warps
-// 2-5 read the other accumulator back (tcgen05.ld, one row per thread), apply
-// the epilogue and store, so the epilogue of tile i overlaps the main loop of
-// tile i + 1. Tiles are visited in groups of 4096 rows (all column tiles of
-// a group before the next group) so the CTAs in flight share x and w in L2.
+// Kernel: persistent, one CTA per SM, 128 x BN accumulator tiles with BN in
+// {256, 224, 192, 128} chosen per problem (pick_tile_width: tiles that fit n,
+// a last wave that is not mostly idle); a SwiGLU tile is BN / 2 output
+// columns: BN / 2 gate rows and BN / 2 up rows of the weights stacked as the
+// UMMA's N. Warp 0 issues TMA loads of 64-wide k slices (128-byte swizzle)
+// into a ring of 4 to 6 stages; warp 1 issues tcgen05.mma (M 128, N BN,
+// K 16) into one of two fp32 accumulators in tensor memory; warps 2-5 read
+// the other accumulator back (tcgen05.ld, one row per thread), apply the
+// epilogue and write each warp's 32 x 32 output chunks through shared memory
+// with TMA stores, so the epilogue of tile i overlaps the main loop of tile
+// i + 1. Tiles are visited in groups of 4096 rows (all column tiles of a
+// group before the next group) so the CTAs in flight share x and w in L2.
 // Every mbarrier wait is bounded; a wait that runs out sets
 // KLLM_B200_FLAG_TIMEOUT and the CTA drains its copies and MMAs and returns.
 #include <cuda.h>
@@ -50,10 +51,11 @@ constexpr int kThreads = (2 + kEpiWarps) * 32;
 constexpr int kGroupRows = 4096;              // rows of x per raster group (x slab resident in L2)
 constexpr int kMaxStages = 6;
 
-// Tile width BN (the UMMA N, accumulator columns per tile): 256, or 128 for
-// problems whose 256-wide tiles would leave the last wave of SMs mostly idle.
-// The ring holds as many stages as fit in 192 KB.
-__host__ __device__ constexpr int gemm_stages(int bn) { return bn == 256 ? 4 : 6; }
+// Tile width BN (the UMMA N, accumulator columns per tile): 256, 224, 192 or
+// 128, chosen per problem by the host (pick_tile_width) so that the column
+// tiles fit n and the last wave of SMs is not left mostly idle. The ring
+// holds as many stages as fit beside the epilogue's staging buffers.
+__host__ __device__ constexpr int gemm_stages(int bn) { return bn >= 224 ? 4 : (bn == 192 ? 5 : 6); }
 __host__ __device__ constexpr int gemm_stage_bytes(int bn) { return kABytes + bn * kBK * 2; }
 // Output staging of the epilogue: per epilogue warp two 2 KB buffers, each
 // one 32-row x 32-column fp16 chunk on its way to a TMA store.
@@ -411,7 +413,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
   constexpr int kStages = gemm_stages(kBN);
   constexpr int kStageBytes = gemm_stage_bytes(kBN);
   constexpr int kBBytes = kBN * kBK * 2;
-  constexpr uint32_t kTmemCols = 2 * kBN;  // two accumulators
+  constexpr uint32_t kTmemCols = kBN <= 128 ? 256 : 512;  // two accumulators, a power-of-two allocation
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   __shared__ __align__(8) uint64_t s_bar[kNumBars];
   __shared__ uint32_t s_tmem;
@@ -669,26 +671,37 @@ int launch_gemm(GemmArgs& a, const LaunchOpts& o, const char* what) {
   return launch_status(err, what);
 }
 
-// Tile width for an m x n problem: 256, or 128 when the 256-wide tiling
-// leaves the last wave of SMs mostly idle. Cost = tiles per CTA x width, with
+// Tile width for an m x n problem: the candidate with the fewest accumulator
+// columns swept by the busiest CTA (tiles per CTA x width; a narrower tile
+// that fits n exactly, e.g. 224 for n = 896, wins over a half-empty last
+// 256-wide tile), with
 // 128-wide tiles charged 45% extra per column (measured on B200: an N = 128
 // UMMA reads 4/3 the shared-memory bytes per FLOP and each x tile is fetched
 // twice as often; 832 against 1190 TFLOP/s on the Qwen2.5-0.5B MLP).
-int pick_tile_width(int64_t m, int64_t n, bool swiglu) {
+// `only_128_256` restricts the choice to the two widths the q/k/v epilogue
+// has (whole heads of one segment per tile).
+int pick_tile_width(int64_t m, int64_t n, bool swiglu, bool only_128_256 = false) {
   const int64_t sms = sm_count();
   const int64_t m_tiles = (m + kBM - 1) / kBM;
   int64_t best_cost = -1;
   int best = 256;
-  for (int bn : {256, 128}) {
+  for (int bn : {256, 224, 192, 128}) {
+    if (swiglu && bn == 224) continue;  // a SwiGLU tile's gate and up halves are whole 32-column chunks
+    if (only_128_256 && bn != 256 && bn != 128) continue;
     const int64_t cols = swiglu ? bn / 2 : bn;
     const int64_t tiles = m_tiles * ((n + cols - 1) / cols);
-    const int64_t cost = (tiles + sms - 1) / sms * bn * (bn == 256 ? 20 : 29);
+    const int64_t cost = (tiles + sms - 1) / sms * bn * (bn >= 192 ? 20 : 29);
     if (best_cost < 0 || cost < best_cost) {
       best_cost = cost;
       best = bn;
     }
   }
   return best;
+}
+
+template <int kBN>
+int dispatch_linear(GemmArgs& a, bool f32_bias, const LaunchOpts& o, const char* what) {
+  return f32_bias ? launch_gemm<kBN, kEpiLinear, float>(a, o, what) : launch_gemm<kBN, kEpiLinear, __half>(a, o, what);
 }
 
 template <int kBN>
@@ -730,11 +743,17 @@ int run_gemm(const void* x, const void* w, const void* w2, const void* bias, con
     a.tma_out = 1;
   }
   const bool f32_bias = (bias || bias2) && bias_dtype == KLLM_B200_F32;
-  return bn == 256 ? dispatch_gemm<256>(a, swiglu, f32_bias, o, what) : dispatch_gemm<128>(a, swiglu, f32_bias, o, what);
+  switch (bn) {
+    case 256: return dispatch_gemm<256>(a, swiglu, f32_bias, o, what);
+    case 192: return dispatch_gemm<192>(a, swiglu, f32_bias, o, what);
+    case 128: return dispatch_gemm<128>(a, swiglu, f32_bias, o, what);
+    default: return dispatch_linear<224>(a, f32_bias, o, what);  // linear only
+  }
 }
 
 template <typename TB>
 int launch_qkv(GemmArgs& a, int bn, const LaunchOpts& o, const char* what) {
+  if (bn != 256 && bn != 128) return fail(KLLM_B200_ERR_SHAPE, "%s: tile width %d has no q/k/v epilogue", what, bn);
   return bn == 256 ? launch_gemm<256, kEpiQkvRope, TB>(a, o, what) : launch_gemm<128, kEpiQkvRope, TB>(a, o, what);
 }
 
@@ -779,7 +798,7 @@ int qkv_linear_rope_kv_append(const void* x, const void* wq, const void* wk, con
   const int64_t qd = n_heads * head_dim, kvd = n_kv_heads * head_dim;
   // a tile never spans two segments: 256-wide tiles only when both segment
   // widths are multiples of 256, and then only where the tile model prefers them
-  const int bn = (qd % 256 == 0 && kvd % 256 == 0) ? pick_tile_width(n_tokens, qd + 2 * kvd, false) : 128;
+  const int bn = (qd % 256 == 0 && kvd % 256 == 0) ? pick_tile_width(n_tokens, qd + 2 * kvd, false, true) : 128;
   GemmArgs a;
   memset(&a, 0, sizeof(a));
   int rc;

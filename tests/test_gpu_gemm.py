@@ -140,10 +140,15 @@ def test_repeated_calls_are_deterministic(cuda, ops):
     ("linear, ragged m, n and k", 4100, 4100, 200, torch.float16),
     ("linear, square", 8192, 8192, 256, None),
     ("swiglu, ragged n and k, fp32 bias", 8192, 3000, 136, torch.float32),
+    ("linear, 224-wide tiles (n = 896)", 4096, 896, 896, torch.float16),
+    ("linear, 224-wide tiles, long k", 300, 896, 4864, None),
+    ("linear, 192-wide tiles", 8192, 1152, 256, torch.float32),
+    ("swiglu, 192-wide tiles", 2048, 1440, 512, torch.float16),
 ])
 def test_large_tilings_vs_torch_fp32(cuda, ops, what, m, n, k, bias):
-    """Problems of many waves (several raster groups of 4096 rows), with
-    partial row and column tiles and a k tail, against torch fp32."""
+    """Problems of many waves (several raster groups of 4096 rows) and the
+    192- and 224-wide tilings, with partial row and column tiles and a k tail,
+    against torch fp32."""
     g = torch.Generator(device=cuda).manual_seed(m ^ n ^ k)
     x = torch.randn(m, k, device=cuda, generator=g).half()
     w = (torch.randn(n, k, device=cuda, generator=g) / k ** 0.5).half()
