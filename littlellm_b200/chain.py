@@ -1,4 +1,4 @@
-"""The non-GEMM layer-op chain of a decoder forward step on one GPU.
+"""The layer-op chain of a decoder forward step on one GPU.
 
 ``ChainRunner`` owns the device buffers of one step of LlamaRunner::forward's
 non-GEMM work (src/model/llama.cpp:78-178) for a model shape and a batch, fills
@@ -6,7 +6,10 @@ them with seeded synthetic data (GEMM outputs ~N(0,1), norm weights
 ~U(0.5,1.5), biases and the embedding table ~N(0,0.02)) and launches the whole
 chain through ``kllm_b200_chain_run``. Every layer has its own input and output
 buffers, so one step streams its whole working set (several GB) and nothing is
-served from the 126 MB L2 across layers or steps.
+served from the 126 MB L2 across layers or steps. With ``attention=True,
+gemm=True`` the step is the whole forward (attention, the tcgen05 GEMMs with
+random N(0, 1/fan_in) weights, the lm_head), and ``decode_runner`` continues
+it with decode steps over the same weights and KV caches.
 
 Model shapes and workloads are the ones the benchmark is quoted on:
 Qwen2.5-0.5B (hidden 896, 14/2 heads x 64, intermediate 4864, vocab 151936,
@@ -219,6 +222,60 @@ class ChainRunner:
                 self.attn_workspace = torch.zeros(max(nbytes, 16), dtype=torch.uint8, device=dev)
         self.weight_dtype = weight_dtype
         self._build_desc(use_pdl)
+
+    # tensors of a layer that a decode runner shares with the runner it follows
+    _SHARED = ("q_bias", "k_bias", "v_bias", "input_norm_w", "post_norm_w", "k_cache", "v_cache")
+
+    def decode_runner(self, ids: torch.Tensor, positions: torch.Tensor,
+                      use_pdl: bool = True) -> "ChainRunner":
+        """A runner for one new token per sequence (slot b for sequence b) that
+        shares this runner's weights, norms, biases, embedding table, lm_head
+        and KV caches, so a prefill step followed by decode steps runs as
+        LlamaRunner::forward does across calls (src/model/llama.cpp:68-184):
+        each decode step appends its k/v at positions[b] and attends to the
+        cache rows the earlier steps wrote. Needs the whole forward
+        (attention=True, gemm=True)."""
+        if not (self.attention and self.gemm):
+            raise ValueError("a decode runner needs the whole forward step (attention and GEMMs)")
+        m = self.w.model
+        B = self.w.n_seqs
+        if ids.numel() != B or positions.numel() != B:
+            raise ValueError("one id and one position per sequence")
+        dev, f16 = self.device, torch.float16
+        qd, kvd, H, I = m.n_heads * m.head_dim, m.n_kv_heads * m.head_dim, m.hidden, m.intermediate
+        r = ChainRunner.__new__(ChainRunner)
+        r.device, r.n_layers, r.weight_dtype = dev, self.n_layers, self.weight_dtype
+        r.w = replace(self.w, seq_len=1, decode=True)
+        r.attention, r.gemm = True, True
+        r.table, r.final_norm_w, r.weights = self.table, self.final_norm_w, self.weights
+        with torch.cuda.device(dev):
+            r.ids = ids.to(device=dev, dtype=torch.int32).contiguous()
+            r.positions = positions.to(device=dev, dtype=torch.int32).contiguous()
+            r.slots = torch.arange(B, device=dev, dtype=torch.int32)
+            r.residual = torch.empty((B, H), dtype=f16, device=dev)
+            r.final_norm_out = torch.empty((B, H), dtype=f16, device=dev)
+            r.last_rows = torch.empty((B, H), dtype=f16, device=dev)
+            r.err_flags = torch.zeros((1,), dtype=torch.int32, device=dev)
+            r.layers = []
+            for L in self.layers:
+                D = {k: L[k] for k in self._SHARED}
+                D.update({"q": torch.empty((B, qd), dtype=f16, device=dev),
+                          "k": torch.empty((B, kvd), dtype=f16, device=dev),
+                          "v": torch.empty((B, kvd), dtype=f16, device=dev),
+                          "attn_out": torch.empty((B, H), dtype=f16, device=dev),
+                          "ffn_out": torch.empty((B, H), dtype=f16, device=dev),
+                          "attn_norm_out": torch.empty((B, H), dtype=f16, device=dev),
+                          "ffn_norm_out": torch.empty((B, H), dtype=f16, device=dev),
+                          "swiglu_out": torch.empty((B, I), dtype=f16, device=dev),
+                          "attn_ctx": torch.empty((B, qd), dtype=f16, device=dev)})
+                r.layers.append(D)
+            r.lm_head = self.lm_head
+            r.logits = torch.empty((B, m.vocab), dtype=f16, device=dev)
+            from . import ops
+            nbytes = ops.attention_workspace_bytes(B, m.n_heads, m.n_kv_heads, m.head_dim, r.w.max_seq)
+            r.attn_workspace = torch.zeros(max(nbytes, 16), dtype=torch.uint8, device=dev)
+        r._build_desc(use_pdl)
+        return r
 
     def _build_desc(self, use_pdl: bool) -> None:
         w, m = self.w, self.w.model

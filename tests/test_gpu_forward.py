@@ -80,3 +80,34 @@ def test_forward_graph_replay_is_deterministic(cuda):
     assert torch.equal(first, r.logits)
     assert bool(torch.isfinite(r.logits.float()).all())
     assert int(r.err_flags.item()) == 0
+
+
+def test_prefill_then_decode_steps_match_oracle(cuda, oracle):
+    """A prefill step (three 40-token sequences) followed by two decode steps
+    through decode runners that share the prefill runner's weights and KV
+    caches: each decode token attends to the cache rows the prefill and the
+    earlier decode step wrote, as LlamaRunner::forward does across calls. The
+    oracle forward carries its own caches from step to step."""
+    from littlellm_b200.chain import ChainRunner, ModelShape, Workload
+    shape = ModelShape("tiny-2l", 256, 4, 2, 64, 512, 512, 2, 1e-6, 1e6)
+    r = ChainRunner(Workload("p", shape, n_seqs=3, seq_len=40, max_seq=64, decode=False), device=cuda, seed=21,
+                    attention=True, gemm=True)
+    params = forward_params(r)
+    r.run()
+    torch.cuda.synchronize()
+    last, logits, caches = oracle.forward(params)
+    assert_tol(_np(r.logits), logits, what="prefill logits")
+    g = torch.Generator(device=cuda).manual_seed(5)
+    for step, pos in enumerate((40, 41)):
+        ids = torch.randint(0, shape.vocab, (3,), generator=g, device=cuda, dtype=torch.int32)
+        d = r.decode_runner(ids, torch.full((3,), pos, dtype=torch.int32, device=cuda))
+        d.run()
+        torch.cuda.synchronize()
+        assert int(d.err_flags.item()) == 0
+        p = dict(params, ids=_np(ids).astype(np.int32), positions=np.full(3, pos, np.int32),
+                 slots=np.arange(3, dtype=np.int32), seq_len=1, n_seqs=3,
+                 layers=[dict(L, k_cache=kc, v_cache=vc) for L, (kc, vc) in zip(params["layers"], caches)])
+        _, logits, caches = oracle.forward(p)
+        assert_tol(_np(d.logits), logits, what=f"decode step {step} logits")
+        for i, (L, (kc, vc)) in enumerate(zip(r.layers, caches)):
+            assert_tol(_np(L["k_cache"]), kc, what=f"decode step {step} layer {i} k cache")
