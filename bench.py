@@ -353,6 +353,11 @@ def run_reference(args):
         return run_reference_attention(args)
     if args.workload in GEMM_WORKLOADS:
         return run_reference_gemm(args)
+    if args.workload in GENERATE_WORKLOADS:
+        emit({"impl": "reference", "metric": GENERATE_METRIC,
+              "unavailable": "the reference's generation loop runs only from a .kllm checkpoint; "
+                             "not timed for this synthetic workload"})
+        return None
     if args.workload == "llama_int8_load":
         return run_reference_load(args)
     w = WORKLOADS[args.workload]
@@ -1629,6 +1634,107 @@ def run_forward(args):
         dist.destroy_process_group()
 
 
+GENERATE_WORKLOADS = {
+    # Qwen2.5-0.5B: an 8 x 512 prefill, then decode steps of the 8 sequences (one token each per step)
+    "qwen_generate": "qwen_prefill",
+}
+GENERATE_METRIC = "decode tokens/s"
+
+
+def run_generate(args):
+    """Serving loop: one prefill of the workload's sequences through the whole
+    forward step (KLLM_B200_OP_GEMM), then decode steps: every step runs the
+    whole forward for one new token per sequence at the next position over
+    the caches the earlier steps filled (ChainRunner.decode_runner), one CUDA
+    graph replay that also advances the positions. Token ids are seeded random
+    (sampling is outside the library). Each decode step streams all the
+    weights (lm_head included) and the cache rows attended: the HBM roofline."""
+    import torch
+
+    from littlellm_b200 import build as kbuild
+    from littlellm_b200.chain import WORKLOADS, ChainRunner
+
+    world, rank, local = dist_env()
+    if world > 1:
+        raise SystemExit("qwen_generate runs on one GPU (a replica per GPU would be independent)")
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA GPU")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    kbuild.build()
+    w = WORKLOADS[GENERATE_WORKLOADS[args.workload]]
+    m = w.model
+    r = ChainRunner(w, device=device, seed=1000, attention=True, gemm=True, n_layers=args.layers)
+    L, B = r.n_layers, w.n_seqs
+    stream = torch.cuda.Stream(device)
+    total_steps = max(args.warmup, 3) + args.steps + 2
+    if w.seq_len + total_steps > w.max_seq:
+        raise SystemExit("too many decode steps for the cache")
+    gen = torch.Generator(device=device)
+    gen.manual_seed(77)
+    ids_all = torch.randint(0, m.vocab, (total_steps, B), generator=gen, device=device, dtype=torch.int32)
+    step_idx = torch.zeros((), dtype=torch.int64, device=device)
+    with torch.cuda.stream(stream):
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        p0.record(stream)
+        r.run(stream)
+        p1.record(stream)
+        p1.synchronize()
+        prefill_ms = p0.elapsed_time(p1)
+        d = r.decode_runner(ids_all[0], torch.full((B,), w.seq_len, dtype=torch.int32, device=device))
+        launches = d.run(stream)  # the first decode step (position seq_len)
+
+        def step():
+            # next token: ids of this step, one position further
+            step_idx.add_(1)
+            d.ids.copy_(ids_all.index_select(0, step_idx.view(1)).view(-1))
+            d.positions.add_(1)
+            d.run(stream)
+
+        stream.synchronize()
+        graph = capture(step, stream)
+        for _ in range(max(args.warmup, 3)):
+            graph.replay()
+        stream.synchronize()
+        sampler = ClockSampler(device)
+        sampler.start()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        end.record(stream)
+        end.synchronize()
+    clocks = sampler.stop()
+    ms = start.elapsed_time(end) / args.steps
+    last_pos = int(d.positions[0].item())
+    flags = int(d.err_flags.item()) | int(r.err_flags.item())
+    finite = bool(torch.isfinite(d.logits.float()).all().item())
+    weight_bytes = sum(t.numel() * 2 for W in r.weights for t in W.values()) + r.lm_head.numel() * 2
+    mean_pos = last_pos - args.steps / 2.0
+    kv_bytes = L * B * (mean_pos + 1) * m.n_kv_heads * m.head_dim * 2 * 2
+    bytes_step = weight_bytes + kv_bytes
+    gbs = bytes_step / (ms * 1e-3) / 1e9
+    peaks = load_peaks()
+    roofline = {"bound": "hbm", "kernel": "the decode step (GEMMs streaming the weights, attention)",
+                "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": gbs / peaks["hbm_gbs"],
+                "traffic": None, "peak_source": peaks["source"], "bytes_per_step": int(bytes_step),
+                "timing": "one CUDA graph replay per decode step, CUDA events"}
+    del graph
+    emit({
+        "metric": GENERATE_METRIC, "value": B / (ms * 1e-3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": args.workload, "model": m.name, "layers": L, "sequences": B,
+                   "prompt_tokens": w.seq_len, "decode_positions": [w.seq_len + 1, last_pos],
+                   "weights": "random, N(0, 1/fan_in), fp16", "cuda_graph": True, "pdl": True,
+                   "ids": "seeded random per step (no sampler)"},
+        "prefill_ms": prefill_ms, "prefill_tokens_per_s": w.n_tokens / (prefill_ms * 1e-3),
+        "roofline": roofline, "clocks": clocks, "gpu_launches": launches * args.steps,
+        "launches_per_step": launches, "e2e": None, "cpu_baseline": None,
+        "verification": {"logits_finite": finite, "err_flags": flags},
+    })
+
+
 def time_oracle_forward(r, seconds: float) -> dict:
     """The oracle forward (the reference forward restated on the C oracle's
     operators, single thread, fp32) on a bounded sample: one 8-token sequence
@@ -1745,6 +1851,8 @@ def main():
         run_attention(args)
     elif args.workload in GEMM_WORKLOADS:
         run_gemm(args)
+    elif args.workload in GENERATE_WORKLOADS:
+        run_generate(args)
     elif args.forward:
         run_forward(args)
     else:
