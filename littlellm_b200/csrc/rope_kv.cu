@@ -53,32 +53,11 @@ struct RopeArgs {
   float inv_freq[kMaxHalf];
 };
 
-// Eight bias values at element `off`; `bias` may point to global or shared
-// memory (generic loads).
-template <typename TB>
-__device__ __forceinline__ void load_bias8(const void* bias, int64_t off, float (&b)[8]);
-
-template <>
-__device__ __forceinline__ void load_bias8<__half>(const void* bias, int64_t off, float (&b)[8]) {
-  const uint4 v = *reinterpret_cast<const uint4*>(static_cast<const __half*>(bias) + off);
-  const float2 a = h2_to_f2(v.x), c = h2_to_f2(v.y), d = h2_to_f2(v.z), e = h2_to_f2(v.w);
-  b[0] = a.x; b[1] = a.y; b[2] = c.x; b[3] = c.y; b[4] = d.x; b[5] = d.y; b[6] = e.x; b[7] = e.y;
-}
-
-template <>
-__device__ __forceinline__ void load_bias8<float>(const void* bias, int64_t off, float (&b)[8]) {
-  const float* p = static_cast<const float*>(bias) + off;
-  const float4 x = *reinterpret_cast<const float4*>(p);
-  const float4 y = *reinterpret_cast<const float4*>(p + 4);
+// Eight fp32 bias values at element `off`.
+__device__ __forceinline__ void load_bias8(const float* p, int64_t off, float (&b)[8]) {
+  const float4 x = *reinterpret_cast<const float4*>(p + off);
+  const float4 y = *reinterpret_cast<const float4*>(p + off + 4);
   b[0] = x.x; b[1] = x.y; b[2] = x.z; b[3] = x.w; b[4] = y.x; b[5] = y.y; b[6] = y.z; b[7] = y.w;
-}
-
-// Copies `bytes` (a multiple of 16) from global `src` to shared `dst` with the
-// whole CTA.
-__device__ __forceinline__ void stage16(void* dst, const void* src, int bytes) {
-  const uint4* s = static_cast<const uint4*>(src);
-  uint4* d = static_cast<uint4*>(dst);
-  for (int i = threadIdx.x; i < (bytes >> 4); i += blockDim.x) d[i] = ld_keep(s + i);
 }
 
 __device__ __forceinline__ void unpack8(uint4 v, float (&f)[8]) {
@@ -112,7 +91,7 @@ __device__ __forceinline__ uint4 add_bias8<__half>(uint4 x, const __half* bias, 
 template <>
 __device__ __forceinline__ uint4 add_bias8<float>(uint4 x, const float* bias, int off) {
   float b[8];
-  load_bias8<float>(bias, off, b);
+  load_bias8(bias, off, b);
   const float2 a0 = h2_to_f2(x.x), a1 = h2_to_f2(x.y), a2 = h2_to_f2(x.z), a3 = h2_to_f2(x.w);
   return make_uint4(f2_to_h2(a0.x + b[0], a0.y + b[1]), f2_to_h2(a1.x + b[2], a1.y + b[3]),
                     f2_to_h2(a2.x + b[4], a2.y + b[5]), f2_to_h2(a3.x + b[6], a3.y + b[7]));
