@@ -44,6 +44,10 @@ int resident_ctas(Kernel kernel, int threads, size_t smem) {
   return resident_ctas_raw(reinterpret_cast<const void*>(kernel), threads, smem);
 }
 
+// Clusters of `cluster` CTAs of `kernel` that can be resident on the device at
+// once (0 when none can be scheduled).
+int active_clusters_raw(const void* kernel, int threads, size_t smem, int cluster);
+
 // Opt `kernel` in to `smem` bytes of dynamic shared memory when that exceeds
 // the 48 KB default (once per kernel and size).
 cudaError_t allow_smem(const void* kernel, size_t smem);
@@ -78,6 +82,32 @@ cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
     cfg.attrs = attr;
     cfg.numAttrs = 1;
   }
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+// launch() with the grid divided into clusters of `cluster` CTAs along x.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_clustered(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                             bool pdl, int cluster, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  attr[n].id = cudaLaunchAttributeClusterDimension;
+  attr[n].val.clusterDim.x = static_cast<unsigned>(cluster);
+  attr[n].val.clusterDim.y = 1;
+  attr[n].val.clusterDim.z = 1;
+  ++n;
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 

@@ -49,20 +49,28 @@ constexpr int kABytes = kBM * kBK * 2;        // 16 KB
 constexpr int kEpiWarps = 4;
 constexpr int kThreads = (2 + kEpiWarps) * 32;
 constexpr int kGroupRows = 4096;              // rows of x per raster group (x slab resident in L2)
-constexpr int kMaxStages = 6;
+constexpr int kMaxStages = 16;                // ring depth with a compact x region (one row tile)
 
 // Tile width BN (the UMMA N, accumulator columns per tile): 256, 224, 192 or
 // 128, chosen per problem by the host (pick_tile_width) so that the column
 // tiles fit n and the last wave of SMs is not left mostly idle. The ring
 // holds as many stages as fit beside the epilogue's staging buffers.
-__host__ __device__ constexpr int gemm_stages(int bn) { return bn >= 224 ? 4 : (bn == 192 ? 5 : 6); }
+// A split-K launch (kSplit) holds 4 stages and beside them the 64 KB of
+// fp32 partial sums its peer CTAs hand to the cluster's leader CTA.
+__host__ __device__ constexpr int gemm_stages(int bn, bool split = false) {
+  return split ? 4 : (bn >= 224 ? 4 : (bn == 192 ? 5 : 6));
+}
 __host__ __device__ constexpr int gemm_stage_bytes(int bn) { return kABytes + bn * kBK * 2; }
 // Output staging of the epilogue: per epilogue warp two 2 KB buffers, each
 // one 32-row x 32-column fp16 chunk on its way to a TMA store.
 constexpr int kEpiChunkBytes = 32 * 32 * 2;
 constexpr int kEpiStageBytes = kEpiWarps * 2 * kEpiChunkBytes;
-constexpr size_t gemm_smem(int bn) {
-  return static_cast<size_t>(gemm_stages(bn)) * gemm_stage_bytes(bn) + kEpiStageBytes + 1024;  // + alignment
+constexpr int kSplitBN = 128;                         // the tile width of split-K launches
+constexpr int kPartBytes = 64 * 1024;                 // the leader's partial-sum slots
+constexpr int kMaxSplit = 8;                          // CTAs per cluster (portable cluster size)
+constexpr size_t gemm_smem(int bn, bool split = false) {
+  return static_cast<size_t>(gemm_stages(bn, split)) * gemm_stage_bytes(bn) + kEpiStageBytes +
+         (split ? kPartBytes : 0) + 1024;  // + alignment
 }
 
 // mbarriers: stage full (TMA bytes landed) / empty (MMAs that read it done);
@@ -73,7 +81,9 @@ enum GemmBar {
   kAccFull = kEmpty + kMaxStages,
   kAccEmpty = kAccFull + 2,
   kMmaDone = kAccEmpty + 2,
-  kNumBars = kMmaDone + 1
+  kPartFull = kMmaDone + 1,  // split-K, leader CTA, per accumulator: every peer's partial sums are in place
+  kPartFree = kPartFull + 2, // split-K, peer CTA, per accumulator: the leader has read this CTA's sums
+  kNumBars = kPartFree + 2
 };
 
 // Epilogue kinds: linear (bias), SwiGLU over stacked gate/up rows, and the
@@ -96,6 +106,11 @@ struct alignas(64) GemmArgs {
   int64_t m, n;        // output rows and columns
   int m_tiles, n_tiles, k_blocks;
   int group;           // row tiles per raster group
+  int split;           // CTAs per cluster sharing each tile's k range (1: no split)
+  int part_rows;       // rows of the x box: m rounded up to 8 for one row tile, else 128
+  uint32_t stage_tx;   // bytes one stage's TMA loads deliver
+  uint32_t a_region;   // bytes of a stage's x region (part_rows x 128 bytes, rounded up to 1 KB)
+  int stages;          // ring depth: as many stages as the ring's shared memory holds, <= kMaxStages
   int vec_out;         // n % 8 == 0: 16-byte stores
   int tma_out;         // linear / SwiGLU output written by TMA stores from shared memory
   // QKV + RoPE epilogue: the column tiles are q_tiles of wq, k_tiles of wk,
@@ -305,14 +320,48 @@ __device__ __forceinline__ void store_swiglu(const GemmArgs& a, int64_t row, int
   }
 }
 
+// Split-K partial sums in the leader CTA's shared memory: for each of the two
+// accumulators and each peer CTA (rank 1 .. split - 1) a slot of
+// kSplitBN / 4 four-column groups x part_rows rows x 16 bytes, so the rows of
+// one group a warp writes or reads are contiguous (no bank conflicts). Byte
+// offset of (accumulator b, peer, group, row).
+__device__ __forceinline__ uint32_t part_off(const GemmArgs& a, int b, int peer, int col4, int r) {
+  return static_cast<uint32_t>((((b * (a.split - 1) + peer - 1) * (kSplitBN / 4)) + col4) * a.part_rows + r) << 4;
+}
+
+// Split-K leader: add to the 32 accumulator columns col .. col + 31 of tile
+// row r the peers' partial sums, in rank order, so the order of the sum and
+// its rounding are fixed.
+template <bool kSplit>
+__device__ __forceinline__ void add_peer_partials(const GemmArgs& a, uint32_t part, int b, int r, bool live, int col,
+                                                  float (&v)[32]) {
+  if constexpr (kSplit) {
+    if (!live) return;
+#pragma unroll 1
+    for (int p = 1; p < a.split; ++p) {
+      float4 f[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) f[q] = ld_shared_f4(part + part_off(a, b, p, (col >> 2) + q, r));
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        v[q * 4 + 0] += f[q].x;
+        v[q * 4 + 1] += f[q].y;
+        v[q * 4 + 2] += f[q].z;
+        v[q * 4 + 3] += f[q].w;
+      }
+    }
+  }
+}
+
 // The q/k/v tile's epilogue (kEpiQkvRope; a tile of kBN columns holds whole
 // heads of 64 or 128 columns, all of one segment). Bias and rounding as linear() + add_bias_inplace store
 // them, then for q and k the rotate-half RoPE of pairs (d, d + D/2) at the
 // row's position with the same arithmetic as the fused RoPE kernel; q to its
 // buffer, k and v into the caches (rows whose position or slot is out of
 // range write no cache row and set the error flag).
-template <int kBN, typename TB>
-__device__ __forceinline__ void qkv_rope_epilogue(const GemmArgs& a, uint32_t t, int64_t row, int nt) {
+template <int kBN, typename TB, bool kSplit>
+__device__ __forceinline__ void qkv_rope_epilogue(const GemmArgs& a, uint32_t t, int64_t row, int nt, uint32_t part,
+                                                  int b, int r) {
   const int D = a.head_dim;
   int seg, ct;
   if (nt < a.q_tiles) {
@@ -350,7 +399,9 @@ __device__ __forceinline__ void qkv_rope_epilogue(const GemmArgs& a, uint32_t t,
       tmem_ld32(t + c * 32, v);
       tc_wait_ld();
       const int col = col0 + c * 32;
-      if (live && cache_ok && col < seg_cols) {
+      if (col >= seg_cols) break;  // a segment that ends inside the tile (uniform)
+      add_peer_partials<kSplit>(a, part, b, r, live, c * 32, v);
+      if (live && cache_ok) {
         __half* dst = cache_row(a.v_cache, col / D) + col % D;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -385,6 +436,8 @@ __device__ __forceinline__ void qkv_rope_epilogue(const GemmArgs& a, uint32_t t,
       tmem_ld32(t + hc + half + j * 32, x2);
       tc_wait_ld();
       if (!live || (seg == 1 && !cache_ok)) continue;
+      add_peer_partials<kSplit>(a, part, b, r, live, hc + j * 32, x1);
+      add_peer_partials<kSplit>(a, part, b, r, live, hc + half + j * 32, x2);
       uint32_t p1[16], p2[16];
 #pragma unroll
       for (int i = 0; i < 32; i += 2) {
@@ -407,11 +460,18 @@ __device__ __forceinline__ void qkv_rope_epilogue(const GemmArgs& a, uint32_t t,
   }
 }
 
-template <int kBN, int kEpi, typename TB>
+template <int kBN, int kEpi, typename TB, bool kSplit>
 __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_constant__ GemmArgs a) {
+  static_assert(!kSplit || kBN == kSplitBN, "split-K tiles are kSplitBN wide");
   constexpr bool kSwiGLU = kEpi == kEpiSwiGLU;
-  constexpr int kStages = gemm_stages(kBN);
-  constexpr int kStageBytes = gemm_stage_bytes(kBN);
+  // The ring's shared memory is fixed per kernel; its depth is a runtime
+  // value: with one row tile the x region of a stage shrinks to the rows
+  // loaded (the UMMA's reads of rows past them land in the same stage's
+  // weight region and only feed accumulator rows that are never stored), so
+  // more stages fit.
+  constexpr uint32_t kRingBytes = gemm_stages(kBN, kSplit) * gemm_stage_bytes(kBN);
+  const int stages = a.stages;
+  const uint32_t stage_bytes = a.a_region + kBN * kBK * 2;
   constexpr int kBBytes = kBN * kBK * 2;
   constexpr uint32_t kTmemCols = kBN <= 128 ? 256 : 512;  // two accumulators, a power-of-two allocation
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -419,10 +479,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
   __shared__ uint32_t s_tmem;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;  // stage s: A at base + s * kStageBytes, then B
+  const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;  // stage s: A at base + s * stage_bytes, then B
   const int n_tiles_total = a.m_tiles * a.n_tiles;
   constexpr int kOutCols = kSwiGLU ? kBN / 2 : kBN;  // output columns per tile
   auto bar = [&](int i) { return smem_u32(&s_bar[i]); };
+  // Tiles are dealt to clusters (without split-K a CTA is a cluster of one);
+  // the `split` CTAs of a cluster take consecutive k ranges of each tile.
+  const int rank = kSplit ? static_cast<int>(cluster_rank()) : 0;
+  const int first_tile = kSplit ? static_cast<int>(cluster_id_x()) : static_cast<int>(blockIdx.x);
+  const int tile_step = kSplit ? static_cast<int>(cluster_count_x()) : static_cast<int>(gridDim.x);
+  const int kb0 = kSplit ? rank * a.k_blocks / a.split : 0;
+  const int kb1 = kSplit ? (rank + 1) * a.k_blocks / a.split : a.k_blocks;
 
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
@@ -430,13 +497,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < stages; ++s) {
       mbar_init(bar(kFull + s), 1);
       mbar_init(bar(kEmpty + s), 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(bar(kAccFull + b), 1);
       mbar_init(bar(kAccEmpty + b), kEpiWarps);
+      if (kSplit) {
+        mbar_init(bar(kPartFull + b), (a.split - 1) * kEpiWarps);  // every epilogue warp of every peer
+        mbar_init(bar(kPartFree + b), kEpiWarps);                  // every epilogue warp of the leader
+      }
     }
     mbar_init(bar(kMmaDone), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -448,6 +519,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if (kSplit) cluster_sync();  // every CTA's barriers are initialised before a peer arrives on them
   const uint32_t tmem = s_tmem;
   // x may come from the previous kernel on the stream and out may be read by it
   grid_dep_wait();
@@ -456,8 +528,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
   if (warp == 0) {
     // ---------------- TMA producer: lane 0 ----------------
     if (lane == 0) {
-      int it = 0;  // k slices issued by this CTA
-      for (int tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x) {
+      int it = 0;          // k slices issued by this CTA
+      int s = 0, round = 0;  // the stage of slice `it` and how often the ring wrapped before it
+      for (int tile = first_tile; tile < n_tiles_total && ok; tile += tile_step) {
         int mt, nt;
         tile_coords(tile, a.m_tiles, a.n_tiles, a.group, mt, nt);
         const int m0 = mt * kBM;
@@ -472,14 +545,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
             n0 = (nt - a.q_tiles) * kOutCols;
           }
         }
-        for (int kb = 0; kb < a.k_blocks; ++kb, ++it) {
-          const int s = it % kStages;
-          if (it >= kStages) {  // the slice issued kStages ago into this stage has been consumed
-            ok = mbar_wait(bar(kEmpty + s), ((it / kStages) - 1) & 1);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          if (round > 0) {  // the slice issued one round ago into this stage has been consumed
+            ok = mbar_wait(bar(kEmpty + s), (round - 1) & 1);
             if (!ok) break;
           }
-          const uint32_t sa = base + s * kStageBytes, sb = sa + kABytes;
-          mbar_expect_tx(bar(kFull + s), kStageBytes);
+          const uint32_t sa = base + s * stage_bytes, sb = sa + a.a_region;
+          mbar_expect_tx(bar(kFull + s), a.stage_tx);
           tma_load_2d(sa, &a.map_a, kb * kBK, m0, bar(kFull + s));
           if (kSwiGLU) {
             tma_load_2d(sb, &a.map_b, kb * kBK, n0, bar(kFull + s));
@@ -487,12 +559,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
           } else {
             tma_load_2d(sb, bmap, kb * kBK, n0, bar(kFull + s));
           }
+          if (++s == stages) {
+            s = 0;
+            ++round;
+          }
         }
       }
       // every copy issued has landed before the CTA may exit (on the normal
       // path these phases completed long ago)
-      for (int j = it > kStages ? it - kStages : 0; j < it; ++j) {
-        if (!mbar_wait(bar(kFull + j % kStages), (j / kStages) & 1)) ok = false;
+      for (int j = it > stages ? it - stages : 0; j < it; ++j) {
+        if (!mbar_wait(bar(kFull + j % stages), (j / stages) & 1)) ok = false;
       }
     }
   } else if (warp == 1) {
@@ -500,9 +576,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     if (lane == 0) {
       constexpr uint32_t kIdesc = umma_idesc(kBM, kBN, false);
       const uint64_t adesc = umma_desc(base, 16, 1024);
-      const uint64_t bdesc = umma_desc(base + kABytes, 16, 1024);
-      int it = 0, i = 0;
-      for (int tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x, ++i) {
+      const uint64_t bdesc = umma_desc(base + a.a_region, 16, 1024);
+      int i = 0, s = 0, round = 0;
+      for (int tile = first_tile; tile < n_tiles_total && ok; tile += tile_step, ++i) {
         const int b = i & 1;
         if (i >= 2) {  // the epilogue has read this accumulator's previous tile
           ok = mbar_wait(bar(kAccEmpty + b), ((i >> 1) - 1) & 1);
@@ -510,18 +586,21 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
           tc_fence_after();
         }
         const uint32_t d = tmem + b * kBN;
-        for (int kb = 0; kb < a.k_blocks; ++kb, ++it) {
-          const int s = it % kStages;
-          ok = mbar_wait(bar(kFull + s), (it / kStages) & 1);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          ok = mbar_wait(bar(kFull + s), round & 1);
           if (!ok) break;
           tc_fence_after();
-          const uint64_t so = static_cast<uint64_t>((s * kStageBytes) >> 4);
+          const uint64_t so = static_cast<uint64_t>((s * stage_bytes) >> 4);
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k) {
             // k step: 16 elements = 32 bytes along the swizzled 128-byte row
-            umma_f16(d, adesc + so + 2 * k, bdesc + so + 2 * k, kIdesc, (kb > 0 || k > 0) ? 1u : 0u);
+            umma_f16(d, adesc + so + 2 * k, bdesc + so + 2 * k, kIdesc, (kb > kb0 || k > 0) ? 1u : 0u);
           }
           umma_commit(bar(kEmpty + s));
+          if (++s == stages) {
+            s = 0;
+            ++round;
+          }
         }
         if (!ok) break;
         umma_commit(bar(kAccFull + b));
@@ -534,10 +613,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     // ---------------- epilogue: warps 2-5, one accumulator row per thread ----------------
     const int quad = warp & 3;  // tensor-memory lanes 32 * quad .. + 31 are this warp's
     const int r = quad * 32 + lane;
-    const uint32_t ebuf0 = base + kStages * kStageBytes + quad * 2 * kEpiChunkBytes;  // this warp's buffers
+    const uint32_t ebuf0 = base + kRingBytes + quad * 2 * kEpiChunkBytes;  // this warp's buffers
+    const uint32_t part = base + kRingBytes + kEpiStageBytes;  // split-K: the peers' partial sums
     int ebuf = 0;
     int i = 0;
-    for (int tile = blockIdx.x; tile < n_tiles_total; tile += gridDim.x, ++i) {
+    for (int tile = first_tile; tile < n_tiles_total; tile += tile_step, ++i) {
       int mt, nt;
       tile_coords(tile, a.m_tiles, a.n_tiles, a.group, mt, nt);
       const int b = i & 1;
@@ -545,22 +625,62 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
       if (!ok) break;
       tc_fence_after();
       const int64_t row = static_cast<int64_t>(mt) * kBM + r;
+      const bool live = row < a.m;
+      const bool warp_live = static_cast<int64_t>(mt) * kBM + quad * 32 < a.m;  // any output row in this warp
       const int64_t n0 = static_cast<int64_t>(nt) * kOutCols;
       const uint32_t t = tmem + (static_cast<uint32_t>(quad * 32) << 16) + b * kBN;
-      if constexpr (kEpi == kEpiQkvRope) {
-        qkv_rope_epilogue<kBN, TB>(a, t, row, nt);
+      if (kSplit && rank > 0) {
+        // peer: this CTA's k range of the tile -> its slot in the leader's shared memory
+        if (i >= 2) {  // the leader has read the sums this slot held two tiles ago
+          ok = __all_sync(0xffffffffu, mbar_wait_cluster(bar(kPartFree + b), ((i >> 1) - 1) & 1));
+          if (!ok) break;
+        }
+        if (warp_live) {
+          const uint32_t dst = cluster_map(part, 0);
+#pragma unroll 1
+          for (int c = 0; c < kBN / 32; ++c) {
+            float v[32];
+            tmem_ld32(t + c * 32, v);
+            tc_wait_ld();
+            if (live) {
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                st_cluster_f4(dst + part_off(a, b, rank, c * 8 + q, r), v[q * 4], v[q * 4 + 1], v[q * 4 + 2],
+                              v[q * 4 + 3]);
+              }
+            }
+          }
+        }
+        fence_acq_rel_cluster();  // the sums are visible to the leader before this warp's arrival
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(bar(kAccEmpty + b));
+          mbar_arrive_cluster(bar(kPartFull + b), 0);
+        }
+        continue;
+      }
+      if (kSplit) {  // leader: every peer's sums of this tile are in place
+        ok = __all_sync(0xffffffffu, mbar_wait_cluster(bar(kPartFull + b), (i >> 1) & 1));
+        if (!ok) break;
+      }
+      if (!warp_live) {
+        // no output row in this warp: nothing to store
+      } else if constexpr (kEpi == kEpiQkvRope) {
+        qkv_rope_epilogue<kBN, TB, kSplit>(a, t, row, nt, part, b, r);
       } else if constexpr (!kSwiGLU) {
 #pragma unroll 1
         for (int c = 0; c < kBN / 32; ++c) {
           float v[32];
           tmem_ld32(t + c * 32, v);
           tc_wait_ld();
+          add_peer_partials<kSplit>(a, part, b, r, live, c * 32, v);
           if (a.tma_out) {
             uint4 w[4];
             linear_chunk<TB>(a, n0 + c * 32, v, w);
             stage_and_store(a, ebuf0 + ebuf * kEpiChunkBytes, lane, n0 + c * 32, row - lane, w);
             ebuf ^= 1;
-          } else if (row < a.m) {
+          } else if (live) {
             store_linear<TB>(a, row, n0 + c * 32, v);
           }
         }
@@ -571,19 +691,27 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
           tmem_ld32(t + c * 32, g);
           tmem_ld32(t + kBN / 2 + c * 32, u);
           tc_wait_ld();
+          add_peer_partials<kSplit>(a, part, b, r, live, c * 32, g);
+          add_peer_partials<kSplit>(a, part, b, r, live, kBN / 2 + c * 32, u);
           if (a.tma_out) {
             uint4 w[4];
             swiglu_chunk<TB>(a, n0 + c * 32, g, u, w);
             stage_and_store(a, ebuf0 + ebuf * kEpiChunkBytes, lane, n0 + c * 32, row - lane, w);
             ebuf ^= 1;
-          } else if (row < a.m) {
+          } else if (live) {
             store_swiglu<TB>(a, row, n0 + c * 32, g, u);
           }
         }
       }
+      if (kSplit) fence_acq_rel_cluster();  // the reads of the peers' slots are done before the slots are freed
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(kAccEmpty + b));
+      if (lane == 0) {
+        mbar_arrive(bar(kAccEmpty + b));
+        if (kSplit) {
+          for (int p = 1; p < a.split; ++p) mbar_arrive_cluster(bar(kPartFree + b), p);
+        }
+      }
     }
     if (lane == 0) tma_store_wait_all();  // the TMA stores have read their buffers and written the output
   }
@@ -591,6 +719,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
   if (!ok) set_flag(a.err_flags, KLLM_B200_FLAG_TIMEOUT);
   tc_fence_before();
   __syncthreads();
+  // split-K: no CTA leaves while a peer may still write its shared memory or arrive on its barriers
+  if (kSplit) cluster_sync();
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
@@ -659,16 +789,72 @@ int check_gemm_args(const char* what, const void* x, const void* w, const void* 
   return KLLM_B200_OK;
 }
 
-template <int kBN, int kEpi, typename TB>
+template <int kBN, int kEpi, typename TB, bool kSplit>
 int launch_gemm(GemmArgs& a, const LaunchOpts& o, const char* what) {
-  auto kernel = gemm_tc_kernel<kBN, kEpi, TB>;
-  constexpr size_t smem = gemm_smem(kBN);
+  auto kernel = gemm_tc_kernel<kBN, kEpi, TB, kSplit>;
+  constexpr size_t smem = gemm_smem(kBN, kSplit);
   cudaError_t err = allow_smem(reinterpret_cast<const void*>(kernel), smem);
   if (err != cudaSuccess) return launch_status(err, what);
   const int64_t tiles = static_cast<int64_t>(a.m_tiles) * a.n_tiles;
-  const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
-  err = launch(kernel, dim3(grid), dim3(kThreads), smem, o.stream, o.pdl, a);
+  if (kSplit) {
+    const int clusters = active_clusters_raw(reinterpret_cast<const void*>(kernel), kThreads, smem, a.split);
+    if (clusters < 1) return fail(KLLM_B200_ERR_CUDA, "%s: no cluster of %d CTAs fits the device", what, a.split);
+    const int n = static_cast<int>(tiles < clusters ? tiles : clusters);
+    err = launch_clustered(kernel, dim3(n * a.split), dim3(kThreads), smem, o.stream, o.pdl, a.split, a);
+  } else {
+    const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
+    err = launch(kernel, dim3(grid), dim3(kThreads), smem, o.stream, o.pdl, a);
+  }
   return launch_status(err, what);
+}
+
+// Split-K: CTAs per cluster sharing each tile's k range. Only for GEMMs of
+// one row tile (m <= 128: decode batches) with few column tiles (n <= 2048)
+// and a long k (>= 32 slices of 64), whose handful of CTAs would otherwise
+// each stream a long strip of weights alone (measured on B200 at m = 8: the
+// 896 x 4864 down projection 26 -> 13 us; splits of shorter k or of wide n
+// cost more in per-tile hand-offs than they gain). One CTA per 8 k slices, at
+// most kMaxSplit, and two tiles' partial sums of the peers within
+// kPartBytes. `n` is the output columns of one weight: a fused op passes the
+// width its separate linear would have, so both split alike and stay
+// bit-identical.
+int pick_split(int64_t m, int64_t n, int64_t k) {
+  if (m > kBM || m <= 0 || n > 2048) return 1;
+  const int64_t k_blocks = (k + kBK - 1) / kBK;
+  if (k_blocks < 32) return 1;
+  const int64_t rows = (m + 7) / 8 * 8;
+  int64_t s = k_blocks / 8;
+  if (s > kMaxSplit) s = kMaxSplit;
+  const int64_t by_smem = 1 + kPartBytes / (2 * rows * kSplitBN * 4);
+  if (s > by_smem) s = by_smem;
+  if (s < 2) return 1;
+  // clusters of s CTAs must fit the device (every split kernel has the same
+  // shared memory and threads)
+  auto probe = gemm_tc_kernel<kSplitBN, kEpiLinear, __half, true>;
+  const size_t smem = gemm_smem(kSplitBN, true);
+  if (allow_smem(reinterpret_cast<const void*>(probe), smem) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return 1;
+  }
+  while (s >= 2 && active_clusters_raw(reinterpret_cast<const void*>(probe), kThreads, smem, (int)s) < 1) --s;
+  return s >= 2 ? static_cast<int>(s) : 1;
+}
+
+// The x operand's box and the ring: with one row tile the x box is m
+// rounded up to 8 rows and a stage's x region only that many rows (rounded
+// up to 1 KB, the swizzle atom), so the ring of the kernel's fixed shared
+// memory holds more stages. `bn` is the tile width, `split` the CTAs per
+// cluster.
+int setup_a(GemmArgs& a, const void* x, int64_t m, int64_t k, int bn, int split, const char* what) {
+  const int rows = m <= kBM ? static_cast<int>((m + 7) / 8 * 8) : kBM;
+  a.split = split;
+  a.part_rows = rows;
+  a.a_region = static_cast<uint32_t>((rows * kBK * 2 + 1023) / 1024 * 1024);
+  const uint32_t ring = static_cast<uint32_t>(gemm_stages(bn, split > 1) * gemm_stage_bytes(bn));
+  const uint32_t stage = a.a_region + static_cast<uint32_t>(bn * kBK * 2);
+  a.stages = static_cast<int>(ring / stage < kMaxStages ? ring / stage : kMaxStages);
+  a.stage_tx = static_cast<uint32_t>(rows * kBK * 2 + bn * kBK * 2);
+  return make_map(&a.map_a, x, m, k, rows, what);
 }
 
 // Tile width for an m x n problem: the candidate with the fewest accumulator
@@ -699,18 +885,19 @@ int pick_tile_width(int64_t m, int64_t n, bool swiglu, bool only_128_256 = false
   return best;
 }
 
-template <int kBN>
+template <int kBN, bool kSplit = false>
 int dispatch_linear(GemmArgs& a, bool f32_bias, const LaunchOpts& o, const char* what) {
-  return f32_bias ? launch_gemm<kBN, kEpiLinear, float>(a, o, what) : launch_gemm<kBN, kEpiLinear, __half>(a, o, what);
+  return f32_bias ? launch_gemm<kBN, kEpiLinear, float, kSplit>(a, o, what)
+                  : launch_gemm<kBN, kEpiLinear, __half, kSplit>(a, o, what);
 }
 
-template <int kBN>
+template <int kBN, bool kSplit = false>
 int dispatch_gemm(GemmArgs& a, bool swiglu, bool f32_bias, const LaunchOpts& o, const char* what) {
   if (swiglu) {
-    return f32_bias ? launch_gemm<kBN, kEpiSwiGLU, float>(a, o, what)
-                    : launch_gemm<kBN, kEpiSwiGLU, __half>(a, o, what);
+    return f32_bias ? launch_gemm<kBN, kEpiSwiGLU, float, kSplit>(a, o, what)
+                    : launch_gemm<kBN, kEpiSwiGLU, __half, kSplit>(a, o, what);
   }
-  return f32_bias ? launch_gemm<kBN, kEpiLinear, float>(a, o, what) : launch_gemm<kBN, kEpiLinear, __half>(a, o, what);
+  return dispatch_linear<kBN, kSplit>(a, f32_bias, o, what);
 }
 
 int run_gemm(const void* x, const void* w, const void* w2, const void* bias, const void* bias2, int bias_dtype,
@@ -718,13 +905,14 @@ int run_gemm(const void* x, const void* w, const void* w2, const void* bias, con
   const char* what = swiglu ? "linear_swiglu" : "linear";
   int rc = check_gemm_args(what, x, w, w2, bias, bias2, bias_dtype, out, m, n, k, swiglu);
   if (rc != KLLM_B200_OK || m == 0 || n == 0) return rc;
-  const int bn = pick_tile_width(m, n, swiglu);
+  const int split = pick_split(m, n, k);
+  const int bn = split > 1 ? kSplitBN : pick_tile_width(m, n, swiglu);
   const int out_cols = swiglu ? bn / 2 : bn;  // output columns per tile
   const int64_t m_tiles = (m + kBM - 1) / kBM, n_tiles = (n + out_cols - 1) / out_cols;
   if (m_tiles * n_tiles > 0x7fffffffLL) return fail(KLLM_B200_ERR_SHAPE, "%s: too many tiles", what);
   GemmArgs a;
   memset(&a, 0, sizeof(a));
-  if ((rc = make_map(&a.map_a, x, m, k, kBM, what)) != KLLM_B200_OK) return rc;
+  if ((rc = setup_a(a, x, m, k, bn, split, what)) != KLLM_B200_OK) return rc;
   if ((rc = make_map(&a.map_b, w, n, k, out_cols, what)) != KLLM_B200_OK) return rc;
   if (swiglu && (rc = make_map(&a.map_b2, w2, n, k, out_cols, what)) != KLLM_B200_OK) return rc;
   a.out = static_cast<__half*>(out);
@@ -743,6 +931,7 @@ int run_gemm(const void* x, const void* w, const void* w2, const void* bias, con
     a.tma_out = 1;
   }
   const bool f32_bias = (bias || bias2) && bias_dtype == KLLM_B200_F32;
+  if (split > 1) return dispatch_gemm<kSplitBN, true>(a, swiglu, f32_bias, o, what);
   switch (bn) {
     case 256: return dispatch_gemm<256>(a, swiglu, f32_bias, o, what);
     case 192: return dispatch_gemm<192>(a, swiglu, f32_bias, o, what);
@@ -754,7 +943,9 @@ int run_gemm(const void* x, const void* w, const void* w2, const void* bias, con
 template <typename TB>
 int launch_qkv(GemmArgs& a, int bn, const LaunchOpts& o, const char* what) {
   if (bn != 256 && bn != 128) return fail(KLLM_B200_ERR_SHAPE, "%s: tile width %d has no q/k/v epilogue", what, bn);
-  return bn == 256 ? launch_gemm<256, kEpiQkvRope, TB>(a, o, what) : launch_gemm<128, kEpiQkvRope, TB>(a, o, what);
+  if (a.split > 1) return launch_gemm<kSplitBN, kEpiQkvRope, TB, true>(a, o, what);
+  return bn == 256 ? launch_gemm<256, kEpiQkvRope, TB, false>(a, o, what)
+                   : launch_gemm<128, kEpiQkvRope, TB, false>(a, o, what);
 }
 
 }  // namespace
@@ -798,11 +989,16 @@ int qkv_linear_rope_kv_append(const void* x, const void* wq, const void* wk, con
   const int64_t qd = n_heads * head_dim, kvd = n_kv_heads * head_dim;
   // a tile never spans two segments: 256-wide tiles only when both segment
   // widths are multiples of 256, and then only where the tile model prefers them
-  const int bn = (qd % 256 == 0 && kvd % 256 == 0) ? pick_tile_width(n_tokens, qd + 2 * kvd, false, true) : 128;
+  // split as the q linear would (the k and v linears split alike whenever they
+  // are on the same side of pick_split's column limit as q)
+  const int split = pick_split(n_tokens, n_heads * head_dim, hidden);
+  const int bn = split > 1 ? kSplitBN
+                           : ((qd % 256 == 0 && kvd % 256 == 0) ? pick_tile_width(n_tokens, qd + 2 * kvd, false, true)
+                                                                 : 128);
   GemmArgs a;
   memset(&a, 0, sizeof(a));
   int rc;
-  if ((rc = make_map(&a.map_a, x, n_tokens, hidden, kBM, what)) != KLLM_B200_OK) return rc;
+  if ((rc = setup_a(a, x, n_tokens, hidden, bn, split, what)) != KLLM_B200_OK) return rc;
   if ((rc = make_map(&a.map_b, wq, qd, hidden, bn, what)) != KLLM_B200_OK) return rc;
   if ((rc = make_map(&a.map_b2, wk, kvd, hidden, bn, what)) != KLLM_B200_OK) return rc;
   if ((rc = make_map(&a.map_b3, wv, kvd, hidden, bn, what)) != KLLM_B200_OK) return rc;

@@ -55,6 +55,7 @@ struct OccEntry {
   const void* kernel;
   int threads;
   size_t smem;
+  int cluster;  // 0: resident CTAs per SM; else co-resident clusters of this size on the device
   int ctas;
 };
 std::mutex g_occ_mutex;
@@ -72,14 +73,44 @@ int g_smem_n = 0;
 int resident_ctas_raw(const void* kernel, int threads, size_t smem) {
   std::lock_guard<std::mutex> lock(g_occ_mutex);
   for (int i = 0; i < g_occ_n; ++i) {
-    if (g_occ[i].kernel == kernel && g_occ[i].threads == threads && g_occ[i].smem == smem) return g_occ[i].ctas;
+    if (g_occ[i].kernel == kernel && g_occ[i].threads == threads && g_occ[i].smem == smem && g_occ[i].cluster == 0) {
+      return g_occ[i].ctas;
+    }
   }
   int n = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, smem) != cudaSuccess || n < 1) {
     (void)cudaGetLastError();
     n = 1;
   }
-  if (g_occ_n < 256) g_occ[g_occ_n++] = {kernel, threads, smem, n};
+  if (g_occ_n < 256) g_occ[g_occ_n++] = {kernel, threads, smem, 0, n};
+  return n;
+}
+
+int active_clusters_raw(const void* kernel, int threads, size_t smem, int cluster) {
+  std::lock_guard<std::mutex> lock(g_occ_mutex);
+  for (int i = 0; i < g_occ_n; ++i) {
+    if (g_occ[i].kernel == kernel && g_occ[i].threads == threads && g_occ[i].smem == smem &&
+        g_occ[i].cluster == cluster) {
+      return g_occ[i].ctas;
+    }
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(cluster * sm_count()));
+  cfg.blockDim = dim3(static_cast<unsigned>(threads));
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(cluster);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess || n < 1) {
+    (void)cudaGetLastError();
+    n = 0;  // not schedulable (or unknown): the caller does not split
+  }
+  if (g_occ_n < 256) g_occ[g_occ_n++] = {kernel, threads, smem, cluster, n};
   return n;
 }
 

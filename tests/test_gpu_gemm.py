@@ -59,7 +59,8 @@ def test_linear_vs_oracle(cuda, ops, oracle, m, n, k, bias):
     assert_tol(host(out), want, what=f"linear {m}x{n}x{k}")
 
 
-@pytest.mark.parametrize("m,n,k", [(5, 128, 64), (300, 640, 896), (129, 203, 136), (1, 4864, 896)])
+@pytest.mark.parametrize("m,n,k", [(5, 128, 64), (300, 640, 896), (129, 203, 136), (1, 4864, 896),
+                                   (8, 4864, 896), (64, 1000, 512), (8, 1024, 2048)])
 @pytest.mark.parametrize("bias", [None, torch.float16, torch.float32])
 def test_swiglu_vs_oracle_and_unfused(cuda, ops, oracle, m, n, k, bias):
     rng = np.random.default_rng(m * 11 + n + k * 5)
@@ -136,6 +137,35 @@ def test_repeated_calls_are_deterministic(cuda, ops):
         assert torch.equal(first, again)
 
 
+@pytest.mark.parametrize("m", [1, 8, 32, 64, 100, 128])
+@pytest.mark.parametrize("n,k,bias", [
+    (896, 4864, torch.float16),   # Qwen2.5-0.5B down projection: clusters of 8 CTAs (m <= 8), 3, 2, none (m > 64)
+    (896, 896, None),             # o projection: short k, no split
+    (203, 2056, torch.float32),   # ragged n (element-wise stores) and k (a partial last k slice): clusters of 4
+    (4096, 256, torch.float16),   # many column tiles, no split
+])
+def test_single_row_tile_vs_torch_fp32(cuda, ops, m, n, k, bias):
+    """GEMMs of one row tile (m <= 128: decode batches) load an x box of m
+    rows rounded up to 8 into a deeper ring, and with a long k and few
+    columns split each tile's k range over a cluster of CTAs whose fp32
+    partial sums the leader CTA adds in rank order: against torch fp32,
+    deterministic from call to call."""
+    g = torch.Generator(device=cuda).manual_seed(m * 1000 + n + k)
+    x = torch.randn(m, k, device=cuda, generator=g).half()
+    w = (torch.randn(n, k, device=cuda, generator=g) / k ** 0.5).half()
+    b = (torch.randn(n, device=cuda, generator=g) * 0.1).to(bias) if bias is not None else None
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    out = ops.linear(x, w, b, err_flags=err)
+    again = ops.linear(x, w, b, err_flags=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert torch.equal(out, again)
+    ref = x.float() @ w.float().T + (b.float() if b is not None else 0)
+    diff = (out.float() - ref).abs()
+    bad = diff > TOL + TOL * ref.abs()
+    assert not bool(bad.any()), f"{m}x{n}x{k}: {int(bad.sum())} outside tolerance, max abs err {float(diff.max()):.3g}"
+
+
 @pytest.mark.parametrize("what,m,n,k,bias", [
     ("linear, ragged m, n and k", 4100, 4100, 200, torch.float16),
     ("linear, square", 8192, 8192, 256, None),
@@ -178,6 +208,9 @@ def test_large_tilings_vs_torch_fp32(cuda, ops, what, m, n, k, bias):
     (300, 896, 14, 2, 64, torch.float16),   # Qwen2.5-0.5B heads, fp16 biases
     (130, 512, 8, 8, 128, None),            # Llama-style heads, no bias
     (77, 256, 7, 1, 64, torch.float32),     # odd q heads: the last q tile is half full; fp32 biases
+    (8, 896, 14, 2, 64, torch.float16),     # a decode batch of Qwen2.5-0.5B (one row tile, no split)
+    (8, 2048, 16, 4, 128, torch.float16),   # a decode batch with k = 2048: split over clusters of 4 CTAs
+    (24, 4096, 8, 2, 64, torch.float32),    # k = 4096 split over clusters of 3 (24 rows of partial sums)
     (4096, 512, 16, 16, 128, torch.float16),  # large enough for 256-wide tiles (two heads per tile)
     (4096, 512, 16, 4, 64, None),             # 256-wide tiles of four 64-column heads
 ])
