@@ -124,6 +124,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
   const int G = a.groups;
 
   grid_dep_wait();
+  grid_dep_launch();  // the next kernel's CTAs may take idle SMs and wait there
   const int pos = a.positions[t];
   const int slot = a.slots[t];
   __half* out_t = a.out + (t * a.n_heads + static_cast<int64_t>(g) * G) * D;
@@ -326,6 +327,7 @@ __global__ void __launch_bounds__(kCombineWarps * 32) attn_combine_kernel(const 
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kCombineWarps + (threadIdx.x >> 5);
   grid_dep_wait();
+  grid_dep_launch();  // the next kernel's CTAs may take idle SMs and wait there
   if (row >= a.n_tokens * a.n_heads) return;
   const int64_t t = row / a.n_heads;
   const int pos = a.positions[t], slot = a.slots[t];
@@ -382,6 +384,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(const AttnAr
   const int rows = static_cast<int>(min(static_cast<int64_t>(kPfRows), run_end - tok0));
 
   grid_dep_wait();
+  grid_dep_launch();  // the next kernel's CTAs may take idle SMs and wait there
   const int run_slot = a.slots[run_start];
   const bool run_slot_ok = run_slot >= 0 && run_slot < a.n_slots;
   if (threadIdx.x == 0) s_max_pos = -1;
@@ -642,6 +645,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_prefill_tc_kernel(const At
   const int rows = static_cast<int>(min(static_cast<int64_t>(kRowsCta), run_end - tok0));
 
   grid_dep_wait();
+  grid_dep_launch();  // the next kernel's CTAs may take idle SMs and wait there
   const int run_slot = a.slots[run_start];
   const bool run_slot_ok = run_slot >= 0 && run_slot < a.n_slots;
   if (tid < kTcQTiles) s_max_pos[tid] = -1;

@@ -31,6 +31,13 @@
 // group before the next group) so the CTAs in flight share x and w in L2.
 // Every mbarrier wait is bounded; a wait that runs out sets
 // KLLM_B200_FLAG_TIMEOUT and the CTA drains its copies and MMAs and returns.
+//
+// Decode-sized GEMMs (one row tile, m <= 128) load an x box of m rows
+// (rounded up to 8) into a deeper ring, and those with a long k and few
+// columns split each tile's k range over a thread-block cluster (split-K,
+// pick_split): every peer CTA stores the fp32 sums of its live rows into its
+// slot in the leader CTA's shared memory, and the leader adds them to its
+// accumulator in rank order before the epilogue.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -523,6 +530,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
   const uint32_t tmem = s_tmem;
   // x may come from the previous kernel on the stream and out may be read by it
   grid_dep_wait();
+  grid_dep_launch();  // the next kernel's CTAs may take the SMs this grid leaves idle and wait there
   bool ok = true;
 
   if (warp == 0) {
