@@ -336,26 +336,53 @@ __device__ __forceinline__ uint32_t part_off(const GemmArgs& a, int b, int peer,
   return static_cast<uint32_t>((((b * (a.split - 1) + peer - 1) * (kSplitBN / 4)) + col4) * a.part_rows + r) << 4;
 }
 
+// Split-K leader, one warp: the rows of this warp (tile rows 32 * quad ..,
+// all live) in the slots of peers 2 .. split - 1 are added into peer 1's
+// slot, in rank order, with the warp's lanes spread over (four-column
+// group, row) items so the loads of all peers are in flight together.
+__device__ __forceinline__ void prereduce_peers(const GemmArgs& a, uint32_t part, int b, int quad, int lane) {
+  const int64_t left = a.m - quad * 32;
+  const int nr = static_cast<int>(left < 32 ? left : 32);
+  for (int item = lane; item < nr * (kSplitBN / 4); item += 32) {
+    const int c4 = item / nr, r = quad * 32 + item % nr;
+    const uint32_t dst = part + part_off(a, b, 1, c4, r);
+    float4 sum = ld_shared_f4(dst);
+    float4 f[kMaxSplit - 2];
+#pragma unroll
+    for (int p = 2; p < kMaxSplit; ++p) {
+      if (p < a.split) f[p - 2] = ld_shared_f4(part + part_off(a, b, p, c4, r));
+    }
+#pragma unroll
+    for (int p = 2; p < kMaxSplit; ++p) {
+      if (p < a.split) {
+        sum.x += f[p - 2].x;
+        sum.y += f[p - 2].y;
+        sum.z += f[p - 2].z;
+        sum.w += f[p - 2].w;
+      }
+    }
+    st_shared_f4(dst, sum);
+  }
+  __syncwarp();
+}
+
 // Split-K leader: add to the 32 accumulator columns col .. col + 31 of tile
-// row r the peers' partial sums, in rank order, so the order of the sum and
-// its rounding are fixed.
+// row r the peers' partial sums (peer 1's slot, into which prereduce_peers
+// gathered the others), so the sum is acc + (p1 + p2 + ...) in a fixed order.
 template <bool kSplit>
 __device__ __forceinline__ void add_peer_partials(const GemmArgs& a, uint32_t part, int b, int r, bool live, int col,
                                                   float (&v)[32]) {
   if constexpr (kSplit) {
     if (!live) return;
-#pragma unroll 1
-    for (int p = 1; p < a.split; ++p) {
-      float4 f[8];
+    float4 f[8];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) f[q] = ld_shared_f4(part + part_off(a, b, p, (col >> 2) + q, r));
+    for (int q = 0; q < 8; ++q) f[q] = ld_shared_f4(part + part_off(a, b, 1, (col >> 2) + q, r));
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        v[q * 4 + 0] += f[q].x;
-        v[q * 4 + 1] += f[q].y;
-        v[q * 4 + 2] += f[q].z;
-        v[q * 4 + 3] += f[q].w;
-      }
+    for (int q = 0; q < 8; ++q) {
+      v[q * 4 + 0] += f[q].x;
+      v[q * 4 + 1] += f[q].y;
+      v[q * 4 + 2] += f[q].z;
+      v[q * 4 + 3] += f[q].w;
     }
   }
 }
@@ -512,8 +539,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
       mbar_init(bar(kAccFull + b), 1);
       mbar_init(bar(kAccEmpty + b), kEpiWarps);
       if (kSplit) {
-        mbar_init(bar(kPartFull + b), (a.split - 1) * kEpiWarps);  // every epilogue warp of every peer
-        mbar_init(bar(kPartFree + b), kEpiWarps);                  // every epilogue warp of the leader
+        mbar_init(bar(kPartFull + b), 1);          // the leader's arming; the peers' stores complete its bytes
+        mbar_init(bar(kPartFree + b), kEpiWarps);  // every epilogue warp of the leader
       }
     }
     mbar_init(bar(kMmaDone), 1);
@@ -644,7 +671,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
           if (!ok) break;
         }
         if (warp_live) {
+          // asynchronous stores that complete their bytes on the leader's barrier
           const uint32_t dst = cluster_map(part, 0);
+          const uint32_t full = cluster_map(bar(kPartFull + b), 0);
 #pragma unroll 1
           for (int c = 0; c < kBN / 32; ++c) {
             float v[32];
@@ -653,24 +682,24 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
             if (live) {
 #pragma unroll
               for (int q = 0; q < 8; ++q) {
-                st_cluster_f4(dst + part_off(a, b, rank, c * 8 + q, r), v[q * 4], v[q * 4 + 1], v[q * 4 + 2],
-                              v[q * 4 + 3]);
+                st_async_f4(dst + part_off(a, b, rank, c * 8 + q, r), v[q * 4], v[q * 4 + 1], v[q * 4 + 2],
+                            v[q * 4 + 3], full);
               }
             }
           }
         }
-        fence_acq_rel_cluster();  // the sums are visible to the leader before this warp's arrival
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(bar(kAccEmpty + b));
-          mbar_arrive_cluster(bar(kPartFull + b), 0);
-        }
+        if (lane == 0) mbar_arrive(bar(kAccEmpty + b));
         continue;
       }
       if (kSplit) {  // leader: every peer's sums of this tile are in place
+        if (quad == 0 && lane == 0) {  // the bytes the peers' live rows send (one tile is all of m)
+          mbar_expect_tx(bar(kPartFull + b), static_cast<uint32_t>((a.split - 1) * a.m * kSplitBN * 4));
+        }
         ok = __all_sync(0xffffffffu, mbar_wait_cluster(bar(kPartFull + b), (i >> 1) & 1));
         if (!ok) break;
+        if (a.split > 2 && warp_live) prereduce_peers(a, part, b, quad, lane);
       }
       if (!warp_live) {
         // no output row in this warp: nothing to store
@@ -711,15 +740,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
           }
         }
       }
-      if (kSplit) fence_acq_rel_cluster();  // the reads of the peers' slots are done before the slots are freed
       tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(bar(kAccEmpty + b));
-        if (kSplit) {
-          for (int p = 1; p < a.split; ++p) mbar_arrive_cluster(bar(kPartFree + b), p);
-        }
-      }
+      __syncwarp();  // the warp's reads of the peers' slots are done
+      if (lane == 0) mbar_arrive(bar(kAccEmpty + b));
+      // lane p frees peer p's slot (a release arrive at cluster scope)
+      if (kSplit && lane >= 1 && lane < a.split) mbar_arrive_cluster(bar(kPartFree + b), lane);
     }
     if (lane == 0) tma_store_wait_all();  // the TMA stores have read their buffers and written the output
   }
@@ -817,25 +842,26 @@ int launch_gemm(GemmArgs& a, const LaunchOpts& o, const char* what) {
 }
 
 // Split-K: CTAs per cluster sharing each tile's k range. Only for GEMMs of
-// one row tile (m <= 128: decode batches) with few column tiles (n <= 2048)
-// and a long k (>= 32 slices of 64), whose handful of CTAs would otherwise
-// each stream a long strip of weights alone (measured on B200 at m = 8: the
-// 896 x 4864 down projection 26 -> 13 us; splits of shorter k or of wide n
-// cost more in per-tile hand-offs than they gain). One CTA per 8 k slices, at
-// most kMaxSplit, and two tiles' partial sums of the peers within
-// kPartBytes. `n` is the output columns of one weight: a fused op passes the
-// width its separate linear would have, so both split alike and stay
-// bit-identical.
+// one row tile (m <= 128: decode batches) with few column tiles (n <= 2048),
+// whose handful of CTAs would otherwise each stream a strip of weights alone.
+// Half as many CTAs as k slices of 64, at most kMaxSplit, and two tiles'
+// partial sums of the peers within kPartBytes; a long k (>= 32 slices) splits
+// from 2 CTAs, a shorter one only from 4 (measured on B200 at m = 8: the
+// 896 x 4864 down projection 26.7 -> 10.5 us with 8 CTAs, the 896 x 896 o
+// projection 8.4 -> 7.9 us with 7; at m = 64, where the slots allow 2, only
+// the long k gains; splits of wide n lose: per-tile hand-offs cost more than
+// the extra CTAs gain). `n` is the output columns of one weight: a fused op
+// passes the width its separate linear would have, so both split alike and
+// stay bit-identical.
 int pick_split(int64_t m, int64_t n, int64_t k) {
   if (m > kBM || m <= 0 || n > 2048) return 1;
   const int64_t k_blocks = (k + kBK - 1) / kBK;
-  if (k_blocks < 32) return 1;
   const int64_t rows = (m + 7) / 8 * 8;
-  int64_t s = k_blocks / 8;
+  int64_t s = k_blocks / 2;
   if (s > kMaxSplit) s = kMaxSplit;
   const int64_t by_smem = 1 + kPartBytes / (2 * rows * kSplitBN * 4);
   if (s > by_smem) s = by_smem;
-  if (s < 2) return 1;
+  if (s < (k_blocks >= 32 ? 2 : 4)) return 1;
   // clusters of s CTAs must fit the device (every split kernel has the same
   // shared memory and threads)
   auto probe = gemm_tc_kernel<kSplitBN, kEpiLinear, __half, true>;

@@ -142,7 +142,6 @@ __device__ __forceinline__ uint32_t cluster_map(uint32_t addr, uint32_t rank) {
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-__device__ __forceinline__ void fence_acq_rel_cluster() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }
 // Arrive on the mbarrier at the same offset in CTA `rank`, releasing this
 // thread's earlier memory operations at cluster scope.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar, uint32_t rank) {
@@ -168,9 +167,18 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity)
     if (clock64() - t0 > kWaitCycles) return false;
   }
 }
-// 16-byte store into the shared memory of a peer CTA (address from cluster_map).
-__device__ __forceinline__ void st_cluster_f4(uint32_t addr, float a, float b, float c, float d) {
-  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+// 16-byte store into the shared memory of a peer CTA that completes 16 bytes
+// of the transaction count of the peer's mbarrier `remote_bar` (both
+// addresses from cluster_map, in the same CTA).
+__device__ __forceinline__ void st_async_f4(uint32_t addr, float a, float b, float c, float d, uint32_t remote_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                   addr),
+               "r"(__float_as_uint(a)), "r"(__float_as_uint(b)), "r"(__float_as_uint(c)), "r"(__float_as_uint(d)),
+               "r"(remote_bar)
+               : "memory");
+}
+__device__ __forceinline__ void st_shared_f4(uint32_t addr, float4 v) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
                : "memory");
 }
 __device__ __forceinline__ float4 ld_shared_f4(uint32_t addr) {

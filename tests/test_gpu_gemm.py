@@ -140,7 +140,7 @@ def test_repeated_calls_are_deterministic(cuda, ops):
 @pytest.mark.parametrize("m", [1, 8, 32, 64, 100, 128])
 @pytest.mark.parametrize("n,k,bias", [
     (896, 4864, torch.float16),   # Qwen2.5-0.5B down projection: clusters of 8 CTAs (m <= 8), 3, 2, none (m > 64)
-    (896, 896, None),             # o projection: short k, no split
+    (896, 896, None),             # o projection: clusters of 7 (m <= 16), none from m = 32 (short k)
     (203, 2056, torch.float32),   # ragged n (element-wise stores) and k (a partial last k slice): clusters of 4
     (4096, 256, torch.float16),   # many column tiles, no split
 ])
@@ -208,7 +208,7 @@ def test_large_tilings_vs_torch_fp32(cuda, ops, what, m, n, k, bias):
     (300, 896, 14, 2, 64, torch.float16),   # Qwen2.5-0.5B heads, fp16 biases
     (130, 512, 8, 8, 128, None),            # Llama-style heads, no bias
     (77, 256, 7, 1, 64, torch.float32),     # odd q heads: the last q tile is half full; fp32 biases
-    (8, 896, 14, 2, 64, torch.float16),     # a decode batch of Qwen2.5-0.5B (one row tile, no split)
+    (8, 896, 14, 2, 64, torch.float16),     # a decode batch of Qwen2.5-0.5B: clusters of 7 CTAs
     (8, 2048, 16, 4, 128, torch.float16),   # a decode batch with k = 2048: split over clusters of 4 CTAs
     (24, 4096, 8, 2, 64, torch.float32),    # k = 4096 split over clusters of 3 (24 rows of partial sums)
     (4096, 512, 16, 16, 128, torch.float16),  # large enough for 256-wide tiles (two heads per tile)
