@@ -37,10 +37,12 @@ def forward_params(r) -> dict:
             "eps": m.eps, "theta": m.theta, "seq_len": w.seq_len, "n_seqs": w.n_seqs}
 
 
-@pytest.mark.parametrize("decode", [False, True])
-def test_forward_step_matches_oracle(cuda, oracle, decode):
+@pytest.mark.parametrize("decode,hidden,inter", [(False, 256, 512), (True, 256, 512), (True, 1024, 2048)])
+def test_forward_step_matches_oracle(cuda, oracle, decode, hidden, inter):
+    """hidden 1024 with intermediate 2048 makes every GEMM of the decode step
+    (q/k/v, o, gate/up + SwiGLU, down) split its k range over a cluster."""
     from littlellm_b200.chain import ChainRunner, ModelShape, Workload
-    shape = ModelShape("tiny-2l", 256, 4, 2, 64, 512, 512, 2, 1e-6, 1e4)
+    shape = ModelShape("tiny-2l", hidden, hidden // 64, 2, 64, inter, 512, 2, 1e-6, 1e4)
     w = (Workload("d", shape, n_seqs=6, seq_len=1, max_seq=64, decode=True) if decode
          else Workload("p", shape, n_seqs=3, seq_len=40, max_seq=64, decode=False))
     r = ChainRunner(w, device=cuda, seed=11, use_pdl=True, attention=True, gemm=True)
