@@ -338,19 +338,26 @@ __device__ __forceinline__ uint32_t part_off(const GemmArgs& a, int b, int peer,
 
 // Split-K leader, one warp: the rows of this warp (tile rows 32 * quad ..,
 // all live) in the slots of peers 2 .. split - 1 are added into peer 1's
-// slot, in rank order, with the warp's lanes spread over (four-column
-// group, row) items so the loads of all peers are in flight together.
+// slot, in rank order. The warp's lanes cover (four-column group, row)
+// items: the live rows padded to a power of two on the low lane bits (no
+// divisions), consecutive rows on consecutive lanes (contiguous 16-byte
+// loads), and the loads of all peers of an item in flight together.
 __device__ __forceinline__ void prereduce_peers(const GemmArgs& a, uint32_t part, int b, int quad, int lane) {
   const int64_t left = a.m - quad * 32;
   const int nr = static_cast<int>(left < 32 ? left : 32);
-  for (int item = lane; item < nr * (kSplitBN / 4); item += 32) {
-    const int c4 = item / nr, r = quad * 32 + item % nr;
+  int lg = 0;
+  while ((1 << lg) < nr) ++lg;
+  const int rr = lane & ((1 << lg) - 1);
+  if (rr >= nr) return;  // a padding lane (no __syncwarp follows: the caller syncs the warp)
+  const int r = quad * 32 + rr;
+  const uint32_t slot = static_cast<uint32_t>(kSplitBN / 4 * a.part_rows * 16);  // bytes of one peer's slot
+  for (int c4 = lane >> lg; c4 < kSplitBN / 4; c4 += 32 >> lg) {
     const uint32_t dst = part + part_off(a, b, 1, c4, r);
     float4 sum = ld_shared_f4(dst);
     float4 f[kMaxSplit - 2];
 #pragma unroll
     for (int p = 2; p < kMaxSplit; ++p) {
-      if (p < a.split) f[p - 2] = ld_shared_f4(part + part_off(a, b, p, c4, r));
+      if (p < a.split) f[p - 2] = ld_shared_f4(dst + (p - 1) * slot);
     }
 #pragma unroll
     for (int p = 2; p < kMaxSplit; ++p) {
@@ -363,7 +370,6 @@ __device__ __forceinline__ void prereduce_peers(const GemmArgs& a, uint32_t part
     }
     st_shared_f4(dst, sum);
   }
-  __syncwarp();
 }
 
 // Split-K leader: add to the 32 accumulator columns col .. col + 31 of tile
@@ -699,7 +705,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
         }
         ok = __all_sync(0xffffffffu, mbar_wait_cluster(bar(kPartFull + b), (i >> 1) & 1));
         if (!ok) break;
-        if (a.split > 2 && warp_live) prereduce_peers(a, part, b, quad, lane);
+        if (a.split > 2 && warp_live) {
+          prereduce_peers(a, part, b, quad, lane);
+          __syncwarp();  // the lanes read each other's sums below
+        }
       }
       if (!warp_live) {
         // no output row in this warp: nothing to store
