@@ -22,7 +22,7 @@
 // a last wave that is not mostly idle); a SwiGLU tile is BN / 2 output
 // columns: BN / 2 gate rows and BN / 2 up rows of the weights stacked as the
 // UMMA's N. Warp 0 issues TMA loads of 64-wide k slices (128-byte swizzle)
-// into a ring of 4 to 6 stages; warp 1 issues tcgen05.mma (M 128, N BN,
+// into a ring of 4 to 6 stages (up to 16 for a few rows of x); warp 1 issues tcgen05.mma (M 128, N BN,
 // K 16) into one of two fp32 accumulators in tensor memory; warps 2-5 read
 // the other accumulator back (tcgen05.ld, one row per thread), apply the
 // epilogue and write each warp's 32 x 32 output chunks through shared memory
@@ -62,8 +62,10 @@ constexpr int kMaxStages = 16;                // ring depth with a compact x reg
 // 128, chosen per problem by the host (pick_tile_width) so that the column
 // tiles fit n and the last wave of SMs is not left mostly idle. The ring
 // holds as many stages as fit beside the epilogue's staging buffers.
-// A split-K launch (kSplit) holds 4 stages and beside them the 64 KB of
-// fp32 partial sums its peer CTAs hand to the cluster's leader CTA.
+// The ring's shared memory, in stages of full-height x tiles: 4 for a
+// split-K launch (kSplit), beside the 64 KB of fp32 partial sums its peer
+// CTAs hand to the cluster's leader CTA. With one row tile the x region of a
+// stage shrinks and the same memory holds more stages (GemmArgs::stages).
 __host__ __device__ constexpr int gemm_stages(int bn, bool split = false) {
   return split ? 4 : (bn >= 224 ? 4 : (bn == 192 ? 5 : 6));
 }
