@@ -22,8 +22,9 @@
 // a last wave that is not mostly idle); a SwiGLU tile is BN / 2 output
 // columns: BN / 2 gate rows and BN / 2 up rows of the weights stacked as the
 // UMMA's N. Warp 0 issues TMA loads of 64-wide k slices (128-byte swizzle)
-// into a ring of 4 to 6 stages (up to 16 for a few rows of x); warp 1 issues tcgen05.mma (M 128, N BN,
-// K 16) into one of two fp32 accumulators in tensor memory; warps 2-5 read
+// into a ring of 4 to 6 stages (up to 16 for a few rows of x); warp 1
+// issues tcgen05.mma (M 128, N BN, K 16) into one of two fp32 accumulators
+// in tensor memory; warps 2-5 read
 // the other accumulator back (tcgen05.ld, one row per thread), apply the
 // epilogue and write each warp's 32 x 32 output chunks through shared memory
 // with TMA stores, so the epilogue of tile i overlaps the main loop of tile
