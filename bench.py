@@ -343,7 +343,8 @@ def run_reference_load(args):
 
 
 def run_reference(args):
-    from littlellm_b200.chain import WORKLOADS
+    # the shapes only: this arm must not map libkllm_b200.so
+    from littlellm_b200.workloads import WORKLOADS
     world, rank, _ = dist_env()
     if rank != 0:
         return
@@ -965,7 +966,7 @@ def run_attention(args):
 
 
 def run_reference_attention(args):
-    from littlellm_b200.chain import WORKLOADS
+    from littlellm_b200.workloads import WORKLOADS
     w = WORKLOADS[ATTENTION_WORKLOADS[args.workload]]
     L = args.layers or w.model.n_layers
     threads = host_threads()
@@ -1266,7 +1267,7 @@ def run_gemm(args):
 
 
 def run_reference_gemm(args):
-    from littlellm_b200.chain import WORKLOADS
+    from littlellm_b200.workloads import WORKLOADS
     m = WORKLOADS[GEMM_WORKLOADS[args.workload]].model
     L = args.layers or m.n_layers
     threads = host_threads()

@@ -19,90 +19,14 @@ Qwen2.5-0.5B (hidden 896, 14/2 heads x 64, intermediate 4864, vocab 151936,
 from __future__ import annotations
 
 import ctypes
-from dataclasses import dataclass, replace
+from dataclasses import replace
 
 import torch
 
 from . import _capi
-
-
-@dataclass(frozen=True)
-class ModelShape:
-    name: str
-    hidden: int
-    n_heads: int
-    n_kv_heads: int
-    head_dim: int
-    intermediate: int
-    vocab: int
-    n_layers: int
-    eps: float
-    theta: float
-
-
-QWEN2_5_0_5B = ModelShape("qwen2.5-0.5b", 896, 14, 2, 64, 4864, 151936, 24, 1e-6, 1e6)
-LLAMA2_7B = ModelShape("llama-2-7b", 4096, 32, 32, 128, 11008, 32000, 32, 1e-5, 1e4)
-
-
-@dataclass(frozen=True)
-class Workload:
-    name: str
-    model: ModelShape
-    n_seqs: int        # sequences in the step (per GPU for weak scaling)
-    seq_len: int       # new tokens per sequence in this step
-    max_seq: int       # KV cache capacity per sequence
-    decode: bool       # decode: one token per sequence at a random position
-
-    @property
-    def n_tokens(self) -> int:
-        return self.n_seqs * self.seq_len
-
-
-WORKLOADS = {
-    # B=8 x 512 prefill of Qwen2.5-0.5B, cache [24, 2, 8, 2, 4096, 64]
-    "qwen_prefill": Workload("qwen_prefill", QWEN2_5_0_5B, 8, 512, 4096, False),
-    # B=32 x 512 prefill of Llama-2-7B
-    "llama_prefill": Workload("llama_prefill", LLAMA2_7B, 32, 512, 512, False),
-    # 2048 sequences x 1 token, positions U[0, 4095), cache [24, 2, 2048, 2, 4096, 64]
-    "qwen_decode": Workload("qwen_decode", QWEN2_5_0_5B, 2048, 1, 4096, True),
-    # 128 x 512 Llama-2-7B prefill; 16 sequences per GPU at 8 GPUs
-    "llama_prefill_64k": Workload("llama_prefill_64k", LLAMA2_7B, 128, 512, 512, False),
-}
-
-
-def shard(workload: Workload, rank: int, world: int) -> Workload:
-    """The slice of a workload one rank runs when sequences are split evenly."""
-    if workload.n_seqs % world != 0:
-        raise ValueError(f"{workload.n_seqs} sequences do not split over {world} ranks")
-    return replace(workload, n_seqs=workload.n_seqs // world)
-
-
-def chain_bytes(w: Workload, n_layers: int | None = None, positions=None) -> dict:
-    """Algorithmic HBM bytes of one chain step: every logical fp16 tensor read
-    once and written once; norm weights and biases are negligible and not
-    counted; ids/positions/slots are int32. With ``positions`` (host array of
-    the step's token positions) the attention of every layer is included:
-    each sequence's cached K and V rows 0..position read once (decode: per
-    token), q read and the context written."""
-    m, T = w.model, w.n_tokens
-    H, I, L = m.hidden, m.intermediate, n_layers or m.n_layers
-    qkv_elems = T * (m.n_heads + 2 * m.n_kv_heads) * m.head_dim
-    per = {
-        "embedding": 2 * T * H * 2 + 4 * T,
-        "add_rms_norm": (L + 1) * 4 * T * H * 2 + (L - 1) * 4 * T * H * 2 + 2 * T * H * 2,
-        "qkv_bias_rope_kv_append": L * (2 * qkv_elems * 2 + 8 * T),
-        "silu_mul": L * 3 * T * I * 2,
-        "select_last_rows": 2 * w.n_seqs * H * 2,
-    }
-    if positions is not None:
-        kv_rows = int((positions.astype("int64") + 1).sum()) if w.decode else T
-        per["attention"] = L * (kv_rows * m.n_kv_heads * m.head_dim * 2 * 2 + 2 * T * m.n_heads * m.head_dim * 2)
-    per["total"] = sum(per.values())
-    return per
-
-
-def silu_bytes_per_launch(w: Workload) -> int:
-    return 3 * w.n_tokens * w.model.intermediate * 2
+# shapes and workloads live in a module that maps no library (re-exported here)
+from .workloads import (LLAMA2_7B, QWEN2_5_0_5B, WORKLOADS, ModelShape, Workload,  # noqa: F401
+                        chain_bytes, shard, silu_bytes_per_launch)
 
 
 class ChainRunner:
