@@ -48,6 +48,9 @@ def parse_args():
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-other-configs", action="store_true",
+                    help="time only the headline workload (skip the other survey configs and the reference "
+                         "CUDA kernels)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample length")
     ap.add_argument("--layers", type=int, default=None,
                     help="run only this many decoder layers (small profiling cases; not a bench line)")
@@ -472,23 +475,17 @@ LLAMA7B_INT8_TENSORS = (
 )
 
 
-def run_dequant(args):
+def measure_dequant(device, steps: int, warmup: int, peaks: dict) -> dict:
     """INT8 -> fp16 dequant of every Llama-2-7B linear/embedding tensor
     (6.74 B parameters, int8 ~U[-127,127], fp32 scale ~U(1e-3,1e-2) per
     tensor) with the reference weight loader's rounding; one step = the whole
-    checkpoint. Metric: algorithmic GB/s (1 B read + 2 B written per value)."""
+    checkpoint, one CUDA graph. Also times the fp32-output form on four
+    11008 x 4096 tensors, the form the reference's own GPU op has
+    (src/op/cuda/quantize.cu:110-121). Returns the variants and the device
+    tensors of the first one (for the CPU sample)."""
     import torch
 
-    from littlellm_b200 import build as kbuild
     from littlellm_b200 import ops
-    if not torch.cuda.is_available():
-        raise SystemExit("bench.py needs a CUDA GPU")
-    world, rank, local = dist_env()
-    if world > 1:
-        raise SystemExit("the dequant workload runs on one GPU")
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    kbuild.build()
     gen = torch.Generator(device=device)
     gen.manual_seed(5)
     data, scales, outs = [], [], []
@@ -501,25 +498,54 @@ def run_dequant(args):
     nbytes = 3 * n_params + 4 * len(data)
     log(f"dequant: {len(data)} tensors, {n_params} params allocated")
     stream = torch.cuda.Stream(device)
-    peaks = load_peaks()
     results = {}
+    f32_in = [data[128 + i] for i in range(4)]  # four gate/up tensors, 11008 x 4096
+    f32_out = [torch.empty(d.shape, dtype=torch.float32, device=device) for d in f32_in]
+    f32_bytes = sum(5 * d.numel() for d in f32_in)
+    variants = (
+        ("batched", nbytes, 1, lambda: ops.dequantize_int8_batched(data, scales, outs)),
+        ("per_tensor", nbytes, len(data),
+         lambda: [ops.dequantize_int8(d, sc, out=o) for d, sc, o in zip(data, scales, outs)]),
+        ("f32_out_4x11008x4096", f32_bytes, 4,
+         lambda: [ops.dequantize_int8(d, scales[0], out=o) for d, o in zip(f32_in, f32_out)]),
+    )
     with torch.cuda.stream(stream):
-        for name, fn in (("batched", lambda: ops.dequantize_int8_batched(data, scales, outs)),
-                         ("per_tensor", lambda: [ops.dequantize_int8(d, sc, out=o)
-                                                 for d, sc, o in zip(data, scales, outs)])):
+        for name, vbytes, launches, fn in variants:
             fn()
             stream.synchronize()
-            log(f"dequant {name}: eager ok")
             g = capture(fn, stream)
-            log(f"dequant {name}: captured")
-            for _ in range(max(args.warmup, 3)):
+            for _ in range(max(warmup, 3)):
                 g.replay()
             stream.synchronize()
-            ms = time_graph(g, stream, args.steps)
-            results[name] = {"ms_per_step": ms, "gbs": nbytes / (ms * 1e-3) / 1e9,
-                             "frac_of_measured": nbytes / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
-                             "launches_per_step": 1 if name == "batched" else len(data)}
+            ms = time_graph(g, stream, steps)
+            gbs = vbytes / (ms * 1e-3) / 1e9
+            results[name] = {"ms_per_step": ms, "gbs": gbs, "frac_of_measured": gbs / peaks["hbm_gbs"],
+                             "bytes_per_step": vbytes, "launches_per_step": launches}
             del g
+    results["_tensors"] = (data, scales)
+    results["_meta"] = {"tensors": len(data), "params": n_params, "bytes_per_step": nbytes}
+    return results
+
+
+def run_dequant(args):
+    """INT8 -> fp16 dequant of every Llama-2-7B linear/embedding tensor; one
+    step = the whole checkpoint. Metric: algorithmic GB/s (1 B read + 2 B
+    written per value)."""
+    import torch
+
+    from littlellm_b200 import build as kbuild
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA GPU")
+    world, rank, local = dist_env()
+    if world > 1:
+        raise SystemExit("the dequant workload runs on one GPU")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    kbuild.build()
+    peaks = load_peaks()
+    results = measure_dequant(device, args.steps, args.warmup, peaks)
+    data, scales = results.pop("_tensors")
+    meta = results.pop("_meta")
     import numpy as np
     cpu = None
     if not args.no_cpu_baseline:
@@ -542,12 +568,13 @@ def run_dequant(args):
                "kind": "reference" if reference_available() else "port",
                "sample": f"{sample} values x {reps} through the weight loader's loop body "
                          "(float(q) * scale, float_to_half), single thread"}
+    del data, scales
     b = results["batched"]
     emit({"metric": "int8->fp16 dequant throughput", "value": b["gbs"], "unit": "GB/s", "n_gpus": 1,
           "steps": args.steps, "warmup": args.warmup, "ms_per_step": b["ms_per_step"], "higher_is_better": True,
           "scaling": "none", "vs_baseline": None, "dtype": "i8->f16", "data": "synthetic",
-          "config": {"workload": "llama_int8_dequant", "tensors": len(data), "params": n_params,
-                     "bytes_per_step": nbytes, "l2": "no flush: 20.2 GB per step >> 126 MB L2"},
+          "config": {"workload": "llama_int8_dequant", **meta,
+                     "l2": "no flush: 20.2 GB per step >> 126 MB L2"},
           "roofline": {"bound": "hbm", "kernel": "dequant_batched_kernel", "achieved": b["gbs"],
                        "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": b["frac_of_measured"],
                        "traffic": None, "peak_source": peaks["source"]},
@@ -1283,11 +1310,192 @@ def run_reference_gemm(args):
           "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
 
 
+def ref_cuda_ops(w, n_layers: int, dequant_shape=None, timeout: float = 900.0) -> dict:
+    """The reference's own CUDA operators (its src/op/cuda/*.cu built for
+    sm_100a by oracle/Makefile into oracle/_ref/refcuda/ref_cuda_ops), timed
+    on this GPU at the workload's shapes in a child process: eager launches
+    on the legacy stream as the reference issues them, over distinct buffer
+    sets larger than L2, CUDA events. A baseline only, run after our timing.
+    Returns {op: {"us": per call group, "launches": kernels per group}}."""
+    exe = os.path.join(ROOT, "oracle", "_ref", "refcuda", "ref_cuda_ops")
+    if not os.path.exists(exe):
+        return {"unavailable": "oracle/_ref/refcuda/ref_cuda_ops was not built (needs the reference sources)"}
+    m = w.model
+    sets = 8 if m.hidden <= 1024 else 4
+    dq = dequant_shape or (0, 0)
+    argv = [exe, w.n_tokens, m.hidden, m.n_heads, m.n_kv_heads, m.head_dim, m.intermediate, m.vocab, n_layers,
+            sets, 3, m.eps, m.theta, w.n_seqs, dq[0], dq[1]]
+    try:
+        r = subprocess.run([str(a) for a in argv], capture_output=True, text=True, timeout=timeout)
+    except subprocess.TimeoutExpired:
+        return {"unavailable": f"ref_cuda_ops timed out after {timeout:.0f} s"}
+    if r.returncode != 0:
+        return {"unavailable": "ref_cuda_ops failed: " + (r.stderr.strip() or r.stdout.strip())[-300:]}
+    out = {}
+    for line in r.stdout.splitlines():
+        parts = line.split()
+        if len(parts) == 3:
+            out[parts[0]] = {"us": float(parts[1]), "launches": int(parts[2])}
+    out["method"] = (f"reference src/op/cuda ops, eager launches on the legacy stream, {n_layers} calls per pass "
+                     f"over {sets} distinct buffer sets, CUDA events; select_last_rows = one call per sequence")
+    return out
+
+
+def merge_ref_cuda(ops_table: dict, ref: dict, field: str = "ref_cuda_us") -> None:
+    """Adds the reference CUDA time of each op and our speed-up over it."""
+    for name, v in ops_table.items():
+        r = ref.get(name)
+        if isinstance(r, dict) and "us" in r and v.get("us_per_launch"):
+            v[field] = r["us"]
+            v["ref_cuda_launches"] = r["launches"]
+            v["speedup_vs_ref_cuda"] = r["us"] / v["us_per_launch"]
+
+
+def embedding_chain_timing(runner, stream, reps: int) -> dict:
+    """Embedding + layer 0's input RMSNorm as the chain executor launches them
+    (op mask EMBEDDING | INPUT_NORM over one layer, PDL), one chain call per
+    layer's buffers captured into one graph: distinct ids, residual and
+    normed-output buffers per call, so no call re-reads another's rows from
+    L2. Algorithmic bytes per call: the table rows read once, the residual and
+    the normed rows written once, the ids read (3*T*H*2 + 4*T)."""
+    import torch
+
+    from littlellm_b200 import _capi
+    w, m = runner.w, runner.w.model
+    T, H = w.n_tokens, m.hidden
+    L = runner.layers
+    gen = torch.Generator(device=runner.device)
+    gen.manual_seed(7)
+    ids = [torch.randint(0, m.vocab, (T,), generator=gen, device=runner.device, dtype=torch.int32) for _ in L]
+    d = runner.desc
+    # integer fields and addresses (a pointer field read from a ctypes
+    # structure is a view of the structure, not a copy)
+    saved = (d.op_mask, d.n_layers, d.ids, d.residual)
+    arrs = []
+    for i, layer in enumerate(L):
+        a = (_capi.LayerBuffers * 1)()
+        a[0] = runner._layer_arr[i]
+        arrs.append(a)
+
+    def calls():
+        n = 0
+        for i, layer in enumerate(L):
+            d.op_mask = _capi.OP_EMBEDDING | _capi.OP_INPUT_NORM
+            d.n_layers = 1
+            d.ids = ids[i].data_ptr()
+            d.residual = layer["ffn_norm_out"].data_ptr()  # a T x H buffer of this layer's own
+            d.layers = ctypes_cast_layers(arrs[i])
+            n += runner.run(stream)
+        return n
+
+    try:
+        with torch.cuda.stream(stream):
+            n = calls()
+            g = capture(calls, stream)
+            g.replay()
+            ms = time_graph(g, stream, reps) / len(L)
+            del g
+    finally:
+        d.op_mask, d.n_layers, d.ids, d.residual = saved
+        d.layers = ctypes_cast_layers(runner._layer_arr)
+    nbytes = 3 * T * H * 2 + 4 * T
+    return {"us_per_launch": ms * 1000.0, "bytes_per_launch": nbytes, "gbs": nbytes / (ms * 1e-3) / 1e9,
+            "launches_per_replay": n, "kernels_per_call": n // len(L)}
+
+
+def ctypes_cast_layers(arr):
+    import ctypes
+
+    from littlellm_b200 import _capi
+    return ctypes.cast(arr, ctypes.POINTER(_capi.LayerBuffers))
+
+
+def measure_chain(w, args, device, dist, *, seed: int, steps: int, warmup: int, attention: bool = False,
+                  per_op: bool = True, standalone: bool = True):
+    """One chain step of workload `w` (this rank's share) as a CUDA graph:
+    capture, `warmup` replays, clock settling, then `steps` replays between a
+    barrier and device syncs on both sides, CUDA events on the launch stream,
+    the time as the max over ranks. Returns (runner, stream, stats)."""
+    import torch
+
+    from littlellm_b200.chain import ChainRunner, chain_bytes
+    runner = ChainRunner(w, device=device, seed=seed, use_pdl=not args.no_pdl, n_layers=args.layers,
+                         attention=attention)
+    stream = torch.cuda.Stream(device)
+    torch.cuda.synchronize(device)
+    with torch.cuda.stream(stream):
+        launches = runner.run(stream)
+        stream.synchronize()
+        graph = capture(lambda: runner.run(stream), stream)
+        for _ in range(max(warmup, 3)):
+            graph.replay()
+        stream.synchronize()
+        sampler = ClockSampler(device)
+        sampler.start()
+        t_end = time.perf_counter() + args.settle_seconds
+        while time.perf_counter() < t_end:
+            for _ in range(20):
+                graph.replay()
+            stream.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        end.record(stream)
+        end.synchronize()
+        torch.cuda.synchronize(device)
+    if dist is not None:
+        dist.barrier()
+    t = torch.tensor([start.elapsed_time(end)], dtype=torch.float64, device=device)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    clocks = sampler.stop()
+    del graph
+    ms = float(t.item()) / steps
+    peaks = load_peaks()
+    bytes_step = chain_bytes(w, runner.n_layers, positions=runner.positions.cpu().numpy() if attention else None,
+                             fused_embedding=runner.fused_embedding)
+    gbs = bytes_step["total"] / (ms * 1e-3) / 1e9
+    stats = {"ms_per_step": ms, "launches_per_step": launches, "clocks": clocks,
+             "chain_bytes_per_step": bytes_step["total"], "hbm_gbs_chain": gbs,
+             "hbm_frac_chain": gbs / peaks["hbm_gbs"], "peak_gbs": peaks["hbm_gbs"],
+             "peak_source": peaks["source"]}
+    if per_op:
+        op_chain = per_op_chain_timing(runner, stream, max(steps, 5))
+        op_chain["embedding_input_norm"] = embedding_chain_timing(runner, stream, max(steps, 5))
+        tables = [op_chain]
+        stats["ops"] = op_chain
+        if standalone:
+            op_alone = per_op_timing(runner, stream, max(steps, 5))
+            tables.append(op_alone)
+            stats["ops_standalone"] = op_alone
+        for table in tables:
+            for v in table.values():
+                v["frac_of_measured"] = v["gbs"] / peaks["hbm_gbs"]
+    return runner, stream, stats
+
+
+def release_device_memory() -> None:
+    """Returns the memory of tensors no longer referenced to the device (call
+    after dropping the last reference to a runner)."""
+    import gc
+
+    import torch
+    gc.collect()
+    torch.cuda.empty_cache()
+
+
+OTHER_CONFIGS_N1 = ("llama_prefill", "qwen_decode")
+
+
 def run_ours(args):
     import torch
 
     from littlellm_b200 import build as kbuild
-    from littlellm_b200.chain import WORKLOADS, ChainRunner, chain_bytes, shard
+    from littlellm_b200.chain import WORKLOADS, shard
 
     world, rank, local = dist_env()
     if world != args.gpus:
@@ -1308,48 +1516,13 @@ def run_ours(args):
     base = WORKLOADS[args.workload]
     weak = args.workload == "qwen_prefill"
     w = base if weak else shard(base, rank, world)
-    runner = ChainRunner(w, device=device, seed=1000 + rank, use_pdl=not args.no_pdl, n_layers=args.layers,
-                         attention=args.attention)
-    stream = torch.cuda.Stream(device)
-    torch.cuda.synchronize(device)
-
-    # one chain step = one CUDA graph replay; every replay, event and sync
-    # below is issued on `stream` (CUDAGraph.replay() uses the current stream)
-    with torch.cuda.stream(stream):
-        launches = runner.run(stream)
-        stream.synchronize()
-        graph = capture(lambda: runner.run(stream), stream)
-        for _ in range(max(args.warmup, 3)):
-            graph.replay()
-        stream.synchronize()
-
-        sampler = ClockSampler(device)
-        sampler.start()
-        # let clocks settle under load (untimed)
-        t_end = time.perf_counter() + args.settle_seconds
-        while time.perf_counter() < t_end:
-            for _ in range(20):
-                graph.replay()
-            stream.synchronize()
-
-        if dist is not None:
-            dist.barrier()
-        torch.cuda.synchronize(device)
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        start.record(stream)
-        for _ in range(args.steps):
-            graph.replay()
-        end.record(stream)
-        end.synchronize()
-        torch.cuda.synchronize(device)
-    if dist is not None:
-        dist.barrier()
-    elapsed_ms = start.elapsed_time(end)
-    t = torch.tensor([elapsed_ms], dtype=torch.float64, device=device)
-    if dist is not None:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    max_ms = float(t.item())
-    clocks = sampler.stop()
+    single = world == 1
+    runner, stream, st = measure_chain(w, args, device, dist, seed=1000 + rank, steps=args.steps,
+                                       warmup=args.warmup, attention=args.attention, standalone=single)
+    peaks = load_peaks()
+    ms_per_step = st["ms_per_step"]
+    value = w.n_tokens * world / (ms_per_step * 1e-3)
+    op_chain = st["ops"]
 
     # verification: every rank's last rows gathered to rank 0 (NCCL all_gather,
     # off the timed path) and the device error flags OR-ed over ranks
@@ -1360,21 +1533,6 @@ def run_ours(args):
         verification = {"ranks": world, "rows_gathered": int(last.shape[0]),
                         "finite": bool(torch.isfinite(last).all().item()), "err_flags": flags}
 
-    ms_per_step = max_ms / args.steps
-    tokens_total = w.n_tokens * world
-    value = tokens_total / (ms_per_step * 1e-3)
-    bytes_step = chain_bytes(w, runner.n_layers,
-                             positions=runner.positions.cpu().numpy() if args.attention else None)
-    chain_gbs = bytes_step["total"] / (ms_per_step * 1e-3) / 1e9
-    peaks = load_peaks()
-
-    # dominant kernel (SwiGLU) and per-op breakdown: in chain context (op
-    # mask, PDL) and standalone (each op's C-ABI entry, no PDL)
-    op_chain = per_op_chain_timing(runner, stream, max(args.steps, 5))
-    op_stats = per_op_timing(runner, stream, max(args.steps, 5))
-    for table in (op_chain, op_stats):
-        for v in table.values():
-            v["frac_of_measured"] = v["gbs"] / peaks["hbm_gbs"]
     silu = op_chain["silu_mul"]
     roofline = {
         "bound": "hbm", "kernel": "silu_mul_f16_kernel", "achieved": silu["gbs"], "peak": peaks["hbm_gbs"],
@@ -1399,7 +1557,7 @@ def run_ours(args):
         e2e = run_e2e(runner, stream, args.steps, device, dist, world)
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.attention:
+    if rank == 0 and single and not args.no_cpu_baseline and not args.attention:
         threads = 1
         tokens = 128
         v, steps, kind = time_reference_cpu(w.model, tokens, threads, args.cpu_seconds)
@@ -1407,8 +1565,73 @@ def run_ours(args):
                "sample": f"one {tokens}-token sequence through all {w.model.n_layers} layers of the "
                          f"{w.model.name} non-GEMM chain, repeated {len(steps)}x "
                          f"({sum(steps):.1f} s), fp32, single thread (the reference CPU path is single-threaded)"}
+    n_layers = runner.n_layers
+    launches = st["launches_per_step"]
+    fused = runner.fused_embedding
+    del runner
+    release_device_memory()
 
-    del graph
+    # the reference's own CUDA kernels at this workload's shapes (1 GPU only)
+    run_extra = args.layers is None and not args.attention and not args.no_other_configs
+    if rank == 0 and single and run_extra:
+        ref = ref_cuda_ops(w, n_layers)
+        merge_ref_cuda(op_chain, ref)
+        merge_ref_cuda(st.get("ops_standalone", {}), ref)
+        st["ref_cuda"] = ref
+
+    # the survey's other configurations, each its own graph and clock record:
+    # 1 GPU: Llama-2-7B prefill (config 3), Qwen decode 2048 x 1 (config 4),
+    # the Llama-2-7B INT8 dequant (config 5a); N GPUs: config 3 and config 4
+    # split N ways (strong scaling) and, from 4 GPUs, the 64K-token Llama
+    # prefill (config 5b)
+    other = {}
+    if run_extra:
+        names = list(OTHER_CONFIGS_N1)
+        if world >= 4:
+            names.append("llama_prefill_64k")
+        for name in names:
+            wk = WORKLOADS[name]
+            if wk.n_seqs % world != 0:
+                continue
+            ws = shard(wk, rank, world)
+            log(f"other config {name}: {ws.n_seqs} sequences on this rank")
+            r2, _, s2 = measure_chain(ws, args, device, dist, seed=2000 + rank, steps=args.steps,
+                                      warmup=args.warmup, standalone=single)
+            s2["value"] = wk.n_tokens / (s2["ms_per_step"] * 1e-3)
+            s2["unit"] = UNIT
+            s2["scaling"] = "strong"
+            s2["tokens_per_step_all_gpus"] = wk.n_tokens
+            s2["sequences_per_gpu"] = ws.n_seqs
+            s2["kv_cache"] = [r2.n_layers, 2, ws.n_seqs, ws.model.n_kv_heads, ws.max_seq, ws.model.head_dim]
+            s2["err_flags"] = kd.or_over_ranks(int(r2.err_flags.item()), device)
+            nl = r2.n_layers
+            del r2
+            release_device_memory()
+            if rank == 0 and single:
+                ref = ref_cuda_ops(ws, nl, dequant_shape=(11008, 4096) if name == "llama_prefill" else None)
+                merge_ref_cuda(s2["ops"], ref)
+                merge_ref_cuda(s2.get("ops_standalone", {}), ref)
+                s2["ref_cuda"] = ref
+            other[name] = s2
+        if single:
+            log("other config llama_int8_dequant")
+            sampler = ClockSampler(device)
+            sampler.start()
+            dq = measure_dequant(device, args.steps, args.warmup, peaks)
+            dq.pop("_tensors")
+            meta = dq.pop("_meta")
+            dq_clocks = sampler.stop()
+            torch.cuda.empty_cache()
+            b = dq["batched"]
+            entry = {"ms_per_step": b["ms_per_step"], "value": b["gbs"], "unit": "GB/s",
+                     "hbm_frac_chain": b["frac_of_measured"], "variants": dq, "clocks": dq_clocks, **meta}
+            if "llama_prefill" in other and "dequant_f32" in other["llama_prefill"].get("ref_cuda", {}):
+                r = other["llama_prefill"]["ref_cuda"]["dequant_f32"]["us"]
+                ours = dq["f32_out_4x11008x4096"]["ms_per_step"] * 1000.0 / 4
+                entry["f32_vs_ref_cuda"] = {"ref_cuda_us_per_tensor": r, "ours_us_per_tensor": ours,
+                                            "speedup": r / ours}
+            other["llama_int8_dequant"] = entry
+
     if rank == 0:
         line = {
             "metric": METRIC + (" (chain with attention)" if args.attention else ""), "value": value, "unit": UNIT,
@@ -1417,32 +1640,36 @@ def run_ours(args):
             "scaling": "weak" if weak else "strong", "vs_baseline": None, "dtype": "f16",
             "data": "synthetic",
             "config": {
-                "workload": w.name, "model": w.model.name, "layers": runner.n_layers,
+                "workload": w.name, "model": w.model.name, "layers": n_layers,
                 "tokens_per_gpu": w.n_tokens, "sequences_per_gpu": w.n_seqs, "seq_len": w.seq_len,
-                "kv_cache": [runner.n_layers, 2, w.n_seqs, w.model.n_kv_heads, w.max_seq, w.model.head_dim],
+                "kv_cache": [n_layers, 2, w.n_seqs, w.model.n_kv_heads, w.max_seq, w.model.head_dim],
                 "parallelism": f"dp{world} (sequences split, no collective on the path)",
                 "math": "fp16 storage, fp32 arithmetic",
                 "l2": "no flush: each step streams %.2f GB of distinct per-layer buffers (>> 126 MB L2)"
-                      % (bytes_step["total"] / 1e9),
+                      % (st["chain_bytes_per_step"] / 1e9),
                 "pdl": not args.no_pdl, "cuda_graph": True, "attention": bool(args.attention),
+                "embedding_fused_with_input_norm": fused,
             },
-            "hbm_gbs_chain": chain_gbs,
-            "hbm_frac_chain": chain_gbs / peaks["hbm_gbs"],
-            "chain_bytes_per_step": bytes_step["total"],
+            "hbm_gbs_chain": st["hbm_gbs_chain"],
+            "hbm_frac_chain": st["hbm_frac_chain"],
+            "chain_bytes_per_step": st["chain_bytes_per_step"],
             "roofline": roofline,
             "ops": op_chain,
-            "ops_standalone": op_stats,
-            "clocks": clocks,
+            "ops_standalone": st.get("ops_standalone"),
+            "ref_cuda": st.get("ref_cuda"),
+            "clocks": st["clocks"],
             "gpu_launches": launches * args.steps,
             "launches_per_step": launches,
             "e2e": e2e,
             "cpu_baseline": cpu,
             "verification": verification,
+            "other_configs": other,
         }
         emit(line)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
 
 
 FORWARD_METRIC = "forward tokens/s"

@@ -90,6 +90,18 @@ int kllm_b200_embedding(const void* table, int64_t vocab, int64_t hidden, int ta
                         const int32_t* ids, int64_t n_tokens, void* out, int out_dtype,
                         int32_t* err_flags, void* stream);
 
+/* kllm_b200_embedding with the ids in HOST memory, as cuda_embedding takes
+ * them (a std::vector<int>, src/op/cuda/embedding.cu:83-108). The ids travel
+ * inside the kernel launches' parameters (up to KLLM_B200_PARAM_IDS per
+ * launch; longer lists take several launches), so there is no device
+ * buffer, no allocation and no blocking copy: the call returns once the
+ * launches are enqueued and host_ids may be reused at once. Same copy
+ * semantics, flags and dtypes as kllm_b200_embedding. */
+#define KLLM_B200_PARAM_IDS 7680
+int kllm_b200_embedding_host_ids(const void* table, int64_t vocab, int64_t hidden, int table_dtype,
+                                 const int32_t* host_ids, int64_t n_tokens, void* out, int out_dtype,
+                                 int32_t* err_flags, void* stream);
+
 /* out = x * (mean(x^2) + eps)^-1/2 * weight, per row of `hidden` elements.
  * Replaces cuda_rms_norm (src/op/cuda/rms_norm.cu:177-188). x/out share
  * act_dtype in {F32,F16}; weight_dtype in {F32,F16}; fp32 accumulation. */
@@ -178,6 +190,19 @@ int kllm_b200_dequantize_int8_batched(const int8_t* const* data, const float* co
 int kllm_b200_add_rms_norm(void* residual, const void* delta, const void* weight, void* out,
                            int64_t rows, int64_t hidden, float eps, int act_dtype,
                            int weight_dtype, void* stream);
+
+/* The embedding gather fused with the RMSNorm that reads it (layer 0's input
+ * norm): src/model/llama.cpp:84 (cuda_embedding) and :83-87 of the first
+ * layer (cuda_rms_norm), in one launch:
+ *     residual_out[t, :] = table[ids[t], :]                (bit-exact copy)
+ *     norm_out[t, :]     = rms_norm(residual_out[t, :]) * weight
+ * fp16 table and outputs; weight_dtype in {F32,F16}; ids a device array.
+ * Bit-identical to kllm_b200_embedding followed by kllm_b200_rms_norm; the
+ * gathered rows are not re-read from HBM. Ids outside [0, vocab) give zero
+ * rows (both outputs) and set KLLM_B200_FLAG_BAD_TOKEN. */
+int kllm_b200_embedding_rms_norm(const void* table, int64_t vocab, int64_t hidden, const int32_t* ids,
+                                 int64_t n_tokens, const void* weight, int weight_dtype, float eps,
+                                 void* residual_out, void* norm_out, int32_t* err_flags, void* stream);
 
 /* q/k/v bias add + rotate-half RoPE + KV-cache append, one launch.
  * Replaces, per layer, add_bias_inplace x3 (src/model/llama.cpp:89-106 via
@@ -457,11 +482,14 @@ int kllm_b200_kllm_load(const char* path, const kllm_b200_kllm_record* records, 
  * only output buffers by its host application. Rounding as
  * kllm_b200_dequantize_int8 for out_dtype (F16: the reference loader's
  * float_to_half, bit for bit). n above 33554432 (32 MiB) fails with
- * KLLM_B200_ERR_CAPACITY before any GPU work. The first call on a device
- * looks up the array's device address (cudaGetSymbolAddress) and should
- * come before any stream capture. All calls share the array, so calls that
- * overlap on the GPU race; run them in one stream order. host_data must not
- * change until the stream has passed the copy (pinned memory is read
+ * KLLM_B200_ERR_CAPACITY before any GPU work. The array's device address
+ * belongs to the CUDA context current at the call, so every call looks it up
+ * (cudaGetSymbolAddress) in that context; the first call in a context loads
+ * the library's module there and should come before any stream capture.
+ * Inside a stream capture host_data must be pinned (a capture does not
+ * accept a copy from pageable memory). All calls share the array, so calls
+ * that overlap on the GPU race; run them in one stream order. host_data must
+ * not change until the stream has passed the copy (pinned memory is read
  * asynchronously). This entry point has no counterpart in the reference. */
 int kllm_b200_dequantize_int8_host_static(const int8_t* host_data, float scale, void* out,
                                           int64_t n, int out_dtype, void* stream);

@@ -29,6 +29,8 @@ FLAG_BAD_SLOT = 4
 FLAG_BAD_SEQ_END = 8
 FLAG_TIMEOUT = 16
 
+PARAM_IDS = 7680  # host ids carried per launch by kllm_b200_embedding_host_ids
+
 OP_EMBEDDING, OP_INPUT_NORM, OP_QKV_ROPE, OP_POST_NORM, OP_SWIGLU, OP_FINAL_NORM, OP_SELECT = (
     1, 2, 4, 8, 16, 32, 64)
 OP_ATTENTION = 128
@@ -89,6 +91,8 @@ SIGNATURES = {
     "kllm_b200_status_string": [_int],
     "kllm_b200_version": [],
     "kllm_b200_embedding": [_vp, _i64, _i64, _int, _vp, _i64, _vp, _int, _vp, _vp],
+    "kllm_b200_embedding_host_ids": [_vp, _i64, _i64, _int, _vp, _i64, _vp, _int, _vp, _vp],
+    "kllm_b200_embedding_rms_norm": [_vp, _i64, _i64, _vp, _i64, _vp, _int, _f32, _vp, _vp, _vp, _vp],
     "kllm_b200_rms_norm": [_vp, _vp, _vp, _i64, _i64, _f32, _int, _int, _vp],
     "kllm_b200_add_inplace": [_vp, _vp, _i64, _int, _int, _vp],
     "kllm_b200_add_bias_inplace": [_vp, _vp, _i64, _i64, _int, _int, _vp],

@@ -237,6 +237,14 @@ class ChainRunner:
         self.desc = c
         self.full_mask = c.op_mask
 
+    @property
+    def fused_embedding(self) -> bool:
+        """Whether the step runs the embedding and layer 0's input norm as
+        one kernel (the chain executor fuses them when both ops are on)."""
+        mask = self.desc.op_mask or _capi.OP_CHAIN
+        both = _capi.OP_EMBEDDING | _capi.OP_INPUT_NORM
+        return (mask & both) == both
+
     def set_pdl(self, use_pdl: bool) -> None:
         self.desc.use_pdl = int(use_pdl)
 

@@ -5,6 +5,7 @@
 //   embedding                               (llama.cpp:79)
 //   per layer l:
 //     add+RMSNorm  r += ffn_out[l-1]; attn_norm = norm(r)   (l=0: norm only; :83-87, :166)
+//                  (the embedding and layer 0's norm are one kernel when both run)
 //     bias+RoPE+KV q/k/v -> q rotated, cache[l] appended    (:89-114)
 //     [attention   ctx = attn(q, cache[l]), when requested]  (:116-126)
 //     add+RMSNorm  r += attn_out[l]; ffn_norm = norm(r)      (:135-143)
@@ -65,7 +66,14 @@ extern "C" int kllm_b200_chain_run(const kllm_b200_chain* c, int* n_launches, vo
   const int64_t qd = c->n_heads * c->head_dim, I = c->intermediate;
   int launched = 0;
   int rc = KLLM_B200_OK;
-  if (on(KLLM_B200_OP_EMBEDDING)) {
+  // the embedding and layer 0's input norm run as one kernel when both are on
+  const bool fuse_embedding = on(KLLM_B200_OP_EMBEDDING) && on(KLLM_B200_OP_INPUT_NORM);
+  if (fuse_embedding) {
+    rc = embedding_rms_norm(c->embed_table, c->vocab, H, c->ids, T, c->layers[0].input_norm_w, wdt, c->eps,
+                            c->residual, c->layers[0].attn_norm_out, c->err_flags, o);
+    if (rc != KLLM_B200_OK) return rc;
+    ++launched;
+  } else if (on(KLLM_B200_OP_EMBEDDING)) {
     rc = embedding(c->embed_table, c->vocab, H, KLLM_B200_F16, c->ids, T, c->residual, KLLM_B200_F16,
                    c->err_flags, o);
     if (rc != KLLM_B200_OK) return rc;
@@ -74,7 +82,7 @@ extern "C" int kllm_b200_chain_run(const kllm_b200_chain* c, int* n_launches, vo
   for (int64_t l = 0; l < c->n_layers; ++l) {
     const kllm_b200_layer_buffers& L = c->layers[l];
     const void* delta = l == 0 ? nullptr : c->layers[l - 1].ffn_out;
-    if (on(KLLM_B200_OP_INPUT_NORM)) {
+    if (on(KLLM_B200_OP_INPUT_NORM) && !(l == 0 && fuse_embedding)) {
       rc = add_rms_norm(c->residual, delta, L.input_norm_w, L.attn_norm_out, T, H, c->eps, KLLM_B200_F16, wdt, o);
       if (rc != KLLM_B200_OK) return rc;
       ++launched;

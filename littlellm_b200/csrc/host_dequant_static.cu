@@ -12,14 +12,17 @@
 // The array is kStaticStagingBytes (32 MiB) and every GPU that loads the
 // library holds it until the process exits. Host code cannot use the array's
 // name as a device address (it names a host-side stand-in), so the device
-// address is looked up with cudaGetSymbolAddress once per device, with that
-// device current, on the first call on that device; that first call should
-// come before any stream capture. Every call uses the same array: the copy
-// of a call's int8 bytes overwrites the previous contents entirely (nothing
-// needs to start at zero), and calls that overlap on the GPU (different
-// streams, or different host threads on the same device) race on it.
-#include <mutex>
-
+// address comes from cudaGetSymbolAddress with the caller's device current.
+// That address belongs to the CUDA context current at the call: a plugin
+// host that runs its own (non-primary) context, or a cudaDeviceReset between
+// calls, gives the array a different address. So the lookup is done on every
+// call; once the library's module is loaded in that context it is a
+// host-side table lookup. The first call in a context loads the module and
+// should come before any stream capture. Every call uses the same array: the
+// copy of a call's int8 bytes overwrites the previous contents entirely
+// (nothing needs to start at zero), and calls that overlap on the GPU
+// (different streams, or different host threads on the same device) race
+// on it.
 #include "ops.cuh"
 
 namespace kb {
@@ -30,28 +33,15 @@ constexpr int64_t kStaticStagingBytes = int64_t{32} << 20;  // the largest tenso
 // One int8 value per byte; file scope, so every device holds one copy.
 __device__ __align__(256) int8_t g_int8_staging[kStaticStagingBytes];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_setup_mutex;
-int8_t* g_staging_address[kMaxDevices];  // per device, filled on its first call
-
+// The array's device address in the context current on this thread.
 int staging_address(int8_t** out) {
-  int dev = 0;
-  cudaError_t err = cudaGetDevice(&dev);
-  if (err != cudaSuccess) return launch_status(err, "dequantize_int8_host_static: cudaGetDevice");
-  if (dev < 0 || dev >= kMaxDevices) {
-    return fail(KLLM_B200_ERR_INVALID_ARG, "dequantize_int8_host_static: device %d out of range", dev);
+  void* p = nullptr;
+  const cudaError_t err = cudaGetSymbolAddress(&p, g_int8_staging);
+  if (err != cudaSuccess || p == nullptr) {
+    return launch_status(err != cudaSuccess ? err : cudaErrorInvalidSymbol,
+                         "dequantize_int8_host_static: cudaGetSymbolAddress");
   }
-  std::lock_guard<std::mutex> lock(g_setup_mutex);
-  if (g_staging_address[dev] == nullptr) {
-    void* p = nullptr;
-    err = cudaGetSymbolAddress(&p, g_int8_staging);  // device `dev` is current
-    if (err != cudaSuccess || p == nullptr) {
-      return launch_status(err != cudaSuccess ? err : cudaErrorInvalidSymbol,
-                           "dequantize_int8_host_static: cudaGetSymbolAddress");
-    }
-    g_staging_address[dev] = static_cast<int8_t*>(p);
-  }
-  *out = g_staging_address[dev];
+  *out = static_cast<int8_t*>(p);
   return KLLM_B200_OK;
 }
 

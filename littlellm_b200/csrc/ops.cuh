@@ -12,6 +12,12 @@ int embedding(const void* table, int64_t vocab, int64_t hidden, int table_dtype,
 int add_rms_norm(void* residual, const void* delta, const void* weight, void* out, int64_t rows,
                  int64_t hidden, float eps, int act_dtype, int weight_dtype, const LaunchOpts& o);
 
+// residual = table[ids] (fp16 rows, bit-exact) and out = rms_norm(residual) * weight in one launch
+// (embedding + layer 0's input norm).
+int embedding_rms_norm(const void* table, int64_t vocab, int64_t hidden, const int32_t* ids, int64_t n_tokens,
+                       const void* weight, int weight_dtype, float eps, void* residual, void* out,
+                       int32_t* err_flags, const LaunchOpts& o);
+
 int silu_mul(const void* gate, const void* up, void* out, int64_t n, int dtype, const LaunchOpts& o);
 
 int add_inplace(void* x, const void* y, int64_t n, int x_dtype, int y_dtype, const LaunchOpts& o);

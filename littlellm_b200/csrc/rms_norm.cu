@@ -16,6 +16,15 @@
 // Arithmetic: r = fp16_rn(a + d) (what the reference's fp16 add_inplace
 // stores), sum of r^2 in fp32, scale = rsqrt(sum / H + eps), y = (r * scale)
 // * w rounded to fp16.
+//
+// The same kernel also gathers its rows from an embedding table
+// (embedding_rms_norm): r = table[ids[t]] is stored as the residual and its
+// norm written, one launch for the embedding and layer 0's input norm
+// (src/model/llama.cpp:84 then :83-87 of the next layer loop). The gathered
+// row is never re-read from HBM, and the result is bit-identical to the
+// embedding followed by rms_norm. The table and the ids are never written by
+// a kernel of the chain, so under PDL the row loads are issued before the
+// grid-dependency wait.
 #include "ops.cuh"
 
 namespace kb {
@@ -54,12 +63,23 @@ __device__ __forceinline__ float sumsq_h2(uint32_t w) {
   return f.x * f.x + f.y * f.y;
 }
 
-template <int VPT, typename TW, bool HAS_DELTA, bool EARLY>
+// Where a row comes from and what is stored besides the normed output.
+enum NormMode : int {
+  kPlain = 0,     // r = residual row (read only)
+  kAddDelta = 1,  // r = fp16(residual + delta), stored back as the residual
+  kGather = 2,    // r = table[ids[row]] (`src` is the table), stored as the residual
+};
+
+template <int VPT, typename TW, int MODE, bool EARLY>
 __global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __restrict__ residual,
-                                                                    const __half* __restrict__ delta,
+                                                                    const __half* __restrict__ src,
                                                                     const TW* __restrict__ weight,
                                                                     __half* __restrict__ out, int64_t rows,
-                                                                    int hidden, int group, float eps) {
+                                                                    int hidden, int group, float eps,
+                                                                    const int32_t* __restrict__ ids, int64_t vocab,
+                                                                    int32_t* err_flags) {
+  constexpr bool HAS_DELTA = MODE == kAddDelta;
+  constexpr bool GATHER = MODE == kGather;
   extern __shared__ __align__(16) unsigned char s_raw[];
   __shared__ float partial[2][kThreads / 32];
   // The norm weight is staged into shared memory once per CTA and the
@@ -83,8 +103,13 @@ __global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __re
   uint4 wreg = make_uint4(0, 0, 0, 0);
   if (park && static_cast<int>(threadIdx.x) < wvec) wreg = ld_keep(reinterpret_cast<const uint4*>(weight) + threadIdx.x);
   if (!park) stage_weight();
-  grid_dep_wait();
-  grid_dep_launch();
+  // A gathering launch under PDL issues its first rows' loads (table and
+  // ids, which no kernel of the chain writes) before the wait.
+  bool waited = GATHER && EARLY ? false : true;
+  if (waited) {
+    grid_dep_wait();
+    grid_dep_launch();
+  }
   bool staged = !park;
 
   const int nvec = hidden >> 3;
@@ -103,16 +128,34 @@ __global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __re
     __half* rrow = residual + row * hidden;
     uint4 r[VPT], d[VPT];
     float ss = 0.0f;
+    bool id_ok = true;
     if (live) {
+      const __half* rsrc = rrow;
+      if (GATHER) {
+        const int32_t id = __ldg(ids + row);
+        id_ok = id >= 0 && id < vocab;
+        rsrc = src + static_cast<int64_t>(id_ok ? id : 0) * hidden;
+      }
 #pragma unroll
       for (int j = 0; j < VPT; ++j) {
         const int v = j * group + lane_g;
         if (v < nvec) {
-          r[j] = HAS_DELTA ? ld_cg(rrow + v * 8) : ld_stream(rrow + v * 8);
-          if (HAS_DELTA) d[j] = ld_stream(delta + row * hidden + v * 8);
+          if (GATHER) {
+            // table rows are read once (random ids): no L1 allocation
+            r[j] = id_ok ? ld_stream(rsrc + v * 8) : make_uint4(0, 0, 0, 0);
+          } else {
+            r[j] = HAS_DELTA ? ld_cg(rsrc + v * 8) : ld_stream(rsrc + v * 8);
+            if (HAS_DELTA) d[j] = ld_stream(src + row * hidden + v * 8);
+          }
         }
       }
     }
+    if (!waited) {  // uniform over the grid: every thread passes here in its first iteration
+      grid_dep_wait();
+      grid_dep_launch();
+      waited = true;
+    }
+    if (GATHER && live && !id_ok && lane_g == 0) set_flag(err_flags, KLLM_B200_FLAG_BAD_TOKEN);
     // `staged` and the loop trip count are uniform over the CTA, so every
     // thread reaches this barrier.
     if (!staged) {
@@ -132,6 +175,7 @@ __global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __re
                               f2_to_h2(a2.x + b2.x, a2.y + b2.y), f2_to_h2(a3.x + b3.x, a3.y + b3.y));
             st_plain(rrow + v * 8, r[j]);
           }
+          if (GATHER) st_plain(rrow + v * 8, r[j]);
           ss += sumsq_h2(r[j].x) + sumsq_h2(r[j].y) + sumsq_h2(r[j].z) + sumsq_h2(r[j].w);
         }
       }
@@ -224,41 +268,57 @@ FastConfig pick_config(int nvec) {
   return {};
 }
 
-template <int VPT, typename TW, bool HAS_DELTA>
-int launch_fast(void* residual, const void* delta, const void* weight, void* out, int64_t rows, int hidden,
-                int group, float eps, const LaunchOpts& o) {
-  auto k = o.pdl ? add_rms_norm_f16_kernel<VPT, TW, HAS_DELTA, true> : add_rms_norm_f16_kernel<VPT, TW, HAS_DELTA, false>;
+// Extra arguments of a gathering launch (unused otherwise).
+struct GatherArgs {
+  const int32_t* ids = nullptr;
+  int64_t vocab = 0;
+  int32_t* err_flags = nullptr;
+};
+
+template <int VPT, typename TW, int MODE>
+int launch_fast(void* residual, const void* src, const void* weight, void* out, int64_t rows, int hidden,
+                int group, float eps, const GatherArgs& ga, const LaunchOpts& o, const char* what) {
+  auto k = o.pdl ? add_rms_norm_f16_kernel<VPT, TW, MODE, true> : add_rms_norm_f16_kernel<VPT, TW, MODE, false>;
   const int threads = group > kFastThreads ? group : kFastThreads;
   const int rows_per_cta = threads / group;
   const size_t smem = static_cast<size_t>(hidden) * sizeof(TW);
   const cudaError_t attr = allow_smem(reinterpret_cast<const void*>(k), smem);
-  if (attr != cudaSuccess) return launch_status(attr, "add_rms_norm");
+  if (attr != cudaSuccess) return launch_status(attr, what);
   const unsigned grid = persistent_grid(k, threads, smem, rows_per_cta, rows);
   return launch_status(launch(k, grid, threads, smem, o.stream, o.pdl, static_cast<__half*>(residual),
-                              static_cast<const __half*>(delta), static_cast<const TW*>(weight),
-                              static_cast<__half*>(out), rows, hidden, group, eps),
-                       "add_rms_norm");
+                              static_cast<const __half*>(src), static_cast<const TW*>(weight),
+                              static_cast<__half*>(out), rows, hidden, group, eps, ga.ids, ga.vocab, ga.err_flags),
+                       what);
 }
 
 template <int VPT, typename TW>
-int launch_fast_d(void* residual, const void* delta, const void* weight, void* out, int64_t rows, int hidden,
-                  int group, float eps, const LaunchOpts& o) {
-  return delta ? launch_fast<VPT, TW, true>(residual, delta, weight, out, rows, hidden, group, eps, o)
-               : launch_fast<VPT, TW, false>(residual, delta, weight, out, rows, hidden, group, eps, o);
+int launch_fast_d(int mode, void* residual, const void* src, const void* weight, void* out, int64_t rows,
+                  int hidden, int group, float eps, const GatherArgs& ga, const LaunchOpts& o) {
+  switch (mode) {
+    case kAddDelta:
+      return launch_fast<VPT, TW, kAddDelta>(residual, src, weight, out, rows, hidden, group, eps, ga, o,
+                                             "add_rms_norm");
+    case kGather:
+      return launch_fast<VPT, TW, kGather>(residual, src, weight, out, rows, hidden, group, eps, ga, o,
+                                           "embedding_rms_norm");
+    default:
+      return launch_fast<VPT, TW, kPlain>(residual, src, weight, out, rows, hidden, group, eps, ga, o,
+                                          "add_rms_norm");
+  }
 }
 
 template <typename TW>
-int dispatch_fast(const FastConfig& c, void* residual, const void* delta, const void* weight, void* out,
-                  int64_t rows, int hidden, float eps, const LaunchOpts& o) {
+int dispatch_fast(const FastConfig& c, int mode, void* residual, const void* src, const void* weight, void* out,
+                  int64_t rows, int hidden, float eps, const GatherArgs& ga, const LaunchOpts& o) {
   switch (c.vpt) {
-    case 1: return launch_fast_d<1, TW>(residual, delta, weight, out, rows, hidden, c.group, eps, o);
-    case 2: return launch_fast_d<2, TW>(residual, delta, weight, out, rows, hidden, c.group, eps, o);
-    case 3: return launch_fast_d<3, TW>(residual, delta, weight, out, rows, hidden, c.group, eps, o);
-    case 4: return launch_fast_d<4, TW>(residual, delta, weight, out, rows, hidden, c.group, eps, o);
-    case 5: return launch_fast_d<5, TW>(residual, delta, weight, out, rows, hidden, c.group, eps, o);
-    case 6: return launch_fast_d<6, TW>(residual, delta, weight, out, rows, hidden, c.group, eps, o);
-    case 7: return launch_fast_d<7, TW>(residual, delta, weight, out, rows, hidden, c.group, eps, o);
-    default: return launch_fast_d<8, TW>(residual, delta, weight, out, rows, hidden, c.group, eps, o);
+    case 1: return launch_fast_d<1, TW>(mode, residual, src, weight, out, rows, hidden, c.group, eps, ga, o);
+    case 2: return launch_fast_d<2, TW>(mode, residual, src, weight, out, rows, hidden, c.group, eps, ga, o);
+    case 3: return launch_fast_d<3, TW>(mode, residual, src, weight, out, rows, hidden, c.group, eps, ga, o);
+    case 4: return launch_fast_d<4, TW>(mode, residual, src, weight, out, rows, hidden, c.group, eps, ga, o);
+    case 5: return launch_fast_d<5, TW>(mode, residual, src, weight, out, rows, hidden, c.group, eps, ga, o);
+    case 6: return launch_fast_d<6, TW>(mode, residual, src, weight, out, rows, hidden, c.group, eps, ga, o);
+    case 7: return launch_fast_d<7, TW>(mode, residual, src, weight, out, rows, hidden, c.group, eps, ga, o);
+    default: return launch_fast_d<8, TW>(mode, residual, src, weight, out, rows, hidden, c.group, eps, ga, o);
   }
 }
 
@@ -290,9 +350,11 @@ int add_rms_norm(void* residual, const void* delta, const void* weight, void* ou
     if (fast) {
       const FastConfig c = pick_config(static_cast<int>(hidden / 8));
       if (c.vpt > 0) {
+        const int mode = delta ? kAddDelta : kPlain;
+        const GatherArgs ga;
         return weight_dtype == KLLM_B200_F16
-                   ? dispatch_fast<__half>(c, residual, delta, weight, out, rows, (int)hidden, eps, o)
-                   : dispatch_fast<float>(c, residual, delta, weight, out, rows, (int)hidden, eps, o);
+                   ? dispatch_fast<__half>(c, mode, residual, delta, weight, out, rows, (int)hidden, eps, ga, o)
+                   : dispatch_fast<float>(c, mode, residual, delta, weight, out, rows, (int)hidden, eps, ga, o);
       }
     }
     return weight_dtype == KLLM_B200_F16
@@ -304,7 +366,48 @@ int add_rms_norm(void* residual, const void* delta, const void* weight, void* ou
              : launch_generic<float, float>(residual, delta, weight, out, rows, hidden, eps, o);
 }
 
+int embedding_rms_norm(const void* table, int64_t vocab, int64_t hidden, const int32_t* ids, int64_t n_tokens,
+                       const void* weight, int weight_dtype, float eps, void* residual, void* out,
+                       int32_t* err_flags, const LaunchOpts& o) {
+  if (n_tokens < 0 || hidden < 0 || vocab < 0) return fail(KLLM_B200_ERR_INVALID_ARG, "embedding_rms_norm: negative size");
+  if (n_tokens == 0) return KLLM_B200_OK;
+  if (hidden == 0) return fail(KLLM_B200_ERR_SHAPE, "embedding_rms_norm: hidden must be positive");
+  if (!table || !ids || !weight || !residual || !out) {
+    return fail(KLLM_B200_ERR_INVALID_ARG, "embedding_rms_norm: null pointer");
+  }
+  if (!is_float_dtype(weight_dtype)) {
+    return fail(KLLM_B200_ERR_DTYPE, "embedding_rms_norm: weight dtype %d not supported", weight_dtype);
+  }
+  const bool fast = hidden % 8 == 0 && hidden <= 8 * 8 * kThreads && aligned16(table) && aligned16(residual) &&
+                    aligned16(out) && aligned16(weight);
+  if (fast) {
+    const FastConfig c = pick_config(static_cast<int>(hidden / 8));
+    if (c.vpt > 0) {
+      GatherArgs ga;
+      ga.ids = ids;
+      ga.vocab = vocab;
+      ga.err_flags = err_flags;
+      return weight_dtype == KLLM_B200_F16
+                 ? dispatch_fast<__half>(c, kGather, residual, table, weight, out, n_tokens, (int)hidden, eps, ga, o)
+                 : dispatch_fast<float>(c, kGather, residual, table, weight, out, n_tokens, (int)hidden, eps, ga, o);
+    }
+  }
+  // other shapes and alignments: the gather, then the norm of the gathered rows
+  const int rc = embedding(table, vocab, hidden, KLLM_B200_F16, ids, n_tokens, residual, KLLM_B200_F16, err_flags, o);
+  if (rc != KLLM_B200_OK) return rc;
+  return add_rms_norm(residual, nullptr, weight, out, n_tokens, hidden, eps, KLLM_B200_F16, weight_dtype, o);
+}
+
 }  // namespace kb
+
+extern "C" int kllm_b200_embedding_rms_norm(const void* table, int64_t vocab, int64_t hidden, const int32_t* ids,
+                                            int64_t n_tokens, const void* weight, int weight_dtype, float eps,
+                                            void* residual_out, void* norm_out, int32_t* err_flags, void* stream) {
+  kb::LaunchOpts o;
+  o.stream = static_cast<cudaStream_t>(stream);
+  return kb::embedding_rms_norm(table, vocab, hidden, ids, n_tokens, weight, weight_dtype, eps, residual_out,
+                                norm_out, err_flags, o);
+}
 
 extern "C" int kllm_b200_add_rms_norm(void* residual, const void* delta, const void* weight, void* out,
                                       int64_t rows, int64_t hidden, float eps, int act_dtype, int weight_dtype,

@@ -18,9 +18,10 @@
 //    reference's other CUDA work (cuBLAS GEMMs, attention) exactly as before.
 // Token ids arrive as a host std::vector; they are range-checked on the host
 // (the reference CPU path's check, src/op/cpu/embedding.cpp:22-24, which its
-// CUDA path lacks) and copied into a per-thread device buffer, as the
-// reference's TokenIdBufferCache does (src/op/cuda/embedding.cu:13-41).
-#include <cuda_runtime.h>
+// CUDA path lacks) and handed to kllm_b200_embedding_host_ids, which carries
+// them in the kernel launches' parameters: no device buffer to grow (the
+// reference's TokenIdBufferCache, src/op/cuda/embedding.cu:13-41) and no
+// blocking copy.
 
 #include <cstdint>
 #include <stdexcept>
@@ -43,33 +44,7 @@ void check(int status) {
   }
 }
 
-void check_cuda(cudaError_t err) {
-  if (err != cudaSuccess) throw std::runtime_error(cudaGetErrorString(err));
-}
-
 int dt(const Tensor& t) { return static_cast<int>(t.dtype()); }
-
-class DeviceIds {
- public:
-  ~DeviceIds() {
-    if (ptr_ != nullptr) cudaFree(ptr_);
-  }
-  int32_t* upload(const std::vector<int>& ids) {
-    if (ids.size() > cap_) {
-      if (ptr_ != nullptr) cudaFree(ptr_);
-      ptr_ = nullptr;
-      cap_ = 0;
-      check_cuda(cudaMalloc(&ptr_, 2 * ids.size() * sizeof(int32_t)));
-      cap_ = 2 * ids.size();
-    }
-    check_cuda(cudaMemcpy(ptr_, ids.data(), ids.size() * sizeof(int32_t), cudaMemcpyHostToDevice));
-    return ptr_;
-  }
-
- private:
-  int32_t* ptr_ = nullptr;
-  std::size_t cap_ = 0;
-};
 
 }  // namespace
 
@@ -84,10 +59,10 @@ void cuda_embedding(const Tensor& table, const std::vector<int>& token_ids, Tens
     if (id < 0 || id >= vocab) throw std::runtime_error("token id out of vocabulary range");
   }
   if (token_ids.empty()) return;
-  static thread_local DeviceIds ids;
-  const int32_t* d_ids = ids.upload(token_ids);
-  check(kllm_b200_embedding(table.data(), vocab, hidden, dt(table), d_ids,
-                            static_cast<int64_t>(token_ids.size()), out.data(), dt(out), nullptr, nullptr));
+  static_assert(sizeof(int) == sizeof(int32_t), "ids are passed as int32");
+  check(kllm_b200_embedding_host_ids(table.data(), vocab, hidden, dt(table),
+                                     reinterpret_cast<const int32_t*>(token_ids.data()),
+                                     static_cast<int64_t>(token_ids.size()), out.data(), dt(out), nullptr, nullptr));
 }
 
 void cuda_rms_norm(const Tensor& x, const Tensor& weight, Tensor& out, float eps) {

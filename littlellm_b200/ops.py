@@ -71,6 +71,45 @@ def embedding(table: torch.Tensor, ids: torch.Tensor, out: torch.Tensor | None =
     return out
 
 
+def embedding_host_ids(table: torch.Tensor, ids, out: torch.Tensor | None = None,
+                       err_flags: torch.Tensor | None = None) -> torch.Tensor:
+    """out[t] = table[ids[t]] with the ids in host memory (a sequence of ints,
+    as the reference's cuda_embedding takes them); they travel in the kernel
+    launches' parameters, no device buffer or blocking copy."""
+    import numpy as np
+    host = np.ascontiguousarray(np.asarray(ids, dtype=np.int32))
+    if out is None:
+        out = torch.empty((host.size, table.shape[1]), dtype=table.dtype, device=table.device)
+    dev = _dev(table, out, err_flags)
+    with torch.cuda.device(dev):
+        check(lib.kllm_b200_embedding_host_ids(_ptr(table), table.shape[0], table.shape[1], dtype_code(table),
+                                               host.ctypes.data, host.size, _ptr(out), dtype_code(out),
+                                               _ptr(err_flags), _stream(dev)))
+    return out
+
+
+def embedding_rms_norm(table: torch.Tensor, ids: torch.Tensor, weight: torch.Tensor, eps: float,
+                       residual: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                       err_flags: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """residual = table[ids] and out = rms_norm(residual) * weight, one launch
+    (embedding + layer 0's input norm). Returns (residual, out)."""
+    if ids.dtype != torch.int32:
+        raise KllmError(_capi.ERR_DTYPE, "ids must be int32")
+    if table.dtype != torch.float16:
+        raise KllmError(_capi.ERR_DTYPE, "embedding_rms_norm takes an fp16 table")
+    shape = (ids.numel(), table.shape[1])
+    if residual is None:
+        residual = torch.empty(shape, dtype=table.dtype, device=table.device)
+    if out is None:
+        out = torch.empty(shape, dtype=table.dtype, device=table.device)
+    dev = _dev(table, ids, weight, residual, out, err_flags)
+    with torch.cuda.device(dev):
+        check(lib.kllm_b200_embedding_rms_norm(_ptr(table), table.shape[0], table.shape[1], _ptr(ids), ids.numel(),
+                                               _ptr(weight), dtype_code(weight), eps, _ptr(residual), _ptr(out),
+                                               _ptr(err_flags), _stream(dev)))
+    return residual, out
+
+
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float,
              out: torch.Tensor | None = None) -> torch.Tensor:
     if out is None:

@@ -1,6 +1,6 @@
 /*
  * kllm_oracle.c — CPU restatement of LittleLLM's reference CPU operators
- * (src/op/cpu/*.cpp, src/base/half.cpp, src/model/weights.cpp).
+ * (src/op/cpu/ sources, src/base/half.cpp, src/model/weights.cpp).
  *
  * TEST INFRASTRUCTURE ONLY: the checker for the CUDA library's parity tests,
  * smoke check and the benchmark's CPU-baseline leg. Nothing in the product

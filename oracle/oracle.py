@@ -35,19 +35,32 @@ _c_i8p = ctypes.POINTER(ctypes.c_int8)
 _c_i64 = ctypes.c_int64
 
 
+def reference_dir() -> str:
+    """The reference source tree the Makefile compiles: $KLLM_REFERENCE_SRC,
+    else the read-only checkout of this build machine."""
+    return os.environ.get("KLLM_REFERENCE_SRC", "/root/reference")
+
+
 def reference_sources_present() -> bool:
     """Whether the reference source tree the Makefile compiles is here (it is
     not on machines that only run the prebuilt checkers)."""
-    return os.path.isdir("/root/reference")
+    return os.path.isfile(os.path.join(reference_dir(), "include", "kllm", "op", "ops.h"))
+
+
+def make(*targets: str) -> None:
+    """Runs oracle/Makefile for `targets`, with REF set when the reference
+    sources are present."""
+    cmd = ["make", "-C", HERE, "-s"]
+    if reference_sources_present():
+        cmd.append(f"REF={reference_dir()}")
+    subprocess.run(cmd + list(targets), check=True)
 
 
 def build(force: bool = False) -> None:
     """Runs oracle/Makefile (C restatement, plus the compiled reference when
     its source tree is present)."""
-    if force or not os.path.exists(ORACLE_SO):
-        subprocess.run(["make", "-C", HERE, "-s"], check=True)
-    elif reference_sources_present():
-        subprocess.run(["make", "-C", HERE, "-s"], check=True)
+    if force or not os.path.exists(ORACLE_SO) or reference_sources_present():
+        make()
 
 
 def _ptr(a: np.ndarray | None, ctype):

@@ -76,12 +76,27 @@ def test_argument_validation_without_gpu(capi):
     assert lib.kllm_b200_select_last_rows(16, 10, 8, None, 4, 3, 16, capi.F16, None, None) == capi.ERR_SHAPE
     # chain: null descriptor
     assert lib.kllm_b200_chain_run(None, None, None) == capi.ERR_INVALID_ARG
+    # the fused embedding + norm and the host-ids embedding
+    rc, msg = _rc_msg(capi, lib.kllm_b200_embedding_rms_norm(16, 10, 8, None, 4, 16, capi.F16, 1e-6, 16, 16,
+                                                              None, None))
+    assert rc == capi.ERR_INVALID_ARG and "null" in msg
+    assert lib.kllm_b200_embedding_rms_norm(16, 10, 8, 16, 4, 16, capi.I8, 1e-6, 16, 16, None,
+                                            None) == capi.ERR_DTYPE
+    assert lib.kllm_b200_embedding_rms_norm(16, 10, 8, 16, -1, 16, capi.F16, 1e-6, 16, 16, None,
+                                            None) == capi.ERR_INVALID_ARG
+    assert lib.kllm_b200_embedding_host_ids(16, 10, 8, capi.F16, None, 4, 16, capi.F16, None,
+                                            None) == capi.ERR_INVALID_ARG
+    assert lib.kllm_b200_embedding_host_ids(16, 10, 8, capi.I32, 16, 4, 16, capi.F16, None,
+                                            None) == capi.ERR_DTYPE
 
 
 def test_empty_inputs_are_noops(capi):
     lib = capi.lib
     assert lib.kllm_b200_silu_mul(None, None, None, 0, capi.F16, None) == capi.OK
     assert lib.kllm_b200_embedding(None, 10, 8, capi.F16, None, 0, None, capi.F16, None, None) == capi.OK
+    assert lib.kllm_b200_embedding_host_ids(None, 10, 8, capi.F16, None, 0, None, capi.F16, None, None) == capi.OK
+    assert lib.kllm_b200_embedding_rms_norm(None, 10, 8, None, 0, None, capi.F16, 1e-6, None, None, None,
+                                            None) == capi.OK
     assert lib.kllm_b200_add_bias_inplace(16, None, 4, 4, capi.F16, capi.F16, None) == capi.OK  # null bias
     assert lib.kllm_b200_dequantize_int8(None, None, None, 0, capi.F16, None) == capi.OK
 

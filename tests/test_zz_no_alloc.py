@@ -39,7 +39,7 @@ def _bits(t: torch.Tensor) -> np.ndarray:
     return t.cpu().view(torch.int16).numpy().view(np.uint16)
 
 
-def test_two_calls_match_the_allocating_entry_points(cuda, ops, tmp_path):
+def test_two_calls_match_the_allocating_entry_points(cuda, ops, oracle, tmp_path):
     from littlellm_b200 import _capi, loader
     rng = np.random.default_rng(23)
 
@@ -61,6 +61,8 @@ def test_two_calls_match_the_allocating_entry_points(cuda, ops, tmp_path):
     assert _host_static(q2, float(s2), out2, _capi.F16) == _capi.OK, _capi.last_error()
     torch.cuda.synchronize()
     assert np.array_equal(_bits(out1), want1)
+    # and directly against the oracle's restatement of the reference loader's rounding
+    assert np.array_equal(_bits(out2), oracle.dequantize_int8_f16_bits(q2, float(s2)))
     dev_q2 = torch.from_numpy(q2).to(cuda)
     dev_s2 = torch.tensor([s2], dtype=torch.float32, device=cuda)
     assert np.array_equal(_bits(out2), _bits(ops.dequantize_int8(dev_q2, dev_s2, torch.float16)))
@@ -91,3 +93,37 @@ def test_capacity_limit(cuda, ops):
     assert "static staging" in _capi.last_error()
     torch.cuda.synchronize()
     assert bool((out_big == -1234.0).all())
+
+
+def test_pinned_host_buffer(cuda, ops, oracle):
+    """A pinned host buffer (the form a stream capture needs) gives the same
+    bits as a pageable one."""
+    from littlellm_b200 import _capi
+    rng = np.random.default_rng(31)
+    q = rng.integers(-128, 128, 777_777, dtype=np.int8)
+    pinned = torch.empty(q.size, dtype=torch.int8, pin_memory=True)
+    pinned.numpy()[:] = q
+    out = torch.empty(q.size, dtype=torch.float16, device=cuda)
+    stream = torch.cuda.current_stream(cuda).cuda_stream
+    rc = _capi.lib.kllm_b200_dequantize_int8_host_static(pinned.data_ptr(), 0.0031, out.data_ptr(), q.size,
+                                                          _capi.F16, stream)
+    assert rc == _capi.OK, _capi.last_error()
+    torch.cuda.synchronize()
+    assert np.array_equal(_bits(out), oracle.dequantize_int8_f16_bits(q, 0.0031))
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs a second GPU")
+def test_second_device_after_first(cuda, ops, oracle):
+    """The staging address is looked up in each device's own context: a call
+    on device 1 after calls on device 0 lands in device 1's array."""
+    from littlellm_b200 import _capi
+    rng = np.random.default_rng(37)
+    q = rng.integers(-128, 128, 500_001, dtype=np.int8)
+    want = oracle.dequantize_int8_f16_bits(q, 0.0077)
+    for dev in (torch.device("cuda:0"), torch.device("cuda:1"), torch.device("cuda:0")):
+        with torch.cuda.device(dev):
+            out = torch.empty(q.size, dtype=torch.float16, device=dev)
+            assert _host_static(q, 0.0077, out, _capi.F16) == _capi.OK, _capi.last_error()
+            torch.cuda.synchronize(dev)
+            assert np.array_equal(_bits(out), want), dev
