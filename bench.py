@@ -1457,7 +1457,7 @@ def measure_chain(w, args, device, dist, *, seed: int, steps: int, warmup: int, 
     ms = float(t.item()) / steps
     peaks = load_peaks()
     bytes_step = chain_bytes(w, runner.n_layers, positions=runner.positions.cpu().numpy() if attention else None,
-                             fused_embedding=runner.fused_embedding)
+                             fused_embedding=runner.fused_embedding, fused_select=runner.fused_select)
     gbs = bytes_step["total"] / (ms * 1e-3) / 1e9
     stats = {"ms_per_step": ms, "launches_per_step": launches, "clocks": clocks,
              "chain_bytes_per_step": bytes_step["total"], "hbm_gbs_chain": gbs,
@@ -1567,7 +1567,7 @@ def run_ours(args):
                          f"({sum(steps):.1f} s), fp32, single thread (the reference CPU path is single-threaded)"}
     n_layers = runner.n_layers
     launches = st["launches_per_step"]
-    fused = runner.fused_embedding
+    fused, fused_sel = runner.fused_embedding, runner.fused_select
     del runner
     release_device_memory()
 
@@ -1649,6 +1649,7 @@ def run_ours(args):
                       % (st["chain_bytes_per_step"] / 1e9),
                 "pdl": not args.no_pdl, "cuda_graph": True, "attention": bool(args.attention),
                 "embedding_fused_with_input_norm": fused,
+                "select_fused_with_final_norm": fused_sel,
             },
             "hbm_gbs_chain": st["hbm_gbs_chain"],
             "hbm_frac_chain": st["hbm_frac_chain"],

@@ -245,6 +245,15 @@ class ChainRunner:
         both = _capi.OP_EMBEDDING | _capi.OP_INPUT_NORM
         return (mask & both) == both
 
+    @property
+    def fused_select(self) -> bool:
+        """Whether the final norm's kernel also writes the last rows (the
+        chain executor fuses them when both ops are on and every sequence has
+        seq_len rows)."""
+        mask = self.desc.op_mask or _capi.OP_CHAIN
+        both = _capi.OP_FINAL_NORM | _capi.OP_SELECT
+        return (mask & both) == both and not self.desc.seq_ends
+
     def set_pdl(self, use_pdl: bool) -> None:
         self.desc.use_pdl = int(use_pdl)
 

@@ -12,6 +12,7 @@
 //     SwiGLU       swiglu = silu(gate) * up                  (:158)
 //   add+RMSNorm  r += ffn_out[L-1]; normed = norm(r)         (:166, :171)
 //   select_last_rows                                          (:173)
+//                (written by the final norm's kernel when all sequences have seq_len rows)
 // With KLLM_B200_OP_GEMM the GEMMs run in between (tcgen05, gemm.cu), and the
 // step is the whole forward of llama.cpp:78-184:
 //   after the input norm   q, k, v = linear(attn_norm, wq / wk / wv)   (:89-106), with
@@ -63,6 +64,17 @@ extern "C" int kllm_b200_chain_run(const kllm_b200_chain* c, int* n_launches, vo
     }
   }
   auto on = [mask](int bit) { return (mask & bit) != 0; };
+  // Whether the launch before the next one wrote the residual. A residual
+  // add may read its residual rows before its dependency wait (PDL) when the
+  // launch before it did not write them: they were then written two or more
+  // launches back, and every kernel of this library triggers its dependents
+  // only after its own wait. Unknown (true) before the chain's first launch.
+  bool prev_wrote_residual = true;
+  auto norm_opts = [&]() {
+    LaunchOpts n = o;
+    n.early_residual = o.pdl && !prev_wrote_residual;
+    return n;
+  };
   const int64_t qd = c->n_heads * c->head_dim, I = c->intermediate;
   int launched = 0;
   int rc = KLLM_B200_OK;
@@ -73,19 +85,23 @@ extern "C" int kllm_b200_chain_run(const kllm_b200_chain* c, int* n_launches, vo
                             c->residual, c->layers[0].attn_norm_out, c->err_flags, o);
     if (rc != KLLM_B200_OK) return rc;
     ++launched;
+    prev_wrote_residual = true;
   } else if (on(KLLM_B200_OP_EMBEDDING)) {
     rc = embedding(c->embed_table, c->vocab, H, KLLM_B200_F16, c->ids, T, c->residual, KLLM_B200_F16,
                    c->err_flags, o);
     if (rc != KLLM_B200_OK) return rc;
     ++launched;
+    prev_wrote_residual = true;
   }
   for (int64_t l = 0; l < c->n_layers; ++l) {
     const kllm_b200_layer_buffers& L = c->layers[l];
     const void* delta = l == 0 ? nullptr : c->layers[l - 1].ffn_out;
     if (on(KLLM_B200_OP_INPUT_NORM) && !(l == 0 && fuse_embedding)) {
-      rc = add_rms_norm(c->residual, delta, L.input_norm_w, L.attn_norm_out, T, H, c->eps, KLLM_B200_F16, wdt, o);
+      rc = add_rms_norm(c->residual, delta, L.input_norm_w, L.attn_norm_out, T, H, c->eps, KLLM_B200_F16, wdt,
+                        norm_opts());
       if (rc != KLLM_B200_OK) return rc;
       ++launched;
+      prev_wrote_residual = delta != nullptr;
     }
     if (gemm) {  // q/k/v projections with bias + RoPE + KV append in the GEMM's epilogue
       const kllm_b200_layer_weights& W = c->weights[l];
@@ -94,12 +110,14 @@ extern "C" int kllm_b200_chain_run(const kllm_b200_chain* c, int* n_launches, vo
                                      c->theta, L.q, L.k_cache, L.v_cache, c->n_slots, c->max_seq, c->err_flags, o);
       if (rc != KLLM_B200_OK) return rc;
       ++launched;
+      prev_wrote_residual = false;
     } else if (on(KLLM_B200_OP_QKV_ROPE)) {
       rc = qkv_bias_rope_kv_append(L.q, L.k, L.v, L.q_bias, L.k_bias, L.v_bias, wdt, c->positions, c->slots, T,
                                    c->n_heads, c->n_kv_heads, c->head_dim, c->theta, L.k_cache, L.v_cache,
                                    c->n_slots, c->max_seq, c->err_flags, o);
       if (rc != KLLM_B200_OK) return rc;
       ++launched;
+      prev_wrote_residual = false;
     }
     if (on(KLLM_B200_OP_ATTENTION)) {
       // runs of seq_len tokens of one sequence; single tokens for ragged batches
@@ -110,23 +128,27 @@ extern "C" int kllm_b200_chain_run(const kllm_b200_chain* c, int* n_launches, vo
                                 c->attn_workspace_bytes, c->err_flags, o, &n);
       if (rc != KLLM_B200_OK) return rc;
       launched += n;
+      if (n > 0) prev_wrote_residual = false;
     }
     if (gemm) {  // o projection of the attention output
       const kllm_b200_layer_weights& W = c->weights[l];
       rc = linear(L.attn_ctx, W.wo, W.o_bias, wdt, const_cast<void*>(L.attn_out), T, H, qd, c->err_flags, o);
       if (rc != KLLM_B200_OK) return rc;
       ++launched;
+      prev_wrote_residual = false;
     }
     if (on(KLLM_B200_OP_POST_NORM)) {
       rc = add_rms_norm(c->residual, L.attn_out, L.post_norm_w, L.ffn_norm_out, T, H, c->eps, KLLM_B200_F16, wdt,
-                        o);
+                        norm_opts());
       if (rc != KLLM_B200_OK) return rc;
       ++launched;
+      prev_wrote_residual = true;
     }
     if (on(KLLM_B200_OP_SWIGLU) && !gemm) {
       rc = silu_mul(L.gate, L.up, L.swiglu_out, T * c->intermediate, KLLM_B200_F16, o);
       if (rc != KLLM_B200_OK) return rc;
       ++launched;
+      prev_wrote_residual = false;
     }
     if (gemm) {  // gate/up projections with SwiGLU fused, then the down projection
       const kllm_b200_layer_weights& W = c->weights[l];
@@ -137,15 +159,26 @@ extern "C" int kllm_b200_chain_run(const kllm_b200_chain* c, int* n_launches, vo
       }
       if (rc != KLLM_B200_OK) return rc;
       launched += 2;
+      prev_wrote_residual = false;
     }
   }
-  if (on(KLLM_B200_OP_FINAL_NORM)) {
+  // the final norm also writes the last rows when every sequence has seq_len rows
+  const bool fuse_select = on(KLLM_B200_OP_FINAL_NORM) && on(KLLM_B200_OP_SELECT) && c->seq_ends == nullptr &&
+                           c->seq_len >= 1 && c->n_seqs * c->seq_len == T;
+  if (fuse_select) {
+    int n = 0;
+    rc = add_rms_norm_last_rows(c->residual, c->layers[c->n_layers - 1].ffn_out, c->final_norm_w,
+                                c->final_norm_out, T, H, c->eps, wdt, c->last_rows, c->seq_len, c->n_seqs,
+                                c->err_flags, norm_opts(), &n);
+    if (rc != KLLM_B200_OK) return rc;
+    launched += n;
+  } else if (on(KLLM_B200_OP_FINAL_NORM)) {
     rc = add_rms_norm(c->residual, c->layers[c->n_layers - 1].ffn_out, c->final_norm_w, c->final_norm_out, T, H,
-                      c->eps, KLLM_B200_F16, wdt, o);
+                      c->eps, KLLM_B200_F16, wdt, norm_opts());
     if (rc != KLLM_B200_OK) return rc;
     ++launched;
   }
-  if (on(KLLM_B200_OP_SELECT)) {
+  if (on(KLLM_B200_OP_SELECT) && !fuse_select) {
     rc = select_last_rows(c->final_norm_out, T, H, c->seq_ends, c->seq_len, c->n_seqs, c->last_rows,
                           KLLM_B200_F16, c->err_flags, o);
     if (rc != KLLM_B200_OK) return rc;

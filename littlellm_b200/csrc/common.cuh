@@ -115,6 +115,12 @@ cudaError_t launch_clustered(void (*kernel)(KArgs...), dim3 grid, dim3 block, si
 struct LaunchOpts {
   cudaStream_t stream = nullptr;
   bool pdl = false;
+  // add_rms_norm under PDL: the residual was last written two or more
+  // launches back on this stream (the previous launch leaves it alone), so
+  // its rows may be read before the grid-dependency wait. Every kernel of
+  // this library triggers its dependents only after its own wait, so when a
+  // launch starts, all launches two or more back have completed.
+  bool early_residual = false;
 };
 
 // ---------------------------------------------------------------------------
@@ -185,6 +191,38 @@ __device__ __forceinline__ float round_f16(float x) { return __half2float(__floa
 __device__ __forceinline__ void rope_rotate(float x1, float x2, float c, float s, float& y1, float& y2) {
   y1 = __fmaf_rn(x1, c, -__fmul_rn(x2, s));
   y2 = __fmaf_rn(x2, c, __fmul_rn(x1, s));
+}
+
+// Eight rotations (pairs i = 0..7) with the packed fp32x2 multiply / FMA of
+// sm_100 (two pairs per instruction). Element by element the arithmetic is
+// rope_rotate's: y1 = fma(x1, c, x2 * (-s)) where x2 * (-s) equals -(x2 * s)
+// exactly in round-to-nearest, and y2 = fma(x2, c, x1 * s); `ns` holds -s.
+__device__ __forceinline__ unsigned long long f32x2_pack(float lo, float hi) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+
+__device__ __forceinline__ void f32x2_unpack(unsigned long long v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+
+__device__ __forceinline__ void rope_rotate8_x2(const float (&x1)[8], const float (&x2)[8], const float (&c)[8],
+                                                const float (&s)[8], const float (&ns)[8], float (&y1)[8],
+                                                float (&y2)[8]) {
+#pragma unroll
+  for (int i = 0; i < 8; i += 2) {
+    const unsigned long long a1 = f32x2_pack(x1[i], x1[i + 1]), a2 = f32x2_pack(x2[i], x2[i + 1]);
+    const unsigned long long cc = f32x2_pack(c[i], c[i + 1]);
+    const unsigned long long ss = f32x2_pack(s[i], s[i + 1]), nss = f32x2_pack(ns[i], ns[i + 1]);
+    unsigned long long p, q, r1, r2;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(p) : "l"(a2), "l"(nss));
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r1) : "l"(a1), "l"(cc), "l"(p));
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(q) : "l"(a1), "l"(ss));
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r2) : "l"(a2), "l"(cc), "l"(q));
+    f32x2_unpack(r1, y1[i], y1[i + 1]);
+    f32x2_unpack(r2, y2[i], y2[i + 1]);
+  }
 }
 
 // (cos, sin) of the RoPE angle pos * inv_freq, the angle as one fp32 product

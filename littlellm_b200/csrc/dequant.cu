@@ -110,28 +110,48 @@ __global__ void __launch_bounds__(kThreads) dequant_f16_kernel(const int8_t* __r
   }
 }
 
+// 4-byte load through the non-coherent path, not allocated in L1.
+__device__ __forceinline__ uint32_t ld_stream_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+
+// fp32 output: one 4-value word per thread and float4 store, so a warp reads
+// 128 contiguous bytes and writes 512 contiguous bytes per instruction; four
+// words in flight per thread (a CTA covers 4 x 256 consecutive words per
+// step).
+constexpr int kF32Words = 4;
+
 __global__ void __launch_bounds__(kThreads) dequant_f32_kernel(const int8_t* __restrict__ q,
                                                                const float* __restrict__ scale, float scale_value,
                                                                float* __restrict__ out, int64_t n) {
   grid_dep_wait();
   grid_dep_launch();
   const float s = scale != nullptr ? __ldg(scale) : scale_value;
-  const int64_t nvec = n >> 4;
-  const uint4* src = reinterpret_cast<const uint4*>(q);
+  const int64_t nw = n >> 2;
+  const uint32_t* src = reinterpret_cast<const uint32_t*>(q);
   float4* dst = reinterpret_cast<float4*>(out);
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < nvec; i += stride) {
-    const uint4 w = ld_stream(src + i);
-    const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+  const int64_t chunk = static_cast<int64_t>(blockDim.x) * kF32Words;
+  for (int64_t base = static_cast<int64_t>(blockIdx.x) * chunk; base < nw; base += static_cast<int64_t>(gridDim.x) * chunk) {
+    uint32_t w[kF32Words];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const uint32_t x = words[k];
-      dst[4 * i + k] = make_float4(dequant_value(x & 0xffu, s), dequant_value((x >> 8) & 0xffu, s),
-                                   dequant_value((x >> 16) & 0xffu, s), dequant_value(x >> 24, s));
+    for (int k = 0; k < kF32Words; ++k) {
+      const int64_t i = base + k * blockDim.x + threadIdx.x;
+      if (i < nw) w[k] = ld_stream_u32(src + i);
+    }
+#pragma unroll
+    for (int k = 0; k < kF32Words; ++k) {
+      const int64_t i = base + k * blockDim.x + threadIdx.x;
+      if (i < nw) {
+        const uint32_t x = w[k];
+        dst[i] = make_float4(dequant_value(x & 0xffu, s), dequant_value((x >> 8) & 0xffu, s),
+                             dequant_value((x >> 16) & 0xffu, s), dequant_value(x >> 24, s));
+      }
     }
   }
   if (blockIdx.x == 0) {
-    for (int64_t j = (nvec << 4) + threadIdx.x; j < n; j += blockDim.x) {
+    for (int64_t j = (nw << 2) + threadIdx.x; j < n; j += blockDim.x) {
       out[j] = __fmul_rn(static_cast<float>(q[j]), s);
     }
   }
@@ -376,7 +396,7 @@ int dequantize_int8_impl(const int8_t* data, const float* scale, float scale_val
                          "dequantize_int8");
   }
   if (out_dtype == KLLM_B200_F32 && vec) {
-    const unsigned grid = persistent_grid(dequant_f32_kernel, kThreads, 0, kThreads, (n >> 4) + 1);
+    const unsigned grid = persistent_grid(dequant_f32_kernel, kThreads, 0, kThreads * kF32Words, (n >> 2) + 1);
     return launch_status(launch(dequant_f32_kernel, grid, kThreads, 0, o.stream, o.pdl, data, scale, scale_value,
                                 static_cast<float*>(out), n),
                          "dequantize_int8");

@@ -12,6 +12,13 @@ int embedding(const void* table, int64_t vocab, int64_t hidden, int table_dtype,
 int add_rms_norm(void* residual, const void* delta, const void* weight, void* out, int64_t rows,
                  int64_t hidden, float eps, int act_dtype, int weight_dtype, const LaunchOpts& o);
 
+// add_rms_norm (fp16 rows) that also copies the last row of each of n_seqs
+// sequences of seq_len rows to last_rows (select_last_rows fused into the
+// final norm); two launches where the fast path does not apply.
+int add_rms_norm_last_rows(void* residual, const void* delta, const void* weight, void* out, int64_t rows,
+                           int64_t hidden, float eps, int weight_dtype, void* last_rows, int64_t seq_len,
+                           int64_t n_seqs, int32_t* err_flags, const LaunchOpts& o, int* n_launched);
+
 // residual = table[ids] (fp16 rows, bit-exact) and out = rms_norm(residual) * weight in one launch
 // (embedding + layer 0's input norm).
 int embedding_rms_norm(const void* table, int64_t vocab, int64_t hidden, const int32_t* ids, int64_t n_tokens,

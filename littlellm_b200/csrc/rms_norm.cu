@@ -68,6 +68,7 @@ enum NormMode : int {
   kPlain = 0,     // r = residual row (read only)
   kAddDelta = 1,  // r = fp16(residual + delta), stored back as the residual
   kGather = 2,    // r = table[ids[row]] (`src` is the table), stored as the residual
+  kAddSelect = 3, // kAddDelta, and each sequence's last row also written to last_rows
 };
 
 template <int VPT, typename TW, int MODE, bool EARLY>
@@ -77,9 +78,11 @@ __global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __re
                                                                     __half* __restrict__ out, int64_t rows,
                                                                     int hidden, int group, float eps,
                                                                     const int32_t* __restrict__ ids, int64_t vocab,
-                                                                    int32_t* err_flags) {
-  constexpr bool HAS_DELTA = MODE == kAddDelta;
+                                                                    int32_t* err_flags, int early_residual,
+                                                                    __half* __restrict__ last_rows, int64_t seq_len) {
+  constexpr bool HAS_DELTA = MODE == kAddDelta || MODE == kAddSelect;
   constexpr bool GATHER = MODE == kGather;
+  constexpr bool SELECT = MODE == kAddSelect;
   extern __shared__ __align__(16) unsigned char s_raw[];
   __shared__ float partial[2][kThreads / 32];
   // The norm weight is staged into shared memory once per CTA and the
@@ -103,9 +106,11 @@ __global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __re
   uint4 wreg = make_uint4(0, 0, 0, 0);
   if (park && static_cast<int>(threadIdx.x) < wvec) wreg = ld_keep(reinterpret_cast<const uint4*>(weight) + threadIdx.x);
   if (!park) stage_weight();
-  // A gathering launch under PDL issues its first rows' loads (table and
-  // ids, which no kernel of the chain writes) before the wait.
-  bool waited = GATHER && EARLY ? false : true;
+  // Under PDL a gathering launch issues its first rows' loads (table and
+  // ids, which no kernel of the chain writes) before the wait, and so does an
+  // add launch for its residual rows when early_residual says the previous
+  // launch did not write them; the delta always waits.
+  bool waited = EARLY && (GATHER || (HAS_DELTA && early_residual != 0)) ? false : true;
   if (waited) {
     grid_dep_wait();
     grid_dep_launch();
@@ -145,7 +150,7 @@ __global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __re
             r[j] = id_ok ? ld_stream(rsrc + v * 8) : make_uint4(0, 0, 0, 0);
           } else {
             r[j] = HAS_DELTA ? ld_cg(rsrc + v * 8) : ld_stream(rsrc + v * 8);
-            if (HAS_DELTA) d[j] = ld_stream(src + row * hidden + v * 8);
+            if (HAS_DELTA && waited) d[j] = ld_stream(src + row * hidden + v * 8);
           }
         }
       }
@@ -154,6 +159,13 @@ __global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __re
       grid_dep_wait();
       grid_dep_launch();
       waited = true;
+      if (HAS_DELTA && live) {
+#pragma unroll
+        for (int j = 0; j < VPT; ++j) {
+          const int v = j * group + lane_g;
+          if (v < nvec) d[j] = ld_stream(src + row * hidden + v * 8);
+        }
+      }
     }
     if (GATHER && live && !id_ok && lane_g == 0) set_flag(err_flags, KLLM_B200_FLAG_BAD_TOKEN);
     // `staged` and the loop trip count are uniform over the CTA, so every
@@ -194,6 +206,13 @@ __global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __re
     if (live) {
       const float scale = rsqrtf(ss * inv_h + eps);
       __half* orow = out + row * hidden;
+      // the last row of each sequence of seq_len rows also goes to last_rows
+      // (select_last_rows fused into the final norm)
+      __half* lrow = nullptr;
+      if (SELECT) {  // rows < 2^31 and seq_len >= 1 (checked on the host)
+        const int r32 = static_cast<int>(row), sl = static_cast<int>(seq_len);
+        if ((r32 + 1) % sl == 0) lrow = last_rows + static_cast<int64_t>(r32 / sl) * hidden;
+      }
 #pragma unroll
       for (int j = 0; j < VPT; ++j) {
         const int v = j * group + lane_g;
@@ -201,11 +220,12 @@ __global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __re
           float w[8];
           WeightVec<TW>::load(w_src, v * 8, w);
           const float2 a0 = h2_to_f2(r[j].x), a1 = h2_to_f2(r[j].y), a2 = h2_to_f2(r[j].z), a3 = h2_to_f2(r[j].w);
-          st_plain(orow + v * 8,
-                   make_uint4(f2_to_h2(a0.x * scale * w[0], a0.y * scale * w[1]),
-                              f2_to_h2(a1.x * scale * w[2], a1.y * scale * w[3]),
-                              f2_to_h2(a2.x * scale * w[4], a2.y * scale * w[5]),
-                              f2_to_h2(a3.x * scale * w[6], a3.y * scale * w[7])));
+          const uint4 y = make_uint4(f2_to_h2(a0.x * scale * w[0], a0.y * scale * w[1]),
+                                     f2_to_h2(a1.x * scale * w[2], a1.y * scale * w[3]),
+                                     f2_to_h2(a2.x * scale * w[4], a2.y * scale * w[5]),
+                                     f2_to_h2(a3.x * scale * w[6], a3.y * scale * w[7]));
+          st_plain(orow + v * 8, y);
+          if (SELECT && lrow != nullptr) st_plain(lrow + v * 8, y);
         }
       }
     }
@@ -268,11 +288,15 @@ FastConfig pick_config(int nvec) {
   return {};
 }
 
-// Extra arguments of a gathering launch (unused otherwise).
+// Extra arguments: the ids and vocabulary of a gathering launch, and the
+// last-rows output of a final norm that also selects each sequence's last
+// row (unused otherwise).
 struct GatherArgs {
   const int32_t* ids = nullptr;
   int64_t vocab = 0;
   int32_t* err_flags = nullptr;
+  void* last_rows = nullptr;
+  int64_t seq_len = 1;
 };
 
 template <int VPT, typename TW, int MODE>
@@ -287,7 +311,8 @@ int launch_fast(void* residual, const void* src, const void* weight, void* out, 
   const unsigned grid = persistent_grid(k, threads, smem, rows_per_cta, rows);
   return launch_status(launch(k, grid, threads, smem, o.stream, o.pdl, static_cast<__half*>(residual),
                               static_cast<const __half*>(src), static_cast<const TW*>(weight),
-                              static_cast<__half*>(out), rows, hidden, group, eps, ga.ids, ga.vocab, ga.err_flags),
+                              static_cast<__half*>(out), rows, hidden, group, eps, ga.ids, ga.vocab, ga.err_flags,
+                              static_cast<int>(o.early_residual), static_cast<__half*>(ga.last_rows), ga.seq_len),
                        what);
 }
 
@@ -301,6 +326,9 @@ int launch_fast_d(int mode, void* residual, const void* src, const void* weight,
     case kGather:
       return launch_fast<VPT, TW, kGather>(residual, src, weight, out, rows, hidden, group, eps, ga, o,
                                            "embedding_rms_norm");
+    case kAddSelect:
+      return launch_fast<VPT, TW, kAddSelect>(residual, src, weight, out, rows, hidden, group, eps, ga, o,
+                                              "add_rms_norm_last_rows");
     default:
       return launch_fast<VPT, TW, kPlain>(residual, src, weight, out, rows, hidden, group, eps, ga, o,
                                           "add_rms_norm");
@@ -364,6 +392,38 @@ int add_rms_norm(void* residual, const void* delta, const void* weight, void* ou
   return weight_dtype == KLLM_B200_F16
              ? launch_generic<float, __half>(residual, delta, weight, out, rows, hidden, eps, o)
              : launch_generic<float, float>(residual, delta, weight, out, rows, hidden, eps, o);
+}
+
+int add_rms_norm_last_rows(void* residual, const void* delta, const void* weight, void* out, int64_t rows,
+                           int64_t hidden, float eps, int weight_dtype, void* last_rows, int64_t seq_len,
+                           int64_t n_seqs, int32_t* err_flags, const LaunchOpts& o, int* n_launched) {
+  *n_launched = 0;
+  const bool fast = rows > 0 && hidden % 8 == 0 && hidden <= 8 * 8 * kThreads && aligned16(residual) &&
+                    aligned16(out) && aligned16(weight) && (delta == nullptr || aligned16(delta)) &&
+                    delta != nullptr && last_rows != nullptr && aligned16(last_rows) && seq_len >= 1 &&
+                    n_seqs * seq_len == rows && rows < (int64_t{1} << 31) && is_float_dtype(weight_dtype);
+  if (fast) {
+    const FastConfig c = pick_config(static_cast<int>(hidden / 8));
+    if (c.vpt > 0) {
+      GatherArgs ga;
+      ga.last_rows = last_rows;
+      ga.seq_len = seq_len;
+      const int mode = kAddSelect;
+      const int rc = weight_dtype == KLLM_B200_F16
+                         ? dispatch_fast<__half>(c, mode, residual, delta, weight, out, rows, (int)hidden, eps, ga, o)
+                         : dispatch_fast<float>(c, mode, residual, delta, weight, out, rows, (int)hidden, eps, ga, o);
+      if (rc == KLLM_B200_OK) *n_launched = 1;
+      return rc;
+    }
+  }
+  int rc = add_rms_norm(residual, delta, weight, out, rows, hidden, eps, KLLM_B200_F16, weight_dtype, o);
+  if (rc != KLLM_B200_OK) return rc;
+  *n_launched = 1;
+  LaunchOpts plain = o;
+  plain.early_residual = false;
+  rc = select_last_rows(out, rows, hidden, nullptr, seq_len, n_seqs, last_rows, KLLM_B200_F16, err_flags, plain);
+  if (rc == KLLM_B200_OK) *n_launched = 2;
+  return rc;
 }
 
 int embedding_rms_norm(const void* table, int64_t vocab, int64_t hidden, const int32_t* ids, int64_t n_tokens,

@@ -78,14 +78,18 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
 template <typename TB>
 __device__ __forceinline__ uint4 add_bias8(uint4 x, const TB* bias, int off);
 
-template <>
-__device__ __forceinline__ uint4 add_bias8<__half>(uint4 x, const __half* bias, int off) {
-  const uint4 b = *reinterpret_cast<const uint4*>(bias + off);
+// fp16(x + b) for 8 packed fp16 lanes (four HADD2).
+__device__ __forceinline__ uint4 hadd8(uint4 x, uint4 b) {
   auto add = [](uint32_t u, uint32_t v) {
     __half2 r = __hadd2(*reinterpret_cast<const __half2*>(&u), *reinterpret_cast<const __half2*>(&v));
     return *reinterpret_cast<uint32_t*>(&r);
   };
   return make_uint4(add(x.x, b.x), add(x.y, b.y), add(x.z, b.z), add(x.w, b.w));
+}
+
+template <>
+__device__ __forceinline__ uint4 add_bias8<__half>(uint4 x, const __half* bias, int off) {
+  return hadd8(x, *reinterpret_cast<const uint4*>(bias + off));
 }
 
 template <>
@@ -297,6 +301,191 @@ __global__ void __launch_bounds__(kWarpThreads) qkv_rope_warp_kernel(const __gri
   }
 }
 
+// Token kernel: the fused op's fast path for the head layouts of the served
+// models (head_dim, q heads, kv heads as template constants; see
+// kTokenShapes). One token per W warps. A token's rotation units (8 pairs of
+// one q or k head: two 16-byte loads and two 16-byte stores) are numbered
+// head-major, chunk-minor and dealt to the token's warps in rows of 32: unit
+// u = (j * W + part) * 32 + lane. With C = D / 16 units per head dividing
+// 32, every unit of a lane has chunk lane % C, i.e. the same 8 frequencies,
+// so the lane reads its 8 cos/sin from shared memory once into registers.
+// The v units (16 bytes of one v head) are dealt the same way. All index
+// arithmetic is on template constants, positions and slots are loaded once
+// per token (one broadcast load), and a unit picks its source, bias and
+// destination (q in place, or the head-major K cache) by selection, so a row
+// holding both q and k heads runs one instruction stream.
+//
+// Qwen2.5-0.5B (64, 14, 2): one warp per token, 2 rotation units per lane and
+// half a v unit. Llama-2-7B (128, 32, 32): 8 warps per token, 2 + 2.
+template <int D, int HQ, int HKV, int W, typename TB, bool EARLY>
+__global__ void __launch_bounds__(kWarpThreads) qkv_rope_token_kernel(const __grid_constant__ RopeArgs a) {
+  constexpr int C = D / 16;              // rotation units per head
+  constexpr int HALF = D / 2;
+  constexpr int VC = D / 8;              // v units per head
+  constexpr int R = (HQ + HKV) * C;      // rotation units per token
+  constexpr int V = HKV * VC;            // v units per token
+  constexpr int UR = (R + 32 * W - 1) / (32 * W);  // rotation units per lane
+  constexpr int UV = (V + 32 * W - 1) / (32 * W);  // v units per lane
+  static_assert(32 % C == 0, "chunks per head must divide 32");
+  static_assert((W & (W - 1)) == 0, "warps per token must be a power of two");
+  __shared__ __align__(16) float s_cs[kWarpsPerCta][2][HALF];
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * kWarpsPerCta + warp;
+  const int t = gw / W;
+  const int part = gw % W;
+  const bool live = t < a.n_tokens;  // uniform per warp
+
+  // position and slot (never written by a kernel of the chain: loaded before
+  // the dependency wait under PDL)
+  int32_t pos = 0, slot = 0;
+  if (live) {
+    pos = __ldg(a.positions + t);
+    slot = __ldg(a.slots + t);
+  }
+  const bool pos_ok = pos >= 0 && pos < a.max_seq;
+  const bool slot_ok = slot >= 0 && slot < a.n_slots;
+  const bool cache_ok = pos_ok && slot_ok;
+  if (live && part == 0 && lane == 0) {
+    if (!pos_ok) set_flag(a.err_flags, KLLM_B200_FLAG_BAD_POSITION);
+    if (!slot_ok) set_flag(a.err_flags, KLLM_B200_FLAG_BAD_SLOT);
+  }
+
+  const int chunk8 = (lane % C) * 8;
+  uint4 x1[UR], x2[UR], xv[UV];
+  auto unit_head = [&](int j) { return (j * W + part) * (32 / C) + lane / C; };
+
+  const TB* bq = static_cast<const TB*>(a.bq);
+  const TB* bk = static_cast<const TB*>(a.bk);
+  const TB* bv = static_cast<const TB*>(a.bv);
+  // fp16 biases of a one-warp-per-token layout: this lane's slices (16 bytes
+  // per 8 values) are loaded into registers with the position, before the
+  // dependency wait, so no bias round trip sits behind the activation loads
+  // of this latency-bound case. Wider layouts (bandwidth-bound, more units
+  // per lane) and fp32 biases read them through L1 when used: there the
+  // extra registers cost more occupancy than the round trip.
+  constexpr bool kRegBias = sizeof(TB) == 2 && W == 1;
+  uint4 b1[kRegBias ? UR : 1], b2[kRegBias ? UR : 1], bvr[kRegBias ? UV : 1];
+  if (kRegBias && live) {
+#pragma unroll
+    for (int j = 0; j < UR; ++j) {
+      const int head = unit_head(j);
+      const TB* bias = head < HQ ? bq : bk;
+      if (head < HQ + HKV && bias != nullptr) {
+        const int bo = (head < HQ ? head : head - HQ) * D + chunk8;
+        b1[j] = ld_keep(bias + bo);
+        b2[j] = ld_keep(bias + bo + HALF);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < UV; ++j) {
+      const int u = (j * W + part) * 32 + lane;
+      if (u < V && bv != nullptr) bvr[j] = ld_keep(bv + (u / VC) * D + (u % VC) * 8);
+    }
+  }
+  auto issue_loads = [&]() {
+    if (!live) return;
+#pragma unroll
+    for (int j = 0; j < UR; ++j) {
+      const int head = unit_head(j);
+      if (head < HQ + HKV) {
+        const __half* src = head < HQ ? a.q + (t * HQ + head) * D + chunk8
+                                      : a.k + (t * HKV + (head - HQ)) * D + chunk8;
+        x1[j] = ld_cg(src);
+        x2[j] = ld_cg(src + HALF);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < UV; ++j) {
+      const int u = (j * W + part) * 32 + lane;
+      if (u < V) xv[j] = ld_stream(a.v + (t * HKV + u / VC) * D + (u % VC) * 8);
+    }
+  };
+  if (!EARLY) {
+    grid_dep_wait();
+    grid_dep_launch();
+    issue_loads();
+  }
+  // cos/sin of the token's HALF frequencies, HALF / 32 per lane
+#pragma unroll
+  for (int d = lane; d < HALF; d += 32) {
+    float sn, cs;
+    sincosf(__fmul_rn(static_cast<float>(pos), a.inv_freq[d]), &sn, &cs);
+    s_cs[warp][0][d] = cs;
+    s_cs[warp][1][d] = sn;
+  }
+  if (EARLY) {
+    grid_dep_wait();
+    grid_dep_launch();
+    issue_loads();
+  }
+  __syncwarp();
+  float c[8], sn[8], nsn[8];
+  {
+    const float4* cp = reinterpret_cast<const float4*>(&s_cs[warp][0][chunk8]);
+    const float4* sp = reinterpret_cast<const float4*>(&s_cs[warp][1][chunk8]);
+    const float4 c0 = cp[0], c1 = cp[1], s0 = sp[0], s1 = sp[1];
+    c[0] = c0.x; c[1] = c0.y; c[2] = c0.z; c[3] = c0.w; c[4] = c1.x; c[5] = c1.y; c[6] = c1.z; c[7] = c1.w;
+    sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w; sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) nsn[i] = -sn[i];
+  }
+  if (!live) return;
+
+  // head h of this token in a [n_slots, HKV, max_seq, D] plane (the host
+  // checks max_seq * D < 2^31)
+  const int64_t cache_tok = (static_cast<int64_t>(slot) * HKV * a.max_seq + pos) * D + chunk8;
+  const int head_stride = static_cast<int>(a.max_seq) * D;
+#pragma unroll
+  for (int j = 0; j < UR; ++j) {
+    const int head = unit_head(j);
+    if (head >= HQ + HKV) continue;
+    const bool is_q = head < HQ;
+    const int kh = head - HQ;
+    const TB* bias = is_q ? bq : bk;
+    float f1[8], f2[8];
+    if (bias != nullptr) {
+      if constexpr (kRegBias) {
+        unpack8(hadd8(x1[j], b1[j]), f1);
+        unpack8(hadd8(x2[j], b2[j]), f2);
+      } else {
+        const int bo = (is_q ? head : kh) * D + chunk8;
+        unpack8(add_bias8<TB>(x1[j], bias, bo), f1);
+        unpack8(add_bias8<TB>(x2[j], bias, bo + HALF), f2);
+      }
+    } else {
+      unpack8(x1[j], f1);
+      unpack8(x2[j], f2);
+    }
+    float y1[8], y2[8];
+    rope_rotate8_x2(f1, f2, c, sn, nsn, y1, y2);
+    __half* dst = is_q ? a.q + (t * HQ + head) * D + chunk8
+                       : a.k_cache + cache_tok + static_cast<int64_t>(kh) * head_stride;
+    if (is_q || cache_ok) {
+      st_plain(dst, pack8(y1));
+      st_plain(dst + HALF, pack8(y2));
+    }
+  }
+  if (!cache_ok) return;
+#pragma unroll
+  for (int j = 0; j < UV; ++j) {
+    const int u = (j * W + part) * 32 + lane;
+    if (u >= V) continue;
+    const int vh = u / VC;
+    const int vd = (u % VC) * 8;
+    uint4 x = xv[j];
+    if (bv != nullptr) {
+      if constexpr (kRegBias) {
+        x = hadd8(x, bvr[j]);
+      } else {
+        x = add_bias8<TB>(x, bv, vh * D + vd);
+      }
+    }
+    st_plain(a.v_cache + cache_tok - chunk8 + static_cast<int64_t>(vh) * head_stride + vd, x);
+  }
+}
+
 // Any even head_dim, fp16 or fp32 activations: one thread per rotation pair
 // or per v element; no shared tables.
 template <typename TA, typename TB>
@@ -378,6 +567,30 @@ void (*pick_tb(bool bias16, bool pdl))(RopeArgs) {
   return bias16 ? qkv_rope_warp_kernel<DT, UPL, __half, false> : qkv_rope_warp_kernel<DT, UPL, float, false>;
 }
 
+template <int D, int HQ, int HKV, int W>
+void (*pick_token_tb(bool bias16, bool pdl))(RopeArgs) {
+  if (pdl) {
+    return bias16 ? qkv_rope_token_kernel<D, HQ, HKV, W, __half, true> : qkv_rope_token_kernel<D, HQ, HKV, W, float, true>;
+  }
+  return bias16 ? qkv_rope_token_kernel<D, HQ, HKV, W, __half, false> : qkv_rope_token_kernel<D, HQ, HKV, W, float, false>;
+}
+
+struct TokenKernel {
+  void (*kernel)(RopeArgs) = nullptr;
+  int warps_per_token = 0;
+};
+
+// Head layouts (head_dim, q heads, kv heads) with a token kernel: Qwen2.5-0.5B,
+// Llama-2-7B, Qwen2.5-7B and Llama-3-8B. W (warps per token) keeps two to
+// three rotation units per lane. Other layouts take qkv_rope_warp_kernel.
+TokenKernel pick_token_kernel(int D, int hq, int hkv, bool bias16, bool pdl) {
+  if (D == 64 && hq == 14 && hkv == 2) return {pick_token_tb<64, 14, 2, 1>(bias16, pdl), 1};
+  if (D == 128 && hq == 32 && hkv == 32) return {pick_token_tb<128, 32, 32, 8>(bias16, pdl), 8};
+  if (D == 128 && hq == 28 && hkv == 4) return {pick_token_tb<128, 28, 4, 4>(bias16, pdl), 4};
+  if (D == 128 && hq == 32 && hkv == 8) return {pick_token_tb<128, 32, 8, 4>(bias16, pdl), 4};
+  return {};
+}
+
 template <int DT>
 void (*pick_upl(int upl, bool bias16, bool pdl))(RopeArgs) {
   switch (upl) {
@@ -401,6 +614,18 @@ int run_rope(RopeArgs& a, int act_dtype, int bias_dtype, const LaunchOpts& o, co
   auto al = [](const void* p) { return p == nullptr || aligned16(p); };
   const bool fast = act_dtype == KLLM_B200_F16 && D % 16 == 0 && al(a.q) && al(a.k) && al(a.v) && al(a.bq) &&
                     al(a.bk) && al(a.bv) && al(a.k_cache) && al(a.v_cache);
+  if (fast && a.k != nullptr && a.v != nullptr && a.k_cache != nullptr && a.v_cache != nullptr &&
+      a.positions != nullptr && a.slots != nullptr) {
+    const TokenKernel tk = pick_token_kernel(D, a.n_heads, a.n_kv_heads, bias16, o.pdl);
+    const int64_t widest = a.n_heads > a.n_kv_heads ? a.n_heads : a.n_kv_heads;
+    // token-row offsets are 32-bit in the kernel
+    if (tk.kernel != nullptr && a.n_tokens * tk.warps_per_token < (int64_t{1} << 30) &&
+        a.n_tokens * widest * D < (int64_t{1} << 31) && a.max_seq * D < (int64_t{1} << 31)) {
+      const int64_t warps = a.n_tokens * tk.warps_per_token;
+      const unsigned grid = static_cast<unsigned>((warps + kWarpsPerCta - 1) / kWarpsPerCta);
+      return launch_status(launch(tk.kernel, grid, kWarpThreads, 0, o.stream, o.pdl, a), what);
+    }
+  }
   if (fast) {
     const int chunks = D / 16;
     const int units = a.n_heads * chunks + (a.k ? a.n_kv_heads * chunks : 0) + (a.v ? a.n_kv_heads * D / 8 : 0);

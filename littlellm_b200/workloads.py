@@ -67,7 +67,8 @@ def shard(workload: Workload, rank: int, world: int) -> Workload:
     return replace(workload, n_seqs=workload.n_seqs // world)
 
 
-def chain_bytes(w: Workload, n_layers: int | None = None, positions=None, fused_embedding: bool = False) -> dict:
+def chain_bytes(w: Workload, n_layers: int | None = None, positions=None, fused_embedding: bool = False,
+                fused_select: bool = False) -> dict:
     """Algorithmic HBM bytes of one chain step: every logical fp16 tensor read
     once and written once; norm weights and biases are negligible and not
     counted; ids/positions/slots are int32. With ``positions`` (host array of
@@ -79,7 +80,9 @@ def chain_bytes(w: Workload, n_layers: int | None = None, positions=None, fused_
     are one op: the gathered rows are written once (the residual) and never
     re-read, so the pair counts T*H*2 (table rows read) + 2*T*H*2 (residual
     and normed rows written) + 4*T, against 2*T*H*2 + 4*T for the gather plus
-    2*T*H*2 for the norm when they run apart."""
+    2*T*H*2 for the norm when they run apart. With ``fused_select`` the final
+    norm writes each sequence's last row as well: those rows are written
+    (B*H*2) but not re-read."""
     m, T = w.model, w.n_tokens
     H, I, L = m.hidden, m.intermediate, n_layers or m.n_layers
     qkv_elems = T * (m.n_heads + 2 * m.n_kv_heads) * m.head_dim
@@ -97,6 +100,8 @@ def chain_bytes(w: Workload, n_layers: int | None = None, positions=None, fused_
         # and normed rows written, ids read
         per["embedding"] = 3 * T * H * 2 + 4 * T
         per["add_rms_norm"] -= 2 * T * H * 2
+    if fused_select:
+        per["select_last_rows"] = w.n_seqs * H * 2
     if positions is not None:
         kv_rows = int((positions.astype("int64") + 1).sum()) if w.decode else T
         per["attention"] = L * (kv_rows * m.n_kv_heads * m.head_dim * 2 * 2 + 2 * T * m.n_heads * m.head_dim * 2)

@@ -43,8 +43,8 @@ def test_chain_matches_oracle(cuda, oracle, shape, decode, use_pdl):
     pos, slots = r.positions.cpu().numpy(), r.slots.cpu().numpy()
     launches = r.run()
     torch.cuda.synchronize()
-    # the embedding and layer 0's input norm are one kernel
-    assert launches == 4 * m.n_layers + 2
+    # the embedding and layer 0's input norm are one kernel, the final norm writes the last rows
+    assert launches == 4 * m.n_layers + 1
     assert int(r.err_flags.item()) == 0
 
     T, D = w.n_tokens, m.head_dim
@@ -141,7 +141,7 @@ def test_chain_with_attention(cuda, oracle, shape, decode):
     r = ChainRunner(w, device=cuda, seed=7, use_pdl=True, attention=True)
     launches = r.run()
     torch.cuda.synchronize()
-    assert launches == 5 * m.n_layers + 2
+    assert launches == 5 * m.n_layers + 1
     assert int(r.err_flags.item()) == 0
     pos, slots = r.positions.cpu().numpy(), r.slots.cpu().numpy()
     T, D = w.n_tokens, m.head_dim
@@ -150,3 +150,34 @@ def test_chain_with_attention(cuda, oracle, shape, decode):
                                                 host(L["v_cache"]), pos, slots)
         assert bad == 0
         assert_tol(host(L["attn_ctx"]).reshape(T, m.n_heads, D), want, what=f"attention layer {l}")
+
+
+@pytest.mark.parametrize("decode", [False, True])
+def test_final_norm_writes_last_rows(cuda, decode):
+    """Final norm + select: one kernel when every sequence has seq_len rows,
+    the separate select kernel for a ragged batch (seq_ends); the last rows
+    are bit-identical copies of the final norm's rows either way."""
+    from littlellm_b200 import _capi
+    from littlellm_b200.chain import ChainRunner
+    w = _tiny(decode, "qwen")
+    r = ChainRunner(w, device=cuda, seed=13, use_pdl=True)
+    r.run()  # the whole chain once, so the residual holds a step's value
+    r.desc.op_mask = _capi.OP_FINAL_NORM | _capi.OP_SELECT
+    assert r.fused_select
+    saved = r.residual.clone()  # the final norm adds into the residual: each run starts from this
+    r.last_rows.fill_(-7.0)
+    assert r.run() == 1
+    torch.cuda.synchronize()
+    fused = r.last_rows.clone()
+    assert np.array_equal(bits16(fused), bits16(r.final_norm_out)[w.seq_len - 1::w.seq_len])
+    # ragged form of the same batch: every sequence ends where the uniform one does
+    ends = torch.arange(1, w.n_seqs + 1, device=cuda, dtype=torch.int32) * w.seq_len
+    r.desc.seq_ends = ends.data_ptr()
+    assert not r.fused_select
+    r.residual.copy_(saved)
+    r.last_rows.fill_(-7.0)
+    r.run()
+    torch.cuda.synchronize()
+    r.desc.seq_ends = None
+    assert int(r.err_flags.item()) == 0
+    assert torch.equal(r.last_rows, fused)

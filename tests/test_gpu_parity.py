@@ -171,6 +171,7 @@ def test_embedding_oracle(ops, vocab, hidden, n):
 
 
 @pytest.mark.parametrize("T,Hq,Hkv,D,theta", [(512, 14, 2, 64, 1e6), (48, 32, 32, 128, 1e4),
+                                              (40, 28, 4, 128, 1e6), (33, 32, 8, 128, 5e5),
                                               (37, 4, 2, 16, 1e4), (9, 3, 1, 6, 1e4), (5, 2, 2, 256, 1e6)])
 @pytest.mark.parametrize("bias", [True, False])
 def test_qkv_fused_oracle(ops, oracle, T, Hq, Hkv, D, theta, bias):
@@ -207,11 +208,46 @@ def test_qkv_fused_oracle(ops, oracle, T, Hq, Hkv, D, theta, bias):
     assert not kch.transpose(0, 2, 1, 3)[mask].any() and not vch.transpose(0, 2, 1, 3)[mask].any()
 
 
-def test_qkv_fused_equals_composed_legacy_ops(ops):
+@pytest.mark.parametrize("Hq,Hkv,D", [(14, 2, 64), (32, 32, 128), (4, 2, 64)])
+def test_qkv_fused_bad_positions_and_slots(ops, oracle, Hq, Hkv, D):
+    """Tokens whose position or slot is outside the cache set the flags and
+    write no cache row; q is rotated for every token; the other tokens' rows
+    are written as usual."""
+    from littlellm_b200 import _capi
+    rng = np.random.default_rng(D + Hq)
+    T, S, NS, theta = 6, 64, 2, 1e4
+    q, k, v = (f16r(rng.standard_normal((T, H, D))) for H in (Hq, Hkv, Hkv))
+    pos = np.array([0, -1, 5, S, 7, 3], np.int32)
+    slots = np.array([0, 0, NS, 1, -1, 1], np.int32)
+    good = np.array([True, False, False, False, False, True])
+    qd = dev(q)
+    kc = torch.full((NS, Hkv, S, D), 7.0, dtype=F16, device="cuda:0")
+    vc = torch.full_like(kc, 7.0)
+    flags = torch.zeros(1, dtype=torch.int32, device="cuda:0")
+    ops.qkv_bias_rope_kv_append(qd, dev(k), dev(v), None, None, None, dev(pos, torch.int32),
+                                dev(slots, torch.int32), theta, kc, vc, flags)
+    torch.cuda.synchronize()
+    assert int(flags.item()) == _capi.FLAG_BAD_POSITION | _capi.FLAG_BAD_SLOT
+    zeros = np.zeros((NS, Hkv, S, D), np.float32)
+    q_ref, kc_ref, _, _ = oracle.qkv_bias_rope_kv_append(q[good], k[good], v[good], None, None, None, pos[good],
+                                                         slots[good], theta, zeros, zeros)
+    assert_tol(host(qd)[good], q_ref, what="q")
+    kch, vch = host(kc), host(vc)
+    gs, gp = slots[good], pos[good]
+    assert_tol(kch[gs, :, gp], kc_ref[gs, :, gp], what="k cache")
+    assert np.array_equal(vch[gs, :, gp], v[good])
+    mask = np.ones((NS, S), bool)
+    mask[gs, gp] = False
+    assert (kch.transpose(0, 2, 1, 3)[mask] == 7.0).all() and (vch.transpose(0, 2, 1, 3)[mask] == 7.0).all()
+
+
+@pytest.mark.parametrize("Hq,Hkv,D", [(14, 2, 64), (32, 32, 128), (28, 4, 128), (32, 8, 128), (4, 2, 64)])
+def test_qkv_fused_equals_composed_legacy_ops(ops, Hq, Hkv, D):
     """Fused op == add_bias_inplace x3, rope_inplace x2, then the cache write,
-    bit for bit (same rounding points, same rotation arithmetic)."""
+    bit for bit (same rounding points, same rotation arithmetic), for the
+    head layouts with a token kernel and one without."""
     rng = np.random.default_rng(11)
-    T, Hq, Hkv, D, S, theta = 64, 14, 2, 64, 512, 1e6
+    T, S, theta = 64, 512, 1e6
     q, k, v = (f16r(rng.standard_normal((T, H, D))) for H in (Hq, Hkv, Hkv))
     bq, bk, bv = (f16r(rng.normal(0, 0.02, H * D)) for H in (Hq, Hkv, Hkv))
     past = 100
