@@ -359,13 +359,13 @@ __global__ void __launch_bounds__(kWarpThreads) qkv_rope_token_kernel(const __gr
   const TB* bq = static_cast<const TB*>(a.bq);
   const TB* bk = static_cast<const TB*>(a.bk);
   const TB* bv = static_cast<const TB*>(a.bv);
-  // fp16 biases of a one-warp-per-token layout: this lane's slices (16 bytes
+  // fp16 biases of a layout with few units per lane: this lane's slices (16 bytes
   // per 8 values) are loaded into registers with the position, before the
   // dependency wait, so no bias round trip sits behind the activation loads
   // of this latency-bound case. Wider layouts (bandwidth-bound, more units
   // per lane) and fp32 biases read them through L1 when used: there the
   // extra registers cost more occupancy than the round trip.
-  constexpr bool kRegBias = sizeof(TB) == 2 && W == 1;
+  constexpr bool kRegBias = sizeof(TB) == 2 && 2 * UR + UV <= 5;
   uint4 b1[kRegBias ? UR : 1], b2[kRegBias ? UR : 1], bvr[kRegBias ? UV : 1];
   if (kRegBias && live) {
 #pragma unroll

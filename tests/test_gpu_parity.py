@@ -170,13 +170,13 @@ def test_embedding_oracle(ops, vocab, hidden, n):
     assert np.array_equal(bits16(out), table[ids].view(np.uint16))
 
 
-@pytest.mark.parametrize("T,Hq,Hkv,D,theta", [(512, 14, 2, 64, 1e6), (48, 32, 32, 128, 1e4),
+@pytest.mark.parametrize("T,Hq,Hkv,D,theta", [(512, 14, 2, 64, 1e6), (2500, 14, 2, 64, 1e6), (48, 32, 32, 128, 1e4),
                                               (40, 28, 4, 128, 1e6), (33, 32, 8, 128, 5e5),
                                               (37, 4, 2, 16, 1e4), (9, 3, 1, 6, 1e4), (5, 2, 2, 256, 1e6)])
 @pytest.mark.parametrize("bias", [True, False])
 def test_qkv_fused_oracle(ops, oracle, T, Hq, Hkv, D, theta, bias):
     rng = np.random.default_rng(T * 31 + D)
-    S, NS = 4096, 8
+    S, NS = 4096, max(8, -(-T // 64))  # enough slots that positions stay below S
     q = f16r(rng.standard_normal((T, Hq, D)))
     k = f16r(rng.standard_normal((T, Hkv, D)))
     v = f16r(rng.standard_normal((T, Hkv, D)))
