@@ -622,6 +622,30 @@ def per_op_chain_timing(runner, stream, reps: int) -> dict:
                 out[name]["kernel_launches_per_replay"] = n
                 out[name]["note"] = "per layer, not per kernel launch"
             del g
+        # ablation: the whole step with this op kind removed; the difference
+        # is the op's marginal cost where it really sits in the chain (after
+        # the neighbours it has in a forward step, not after itself)
+        full = runner.full_mask or _capi.OP_CHAIN  # op_mask 0 means the seven chain ops
+        runner.desc.op_mask = full
+        n_full = runner.run(stream)
+        g = capture(lambda: runner.run(stream), stream)
+        g.replay()
+        t_full = time_graph(g, stream, reps)
+        del g
+        for name, (mask, nbytes) in kinds.items():
+            if name == "attention":
+                continue
+            runner.desc.op_mask = full & ~mask
+            n_without = runner.run(stream)
+            g = capture(lambda: runner.run(stream), stream)
+            g.replay()
+            t_without = time_graph(g, stream, reps)
+            del g
+            removed = n_full - n_without
+            if removed > 0:
+                us = (t_full - t_without) * 1000.0 / removed
+                out[name]["marginal_us_per_launch"] = us
+                out[name]["marginal_gbs"] = nbytes / (us * 1e-6) / 1e9 if us > 0 else None
         runner.desc.op_mask = runner.full_mask
     return out
 
@@ -1475,6 +1499,8 @@ def measure_chain(w, args, device, dist, *, seed: int, steps: int, warmup: int, 
         for table in tables:
             for v in table.values():
                 v["frac_of_measured"] = v["gbs"] / peaks["hbm_gbs"]
+                if v.get("marginal_gbs"):
+                    v["marginal_frac_of_measured"] = v["marginal_gbs"] / peaks["hbm_gbs"]
     return runner, stream, stats
 
 

@@ -1,7 +1,12 @@
 """Sequence-sharded chain on 2 GPUs (one process each, NCCL only for the
 verification gather) reproduces the single-GPU chain bit for bit, with and
-without attention in the chain, and the whole forward step (GEMMs and
-lm_head included). Skipped when fewer than 2 GPUs are visible."""
+without attention in the chain. The whole forward step (GEMMs and lm_head
+included) is bit-identical for prefill and agrees within the fp16
+tolerance of the parity tests for decode: a decode
+GEMM splits its k range over a cluster by a factor that depends on the rows
+of the call (their fp32 partial sums must fit the leader's shared memory),
+so 8 rows per GPU and 16 rows on one GPU add their partial sums in different
+groupings. Skipped when fewer than 2 GPUs are visible."""
 from __future__ import annotations
 
 import os
@@ -50,12 +55,18 @@ def _worker(rank, world, port, out_dir, decode, attention, gemm=False):
             full = ChainRunner(w, device=dev, seed=77, use_pdl=True, attention=attention, gemm=gemm)
             full.run()
             torch.cuda.synchronize(dev)
-            ok = (torch.equal(last, full.last_rows) and torch.equal(normed, full.final_norm_out)
-                  and torch.equal(swiglu, full.layers[-1]["swiglu_out"]) and flags == 0)
+            if gemm and decode:  # 8 vs 16 decode rows take different split-K factors
+                def same(a, b):  # |a - b| <= 1e-2 + 1e-2 |b|, the parity tolerance
+                    a, b = a.float(), b.float()
+                    return bool(((a - b).abs() <= 1e-2 + 1e-2 * b.abs()).all())
+            else:
+                same = torch.equal
+            ok = (same(last, full.last_rows) and same(normed, full.final_norm_out)
+                  and same(swiglu, full.layers[-1]["swiglu_out"]) and flags == 0)
             if attention:
-                ok = ok and torch.equal(ctx, full.layers[-1]["attn_ctx"])
+                ok = ok and same(ctx, full.layers[-1]["attn_ctx"])
             if gemm:
-                ok = ok and torch.equal(logits, full.logits)
+                ok = ok and same(logits, full.logits)
             with open(os.path.join(out_dir, "result"), "w") as f:
                 f.write("ok" if ok else "mismatch")
         torch.distributed.barrier()
