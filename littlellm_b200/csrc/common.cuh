@@ -185,6 +185,28 @@ __device__ __forceinline__ uint32_t f2_to_h2(float lo, float hi) {
 
 __device__ __forceinline__ float round_f16(float x) { return __half2float(__float2half_rn(x)); }
 
+// Eight fp16 values of a 16-byte vector as floats, and back (round to nearest even).
+__device__ __forceinline__ void unpack8(uint4 v, float (&f)[8]) {
+  const float2 a = h2_to_f2(v.x), b = h2_to_f2(v.y), c = h2_to_f2(v.z), d = h2_to_f2(v.w);
+  f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y; f[4] = c.x; f[5] = c.y; f[6] = d.x; f[7] = d.y;
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  return make_uint4(f2_to_h2(f[0], f[1]), f2_to_h2(f[2], f[3]), f2_to_h2(f[4], f[5]), f2_to_h2(f[6], f[7]));
+}
+
+// fp16(x + b) for 8 packed fp16 lanes (four HADD2). This equals rounding the
+// fp32 sum of the two values to fp16: that sum is itself a rounding of the
+// exact sum, and fp32 carries 24 >= 2 * 11 + 2 significand bits, so the
+// double rounding is innocuous for addition.
+__device__ __forceinline__ uint4 hadd8(uint4 x, uint4 b) {
+  auto add = [](uint32_t u, uint32_t v) {
+    __half2 r = __hadd2(*reinterpret_cast<const __half2*>(&u), *reinterpret_cast<const __half2*>(&v));
+    return *reinterpret_cast<uint32_t*>(&r);
+  };
+  return make_uint4(add(x.x, b.x), add(x.y, b.y), add(x.z, b.z), add(x.w, b.w));
+}
+
 // RoPE pair rotation shared by every RoPE path (the fused bias+RoPE+KV
 // kernel, rope_inplace, the QKV GEMM epilogue) so that they agree bit for bit:
 // y1 = x1*c - x2*s, y2 = x2*c + x1*s, each as one fp32 product and one FMA.
@@ -205,6 +227,13 @@ __device__ __forceinline__ unsigned long long f32x2_pack(float lo, float hi) {
 
 __device__ __forceinline__ void f32x2_unpack(unsigned long long v, float& lo, float& hi) {
   asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+
+// Two fp32 products (round to nearest) in one packed multiply.
+__device__ __forceinline__ unsigned long long f32x2_mul(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
 }
 
 __device__ __forceinline__ void rope_rotate8_x2(const float (&x1)[8], const float (&x2)[8], const float (&c)[8],

@@ -33,36 +33,6 @@ namespace {
 constexpr int kThreads = 256;      // largest CTA (generic path, widest rows)
 constexpr int kFastThreads = 128;  // CTA of the fast path unless a row needs more
 
-// Eight weights starting at element `col` of the weight vector (shared or
-// global memory, generic loads).
-template <typename TW>
-struct WeightVec;
-
-template <>
-struct WeightVec<__half> {
-  __device__ __forceinline__ static void load(const __half* w, int col, float (&out)[8]) {
-    const uint4 v = *reinterpret_cast<const uint4*>(w + col);
-    const float2 a = h2_to_f2(v.x), b = h2_to_f2(v.y), c = h2_to_f2(v.z), d = h2_to_f2(v.w);
-    out[0] = a.x; out[1] = a.y; out[2] = b.x; out[3] = b.y;
-    out[4] = c.x; out[5] = c.y; out[6] = d.x; out[7] = d.y;
-  }
-};
-
-template <>
-struct WeightVec<float> {
-  __device__ __forceinline__ static void load(const float* w, int col, float (&out)[8]) {
-    const float4 a = *reinterpret_cast<const float4*>(w + col);
-    const float4 b = *reinterpret_cast<const float4*>(w + col + 4);
-    out[0] = a.x; out[1] = a.y; out[2] = a.z; out[3] = a.w;
-    out[4] = b.x; out[5] = b.y; out[6] = b.z; out[7] = b.w;
-  }
-};
-
-__device__ __forceinline__ float sumsq_h2(uint32_t w) {
-  const float2 f = h2_to_f2(w);
-  return f.x * f.x + f.y * f.y;
-}
-
 // Where a row comes from and what is stored besides the normed output.
 enum NormMode : int {
   kPlain = 0,     // r = residual row (read only)
@@ -70,6 +40,24 @@ enum NormMode : int {
   kGather = 2,    // r = table[ids[row]] (`src` is the table), stored as the residual
   kAddSelect = 3, // kAddDelta, and each sequence's last row also written to last_rows
 };
+
+// Converts the kWv weight values of one 16-byte vector (8 fp16 or 4 fp32) to
+// fp32 and stores them at dst.
+template <typename TW>
+__device__ __forceinline__ void store_weight_f32(float* dst, uint4 v);
+
+template <>
+__device__ __forceinline__ void store_weight_f32<__half>(float* dst, uint4 v) {
+  float f[8];
+  unpack8(v, f);
+  reinterpret_cast<float4*>(dst)[0] = make_float4(f[0], f[1], f[2], f[3]);
+  reinterpret_cast<float4*>(dst)[1] = make_float4(f[4], f[5], f[6], f[7]);
+}
+
+template <>
+__device__ __forceinline__ void store_weight_f32<float>(float* dst, uint4 v) {
+  reinterpret_cast<uint4*>(dst)[0] = v;
+}
 
 template <int VPT, typename TW, int MODE, bool EARLY>
 __global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __restrict__ residual,
@@ -83,21 +71,19 @@ __global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __re
   constexpr bool HAS_DELTA = MODE == kAddDelta || MODE == kAddSelect;
   constexpr bool GATHER = MODE == kGather;
   constexpr bool SELECT = MODE == kAddSelect;
-  extern __shared__ __align__(16) unsigned char s_raw[];
+  constexpr int kWv = 16 / static_cast<int>(sizeof(TW));  // weight values per 16-byte vector
+  extern __shared__ __align__(16) float s_w[];             // the norm weight as fp32, hidden values
   __shared__ float partial[2][kThreads / 32];
-  // The norm weight is staged into shared memory once per CTA and the
-  // output phase reads it from there. With EARLY (the PDL launch of the chain
-  // executor) the staging runs before the grid-dependency wait, overlapping
-  // the previous kernel's tail (no chain kernel writes the weight).
+  // The norm weight is staged into shared memory as fp32 once per CTA and
+  // the output phase reads it from there. With EARLY (the PDL launch of the
+  // chain executor) the staging runs before the grid-dependency wait,
+  // overlapping the previous kernel's tail (no chain kernel writes the weight).
+  const int wvec = hidden / kWv;
   auto stage_weight = [&]() {
-    const int wvec = static_cast<int>(hidden * sizeof(TW) / 16);  // NOLINT(shadow)
     const uint4* wsrc = reinterpret_cast<const uint4*>(weight);
-    uint4* wdst = reinterpret_cast<uint4*>(s_raw);
-    for (int i = threadIdx.x; i < wvec; i += blockDim.x) wdst[i] = ld_keep(wsrc + i);
+    for (int i = threadIdx.x; i < wvec; i += blockDim.x) store_weight_f32<TW>(s_w + i * kWv, ld_keep(wsrc + i));
     __syncthreads();
   };
-  const TW* w_src = reinterpret_cast<const TW*>(s_raw);
-  const int wvec = static_cast<int>(hidden * sizeof(TW) / 16);
   // Without PDL, a weight that fits one 16-byte vector per thread is loaded
   // into a register first and parked in shared memory after the first row
   // loads are issued, so the two round trips overlap; wider weights are
@@ -132,7 +118,6 @@ __global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __re
     const bool live = row < rows;
     __half* rrow = residual + row * hidden;
     uint4 r[VPT], d[VPT];
-    float ss = 0.0f;
     bool id_ok = true;
     if (live) {
       const __half* rsrc = rrow;
@@ -171,24 +156,28 @@ __global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __re
     // `staged` and the loop trip count are uniform over the CTA, so every
     // thread reaches this barrier.
     if (!staged) {
-      if (static_cast<int>(threadIdx.x) < wvec) reinterpret_cast<uint4*>(s_raw)[threadIdx.x] = wreg;
+      if (static_cast<int>(threadIdx.x) < wvec) store_weight_f32<TW>(s_w + threadIdx.x * kWv, wreg);
       __syncthreads();
       staged = true;
     }
+    // the rounded row stays packed in r (four registers per 16-byte vector);
+    // it is unpacked for the sum of squares and again for the output
+    float ss = 0.0f;
     if (live) {
 #pragma unroll
       for (int j = 0; j < VPT; ++j) {
         const int v = j * group + lane_g;
         if (v < nvec) {
-          if (HAS_DELTA) {
-            const float2 a0 = h2_to_f2(r[j].x), a1 = h2_to_f2(r[j].y), a2 = h2_to_f2(r[j].z), a3 = h2_to_f2(r[j].w);
-            const float2 b0 = h2_to_f2(d[j].x), b1 = h2_to_f2(d[j].y), b2 = h2_to_f2(d[j].z), b3 = h2_to_f2(d[j].w);
-            r[j] = make_uint4(f2_to_h2(a0.x + b0.x, a0.y + b0.y), f2_to_h2(a1.x + b1.x, a1.y + b1.y),
-                              f2_to_h2(a2.x + b2.x, a2.y + b2.y), f2_to_h2(a3.x + b3.x, a3.y + b3.y));
-            st_plain(rrow + v * 8, r[j]);
-          }
-          if (GATHER) st_plain(rrow + v * 8, r[j]);
-          ss += sumsq_h2(r[j].x) + sumsq_h2(r[j].y) + sumsq_h2(r[j].z) + sumsq_h2(r[j].w);
+          // r = fp16(residual + delta): the rounded sum the reference's fp16
+          // add_inplace stores (HADD2 equals the fp32 sum rounded to fp16)
+          if (HAS_DELTA) r[j] = hadd8(r[j], d[j]);
+          if (HAS_DELTA || GATHER) st_plain(rrow + v * 8, r[j]);
+          float f[8];
+          unpack8(r[j], f);
+          float sj = 0.0f;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) sj = fmaf(f[i], f[i], sj);
+          ss += sj;
         }
       }
     }
@@ -205,6 +194,7 @@ __global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __re
     }
     if (live) {
       const float scale = rsqrtf(ss * inv_h + eps);
+      const unsigned long long scale2 = f32x2_pack(scale, scale);
       __half* orow = out + row * hidden;
       // the last row of each sequence of seq_len rows also goes to last_rows
       // (select_last_rows fused into the final norm)
@@ -217,13 +207,22 @@ __global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __re
       for (int j = 0; j < VPT; ++j) {
         const int v = j * group + lane_g;
         if (v < nvec) {
-          float w[8];
-          WeightVec<TW>::load(w_src, v * 8, w);
-          const float2 a0 = h2_to_f2(r[j].x), a1 = h2_to_f2(r[j].y), a2 = h2_to_f2(r[j].z), a3 = h2_to_f2(r[j].w);
-          const uint4 y = make_uint4(f2_to_h2(a0.x * scale * w[0], a0.y * scale * w[1]),
-                                     f2_to_h2(a1.x * scale * w[2], a1.y * scale * w[3]),
-                                     f2_to_h2(a2.x * scale * w[4], a2.y * scale * w[5]),
-                                     f2_to_h2(a3.x * scale * w[6], a3.y * scale * w[7]));
+          const float4* wp = reinterpret_cast<const float4*>(s_w + v * 8);
+          const float4 w0 = wp[0], w1 = wp[1];
+          const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+          float x[8];
+          unpack8(r[j], x);
+          // y = (x * scale) * w, two roundings per element as the reference
+          // evaluates it, two elements per packed multiply
+          uint32_t h[4];
+#pragma unroll
+          for (int i = 0; i < 8; i += 2) {
+            const unsigned long long xs = f32x2_mul(f32x2_pack(x[i], x[i + 1]), scale2);
+            float y0, y1;
+            f32x2_unpack(f32x2_mul(xs, f32x2_pack(w[i], w[i + 1])), y0, y1);
+            h[i / 2] = f2_to_h2(y0, y1);
+          }
+          const uint4 y = make_uint4(h[0], h[1], h[2], h[3]);
           st_plain(orow + v * 8, y);
           if (SELECT && lrow != nullptr) st_plain(lrow + v * 8, y);
         }
@@ -305,7 +304,7 @@ int launch_fast(void* residual, const void* src, const void* weight, void* out, 
   auto k = o.pdl ? add_rms_norm_f16_kernel<VPT, TW, MODE, true> : add_rms_norm_f16_kernel<VPT, TW, MODE, false>;
   const int threads = group > kFastThreads ? group : kFastThreads;
   const int rows_per_cta = threads / group;
-  const size_t smem = static_cast<size_t>(hidden) * sizeof(TW);
+  const size_t smem = static_cast<size_t>(hidden) * sizeof(float);  // the weight staged as fp32
   const cudaError_t attr = allow_smem(reinterpret_cast<const void*>(k), smem);
   if (attr != cudaSuccess) return launch_status(attr, what);
   const unsigned grid = persistent_grid(k, threads, smem, rows_per_cta, rows);

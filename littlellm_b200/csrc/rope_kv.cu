@@ -60,14 +60,6 @@ __device__ __forceinline__ void load_bias8(const float* p, int64_t off, float (&
   b[0] = x.x; b[1] = x.y; b[2] = x.z; b[3] = x.w; b[4] = y.x; b[5] = y.y; b[6] = y.z; b[7] = y.w;
 }
 
-__device__ __forceinline__ void unpack8(uint4 v, float (&f)[8]) {
-  const float2 a = h2_to_f2(v.x), b = h2_to_f2(v.y), c = h2_to_f2(v.z), d = h2_to_f2(v.w);
-  f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y; f[4] = c.x; f[5] = c.y; f[6] = d.x; f[7] = d.y;
-}
-
-__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
-  return make_uint4(f2_to_h2(f[0], f[1]), f2_to_h2(f[2], f[3]), f2_to_h2(f[4], f[5]), f2_to_h2(f[6], f[7]));
-}
 
 // fp16(x + b) for 8 lanes, b at element `off` of a bias vector (shared or
 // global memory): the fp32 sum rounded to nearest even, which is what the
@@ -77,15 +69,6 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
 // (double rounding through such a format is innocuous for addition).
 template <typename TB>
 __device__ __forceinline__ uint4 add_bias8(uint4 x, const TB* bias, int off);
-
-// fp16(x + b) for 8 packed fp16 lanes (four HADD2).
-__device__ __forceinline__ uint4 hadd8(uint4 x, uint4 b) {
-  auto add = [](uint32_t u, uint32_t v) {
-    __half2 r = __hadd2(*reinterpret_cast<const __half2*>(&u), *reinterpret_cast<const __half2*>(&v));
-    return *reinterpret_cast<uint32_t*>(&r);
-  };
-  return make_uint4(add(x.x, b.x), add(x.y, b.y), add(x.z, b.z), add(x.w, b.w));
-}
 
 template <>
 __device__ __forceinline__ uint4 add_bias8<__half>(uint4 x, const __half* bias, int off) {
