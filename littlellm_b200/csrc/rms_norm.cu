@@ -59,12 +59,16 @@ __device__ __forceinline__ void store_weight_f32<float>(float* dst, uint4 v) {
   reinterpret_cast<uint4*>(dst)[0] = v;
 }
 
-template <int VPT, typename TW, int MODE, bool EARLY>
+// GROUP and NVEC are the row group's threads and the row's 16-byte vectors
+// when they are compile-time constants (the served hidden sizes: the
+// per-vector bounds checks and the reduction loop then resolve at compile
+// time), 0 when they come from the arguments.
+template <int VPT, int GROUP, int NVEC, typename TW, int MODE, bool EARLY>
 __global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __restrict__ residual,
                                                                     const __half* __restrict__ src,
                                                                     const TW* __restrict__ weight,
                                                                     __half* __restrict__ out, int64_t rows,
-                                                                    int hidden, int group, float eps,
+                                                                    int hidden, int group_arg, float eps,
                                                                     const int32_t* __restrict__ ids, int64_t vocab,
                                                                     int32_t* err_flags, int early_residual,
                                                                     __half* __restrict__ last_rows, int64_t seq_len) {
@@ -103,7 +107,8 @@ __global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __re
   }
   bool staged = !park;
 
-  const int nvec = hidden >> 3;
+  const int nvec = NVEC != 0 ? NVEC : hidden >> 3;
+  const int group = GROUP != 0 ? GROUP : group_arg;
   const int rows_per_cta = blockDim.x / group;
   const int lane_g = threadIdx.x % group;          // position inside the row group
   const int row_in_cta = threadIdx.x / group;
@@ -184,7 +189,10 @@ __global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __re
     // Reduce over the row group: shuffles inside the warp, then (groups
     // wider than a warp) one exchange of per-warp partials in shared memory.
     const int sub = group < 32 ? group : 32;
-    for (int m = sub >> 1; m > 0; m >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) {
+      if (m < sub) ss += __shfl_xor_sync(0xffffffffu, ss, m);
+    }
     if (warps_per_group > 1) {
       if ((threadIdx.x & 31) == 0) partial[parity][warp] = ss;
       __syncthreads();
@@ -298,10 +306,11 @@ struct GatherArgs {
   int64_t seq_len = 1;
 };
 
-template <int VPT, typename TW, int MODE>
+template <int VPT, int GROUP, int NVEC, typename TW, int MODE>
 int launch_fast(void* residual, const void* src, const void* weight, void* out, int64_t rows, int hidden,
                 int group, float eps, const GatherArgs& ga, const LaunchOpts& o, const char* what) {
-  auto k = o.pdl ? add_rms_norm_f16_kernel<VPT, TW, MODE, true> : add_rms_norm_f16_kernel<VPT, TW, MODE, false>;
+  auto k = o.pdl ? add_rms_norm_f16_kernel<VPT, GROUP, NVEC, TW, MODE, true>
+                 : add_rms_norm_f16_kernel<VPT, GROUP, NVEC, TW, MODE, false>;
   const int threads = group > kFastThreads ? group : kFastThreads;
   const int rows_per_cta = threads / group;
   const size_t smem = static_cast<size_t>(hidden) * sizeof(float);  // the weight staged as fp32
@@ -315,23 +324,38 @@ int launch_fast(void* residual, const void* src, const void* weight, void* out, 
                        what);
 }
 
-template <int VPT, typename TW>
-int launch_fast_d(int mode, void* residual, const void* src, const void* weight, void* out, int64_t rows,
+template <int VPT, int GROUP, int NVEC, typename TW>
+int launch_fast_m(int mode, void* residual, const void* src, const void* weight, void* out, int64_t rows,
                   int hidden, int group, float eps, const GatherArgs& ga, const LaunchOpts& o) {
   switch (mode) {
     case kAddDelta:
-      return launch_fast<VPT, TW, kAddDelta>(residual, src, weight, out, rows, hidden, group, eps, ga, o,
-                                             "add_rms_norm");
+      return launch_fast<VPT, GROUP, NVEC, TW, kAddDelta>(residual, src, weight, out, rows, hidden, group, eps, ga,
+                                                          o, "add_rms_norm");
     case kGather:
-      return launch_fast<VPT, TW, kGather>(residual, src, weight, out, rows, hidden, group, eps, ga, o,
-                                           "embedding_rms_norm");
+      return launch_fast<VPT, GROUP, NVEC, TW, kGather>(residual, src, weight, out, rows, hidden, group, eps, ga,
+                                                        o, "embedding_rms_norm");
     case kAddSelect:
-      return launch_fast<VPT, TW, kAddSelect>(residual, src, weight, out, rows, hidden, group, eps, ga, o,
-                                              "add_rms_norm_last_rows");
+      return launch_fast<VPT, GROUP, NVEC, TW, kAddSelect>(residual, src, weight, out, rows, hidden, group, eps,
+                                                           ga, o, "add_rms_norm_last_rows");
     default:
-      return launch_fast<VPT, TW, kPlain>(residual, src, weight, out, rows, hidden, group, eps, ga, o,
-                                          "add_rms_norm");
+      return launch_fast<VPT, GROUP, NVEC, TW, kPlain>(residual, src, weight, out, rows, hidden, group, eps, ga, o,
+                                                       "add_rms_norm");
   }
+}
+
+// Runtime geometry, or the compile-time one of a served hidden size:
+// 896 (Qwen2.5-0.5B: one warp per row, 4 vectors per lane, 112 in the row)
+// and 4096 (Llama-2-7B: 128 threads per row, 4 vectors per lane).
+template <int VPT, typename TW>
+int launch_fast_d(int mode, void* residual, const void* src, const void* weight, void* out, int64_t rows,
+                  int hidden, int group, float eps, const GatherArgs& ga, const LaunchOpts& o) {
+  if (VPT == 4 && group == 32 && hidden == 896) {
+    return launch_fast_m<4, 32, 112, TW>(mode, residual, src, weight, out, rows, hidden, group, eps, ga, o);
+  }
+  if (VPT == 4 && group == 128 && hidden == 4096) {
+    return launch_fast_m<4, 128, 512, TW>(mode, residual, src, weight, out, rows, hidden, group, eps, ga, o);
+  }
+  return launch_fast_m<VPT, 0, 0, TW>(mode, residual, src, weight, out, rows, hidden, group, eps, ga, o);
 }
 
 template <typename TW>
