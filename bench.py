@@ -2031,7 +2031,9 @@ def time_oracle_forward(r, seconds: float) -> dict:
 def run_e2e(runner, stream, steps: int, device, dist, world: int) -> dict:
     """tokens/s through the C ABI with host buffers: every step copies its
     inputs (ids, positions, slots, each layer's GEMM outputs) from pinned host
-    memory, runs the chain and copies the result (last rows) back."""
+    memory, runs the chain and copies the result (last rows) back. (Spreading
+    the copies over four streams measured no faster: the host link is the
+    bound.)"""
     import torch
     inputs = runner.step_inputs()
     hosts = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in inputs]

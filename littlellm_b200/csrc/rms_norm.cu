@@ -41,22 +41,24 @@ enum NormMode : int {
   kAddSelect = 3, // kAddDelta, and each sequence's last row also written to last_rows
 };
 
-// Converts the kWv weight values of one 16-byte vector (8 fp16 or 4 fp32) to
-// fp32 and stores them at dst.
+// Stages weight vector i (16 bytes: 8 fp16 or 4 fp32 values) as fp32 into
+// two planes of float4: plane 0 holds values 0-3 and plane 1 values 4-7 of
+// every 8-value group, so the output phase's two 16-byte reads per group are
+// both consecutive across the lanes of a warp (no bank conflicts).
 template <typename TW>
-__device__ __forceinline__ void store_weight_f32(float* dst, uint4 v);
+__device__ __forceinline__ void stage_weight_vec(float4* planes, int ngroups, int i, uint4 v);
 
 template <>
-__device__ __forceinline__ void store_weight_f32<__half>(float* dst, uint4 v) {
+__device__ __forceinline__ void stage_weight_vec<__half>(float4* planes, int ngroups, int i, uint4 v) {
   float f[8];
   unpack8(v, f);
-  reinterpret_cast<float4*>(dst)[0] = make_float4(f[0], f[1], f[2], f[3]);
-  reinterpret_cast<float4*>(dst)[1] = make_float4(f[4], f[5], f[6], f[7]);
+  planes[i] = make_float4(f[0], f[1], f[2], f[3]);
+  planes[ngroups + i] = make_float4(f[4], f[5], f[6], f[7]);
 }
 
 template <>
-__device__ __forceinline__ void store_weight_f32<float>(float* dst, uint4 v) {
-  reinterpret_cast<uint4*>(dst)[0] = v;
+__device__ __forceinline__ void stage_weight_vec<float>(float4* planes, int ngroups, int i, uint4 v) {
+  planes[(i & 1) * ngroups + (i >> 1)] = *reinterpret_cast<const float4*>(&v);
 }
 
 // GROUP and NVEC are the row group's threads and the row's 16-byte vectors
@@ -76,16 +78,17 @@ __global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __re
   constexpr bool GATHER = MODE == kGather;
   constexpr bool SELECT = MODE == kAddSelect;
   constexpr int kWv = 16 / static_cast<int>(sizeof(TW));  // weight values per 16-byte vector
-  extern __shared__ __align__(16) float s_w[];             // the norm weight as fp32, hidden values
+  extern __shared__ __align__(16) float4 s_w4[];          // the norm weight as fp32, two planes
   __shared__ float partial[2][kThreads / 32];
   // The norm weight is staged into shared memory as fp32 once per CTA and
   // the output phase reads it from there. With EARLY (the PDL launch of the
   // chain executor) the staging runs before the grid-dependency wait,
   // overlapping the previous kernel's tail (no chain kernel writes the weight).
   const int wvec = hidden / kWv;
+  const int wgroups = hidden >> 3;
   auto stage_weight = [&]() {
     const uint4* wsrc = reinterpret_cast<const uint4*>(weight);
-    for (int i = threadIdx.x; i < wvec; i += blockDim.x) store_weight_f32<TW>(s_w + i * kWv, ld_keep(wsrc + i));
+    for (int i = threadIdx.x; i < wvec; i += blockDim.x) stage_weight_vec<TW>(s_w4, wgroups, i, ld_keep(wsrc + i));
     __syncthreads();
   };
   // Without PDL, a weight that fits one 16-byte vector per thread is loaded
@@ -161,7 +164,7 @@ __global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __re
     // `staged` and the loop trip count are uniform over the CTA, so every
     // thread reaches this barrier.
     if (!staged) {
-      if (static_cast<int>(threadIdx.x) < wvec) store_weight_f32<TW>(s_w + threadIdx.x * kWv, wreg);
+      if (static_cast<int>(threadIdx.x) < wvec) stage_weight_vec<TW>(s_w4, wgroups, threadIdx.x, wreg);
       __syncthreads();
       staged = true;
     }
@@ -215,8 +218,7 @@ __global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __re
       for (int j = 0; j < VPT; ++j) {
         const int v = j * group + lane_g;
         if (v < nvec) {
-          const float4* wp = reinterpret_cast<const float4*>(s_w + v * 8);
-          const float4 w0 = wp[0], w1 = wp[1];
+          const float4 w0 = s_w4[v], w1 = s_w4[wgroups + v];
           const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
           float x[8];
           unpack8(r[j], x);
