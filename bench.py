@@ -449,12 +449,19 @@ def per_op_timing(runner, stream, reps: int) -> dict:
         for layer in L:
             ops.silu_mul(layer["gate"], layer["up"], out=layer["swiglu_out"])
 
+    def select():
+        # the last row of every sequence, from each layer's own T x H buffer
+        for layer in L:
+            ops.select_last_rows(layer["ffn_norm_out"], seq_len=w.seq_len, n_seqs=w.n_seqs,
+                                 out=layer["attn_norm_out"][:w.n_seqs])
+
     qkv_bytes = 2 * T * (m.n_heads + 2 * m.n_kv_heads) * D * 2 + 8 * T
     table = {
         "embedding": (embed, 2 * T * H * 2 + 4 * T),
         "add_rms_norm": (norm, 4 * T * H * 2),
         "qkv_bias_rope_kv_append": (qkv, qkv_bytes),
         "silu_mul": (silu, 3 * T * m.intermediate * 2),
+        "select_last_rows": (select, 2 * w.n_seqs * H * 2),
     }
     out = {}
     with torch.cuda.stream(stream):
@@ -1366,7 +1373,13 @@ def ref_cuda_ops(w, n_layers: int, dequant_shape=None, timeout: float = 900.0) -
 
 
 def merge_ref_cuda(ops_table: dict, ref: dict, field: str = "ref_cuda_us") -> None:
-    """Adds the reference CUDA time of each op and our speed-up over it."""
+    """Adds the reference CUDA time of each op and our speed-up over it. The
+    fused embedding + input norm compares with the reference's embedding
+    followed by its plain rms_norm."""
+    ref = dict(ref)
+    if "embedding" in ref and "rms_norm" in ref:
+        ref["embedding_input_norm"] = {"us": ref["embedding"]["us"] + ref["rms_norm"]["us"],
+                                       "launches": ref["embedding"]["launches"] + ref["rms_norm"]["launches"]}
     for name, v in ops_table.items():
         r = ref.get(name)
         if isinstance(r, dict) and "us" in r and v.get("us_per_launch"):

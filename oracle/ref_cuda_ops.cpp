@@ -9,6 +9,7 @@
 //
 //   embedding      cuda_embedding(table, ids, out)                  (:84)
 //   add_rms_norm   cuda_add_inplace(r, delta); cuda_rms_norm(r, w)  (:135-143, :166 -> :83)
+//   rms_norm       cuda_rms_norm(r, w) alone (layer 0's input norm, :83)
 //   qkv_rope_kv    cuda_add_bias_inplace x3; cuda_rope_inplace x2;
 //                  cuda_copy_kv_to_cache                             (:89-114)
 //   silu_mul       cuda_silu_mul(gate, up, out)                      (:158)
@@ -177,6 +178,14 @@ int main(int argc, char** argv) {
       }
     });
     std::printf("add_rms_norm %.4f 2\n", us);
+
+    us = tm.us_per_group(reps, layers, [&] {
+      for (int l = 0; l < layers; ++l) {
+        Set& s = *S[l % sets];
+        kllm::op::cuda_rms_norm(s.residual, s.norm_w, s.norm_out, eps);
+      }
+    });
+    std::printf("rms_norm %.4f 1\n", us);
 
     us = tm.us_per_group(reps, layers, [&] {
       for (int l = 0; l < layers; ++l) {
