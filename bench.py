@@ -411,9 +411,22 @@ def capture(fn, stream):
     return g
 
 
-def per_op_timing(runner, stream, reps: int) -> dict:
-    """Each op kind timed alone: one graph of that op over all layers' buffers
-    (several GB, larger than L2), replayed `reps` times."""
+def per_op_timing(runner, stream, reps: int, pdl: bool = False) -> dict:
+    """Each op kind timed alone: one graph of that op's C-ABI entry over all
+    layers' buffers (several GB, larger than L2), replayed `reps` times. With
+    `pdl` the entries launch with programmatic dependent launch
+    (kllm_b200_set_pdl), as a runner calling them one by one can ask for."""
+    import torch
+
+    from littlellm_b200 import ops
+    prev = ops.set_pdl(pdl)
+    try:
+        return _per_op_timing(runner, stream, reps)
+    finally:
+        ops.set_pdl(prev)
+
+
+def _per_op_timing(runner, stream, reps: int) -> dict:
     import torch
 
     from littlellm_b200 import ops
@@ -1507,8 +1520,10 @@ def measure_chain(w, args, device, dist, *, seed: int, steps: int, warmup: int, 
         stats["ops"] = op_chain
         if standalone:
             op_alone = per_op_timing(runner, stream, max(steps, 5))
-            tables.append(op_alone)
+            op_alone_pdl = per_op_timing(runner, stream, max(steps, 5), pdl=True)
+            tables += [op_alone, op_alone_pdl]
             stats["ops_standalone"] = op_alone
+            stats["ops_standalone_pdl"] = op_alone_pdl
         for table in tables:
             for v in table.values():
                 v["frac_of_measured"] = v["gbs"] / peaks["hbm_gbs"]
@@ -1616,6 +1631,7 @@ def run_ours(args):
         ref = ref_cuda_ops(w, n_layers)
         merge_ref_cuda(op_chain, ref)
         merge_ref_cuda(st.get("ops_standalone", {}), ref)
+        merge_ref_cuda(st.get("ops_standalone_pdl", {}), ref)
         st["ref_cuda"] = ref
 
     # the survey's other configurations, each its own graph and clock record:
@@ -1650,6 +1666,7 @@ def run_ours(args):
                 ref = ref_cuda_ops(ws, nl, dequant_shape=(11008, 4096) if name == "llama_prefill" else None)
                 merge_ref_cuda(s2["ops"], ref)
                 merge_ref_cuda(s2.get("ops_standalone", {}), ref)
+                merge_ref_cuda(s2.get("ops_standalone_pdl", {}), ref)
                 s2["ref_cuda"] = ref
             other[name] = s2
         if single:
@@ -1696,6 +1713,7 @@ def run_ours(args):
             "roofline": roofline,
             "ops": op_chain,
             "ops_standalone": st.get("ops_standalone"),
+            "ops_standalone_pdl": st.get("ops_standalone_pdl"),
             "ref_cuda": st.get("ref_cuda"),
             "clocks": st["clocks"],
             "gpu_launches": launches * args.steps,

@@ -75,6 +75,22 @@ const char* kllm_b200_status_string(int status);
 /* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
 int kllm_b200_version(void);
 
+/* Launch mode of the individual operator entry points, for the calling host
+ * thread (default off; kllm_b200_chain_run follows its descriptor's use_pdl
+ * instead, and the .kllm loader and the no-allocation dequant never use it).
+ * With enable != 0 the entry points launch with programmatic dependent launch,
+ * as the chain does: a kernel's CTAs may be scheduled while the previous
+ * kernel on the stream drains, and before their grid-dependency wait they
+ * read the inputs no kernel of this library writes (norm weights, q/k/v
+ * biases, positions, cache slots, embedding tables and ids). That is correct
+ * when no earlier kernel on the stream that triggers its dependents early
+ * (griddepcontrol.launch_dependents) writes those inputs; this library's own
+ * kernels trigger only after their own wait. A runner that calls the
+ * operators one by one (the C++ binding of LittleLLM's kllm::op::cuda_*)
+ * gets the chain's overlap between consecutive operators. Returns the
+ * previous mode. No reference counterpart (launch configuration only). */
+int kllm_b200_set_pdl(int enable);
+
 /* ======================================================================== *
  *  Reference-compatible operators (same semantics as kllm::op::cuda_*)      *
  * ======================================================================== */

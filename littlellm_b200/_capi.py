@@ -90,6 +90,7 @@ SIGNATURES = {
     "kllm_b200_last_error": [ctypes.c_char_p, ctypes.c_size_t],
     "kllm_b200_status_string": [_int],
     "kllm_b200_version": [],
+    "kllm_b200_set_pdl": [_int],
     "kllm_b200_embedding": [_vp, _i64, _i64, _int, _vp, _i64, _vp, _int, _vp, _vp],
     "kllm_b200_embedding_host_ids": [_vp, _i64, _i64, _int, _vp, _i64, _vp, _int, _vp, _vp],
     "kllm_b200_embedding_rms_norm": [_vp, _i64, _i64, _vp, _i64, _vp, _int, _f32, _vp, _vp, _vp, _vp],

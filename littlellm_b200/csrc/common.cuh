@@ -111,10 +111,14 @@ cudaError_t launch_clustered(void (*kernel)(KArgs...), dim3 grid, dim3 block, si
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
+// Whether the calling thread asked the individual entry points to launch
+// with programmatic dependent launch (kllm_b200_set_pdl).
+bool default_pdl();
+
 // Launch options shared by the individual entry points and the chain runner.
 struct LaunchOpts {
   cudaStream_t stream = nullptr;
-  bool pdl = false;
+  bool pdl = default_pdl();
   // add_rms_norm under PDL: the residual was last written two or more
   // launches back on this stream (the previous launch leaves it alone), so
   // its rows may be read before the grid-dependency wait. Every kernel of

@@ -68,6 +68,7 @@ extern "C" int kllm_b200_dequantize_int8_host_static(const int8_t* host_data, fl
   int rc = staging_address(&staging);
   if (rc != KLLM_B200_OK) return rc;
   LaunchOpts o;
+  o.pdl = false;  // the kernels follow host-to-device copies on the stream
   o.stream = static_cast<cudaStream_t>(stream);
   const cudaError_t err = cudaMemcpyAsync(staging, host_data, static_cast<size_t>(n), cudaMemcpyHostToDevice, o.stream);
   if (err != cudaSuccess) return launch_status(err, "dequantize_int8_host_static: copy to the staging area");

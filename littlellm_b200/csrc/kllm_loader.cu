@@ -191,6 +191,7 @@ extern "C" int kllm_b200_kllm_load(const char* path, const kllm_b200_kllm_record
     }
   }
   LaunchOpts o;
+  o.pdl = false;  // the kernels follow host-to-device copies on the stream
   o.stream = s;
   int rc = KLLM_B200_OK;
   int k = 0;  // chunk counter selects the staging half

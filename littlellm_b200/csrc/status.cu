@@ -155,3 +155,16 @@ extern "C" const char* kllm_b200_status_string(int status) {
 }
 
 extern "C" int kllm_b200_version(void) { return 100; }
+
+namespace kb {
+namespace {
+thread_local bool g_default_pdl = false;  // see kllm_b200_set_pdl
+}  // namespace
+bool default_pdl() { return g_default_pdl; }
+}  // namespace kb
+
+extern "C" int kllm_b200_set_pdl(int enable) {
+  const int previous = kb::g_default_pdl ? 1 : 0;
+  kb::g_default_pdl = enable != 0;
+  return previous;
+}

@@ -56,6 +56,14 @@ def _stream(device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+def set_pdl(enable: bool) -> bool:
+    """Launch mode of the individual entry points for this host thread
+    (kllm_b200_set_pdl): programmatic dependent launch with the inputs no
+    kernel of the library writes read before the dependency wait. Returns the
+    previous mode."""
+    return bool(lib.kllm_b200_set_pdl(1 if enable else 0))
+
+
 def embedding(table: torch.Tensor, ids: torch.Tensor, out: torch.Tensor | None = None,
               err_flags: torch.Tensor | None = None) -> torch.Tensor:
     """out[t] = table[ids[t]] (reference embedding, ids on the device)."""

@@ -281,3 +281,16 @@ def test_qkv_rope_linear_validation_without_gpu(capi):
     assert call(bias=p, bias_dtype=capi.I8) == capi.ERR_DTYPE
     assert call(n_tokens=-1) == capi.ERR_INVALID_ARG
     assert call(n_tokens=0) == capi.OK
+
+
+def test_set_pdl_is_per_thread_and_returns_previous(capi):
+    import threading
+    lib = capi.lib
+    assert lib.kllm_b200_set_pdl(1) == 0
+    assert lib.kllm_b200_set_pdl(1) == 1
+    seen = []
+    t = threading.Thread(target=lambda: seen.append(lib.kllm_b200_set_pdl(0)))
+    t.start()
+    t.join()
+    assert seen == [0]  # another thread starts from the default (off)
+    assert lib.kllm_b200_set_pdl(0) == 1
