@@ -178,6 +178,15 @@ __device__ __forceinline__ void st_plain(void* p, uint4 v) {
   *reinterpret_cast<uint4*>(p) = v;
 }
 
+// 32-byte store of two 16-byte vectors (sm_100; `p` 32-byte aligned).
+__device__ __forceinline__ void st_plain32(void* p, uint4 lo, uint4 hi) {
+  asm volatile("st.global.v8.u32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(lo.x), "r"(lo.y), "r"(lo.z),
+               "r"(lo.w), "r"(hi.x), "r"(hi.y), "r"(hi.z), "r"(hi.w)
+               : "memory");
+}
+
+inline bool aligned32(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 31u) == 0; }
+
 __device__ __forceinline__ float2 h2_to_f2(uint32_t w) {
   return __half22float2(*reinterpret_cast<const __half2*>(&w));
 }

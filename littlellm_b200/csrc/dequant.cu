@@ -85,22 +85,30 @@ __global__ void __launch_bounds__(kThreads) dequant_f16_kernel(const int8_t* __r
   uint4* dst = reinterpret_cast<uint4*>(out);
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  // a thread's 16 results are 32 contiguous bytes: one 32-byte store when the
+  // output is 32-byte aligned (a warp then writes 1 KB contiguously), else two
+  const bool out32 = (reinterpret_cast<uintptr_t>(out) & 31u) == 0;
+  auto store16 = [&](int64_t v, uint4 lo, uint4 hi) {
+    if (out32) {
+      st_plain32(dst + 2 * v, lo, hi);
+    } else {
+      st_plain(dst + 2 * v, lo);
+      st_plain(dst + 2 * v + 1, hi);
+    }
+  };
   for (; i + stride < nvec; i += 2 * stride) {
     const uint4 w0 = ld_stream(src + i);
     const uint4 w1 = ld_stream(src + i + stride);
     uint4 a0, a1, b0, b1;
     lut16(my, w0, a0, a1);
     lut16(my, w1, b0, b1);
-    st_plain(dst + 2 * i, a0);
-    st_plain(dst + 2 * i + 1, a1);
-    st_plain(dst + 2 * (i + stride), b0);
-    st_plain(dst + 2 * (i + stride) + 1, b1);
+    store16(i, a0, a1);
+    store16(i + stride, b0, b1);
   }
   for (; i < nvec; i += stride) {
     uint4 a0, a1;
     lut16(my, ld_stream(src + i), a0, a1);
-    st_plain(dst + 2 * i, a0);
-    st_plain(dst + 2 * i + 1, a1);
+    store16(i, a0, a1);
   }
   if (blockIdx.x == 0) {
     unsigned short* o16 = reinterpret_cast<unsigned short*>(out);
@@ -336,6 +344,9 @@ __global__ void __launch_bounds__(kThreads) dequant_batched_kernel(const __grid_
     }
     const DequantTask& t = batch.task[ti];
     const int64_t e0 = (c - t.first_chunk) * kChunk;     // first element of this chunk
+    // e0 * 2 bytes is a multiple of 32 (kChunk is), so the chunk's output is
+    // 32-byte aligned exactly when the tensor's is
+    const bool out32 = (reinterpret_cast<uintptr_t>(t.out) & 31u) == 0;
     const int64_t e1 = e0 + kChunk < t.n ? e0 + kChunk : t.n;
     const int64_t nvec = (e1 - e0) >> 4;
     const uint4* src = reinterpret_cast<const uint4*>(t.q + e0);
@@ -353,8 +364,12 @@ __global__ void __launch_bounds__(kThreads) dequant_batched_kernel(const __grid_
         uint4 o0, o1;
         lut16(my, w[k], o0, o1);
         uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(t.out) + e0);
-        st_plain(dst + 2 * i, o0);
-        st_plain(dst + 2 * i + 1, o1);
+        if (out32) {  // uniform per task: one 32-byte store per thread, 1 KB per warp
+          st_plain32(dst + 2 * i, o0, o1);
+        } else {
+          st_plain(dst + 2 * i, o0);
+          st_plain(dst + 2 * i + 1, o1);
+        }
       } else {
         float4* dst = reinterpret_cast<float4*>(static_cast<float*>(t.out) + e0);
         const uint32_t words[4] = {w[k].x, w[k].y, w[k].z, w[k].w};
