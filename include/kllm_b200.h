@@ -434,6 +434,13 @@ typedef struct kllm_b200_chain {
  * With KLLM_B200_OP_GEMM the layer's GEMMs run in between and the step is
  * the whole forward: q, attn_out and ffn_out are then written (k and v go
  * straight into the caches).
+ * When both the embedding and the input norm run, they are one kernel
+ * (kllm_b200_embedding_rms_norm for layer 0); when both the final norm and
+ * select run and seq_ends is NULL, the final norm's kernel writes the last
+ * rows. With use_pdl, an add+RMSNorm whose previous launch left the residual
+ * alone reads the residual rows before its grid-dependency wait (they were
+ * written two or more launches back, and this library's kernels trigger their
+ * dependents only after their own wait).
  * *n_launches (if given) receives the number of kernels launched. Can be
  * captured into a CUDA graph. */
 int kllm_b200_chain_run(const kllm_b200_chain* chain, int* n_launches, void* stream);
