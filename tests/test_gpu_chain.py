@@ -30,14 +30,17 @@ def _tiny(decode: bool, shape: str = "tiny"):
     return Workload(f"{shape}_prefill", m, n_seqs=3, seq_len=17, max_seq=64, decode=False)
 
 
-@pytest.mark.parametrize("shape", ["tiny", "qwen", "llama"])
+@pytest.mark.parametrize("shape,wdt", [("tiny", "f16"), ("qwen", "f16"), ("llama", "f16"), ("qwen", "f32")])
 @pytest.mark.parametrize("decode", [False, True])
 @pytest.mark.parametrize("use_pdl", [False, True])
-def test_chain_matches_oracle(cuda, oracle, shape, decode, use_pdl):
+def test_chain_matches_oracle(cuda, oracle, shape, wdt, decode, use_pdl):
+    """fp16 activations; norm weights and q/k/v biases in fp16, or fp32 (the
+    weight dtype the reference's dispatch also accepts)."""
     from littlellm_b200.chain import ChainRunner
     w = _tiny(decode, shape)
     m = w.model
-    r = ChainRunner(w, device=cuda, seed=3, use_pdl=use_pdl)
+    r = ChainRunner(w, device=cuda, seed=3, use_pdl=use_pdl,
+                    weight_dtype=torch.float32 if wdt == "f32" else torch.float16)
     snap = [{k: host(t) for k, t in L.items()} for L in r.layers]
     table, ids = host(r.table), r.ids.cpu().numpy()
     pos, slots = r.positions.cpu().numpy(), r.slots.cpu().numpy()

@@ -173,14 +173,16 @@ def test_embedding_oracle(ops, vocab, hidden, n):
 @pytest.mark.parametrize("T,Hq,Hkv,D,theta", [(512, 14, 2, 64, 1e6), (2500, 14, 2, 64, 1e6), (48, 32, 32, 128, 1e4),
                                               (40, 28, 4, 128, 1e6), (33, 32, 8, 128, 5e5),
                                               (37, 4, 2, 16, 1e4), (9, 3, 1, 6, 1e4), (5, 2, 2, 256, 1e6)])
-@pytest.mark.parametrize("bias", [True, False])
+@pytest.mark.parametrize("bias", ["f16", "f32", "none"])
 def test_qkv_fused_oracle(ops, oracle, T, Hq, Hkv, D, theta, bias):
     rng = np.random.default_rng(T * 31 + D)
     S, NS = 4096, max(8, -(-T // 64))  # enough slots that positions stay below S
     q = f16r(rng.standard_normal((T, Hq, D)))
     k = f16r(rng.standard_normal((T, Hkv, D)))
     v = f16r(rng.standard_normal((T, Hkv, D)))
-    bq, bk, bv = ((f16r(rng.normal(0, 0.02, H * D)) for H in (Hq, Hkv, Hkv)) if bias else (None, None, None))
+    bq, bk, bv = ((f16r(rng.normal(0, 0.02, H * D)) for H in (Hq, Hkv, Hkv)) if bias != "none"
+                  else (None, None, None))
+    bdt = F32 if bias == "f32" else F16  # fp16-representable values either way
     # distinct (slot, pos) per token so the expected cache does not depend on
     # write order; positions reach S - 1
     slots = (np.arange(T) % NS).astype(np.int32)
@@ -189,8 +191,8 @@ def test_qkv_fused_oracle(ops, oracle, T, Hq, Hkv, D, theta, bias):
     qd = dev(q)
     kc = torch.zeros((NS, Hkv, S, D), dtype=F16, device="cuda:0")
     vc = torch.zeros_like(kc)
-    ops.qkv_bias_rope_kv_append(qd, dev(k), dev(v), None if bq is None else dev(bq),
-                                None if bk is None else dev(bk), None if bv is None else dev(bv),
+    ops.qkv_bias_rope_kv_append(qd, dev(k), dev(v), None if bq is None else dev(bq, bdt),
+                                None if bk is None else dev(bk, bdt), None if bv is None else dev(bv, bdt),
                                 dev(pos, torch.int32), dev(slots, torch.int32), theta, kc, vc)
     zeros = np.zeros((NS, Hkv, S, D), np.float32)
     q_ref, kc_ref, vc_ref, skipped = oracle.qkv_bias_rope_kv_append(q, k, v, bq, bk, bv, pos, slots, theta,
@@ -200,7 +202,7 @@ def test_qkv_fused_oracle(ops, oracle, T, Hq, Hkv, D, theta, bias):
     kch, vch = host(kc), host(vc)
     assert_tol(kch[slots, :, pos], kc_ref[slots, :, pos], what="k cache")
     # v rows: the fp16 (RNE) bias sum, bit-exact
-    v_exp = (v + (bv.reshape(Hkv, D) if bias else 0)).astype(np.float16)
+    v_exp = (v + (bv.reshape(Hkv, D) if bias != "none" else 0)).astype(np.float16)
     assert np.array_equal(vch[slots, :, pos].astype(np.float16).view(np.uint16), v_exp.view(np.uint16))
     # nothing else of the cache was touched
     mask = np.ones((NS, S), bool)
