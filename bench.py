@@ -2099,6 +2099,9 @@ def run_e2e(runner, stream, steps: int, device, dist, world: int) -> dict:
     ms_step = float(t.item()) / steps
     return {"value": runner.w.n_tokens * world / (ms_step * 1e-3), "unit": UNIT, "ms_per_step": ms_step,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            # the step's bytes over the host link per second of the whole step: the e2e bound when it
+            # nears the link's rate (about 55 GB/s host to device on PCIe 5.0 x16)
+            "host_link_gbs": (h2d + d2h) / (ms_step * 1e-3) / 1e9,
             "path": "pinned host -> cudaMemcpyAsync -> kllm_b200_chain_run -> last rows -> pinned host"}
 
 
