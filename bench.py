@@ -489,12 +489,6 @@ def _per_op_timing(runner, stream, reps: int) -> dict:
     return out
 
 
-LLAMA7B_INT8_TENSORS = (
-    # (rows, cols, count): q/k/v/o, gate/up, down per layer x 32, embed + lm_head
-    (4096, 4096, 4 * 32), (11008, 4096, 2 * 32), (4096, 11008, 32), (32000, 4096, 2),
-)
-
-
 def measure_dequant(device, steps: int, warmup: int, peaks: dict) -> dict:
     """INT8 -> fp16 dequant of every Llama-2-7B linear/embedding tensor
     (6.74 B parameters, int8 ~U[-127,127], fp32 scale ~U(1e-3,1e-2) per
@@ -506,10 +500,11 @@ def measure_dequant(device, steps: int, warmup: int, peaks: dict) -> dict:
     import torch
 
     from littlellm_b200 import ops
+    from littlellm_b200.workloads import LLAMA2_7B_INT8_TENSORS
     gen = torch.Generator(device=device)
     gen.manual_seed(5)
     data, scales, outs = [], [], []
-    for rows, cols, count in LLAMA7B_INT8_TENSORS:
+    for rows, cols, count in LLAMA2_7B_INT8_TENSORS:
         for _ in range(count):
             data.append(torch.randint(-127, 128, (rows, cols), generator=gen, device=device, dtype=torch.int8))
             scales.append(torch.rand((1,), generator=gen, device=device) * 9e-3 + 1e-3)

@@ -60,6 +60,12 @@ WORKLOADS = {
 }
 
 
+# The linear and embedding tensors of a Llama-2-7B checkpoint as (rows, cols,
+# count): q/k/v/o, gate/up and down of each of the 32 layers, then the
+# embedding and lm_head (6.74 B values).
+LLAMA2_7B_INT8_TENSORS = ((4096, 4096, 4 * 32), (11008, 4096, 2 * 32), (4096, 11008, 32), (32000, 4096, 2))
+
+
 def shard(workload: Workload, rank: int, world: int) -> Workload:
     """The slice of a workload one rank runs when sequences are split evenly."""
     if workload.n_seqs % world != 0:

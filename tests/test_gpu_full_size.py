@@ -8,6 +8,8 @@ eager step with programmatic dependent launch:
   layer and the cache rows each token appends.
 - Llama-2-7B prefill, 32 x 512 tokens, all 32 layers: the first and last layers
   op by op, the residual stream bit for bit through every layer.
+- INT8 -> fp16 dequant of a whole Llama-2-7B checkpoint (6.74 B values), bit
+  for bit.
 
 The oracle runs op by op in the reference's order (src/model/llama.cpp:78-178)
 with the residual stream held in fp16, as the reference's CUDA runner holds it.
@@ -144,3 +146,35 @@ def test_llama_prefill_full_size(cuda, oracle, room):
             res = f16_add(res, f32(r.layers[l]["attn_out"]))
     check_end(oracle, r, f16_add(res, f32(r.layers[-1]["ffn_out"])))
     del r, q_in
+
+
+def test_llama_int8_checkpoint_dequant_full_size(cuda, oracle, room):
+    """INT8 -> fp16 of every Llama-2-7B linear/embedding tensor (6.74 B values,
+    int8 over the whole [-128, 127], one fp32 scale per tensor) in one batched
+    launch, bit for bit: each tensor's output equals, element by element, the
+    oracle's rounding of its int8 value at that tensor's scale (the oracle run
+    on all 256 int8 values per tensor, looked up on the device). The
+    per-tensor entry on the largest tensors gives the same bits."""
+    from littlellm_b200 import ops
+    from littlellm_b200.workloads import LLAMA2_7B_INT8_TENSORS
+    gen = torch.Generator(device=cuda)
+    gen.manual_seed(11)
+    data, scales, outs = [], [], []
+    for rows, cols, count in LLAMA2_7B_INT8_TENSORS:
+        for _ in range(count):
+            data.append(torch.randint(-128, 128, (rows, cols), generator=gen, device=cuda, dtype=torch.int8))
+            scales.append(torch.rand((1,), generator=gen, device=cuda) * 9e-3 + 1e-3)
+            outs.append(torch.empty((rows, cols), dtype=torch.float16, device=cuda))
+    assert sum(d.numel() for d in data) == 6_738_149_376
+    ops.dequantize_int8_batched(data, scales, outs)
+    torch.cuda.synchronize()
+    values = np.arange(-128, 128, dtype=np.int8)
+    for i, (d, sc, o) in enumerate(zip(data, scales, outs)):
+        lut = torch.from_numpy(oracle.dequantize_int8_f16_bits(values, float(sc.item())).view(np.int16)).to(cuda)
+        assert torch.equal(o.view(torch.int16), lut[d.long() + 128]), f"tensor {i} {tuple(d.shape)}"
+    for i in (len(data) - 1, 128):  # lm_head 32000 x 4096, a gate/up 11008 x 4096
+        single = torch.empty_like(outs[i])
+        ops.dequantize_int8(data[i], scales[i], out=single)
+        torch.cuda.synchronize()
+        assert torch.equal(single.view(torch.int16), outs[i].view(torch.int16)), f"per-tensor {i}"
+    del data, scales, outs
