@@ -78,17 +78,16 @@ int kllm_b200_version(void);
 /* Launch mode of the individual operator entry points, for the calling host
  * thread (default off; kllm_b200_chain_run follows its descriptor's use_pdl
  * instead, and the .kllm loader and the no-allocation dequant never use it).
- * With enable != 0 the entry points launch with programmatic dependent launch,
- * as the chain does: a kernel's CTAs may be scheduled while the previous
- * kernel on the stream drains, and before their grid-dependency wait they
- * read the inputs no kernel of this library writes (norm weights, q/k/v
- * biases, positions, cache slots, embedding tables and ids). That is correct
- * when no earlier kernel on the stream that triggers its dependents early
- * (griddepcontrol.launch_dependents) writes those inputs; this library's own
- * kernels trigger only after their own wait. A runner that calls the
- * operators one by one (the C++ binding of LittleLLM's kllm::op::cuda_*)
- * gets the chain's overlap between consecutive operators. Returns the
- * previous mode. No reference counterpart (launch configuration only). */
+ * With enable != 0 the entry points launch with programmatic dependent launch:
+ * a kernel's CTAs may be scheduled while the previous kernel on the stream
+ * drains, and they wait for it to complete (griddepcontrol.wait) before their
+ * first global read, so the mode is correct whatever the previous kernel
+ * wrote. (Only kllm_b200_chain_run, which knows what each of its launches
+ * writes, also reads weights, biases, positions, slots, tables and ids before
+ * that wait.) A runner that calls the operators one by one (the C++ binding
+ * of LittleLLM's kllm::op::cuda_*) overlaps each operator's launch and
+ * scheduling with its predecessor's tail. Returns the previous mode. No
+ * reference counterpart (launch configuration only). */
 int kllm_b200_set_pdl(int enable);
 
 /* ======================================================================== *
@@ -437,10 +436,14 @@ typedef struct kllm_b200_chain {
  * When both the embedding and the input norm run, they are one kernel
  * (kllm_b200_embedding_rms_norm for layer 0); when both the final norm and
  * select run and seq_ends is NULL, the final norm's kernel writes the last
- * rows. With use_pdl, an add+RMSNorm whose previous launch left the residual
- * alone reads the residual rows before its grid-dependency wait (they were
- * written two or more launches back, and this library's kernels trigger their
- * dependents only after their own wait).
+ * rows. With use_pdl, every launch after the chain's first reads the inputs
+ * that no launch of the chain writes (norm weights, q/k/v biases, positions,
+ * slots, the embedding table and ids) before its grid-dependency wait, and an
+ * add+RMSNorm whose previous launch left the residual alone reads the
+ * residual rows there too (they were written two or more launches back, and
+ * this library's kernels trigger their dependents only after their own wait).
+ * The chain's first launch reads nothing before its wait, so the caller's
+ * launch before chain_run may write any of the chain's inputs.
  * *n_launches (if given) receives the number of kernels launched. Can be
  * captured into a CUDA graph. */
 int kllm_b200_chain_run(const kllm_b200_chain* chain, int* n_launches, void* stream);

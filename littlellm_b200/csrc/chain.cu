@@ -70,25 +70,34 @@ extern "C" int kllm_b200_chain_run(const kllm_b200_chain* c, int* n_launches, vo
   // launches back, and every kernel of this library triggers its dependents
   // only after its own wait. Unknown (true) before the chain's first launch.
   bool prev_wrote_residual = true;
-  auto norm_opts = [&]() {
+  int launched = 0;
+  // Every launch after the chain's first may read the inputs no launch of the
+  // chain writes (weights, biases, positions, slots, table, ids) before its
+  // dependency wait. The first launch reads nothing before its wait: the
+  // caller's launch before it may have written any of them.
+  auto step_opts = [&]() {
     LaunchOpts n = o;
+    n.early_inputs = o.pdl && launched > 0;
+    return n;
+  };
+  auto norm_opts = [&]() {
+    LaunchOpts n = step_opts();
     n.early_residual = o.pdl && !prev_wrote_residual;
     return n;
   };
   const int64_t qd = c->n_heads * c->head_dim, I = c->intermediate;
-  int launched = 0;
   int rc = KLLM_B200_OK;
   // the embedding and layer 0's input norm run as one kernel when both are on
   const bool fuse_embedding = on(KLLM_B200_OP_EMBEDDING) && on(KLLM_B200_OP_INPUT_NORM);
   if (fuse_embedding) {
     rc = embedding_rms_norm(c->embed_table, c->vocab, H, c->ids, T, c->layers[0].input_norm_w, wdt, c->eps,
-                            c->residual, c->layers[0].attn_norm_out, c->err_flags, o);
+                            c->residual, c->layers[0].attn_norm_out, c->err_flags, step_opts());
     if (rc != KLLM_B200_OK) return rc;
     ++launched;
     prev_wrote_residual = true;
   } else if (on(KLLM_B200_OP_EMBEDDING)) {
     rc = embedding(c->embed_table, c->vocab, H, KLLM_B200_F16, c->ids, T, c->residual, KLLM_B200_F16,
-                   c->err_flags, o);
+                   c->err_flags, step_opts());
     if (rc != KLLM_B200_OK) return rc;
     ++launched;
     prev_wrote_residual = true;
@@ -114,7 +123,7 @@ extern "C" int kllm_b200_chain_run(const kllm_b200_chain* c, int* n_launches, vo
     } else if (on(KLLM_B200_OP_QKV_ROPE)) {
       rc = qkv_bias_rope_kv_append(L.q, L.k, L.v, L.q_bias, L.k_bias, L.v_bias, wdt, c->positions, c->slots, T,
                                    c->n_heads, c->n_kv_heads, c->head_dim, c->theta, L.k_cache, L.v_cache,
-                                   c->n_slots, c->max_seq, c->err_flags, o);
+                                   c->n_slots, c->max_seq, c->err_flags, step_opts());
       if (rc != KLLM_B200_OK) return rc;
       ++launched;
       prev_wrote_residual = false;

@@ -119,6 +119,14 @@ bool default_pdl();
 struct LaunchOpts {
   cudaStream_t stream = nullptr;
   bool pdl = default_pdl();
+  // Under PDL, read before the grid-dependency wait the inputs that no launch
+  // of the chain writes (norm weights, q/k/v biases, positions, cache slots,
+  // the embedding table and ids). Valid only when the launch directly before
+  // on the stream does not write them; the chain executor sets it for every
+  // launch after its first, since it knows what each of its launches writes.
+  // An individual entry point cannot know what the caller launched before it,
+  // so without this flag a kernel reads nothing before its wait.
+  bool early_inputs = false;
   // add_rms_norm under PDL: the residual was last written two or more
   // launches back on this stream (the previous launch leaves it alone), so
   // its rows may be read before the grid-dependency wait. Every kernel of

@@ -81,9 +81,15 @@ __global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __re
   extern __shared__ __align__(16) float4 s_w4[];          // the norm weight as fp32, two planes
   __shared__ float partial[2][kThreads / 32];
   // The norm weight is staged into shared memory as fp32 once per CTA and
-  // the output phase reads it from there. With EARLY (the PDL launch of the
-  // chain executor) the staging runs before the grid-dependency wait,
-  // overlapping the previous kernel's tail (no chain kernel writes the weight).
+  // the output phase reads it from there. With EARLY (a PDL launch of the
+  // chain executor after its first, whose predecessor writes no weight, table
+  // or ids) the staging runs before the grid-dependency wait, overlapping the
+  // previous kernel's tail. Without EARLY the kernel waits before its first
+  // global read (a no-op for a launch without PDL).
+  if (!EARLY) {
+    grid_dep_wait();
+    grid_dep_launch();
+  }
   const int wvec = hidden / kWv;
   const int wgroups = hidden >> 3;
   auto stage_weight = [&]() {
@@ -91,7 +97,7 @@ __global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __re
     for (int i = threadIdx.x; i < wvec; i += blockDim.x) stage_weight_vec<TW>(s_w4, wgroups, i, ld_keep(wsrc + i));
     __syncthreads();
   };
-  // Without PDL, a weight that fits one 16-byte vector per thread is loaded
+  // Without EARLY, a weight that fits one 16-byte vector per thread is loaded
   // into a register first and parked in shared memory after the first row
   // loads are issued, so the two round trips overlap; wider weights are
   // staged up front.
@@ -99,12 +105,12 @@ __global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __re
   uint4 wreg = make_uint4(0, 0, 0, 0);
   if (park && static_cast<int>(threadIdx.x) < wvec) wreg = ld_keep(reinterpret_cast<const uint4*>(weight) + threadIdx.x);
   if (!park) stage_weight();
-  // Under PDL a gathering launch issues its first rows' loads (table and
+  // With EARLY a gathering launch issues its first rows' loads (table and
   // ids, which no kernel of the chain writes) before the wait, and so does an
   // add launch for its residual rows when early_residual says the previous
   // launch did not write them; the delta always waits.
-  bool waited = EARLY && (GATHER || (HAS_DELTA && early_residual != 0)) ? false : true;
-  if (waited) {
+  bool waited = !(EARLY && (GATHER || (HAS_DELTA && early_residual != 0)));
+  if (EARLY && waited) {
     grid_dep_wait();
     grid_dep_launch();
   }
@@ -311,8 +317,8 @@ struct GatherArgs {
 template <int VPT, int GROUP, int NVEC, typename TW, int MODE>
 int launch_fast(void* residual, const void* src, const void* weight, void* out, int64_t rows, int hidden,
                 int group, float eps, const GatherArgs& ga, const LaunchOpts& o, const char* what) {
-  auto k = o.pdl ? add_rms_norm_f16_kernel<VPT, GROUP, NVEC, TW, MODE, true>
-                 : add_rms_norm_f16_kernel<VPT, GROUP, NVEC, TW, MODE, false>;
+  auto k = o.pdl && o.early_inputs ? add_rms_norm_f16_kernel<VPT, GROUP, NVEC, TW, MODE, true>
+                                   : add_rms_norm_f16_kernel<VPT, GROUP, NVEC, TW, MODE, false>;
   const int threads = group > kFastThreads ? group : kFastThreads;
   const int rows_per_cta = threads / group;
   const size_t smem = static_cast<size_t>(hidden) * sizeof(float);  // the weight staged as fp32

@@ -97,17 +97,22 @@ __device__ __forceinline__ uint4 add_bias8<float>(uint4 x, const float* bias, in
 // geometry becomes shifts), 0 for a runtime head_dim.
 //
 // Positions, slots and the frequency table are never written by a kernel of
-// the chain, so with EARLY (the PDL launch of the chain executor) the
-// position load and sincos run before the grid-dependency wait, overlapping
-// the previous kernel's tail, and only the activation loads wait. Without
-// PDL the activation loads are issued first and the sincos runs while they
-// are in flight.
+// the chain, so with EARLY (a PDL launch of the chain executor after its
+// first) the position load and sincos run before the grid-dependency wait,
+// overlapping the previous kernel's tail, and only the activation loads wait.
+// Without EARLY the kernel waits before its first global read (a no-op for a
+// launch without PDL), issues the activation loads and runs the sincos while
+// they are in flight.
 template <int DT, int UPL, typename TB, bool EARLY>
 __global__ void __launch_bounds__(kWarpThreads) qkv_rope_warp_kernel(const __grid_constant__ RopeArgs a) {
   __shared__ float s_freq[kMaxHalf];
   __shared__ __align__(16) float s_cos[kWarpsPerCta][kMaxHalf];
   __shared__ __align__(16) float s_sin[kWarpsPerCta][kMaxHalf];
 
+  if (!EARLY) {
+    grid_dep_wait();
+    grid_dep_launch();
+  }
   const int D = DT != 0 ? DT : a.head_dim;
   const int half = D >> 1;
   const int chunks = D >> 4;   // rotation units per head (8 pairs each)
@@ -174,11 +179,7 @@ __global__ void __launch_bounds__(kWarpThreads) qkv_rope_warp_kernel(const __gri
       }
     }
   };
-  if (!EARLY) {
-    grid_dep_wait();
-    grid_dep_launch();
-    issue_loads();
-  }
+  if (!EARLY) issue_loads();
 
   for (int i = threadIdx.x; i < half; i += blockDim.x) s_freq[i] = a.inv_freq[i];
   const TB* bq = static_cast<const TB*>(a.bq);
@@ -313,6 +314,10 @@ __global__ void __launch_bounds__(kWarpThreads) qkv_rope_token_kernel(const __gr
   static_assert((W & (W - 1)) == 0, "warps per token must be a power of two");
   __shared__ __align__(16) float s_cs[kWarpsPerCta][2][HALF];
 
+  if (!EARLY) {  // nothing is read before the wait (a no-op for a launch without PDL)
+    grid_dep_wait();
+    grid_dep_launch();
+  }
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int gw = blockIdx.x * kWarpsPerCta + warp;
@@ -321,7 +326,7 @@ __global__ void __launch_bounds__(kWarpThreads) qkv_rope_token_kernel(const __gr
   const bool live = t < a.n_tokens;  // uniform per warp
 
   // position and slot (never written by a kernel of the chain: loaded before
-  // the dependency wait under PDL)
+  // the dependency wait with EARLY)
   int32_t pos = 0, slot = 0;
   if (live) {
     pos = __ldg(a.positions + t);
@@ -385,11 +390,7 @@ __global__ void __launch_bounds__(kWarpThreads) qkv_rope_token_kernel(const __gr
       if (u < V) xv[j] = ld_stream(a.v + (t * HKV + u / VC) * D + (u % VC) * 8);
     }
   };
-  if (!EARLY) {
-    grid_dep_wait();
-    grid_dep_launch();
-    issue_loads();
-  }
+  if (!EARLY) issue_loads();
   // cos/sin of the token's HALF frequencies, HALF / 32 per lane
 #pragma unroll
   for (int d = lane; d < HALF; d += 32) {
@@ -545,14 +546,14 @@ __global__ void __launch_bounds__(kThreads) qkv_rope_generic_kernel(const __grid
 void fill_inv_freq(RopeArgs& a, float theta) { rope_inv_freq(a.inv_freq, a.head_dim, theta); }
 
 template <int DT, int UPL>
-void (*pick_tb(bool bias16, bool pdl))(RopeArgs) {
-  if (pdl) return bias16 ? qkv_rope_warp_kernel<DT, UPL, __half, true> : qkv_rope_warp_kernel<DT, UPL, float, true>;
+void (*pick_tb(bool bias16, bool early))(RopeArgs) {
+  if (early) return bias16 ? qkv_rope_warp_kernel<DT, UPL, __half, true> : qkv_rope_warp_kernel<DT, UPL, float, true>;
   return bias16 ? qkv_rope_warp_kernel<DT, UPL, __half, false> : qkv_rope_warp_kernel<DT, UPL, float, false>;
 }
 
 template <int D, int HQ, int HKV, int W>
-void (*pick_token_tb(bool bias16, bool pdl))(RopeArgs) {
-  if (pdl) {
+void (*pick_token_tb(bool bias16, bool early))(RopeArgs) {
+  if (early) {
     return bias16 ? qkv_rope_token_kernel<D, HQ, HKV, W, __half, true> : qkv_rope_token_kernel<D, HQ, HKV, W, float, true>;
   }
   return bias16 ? qkv_rope_token_kernel<D, HQ, HKV, W, __half, false> : qkv_rope_token_kernel<D, HQ, HKV, W, float, false>;
@@ -566,29 +567,29 @@ struct TokenKernel {
 // Head layouts (head_dim, q heads, kv heads) with a token kernel: Qwen2.5-0.5B,
 // Llama-2-7B, Qwen2.5-7B and Llama-3-8B. W (warps per token) keeps two to
 // three rotation units per lane. Other layouts take qkv_rope_warp_kernel.
-TokenKernel pick_token_kernel(int D, int hq, int hkv, bool bias16, bool pdl) {
-  if (D == 64 && hq == 14 && hkv == 2) return {pick_token_tb<64, 14, 2, 1>(bias16, pdl), 1};
-  if (D == 128 && hq == 32 && hkv == 32) return {pick_token_tb<128, 32, 32, 8>(bias16, pdl), 8};
-  if (D == 128 && hq == 28 && hkv == 4) return {pick_token_tb<128, 28, 4, 4>(bias16, pdl), 4};
-  if (D == 128 && hq == 32 && hkv == 8) return {pick_token_tb<128, 32, 8, 4>(bias16, pdl), 4};
+TokenKernel pick_token_kernel(int D, int hq, int hkv, bool bias16, bool early) {
+  if (D == 64 && hq == 14 && hkv == 2) return {pick_token_tb<64, 14, 2, 1>(bias16, early), 1};
+  if (D == 128 && hq == 32 && hkv == 32) return {pick_token_tb<128, 32, 32, 8>(bias16, early), 8};
+  if (D == 128 && hq == 28 && hkv == 4) return {pick_token_tb<128, 28, 4, 4>(bias16, early), 4};
+  if (D == 128 && hq == 32 && hkv == 8) return {pick_token_tb<128, 32, 8, 4>(bias16, early), 4};
   return {};
 }
 
 template <int DT>
-void (*pick_upl(int upl, bool bias16, bool pdl))(RopeArgs) {
+void (*pick_upl(int upl, bool bias16, bool early))(RopeArgs) {
   switch (upl) {
-    case 1: return pick_tb<DT, 1>(bias16, pdl);
-    case 2: return pick_tb<DT, 2>(bias16, pdl);
-    case 3: return pick_tb<DT, 3>(bias16, pdl);
-    default: return pick_tb<DT, 4>(bias16, pdl);
+    case 1: return pick_tb<DT, 1>(bias16, early);
+    case 2: return pick_tb<DT, 2>(bias16, early);
+    case 3: return pick_tb<DT, 3>(bias16, early);
+    default: return pick_tb<DT, 4>(bias16, early);
   }
 }
 
 // head_dim 64 and 128 get compile-time unit geometry; others the runtime form.
-void (*pick_warp_kernel(int head_dim, int upl, bool bias16, bool pdl))(RopeArgs) {
-  if (head_dim == 64) return pick_upl<64>(upl, bias16, pdl);
-  if (head_dim == 128) return pick_upl<128>(upl, bias16, pdl);
-  return pick_upl<0>(upl, bias16, pdl);
+void (*pick_warp_kernel(int head_dim, int upl, bool bias16, bool early))(RopeArgs) {
+  if (head_dim == 64) return pick_upl<64>(upl, bias16, early);
+  if (head_dim == 128) return pick_upl<128>(upl, bias16, early);
+  return pick_upl<0>(upl, bias16, early);
 }
 
 int run_rope(RopeArgs& a, int act_dtype, int bias_dtype, const LaunchOpts& o, const char* what) {
@@ -599,7 +600,8 @@ int run_rope(RopeArgs& a, int act_dtype, int bias_dtype, const LaunchOpts& o, co
                     al(a.bk) && al(a.bv) && al(a.k_cache) && al(a.v_cache);
   if (fast && a.k != nullptr && a.v != nullptr && a.k_cache != nullptr && a.v_cache != nullptr &&
       a.positions != nullptr && a.slots != nullptr) {
-    const TokenKernel tk = pick_token_kernel(D, a.n_heads, a.n_kv_heads, bias16, o.pdl);
+    const bool early = o.pdl && o.early_inputs;
+    const TokenKernel tk = pick_token_kernel(D, a.n_heads, a.n_kv_heads, bias16, early);
     const int64_t widest = a.n_heads > a.n_kv_heads ? a.n_heads : a.n_kv_heads;
     // token-row offsets are 32-bit in the kernel
     if (tk.kernel != nullptr && a.n_tokens * tk.warps_per_token < (int64_t{1} << 30) &&
@@ -618,7 +620,7 @@ int run_rope(RopeArgs& a, int act_dtype, int bias_dtype, const LaunchOpts& o, co
     a.warps_per_token = wpt;
     const int64_t warps = a.n_tokens * wpt;
     const unsigned grid = static_cast<unsigned>((warps + kWarpsPerCta - 1) / kWarpsPerCta);
-    void (*k)(RopeArgs) = pick_warp_kernel(D, upl, bias16, o.pdl);
+    void (*k)(RopeArgs) = pick_warp_kernel(D, upl, bias16, o.pdl && o.early_inputs);
     return launch_status(launch(k, grid, kWarpThreads, 0, o.stream, o.pdl, a), what);
   }
   const int per_tok = a.n_heads * (D / 2) + (a.k ? a.n_kv_heads * (D / 2) : 0) + (a.v ? a.n_kv_heads * D : 0);
