@@ -176,6 +176,19 @@ __device__ __forceinline__ void st_stream(void* p, uint4 v) {
                : "memory");
 }
 
+// Asks L2 to fetch [p, p + bytes) from memory (p 16-byte aligned, bytes a
+// multiple of 16). A cache hint that returns no data: it may be issued before
+// the grid-dependency wait for memory the previous kernel is still writing,
+// since the loads after the wait read the coherent values either way.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Asks L2 for the line holding `p` (a hint, as above).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 // Pull the line holding `p` into L1 ahead of a later load.
 __device__ __forceinline__ void prefetch_l1(const void* p) {
   asm volatile("prefetch.global.L1 [%0];" ::"l"(p));

@@ -26,13 +26,26 @@ template <int UNROLL>
 __global__ void __launch_bounds__(kThreads) silu_mul_f16_kernel(const __half* __restrict__ gate,
                                                                 const __half* __restrict__ up,
                                                                 __half* __restrict__ out, int64_t n) {
-  grid_dep_wait();
-  grid_dep_launch();
   const int64_t nvec = n >> 3;
   const uint4* g = reinterpret_cast<const uint4*>(gate);
   const uint4* u = reinterpret_cast<const uint4*>(up);
   uint4* y = reinterpret_cast<uint4*>(out);
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  // this CTA's first gate and up vectors into L2 while the previous kernel
+  // drains (a hint; they are read after the wait)
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int k = 0; k < UNROLL; ++k) {
+      const int64_t v0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + k * stride;
+      if (v0 < nvec) {
+        const int64_t cnt = nvec - v0 < blockDim.x ? nvec - v0 : blockDim.x;
+        prefetch_l2_bulk(g + v0, static_cast<uint32_t>(cnt * 16));
+        prefetch_l2_bulk(u + v0, static_cast<uint32_t>(cnt * 16));
+      }
+    }
+  }
+  grid_dep_wait();
+  grid_dep_launch();
   int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   for (; i + (UNROLL - 1) * stride < nvec; i += UNROLL * stride) {
     uint4 gv[UNROLL], uv[UNROLL];

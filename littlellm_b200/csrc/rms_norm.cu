@@ -86,6 +86,17 @@ __global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __re
   // or ids) the staging runs before the grid-dependency wait, overlapping the
   // previous kernel's tail. Without EARLY the kernel waits before its first
   // global read (a no-op for a launch without PDL).
+  // the delta rows (or the ids) of this CTA's first row group into L2 while
+  // the previous kernel drains (a hint that returns no data)
+  if (threadIdx.x == 0 && (HAS_DELTA || GATHER)) {
+    const int rpc = blockDim.x / (GROUP != 0 ? GROUP : group_arg);
+    const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rpc;
+    if (r0 < rows) {
+      const int64_t nr = rows - r0 < rpc ? rows - r0 : rpc;
+      if (HAS_DELTA) prefetch_l2_bulk(src + r0 * hidden, static_cast<uint32_t>(nr * hidden * 2));
+      if (GATHER) prefetch_l2(ids + r0);
+    }
+  }
   if (!EARLY) {
     grid_dep_wait();
     grid_dep_launch();

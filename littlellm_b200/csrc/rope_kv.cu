@@ -50,6 +50,7 @@ struct RopeArgs {
   int64_t n_slots, max_seq;
   int32_t* err_flags;
   int warps_per_token;
+  int prefetch;  // launched with PDL: ask L2 for the token rows before the dependency wait
   float inv_freq[kMaxHalf];
 };
 
@@ -314,16 +315,24 @@ __global__ void __launch_bounds__(kWarpThreads) qkv_rope_token_kernel(const __gr
   static_assert((W & (W - 1)) == 0, "warps per token must be a power of two");
   __shared__ __align__(16) float s_cs[kWarpsPerCta][2][HALF];
 
-  if (!EARLY) {  // nothing is read before the wait (a no-op for a launch without PDL)
-    grid_dep_wait();
-    grid_dep_launch();
-  }
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int gw = blockIdx.x * kWarpsPerCta + warp;
   const int t = gw / W;
   const int part = gw % W;
   const bool live = t < a.n_tokens;  // uniform per warp
+  // under PDL, the token's q, k and v rows into L2 while the previous kernel
+  // drains (a hint that returns no data; the rows are read after the wait).
+  // Without PDL the loads follow at once and the hint would only duplicate them.
+  if (a.prefetch != 0 && live && part == 0 && lane == 0) {
+    prefetch_l2_bulk(a.q + static_cast<int64_t>(t) * HQ * D, HQ * D * 2);
+    prefetch_l2_bulk(a.k + static_cast<int64_t>(t) * HKV * D, HKV * D * 2);
+    prefetch_l2_bulk(a.v + static_cast<int64_t>(t) * HKV * D, HKV * D * 2);
+  }
+  if (!EARLY) {  // nothing is read before the wait (a no-op for a launch without PDL)
+    grid_dep_wait();
+    grid_dep_launch();
+  }
 
   // position and slot (never written by a kernel of the chain: loaded before
   // the dependency wait with EARLY)
@@ -601,6 +610,7 @@ int run_rope(RopeArgs& a, int act_dtype, int bias_dtype, const LaunchOpts& o, co
   if (fast && a.k != nullptr && a.v != nullptr && a.k_cache != nullptr && a.v_cache != nullptr &&
       a.positions != nullptr && a.slots != nullptr) {
     const bool early = o.pdl && o.early_inputs;
+    a.prefetch = o.pdl ? 1 : 0;
     const TokenKernel tk = pick_token_kernel(D, a.n_heads, a.n_kv_heads, bias16, early);
     const int64_t widest = a.n_heads > a.n_kv_heads ? a.n_heads : a.n_kv_heads;
     // token-row offsets are 32-bit in the kernel
