@@ -511,9 +511,7 @@ int kllm_b200_kllm_load(const char* path, const kllm_b200_kllm_record* records, 
  * KLLM_B200_ERR_CAPACITY before any GPU work. The array's device address
  * belongs to the CUDA context current at the call, so every call looks it up
  * (cudaGetSymbolAddress) in that context; the first call in a context loads
- * the library's module there and should come before any stream capture.
- * Inside a stream capture host_data must be pinned (a capture does not
- * accept a copy from pageable memory). All calls share the array, so calls
+ * the library's module there. All calls share the array, so calls
  * that overlap on the GPU race; run them in one stream order. host_data must
  * not change until the stream has passed the copy (pinned memory is read
  * asynchronously). This entry point has no counterpart in the reference. */

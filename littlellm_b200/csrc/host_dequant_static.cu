@@ -17,8 +17,8 @@
 // host that runs its own (non-primary) context, or a cudaDeviceReset between
 // calls, gives the array a different address. So the lookup is done on every
 // call; once the library's module is loaded in that context it is a
-// host-side table lookup. The first call in a context loads the module and
-// should come before any stream capture. Every call uses the same array: the
+// host-side table lookup; the first call in a context loads the module.
+// Every call uses the same array: the
 // copy of a call's int8 bytes overwrites the previous contents entirely
 // (nothing needs to start at zero), and calls that overlap on the GPU
 // (different streams, or different host threads on the same device) race

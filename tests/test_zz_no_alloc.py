@@ -96,8 +96,7 @@ def test_capacity_limit(cuda, ops):
 
 
 def test_pinned_host_buffer(cuda, ops, oracle):
-    """A pinned host buffer (the form a stream capture needs) gives the same
-    bits as a pageable one."""
+    """A pinned host buffer gives the same bits as a pageable one."""
     from littlellm_b200 import _capi
     rng = np.random.default_rng(31)
     q = rng.integers(-128, 128, 777_777, dtype=np.int8)
