@@ -377,7 +377,7 @@ def run_reference(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak" if args.workload == "qwen_prefill" else "strong", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic",
-        "config": {"workload": w.name, "model": w.model.name, "layers": w.model.n_layers,
+        "config": {"workload": w.name, "shapes": w.model.name, "layers": w.model.n_layers,
                    "tokens_per_step": threads * tokens, "impl_detail": "reference CPU operators (src/op/cpu)"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind, "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -1011,7 +1011,7 @@ def run_attention(args):
             "metric": ATTN_METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak" if weak else "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-            "config": {"workload": args.workload, "model": m.name, "layers": L, "tokens_per_gpu": T,
+            "config": {"workload": args.workload, "shapes": m.name, "layers": L, "tokens_per_gpu": T,
                        "sequences_per_gpu": B, "seq_len": w.seq_len,
                        "kv_cache": [L, 2, B, m.n_kv_heads, S, m.head_dim],
                        "positions": "U[0, %d)" % (S - 1) if w.decode else "0..%d per sequence" % (w.seq_len - 1),
@@ -1041,7 +1041,7 @@ def run_reference_attention(args):
     emit({"metric": ATTN_METRIC, "value": value, "unit": "tokens/s", "impl": "reference", "n_gpus": args.gpus,
           "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * statistics.mean(st),
           "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-          "config": {"workload": args.workload, "model": w.model.name, "layers": L,
+          "config": {"workload": args.workload, "shapes": w.model.name, "layers": L,
                      "tokens_per_step": threads * tokens,
                      "impl_detail": "reference kllm::op::attention on CPU tensors (src/op/cpu/attention.cpp)"},
           "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": kind,
@@ -1314,7 +1314,7 @@ def run_gemm(args):
             "metric": GEMM_METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak" if weak else "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-            "config": {"workload": args.workload, "model": m.name, "layers": L, "tokens_per_gpu": T,
+            "config": {"workload": args.workload, "shapes": m.name, "layers": L, "tokens_per_gpu": T,
                        "gemm": [T, 2 * I, H], "parallelism": f"dp{world} (token rows split, no collective)",
                        "math": "fp16 operands, fp32 accumulate (tcgen05 TMEM), fp16 gate/up rounding then SwiGLU "
                                "in fp32, fp16 out",
@@ -1342,7 +1342,7 @@ def run_reference_gemm(args):
     emit({"metric": GEMM_METRIC, "value": value, "unit": "tokens/s", "impl": "reference", "n_gpus": args.gpus,
           "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * statistics.mean(st),
           "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-          "config": {"workload": args.workload, "model": m.name, "layers": L, "tokens_per_step": threads * rows,
+          "config": {"workload": args.workload, "shapes": m.name, "layers": L, "tokens_per_step": threads * rows,
                      "impl_detail": "reference linear() (kllm::op::matmul, CPU) x2 + silu_mul on CPU F32 tensors"},
           "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": kind,
                            "sample": f"{threads} threads x {rows} token row(s) each through {L} layers per step"},
@@ -1691,7 +1691,7 @@ def run_ours(args):
             "scaling": "weak" if weak else "strong", "vs_baseline": None, "dtype": "f16",
             "data": "synthetic",
             "config": {
-                "workload": w.name, "model": w.model.name, "layers": n_layers,
+                "workload": w.name, "shapes": w.model.name, "layers": n_layers,
                 "tokens_per_gpu": w.n_tokens, "sequences_per_gpu": w.n_seqs, "seq_len": w.seq_len,
                 "kv_cache": [n_layers, 2, w.n_seqs, w.model.n_kv_heads, w.max_seq, w.model.head_dim],
                 "parallelism": f"dp{world} (sequences split, no collective on the path)",
@@ -1899,7 +1899,7 @@ def run_forward(args):
             "metric": FORWARD_METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak" if weak else "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-            "config": {"workload": w.name, "model": m.name, "layers": L, "tokens_per_gpu": T,
+            "config": {"workload": w.name, "shapes": m.name, "layers": L, "tokens_per_gpu": T,
                        "sequences_per_gpu": w.n_seqs, "seq_len": w.seq_len,
                        "kv_cache": [L, 2, w.n_seqs, m.n_kv_heads, w.max_seq, m.head_dim],
                        "weights": "random, N(0, 1/fan_in), fp16", "parallelism": f"dp{world} (sequences split)",
@@ -2005,7 +2005,7 @@ def run_generate(args):
         "metric": GENERATE_METRIC, "value": B / (ms * 1e-3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": {"workload": args.workload, "model": m.name, "layers": L, "sequences": B,
+        "config": {"workload": args.workload, "shapes": m.name, "layers": L, "sequences": B,
                    "prompt_tokens": w.seq_len, "decode_positions": [w.seq_len + 1, last_pos],
                    "weights": "random, N(0, 1/fan_in), fp16", "cuda_graph": True, "pdl": True,
                    "ids": "seeded random per step (no sampler)"},
