@@ -81,7 +81,8 @@ int kllm_b200_version(void);
  * With enable != 0 the entry points launch with programmatic dependent launch:
  * a kernel's CTAs may be scheduled while the previous kernel on the stream
  * drains, and they wait for it to complete (griddepcontrol.wait) before their
- * first global read, so the mode is correct whatever the previous kernel
+ * first global read (before it they only ask L2 to prefetch, a hint that
+ * returns no data), so the mode is correct whatever the previous kernel
  * wrote. (Only kllm_b200_chain_run, which knows what each of its launches
  * writes, also reads weights, biases, positions, slots, tables and ids before
  * that wait.) A runner that calls the operators one by one (the C++ binding
