@@ -120,8 +120,8 @@ def test_dequant_golden(ops, golden):
 # ---------------------------------------------------------------------------
 
 
-@pytest.mark.parametrize("rows,hidden", [(512, 896), (64, 4096), (33, 2048), (7, 40), (5, 900), (3, 7),
-                                         (1, 16384), (2, 17000), (0, 896)])
+@pytest.mark.parametrize("rows,hidden", [(512, 896), (513, 896), (64, 4096), (5, 4096), (33, 2048), (7, 40),
+                                         (5, 900), (3, 7), (1, 16384), (2, 17000), (0, 896)])
 @pytest.mark.parametrize("with_delta", [True, False])
 def test_add_rms_norm_oracle(ops, oracle, rows, hidden, with_delta):
     rng = np.random.default_rng(rows * 7919 + hidden)
