@@ -3,7 +3,9 @@
 // Hot path: fp16 with 16-byte aligned buffers -> grid-stride kernels moving
 // 16 B per load (8 halves), UNROLL independent vectors per thread in flight,
 // grid = one wave of resident CTAs. Other dtypes or alignments take the
-// generic element-per-thread kernels (same arithmetic).
+// generic element-per-thread kernels (same arithmetic). SwiGLU asks L2 for a
+// CTA's first gate and up vectors before its grid-dependency wait (a hint
+// that returns no data).
 #include "common.cuh"
 
 namespace kb {

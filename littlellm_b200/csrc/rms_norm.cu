@@ -23,8 +23,13 @@
 // (src/model/llama.cpp:84 then :83-87 of the next layer loop). The gathered
 // row is never re-read from HBM, and the result is bit-identical to the
 // embedding followed by rms_norm. The table and the ids are never written by
-// a kernel of the chain, so under PDL the row loads are issued before the
-// grid-dependency wait.
+// a kernel of the chain, so a launch with EARLY (a chain launch after the
+// chain's first) issues the row loads before the grid-dependency wait; the
+// chain's first launch and the individual entry point load them after it.
+//
+// Before the wait (any launch), thread 0 of a CTA asks L2 for the delta rows
+// (or the ids) of its first row group: a hint that returns no data, so it is
+// correct whatever the previous kernel is still writing.
 #include "ops.cuh"
 
 namespace kb {
