@@ -41,3 +41,14 @@ def test_reference_arm_does_not_map_the_product_library():
     assert line["impl"] == "reference"
     assert line["value"] > 0
     assert line["cpu_baseline"]["kind"] == "reference"
+
+
+def test_reference_arm_other_ranks_exit_quietly():
+    """Under torchrun only rank 0 runs the reference arm; every other rank exits
+    0 at once, prints no line and joins no process group."""
+    env = dict(os.environ, PYTHONPATH=ROOT, RANK="1", LOCAL_RANK="1", WORLD_SIZE="2",
+               MASTER_ADDR="127.0.0.1", MASTER_PORT="1")
+    r = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--gpus", "2", "--steps", "1",
+                        "--warmup", "0"], cwd=ROOT, env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert r.stdout.strip() == ""
