@@ -1445,7 +1445,9 @@ def embedding_chain_timing(runner, stream, reps: int) -> dict:
         d.layers = ctypes_cast_layers(runner._layer_arr)
     nbytes = 3 * T * H * 2 + 4 * T
     return {"us_per_launch": ms * 1000.0, "bytes_per_launch": nbytes, "gbs": nbytes / (ms * 1e-3) / 1e9,
-            "launches_per_replay": n, "kernels_per_call": n // len(L)}
+            "launches_per_replay": n, "kernels_per_call": n // len(L),
+            "note": "each call's launch is a chain's first: it reads its ids and table rows only after "
+                    "its dependency wait (the launch before a chain may have written them)"}
 
 
 def ctypes_cast_layers(arr):
