@@ -85,14 +85,8 @@ __global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __re
   constexpr int kWv = 16 / static_cast<int>(sizeof(TW));  // weight values per 16-byte vector
   extern __shared__ __align__(16) float4 s_w4[];          // the norm weight as fp32, two planes
   __shared__ float partial[2][kThreads / 32];
-  // The norm weight is staged into shared memory as fp32 once per CTA and
-  // the output phase reads it from there. With EARLY (a PDL launch of the
-  // chain executor after its first, whose predecessor writes no weight, table
-  // or ids) the staging runs before the grid-dependency wait, overlapping the
-  // previous kernel's tail. Without EARLY the kernel waits before its first
-  // global read (a no-op for a launch without PDL).
-  // the delta rows (or the ids) of this CTA's first row group into L2 while
-  // the previous kernel drains (a hint that returns no data)
+  // The delta rows (or the ids) of this CTA's first row group into L2 while
+  // the previous kernel drains (a hint that returns no data).
   if (threadIdx.x == 0 && (HAS_DELTA || GATHER)) {
     const int rpc = blockDim.x / (GROUP != 0 ? GROUP : group_arg);
     const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rpc;
@@ -102,6 +96,12 @@ __global__ void __launch_bounds__(kThreads) add_rms_norm_f16_kernel(__half* __re
       if (GATHER) prefetch_l2(ids + r0);
     }
   }
+  // The norm weight is staged into shared memory as fp32 once per CTA and
+  // the output phase reads it from there. With EARLY (a PDL launch of the
+  // chain executor after its first, whose predecessor writes no weight, table
+  // or ids) the staging runs before the grid-dependency wait, overlapping the
+  // previous kernel's tail. Without EARLY the kernel waits before its first
+  // global read (a no-op for a launch without PDL).
   if (!EARLY) {
     grid_dep_wait();
     grid_dep_launch();
